@@ -1,0 +1,53 @@
+// One sparse-attention decode step: indexer scores -> exact top-k -> sparse MLA
+// attention -> LSE combine, enqueued as four kernels chained with programmatic
+// dependent launch so each kernel's prologue (barrier set-up, TMEM allocation)
+// overlaps the tail of its predecessor.  Replaces, per layer, the host loop of
+// AttentionState.select -> TiledIndexer.select (index_selection.py:79-124)
+// followed by forward_mqa's id assembly and sparse_attention call
+// (vllm_attention.py:231-262).
+#include "common.cuh"
+#include "host_common.h"
+
+namespace {
+inline int64_t round_up(int64_t x, int64_t m) { return (x + m - 1) / m * m; }
+}  // namespace
+
+extern "C" size_t dsr_decode_workspace_bytes(int64_t batch, int64_t max_visible, int64_t heads,
+                                             int64_t k) {
+  const int64_t stride = round_up(max_visible > 0 ? max_visible : 1, 64);
+  return size_t(batch) * size_t(stride) * 4 + dsr::mla_workspace_bytes(batch, heads, k) + 256;
+}
+
+extern "C" int dsr_decode_step(const float* idx_q, const float* idx_w, int64_t idx_heads,
+                               const uint16_t* index_pool, const float* q,
+                               const uint16_t* kv_pool, int64_t heads, int64_t pool_blocks,
+                               const int32_t* block_table, int64_t table_stride,
+                               const int32_t* visible, int64_t max_visible, int64_t k,
+                               const uint16_t* swa, const int32_t* swa_len, const float* sink,
+                               float scale, float* out, int32_t* topk_out, float* scores_out,
+                               void* workspace, size_t workspace_bytes, int32_t* err,
+                               int64_t batch, void* stream) {
+  using namespace dsr;
+  clear_error();
+  DSR_REQUIRE(workspace != nullptr, "decode_step: workspace is required");
+  DSR_REQUIRE(max_visible > 0 && max_visible <= table_stride * 64,
+              "decode_step: max_visible %lld outside [1, table capacity %lld]",
+              (long long)max_visible, (long long)(table_stride * 64));
+  const size_t need = dsr_decode_workspace_bytes(batch, max_visible, heads, k);
+  DSR_REQUIRE(workspace_bytes >= need, "decode_step: workspace %zu < %zu bytes", workspace_bytes,
+              need);
+  const int64_t stride = round_up(max_visible, 64);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  float* scores = scores_out != nullptr ? scores_out : reinterpret_cast<float*>(ws);
+  uint8_t* mla_ws = ws + size_t(batch) * stride * 4;
+  const size_t mla_bytes = workspace_bytes - size_t(batch) * stride * 4;
+  const cudaStream_t s = as_stream(stream);
+  int rc = launch_indexer_decode(idx_q, idx_w, index_pool, pool_blocks, block_table, table_stride,
+                                 visible, scores, stride, err, batch, idx_heads, s, false);
+  if (rc != DSR_OK) return rc;
+  rc = launch_topk(scores, nullptr, visible, topk_out, nullptr, err, batch, stride, k, 0, s, true);
+  if (rc != DSR_OK) return rc;
+  return launch_mla_decode(q, kv_pool, pool_blocks, block_table, table_stride, visible, topk_out, k,
+                           swa, swa_len, sink, scale, out, mla_ws, mla_bytes, err, batch, heads, s,
+                           true);
+}

@@ -1,0 +1,58 @@
+// Host-side helpers shared by the C-ABI translation units.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <string>
+
+#include "../../include/dsr_b200.h"
+
+namespace dsr {
+
+// Records a message for dsr_last_error() and returns `code`.
+int fail(int code, const char* fmt, ...);
+// Clears the calling thread's message.
+void clear_error();
+// Converts a pending launch error into DSR_ECUDA.
+int launch_status(const char* what);
+// Multiprocessor count of the current device (cached per device).
+int sm_count();
+// Encodes a 2-D bf16 tensor map (row-major [outer, inner]) with 128-byte swizzle.
+int encode_tmap_bf16_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer,
+                        uint32_t box_inner, uint32_t box_outer);
+
+inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+#define DSR_REQUIRE(cond, ...)                      \
+  do {                                              \
+    if (!(cond)) return ::dsr::fail(DSR_EINVAL, __VA_ARGS__); \
+  } while (0)
+
+// Launch helpers implemented by the kernel translation units.
+int launch_topk(const float* scores, const int32_t* ids, const int32_t* lengths, int32_t* out_ids,
+                float* out_scores, int32_t* err, int64_t rows, int64_t row_stride, int64_t k,
+                int64_t id_base, cudaStream_t stream, bool pdl);
+int launch_indexer_decode(const float* q, const float* weights, const uint16_t* index_pool,
+                          int64_t pool_blocks, const int32_t* block_table, int64_t table_stride,
+                          const int32_t* visible, float* scores, int64_t score_stride,
+                          int32_t* err, int64_t batch, int64_t heads, cudaStream_t stream,
+                          bool pdl);
+int launch_mla_decode(const float* q, const uint16_t* kv_pool, int64_t pool_blocks,
+                      const int32_t* block_table, int64_t table_stride, const int32_t* visible,
+                      const int32_t* topk, int64_t k, const uint16_t* swa,
+                      const int32_t* swa_len, const float* sink, float scale, float* out,
+                      void* workspace, size_t workspace_bytes, int32_t* err, int64_t batch,
+                      int64_t heads, cudaStream_t stream, bool pdl);
+size_t mla_workspace_bytes(int64_t batch, int64_t heads, int64_t k);
+int launch_lse_combine(const float* part_o, const float* part_m, const float* part_l,
+                       int64_t parts, const float* sink, float* out, float* out_m, float* out_l,
+                       int32_t* err, int64_t batch, int64_t heads, int64_t dv,
+                       cudaStream_t stream, bool pdl);
+
+}  // namespace dsr

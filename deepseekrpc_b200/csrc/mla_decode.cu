@@ -1,0 +1,478 @@
+// Sparse MLA decode attention over the SWA ring plus the top-k selected rows of a
+// paged BF16 KV pool, and the log-sum-exp combine of its partials (sm_100a).
+//
+// Reference equation (native/operations.cu:30-82, reference_attention.py:13-31):
+//   out[b,h] = sum_i e^{s_i} v_i / (e^{sink_h} + sum_i e^{s_i}),  s_i = scale * q[b,h].k_i
+// over the selected rows i (duplicates count, -1 skipped), with v_i = k_i.  The
+// MLA value is the leading 512 latent columns of the 576-wide row, so the
+// output is out[..., :512] of the reference equation.
+//
+// mla_decode_kernel: grid (tiles, batch, head groups); one CTA handles one
+// 128-row tile (tile 0 = SWA window, tiles 1.. = consecutive 128 top-k ids).
+//   warps 0..3  gather the 128 rows (cp.async, 128-byte swizzle), convert the
+//               FP32 query to BF16, softmax of the tile, partial output store
+//   warp 4      TMEM allocator + tcgen05.mma issuer
+//   S^T[key, h]  = K[key,:576] . Q[h,:576]          (M=128 keys, N=heads)
+//   O^T[d, h]    = sum_key V[key,d] P[h,key]         (M=128 dims x 4, N=heads)
+// The KV tile in shared memory serves both products: K-major A operand for S^T
+// and MN-major A operand (V^T) for O^T, so each selected row is read once.
+// Partials (m in log2 units, l, unnormalised o) go to the workspace and
+// lse_combine_kernel merges them with the sink.
+#include "common.cuh"
+#include "host_common.h"
+
+#include <math_constants.h>
+
+namespace dsr {
+namespace {
+
+constexpr int kMlaTile = 128;
+constexpr int kMlaD = DSR_KV_DIM;   // 576
+constexpr int kMlaDv = DSR_V_DIM;   // 512
+constexpr int kMlaBlocks = kMlaD / 64;  // 9 column blocks of 64
+constexpr int kMlaThreads = 160;
+constexpr float kLog2e = 1.4426950408889634f;
+
+template <int HG>
+struct MlaLayout {
+  static constexpr int kKvOff = 0;                         // 9 x 16 KiB
+  static constexpr int kQOff = kMlaBlocks * 16384;         // 9 x HG x 128 B
+  static constexpr int kQBytes = kMlaBlocks * HG * 128;
+  static constexpr int kSPitch = kMlaTile + 1;             // transposed scores, words
+  static constexpr int kPOff = kQOff + ((HG * kSPitch * 4 + 1023) / 1024) * 1024;  // P^T
+  static constexpr int kRedOff = kQOff + kQBytes;
+  static constexpr int kTpk = kMlaTile / HG;               // threads per head
+  static constexpr int kRedBytes = 2 * kTpk * HG * 4;
+  static constexpr int kValidOff = kRedOff + kRedBytes;
+  static constexpr int kBarOff = kValidOff + kMlaTile * 4;
+  static constexpr int kMiscOff = kBarOff + 4 * 8;
+  static constexpr int kBytes = kMiscOff + 16;
+  static constexpr int kAlloc = kBytes + 1024;
+  static constexpr uint32_t kTmemCols = 5 * HG <= 128 ? 128 : (5 * HG <= 256 ? 256 : 512);
+  static_assert(kPOff + 2 * HG * 128 <= kRedOff, "P^T must fit in the query region");
+};
+
+template <int HG>
+__global__ void __launch_bounds__(kMlaThreads, 1)
+    mla_decode_kernel(const float* __restrict__ q, const uint16_t* __restrict__ kv_pool,
+                      int64_t pool_blocks, const int32_t* __restrict__ block_table,
+                      int64_t table_stride, const int32_t* __restrict__ visible,
+                      const int32_t* __restrict__ topk, int k, const uint16_t* __restrict__ swa,
+                      const int32_t* __restrict__ swa_len, float scale_log2,
+                      float* __restrict__ part_o, float* __restrict__ part_m,
+                      float* __restrict__ part_l, int32_t* err, int heads) {
+  using L = MlaLayout<HG>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  const uint32_t sbase = smem_u32(smem);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBarOff);
+  uint64_t* bar_kv = bars + 0;  // rows gathered + Q converted (128 arrivals)
+  uint64_t* bar_s = bars + 1;   // S^T complete (commit)
+  uint64_t* bar_p = bars + 2;   // P^T written (128 arrivals)
+  uint64_t* bar_o = bars + 3;   // O^T complete (commit)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kMiscOff);
+  volatile int* abort = reinterpret_cast<volatile int*>(smem + L::kMiscOff + 4);
+  int* valid = reinterpret_cast<int*>(smem + L::kValidOff);
+  float* red = reinterpret_cast<float*>(smem + L::kRedOff);
+
+  const int tile = blockIdx.x, b = blockIdx.y, hg = blockIdx.z;
+  const int tiles = gridDim.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int h0 = hg * HG;
+
+  if (threadIdx.x == 0) {
+    mbar_init(bar_kv, 128);
+    mbar_init(bar_s, 1);
+    mbar_init(bar_p, 128);
+    mbar_init(bar_o, 1);
+    *abort = 0;
+    fence_barrier_init();
+  }
+  if (warp == 4) {
+    tmem_alloc(tmem_slot, L::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const uint32_t tmem_s = tmem_base;
+  const uint32_t tmem_o = tmem_base + HG;
+
+  pdl_wait();  // top-k ids come from the preceding kernel
+
+  if (warp < 4) {
+    const int t = threadIdx.x;  // key slot of this thread == TMEM lane
+    // ---- resolve the row of key t
+    const uint16_t* src = nullptr;
+    if (tile == 0) {
+      int len = swa_len[b];
+      if (len < 0 || len > DSR_SWA_ROWS) {
+        if (t == 0) flag(err, DSR_ERR_ID);
+        len = 0;
+      }
+      if (t < len) src = swa + (int64_t(b) * DSR_SWA_ROWS + t) * kMlaD;
+    } else {
+      const int idx = (tile - 1) * kMlaTile + t;
+      if (idx < k) {
+        const int id = topk[int64_t(b) * k + idx];
+        if (id != -1) {
+          if (id < 0 || id >= visible[b]) {
+            flag(err, DSR_ERR_ID);
+          } else {
+            const int64_t blk = block_table[int64_t(b) * table_stride + (id >> 6)];
+            if (blk < 0 || blk >= pool_blocks) flag(err, DSR_ERR_ID);
+            else src = kv_pool + (blk * 64 + (id & 63)) * kMlaD;
+          }
+        }
+      }
+    }
+    valid[t] = src != nullptr;
+    // ---- gather: warp w copies rows 32w..32w+31, one row at a time (coalesced)
+    const uint64_t my_src = reinterpret_cast<uint64_t>(src);
+    for (int i = 0; i < 32; ++i) {
+      const int r = warp * 32 + i;
+      const uint64_t rs = __shfl_sync(0xffffffffu, my_src, i);
+      for (int j = lane; j < 72; j += 32) {
+        const int c = j >> 3, ch = j & 7;
+        const uint32_t dst = sbase + L::kKvOff + c * 16384 + r * 128 + ((ch ^ (r & 7)) << 4);
+        if (rs != 0) {
+          cp_async16(dst, reinterpret_cast<const uint16_t*>(rs) + j * 8);
+        } else {
+          asm volatile("st.shared.v4.u32 [%0], {%1,%1,%1,%1};" ::"r"(dst), "r"(0u) : "memory");
+        }
+      }
+    }
+    cp_async_commit();
+    // ---- query: FP32 -> BF16, 128-byte swizzled K-major, 9 column blocks of HG rows
+    {
+      const float4* qsrc = reinterpret_cast<const float4*>(q + (int64_t(b) * heads + h0) * kMlaD);
+      uint8_t* qs = smem + L::kQOff;
+      for (int i = t; i < HG * (kMlaD / 4); i += 128) {
+        const int h = i / (kMlaD / 4), d = (i % (kMlaD / 4)) * 4;
+        const float4 x = qsrc[i];
+        const uint32_t lo = __bfloat16_as_ushort(__float2bfloat16_rn(x.x)) |
+                            (uint32_t(__bfloat16_as_ushort(__float2bfloat16_rn(x.y))) << 16);
+        const uint32_t hi = __bfloat16_as_ushort(__float2bfloat16_rn(x.z)) |
+                            (uint32_t(__bfloat16_as_ushort(__float2bfloat16_rn(x.w))) << 16);
+        *reinterpret_cast<uint2*>(qs + (d >> 6) * (HG * 128) + sw128_offset(h, d & 63)) =
+            make_uint2(lo, hi);
+      }
+    }
+    cp_async_wait_all();
+    fence_proxy_async_smem();
+    mbar_arrive(bar_kv);
+
+    // ---- scores of key t for the HG heads -> transposed fp32 buffer (query region)
+    bool ok = mbar_wait(bar_s, 0, abort, err);
+    float* sT = reinterpret_cast<float*>(smem + L::kQOff);  // [HG][kSPitch]
+    if (ok) {
+      tc_fence_after();
+      const bool v = valid[t] != 0;
+      const uint32_t taddr = tmem_s + (uint32_t(warp * 32) << 16);
+#pragma unroll
+      for (int c = 0; c < HG; c += 16) {
+        uint32_t r[16];
+        tmem_ld16(taddr + c, r);
+        tmem_wait_ld();
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          float s = __uint_as_float(r[j]) * scale_log2;
+          if (v && !isfinite(s)) flag(err, DSR_ERR_NONFINITE);
+          sT[(c + j) * L::kSPitch + t] = v ? s : -CUDART_INF_F;
+        }
+      }
+    }
+    asm volatile("bar.sync 1, 128;" ::: "memory");
+    // ---- per-head max / exp / sum: kTpk threads per head, HG keys each
+    const int h = t % HG, part = t / HG;
+    const int kb = part * HG;  // first key of this thread
+    float mx = -CUDART_INF_F;
+    if (ok) {
+      for (int i = 0; i < HG; ++i) mx = fmaxf(mx, sT[h * L::kSPitch + kb + i]);
+      red[part * HG + h] = mx;
+    }
+    asm volatile("bar.sync 1, 128;" ::: "memory");
+    if (ok) {
+      for (int p = 0; p < L::kTpk; ++p) mx = fmaxf(mx, red[p * HG + h]);
+      const float base = mx == -CUDART_INF_F ? 0.f : mx;
+      uint8_t* pT = smem + L::kPOff;
+      float lsum = 0.f;
+      for (int i0 = 0; i0 < HG; i0 += 8) {
+        uint32_t packed[4];
+#pragma unroll
+        for (int j = 0; j < 8; j += 2) {
+          const float s0 = sT[h * L::kSPitch + kb + i0 + j];
+          const float s1 = sT[h * L::kSPitch + kb + i0 + j + 1];
+          const __nv_bfloat16 p0 = __float2bfloat16_rn(exp2f(s0 - base));
+          const __nv_bfloat16 p1 = __float2bfloat16_rn(exp2f(s1 - base));
+          lsum += __bfloat162float(p0) + __bfloat162float(p1);
+          packed[j >> 1] = __bfloat16_as_ushort(p0) | (uint32_t(__bfloat16_as_ushort(p1)) << 16);
+        }
+        const int key = kb + i0;  // P^T[h][key..key+7], K-major: 64 keys per column block
+        *reinterpret_cast<uint4*>(pT + (key >> 6) * (HG * 128) + sw128_offset(h, key & 63)) =
+            make_uint4(packed[0], packed[1], packed[2], packed[3]);
+      }
+      red[L::kTpk * HG + part * HG + h] = lsum;
+    }
+    fence_proxy_async_smem();
+    mbar_arrive(bar_p);
+    asm volatile("bar.sync 1, 128;" ::: "memory");
+    // ---- partial statistics of this tile
+    const int64_t pidx = (int64_t(b) * tiles + tile) * heads + h0;
+    if (t < HG) {
+      float l = 0.f;
+      for (int p = 0; p < L::kTpk; ++p) l += red[L::kTpk * HG + p * HG + t];
+      part_m[pidx + t] = mx;  // identical in every thread of head t (log2 units)
+      part_l[pidx + t] = l;
+    }
+    // ---- O^T: lane = value column, columns = heads
+    if (ok && mbar_wait(bar_o, 0, abort, err)) {
+      tc_fence_after();
+      float* o = part_o + pidx * kMlaDv;
+#pragma unroll 1
+      for (int c = 0; c < kMlaDv / 128; ++c) {
+        const uint32_t taddr = tmem_o + c * HG + (uint32_t(warp * 32) << 16);
+        const int d = c * 128 + t;
+#pragma unroll
+        for (int hh = 0; hh < HG; hh += 16) {
+          uint32_t r[16];
+          tmem_ld16(taddr + hh, r);
+          tmem_wait_ld();
+#pragma unroll
+          for (int j = 0; j < 16; ++j) o[int64_t(hh + j) * kMlaDv + d] = __uint_as_float(r[j]);
+        }
+      }
+    }
+  } else if (lane == 0) {
+    // ------------------------------------------------------------ MMA issuer
+    if (mbar_wait(bar_kv, 0, abort, err)) {
+      tc_fence_after();
+      constexpr uint32_t idesc_s = umma_idesc_bf16(128, HG, false, false);
+#pragma unroll 4
+      for (int kk = 0; kk < kMlaD / 16; ++kk) {
+        const int c = kk >> 2, sub = kk & 3;
+        const uint64_t ad = umma_desc_sw128(sbase + L::kKvOff + c * 16384 + sub * 32, 16, 1024);
+        const uint64_t bd = umma_desc_sw128(sbase + L::kQOff + c * (HG * 128) + sub * 32, 16, 1024);
+        umma_bf16(tmem_s, ad, bd, idesc_s, kk > 0 ? 1u : 0u);
+      }
+      umma_commit(bar_s);
+      if (mbar_wait(bar_p, 0, abort, err)) {
+        tc_fence_after();
+        constexpr uint32_t idesc_o = umma_idesc_bf16(128, HG, true, false);
+#pragma unroll 1
+        for (int c = 0; c < kMlaDv / 128; ++c) {
+#pragma unroll
+          for (int ks = 0; ks < kMlaTile / 16; ++ks) {
+            // A = V^T (MN-major): 128 value columns = two 64-column blocks (LBO), 16 keys
+            const uint64_t ad =
+                umma_desc_sw128(sbase + L::kKvOff + (2 * c) * 16384 + ks * 2048, 16384, 1024);
+            // B = P^T (K-major): HG rows x 16 keys
+            const uint64_t bd = umma_desc_sw128(
+                sbase + L::kPOff + (ks >> 2) * (HG * 128) + (ks & 3) * 32, 16, 1024);
+            umma_bf16(tmem_o + c * HG, ad, bd, idesc_o, ks > 0 ? 1u : 0u);
+          }
+        }
+        umma_commit(bar_o);
+        mbar_wait(bar_o, 0, abort, err);  // MMAs retire before TMEM is released
+      }
+    }
+  }
+  pdl_launch_dependents();
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 4) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, L::kTmemCols);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// LSE combine.  m in log2 units; with a sink (natural-log units, converted
+// here) the output is normalised, otherwise the merged partial is returned.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(128) lse_combine_kernel(
+    const float* __restrict__ part_o, const float* __restrict__ part_m,
+    const float* __restrict__ part_l, int parts, const float* __restrict__ sink,
+    float* __restrict__ out, float* __restrict__ out_m, float* __restrict__ out_l, int32_t* err,
+    int heads, int dv) {
+  const int b = blockIdx.x, h = blockIdx.y;
+  pdl_wait();
+  float M = -CUDART_INF_F;
+  float sk = 0.f;
+  if (sink != nullptr) {
+    sk = sink[h];
+    if (!isfinite(sk)) {
+      if (threadIdx.x == 0) flag(err, DSR_ERR_NONFINITE);
+      sk = 0.f;
+    }
+    sk *= kLog2e;
+    M = sk;
+  }
+  for (int t = 0; t < parts; ++t) M = fmaxf(M, part_m[(int64_t(b) * parts + t) * heads + h]);
+  const float base = M == -CUDART_INF_F ? 0.f : M;
+  float Lsum = sink != nullptr ? exp2f(sk - base) : 0.f;
+  for (int t = 0; t < parts; ++t) {
+    const int64_t i = (int64_t(b) * parts + t) * heads + h;
+    Lsum += part_l[i] * exp2f(part_m[i] - base);
+  }
+  const float inv = sink != nullptr ? 1.f / Lsum : 1.f;
+  for (int d = threadIdx.x; d < dv; d += blockDim.x) {
+    float acc = 0.f;
+    for (int t = 0; t < parts; ++t) {
+      const int64_t i = (int64_t(b) * parts + t) * heads + h;
+      acc = fmaf(part_o[i * dv + d], exp2f(part_m[i] - base), acc);
+    }
+    const float v = acc * inv;
+    if (!isfinite(v)) flag(err, DSR_ERR_NONFINITE);
+    out[(int64_t(b) * heads + h) * dv + d] = v;
+  }
+  if (sink == nullptr && threadIdx.x == 0) {
+    out_m[int64_t(b) * heads + h] = M;
+    out_l[int64_t(b) * heads + h] = Lsum;
+  }
+}
+
+template <int HG>
+int launch_mla(const float* q, const uint16_t* kv_pool, int64_t pool_blocks,
+               const int32_t* block_table, int64_t table_stride, const int32_t* visible,
+               const int32_t* topk, int64_t k, const uint16_t* swa, const int32_t* swa_len,
+               float scale, float* part_o, float* part_m, float* part_l, int32_t* err,
+               int64_t batch, int64_t heads, int tiles, cudaStream_t stream, bool pdl) {
+  using L = MlaLayout<HG>;
+  static bool configured = false;
+  if (!configured) {
+    const cudaError_t e = cudaFuncSetAttribute(
+        mla_decode_kernel<HG>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kAlloc);
+    if (e != cudaSuccess) return fail(DSR_ECUDA, "mla smem attribute: %s", cudaGetErrorString(e));
+    configured = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(unsigned(tiles), unsigned(batch), unsigned(heads / HG));
+  cfg.blockDim = dim3(kMlaThreads, 1, 1);
+  cfg.dynamicSmemBytes = L::kAlloc;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, mla_decode_kernel<HG>, q, kv_pool, pool_blocks,
+                                           block_table, table_stride, visible, topk, int(k), swa,
+                                           swa_len, scale * kLog2e, part_o, part_m, part_l, err,
+                                           int(heads));
+  if (e != cudaSuccess) return fail(DSR_ECUDA, "mla launch: %s", cudaGetErrorString(e));
+  return DSR_OK;
+}
+
+inline int mla_tiles(int64_t k) { return 1 + int((k + kMlaTile - 1) / kMlaTile); }
+
+}  // namespace
+
+size_t mla_workspace_bytes(int64_t batch, int64_t heads, int64_t k) {
+  const size_t parts = size_t(batch) * mla_tiles(k) * heads;
+  return parts * kMlaDv * 4 + 2 * parts * 4 + 256;
+}
+
+int launch_lse_combine(const float* part_o, const float* part_m, const float* part_l,
+                       int64_t parts, const float* sink, float* out, float* out_m, float* out_l,
+                       int32_t* err, int64_t batch, int64_t heads, int64_t dv,
+                       cudaStream_t stream, bool pdl) {
+  DSR_REQUIRE(part_o && part_m && part_l && out && err, "lse_combine: null pointer");
+  DSR_REQUIRE(sink != nullptr || (out_m != nullptr && out_l != nullptr),
+              "lse_combine: an unnormalised combine needs out_m and out_l");
+  DSR_REQUIRE(parts > 0 && parts <= 4096 && batch > 0 && batch <= 65535 && heads > 0 &&
+                  heads <= 65535 && dv > 0 && dv <= 4096,
+              "lse_combine: invalid shape");
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(unsigned(batch), unsigned(heads), 1);
+  cfg.blockDim = dim3(128, 1, 1);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, lse_combine_kernel, part_o, part_m, part_l,
+                                           int(parts), sink, out, out_m, out_l, err, int(heads),
+                                           int(dv));
+  if (e != cudaSuccess) return fail(DSR_ECUDA, "lse_combine launch: %s", cudaGetErrorString(e));
+  return DSR_OK;
+}
+
+int launch_mla_decode(const float* q, const uint16_t* kv_pool, int64_t pool_blocks,
+                      const int32_t* block_table, int64_t table_stride, const int32_t* visible,
+                      const int32_t* topk, int64_t k, const uint16_t* swa,
+                      const int32_t* swa_len, const float* sink, float scale, float* out,
+                      void* workspace, size_t workspace_bytes, int32_t* err, int64_t batch,
+                      int64_t heads, cudaStream_t stream, bool pdl) {
+  DSR_REQUIRE(q && kv_pool && block_table && visible && topk && swa && swa_len && sink && out &&
+                  err && workspace,
+              "sparse_mla_decode: null pointer");
+  DSR_REQUIRE(heads == 16 || heads == 32 || heads == 64 || heads == 128,
+              "sparse_mla_decode: heads %lld not in {16,32,64,128}", (long long)heads);
+  DSR_REQUIRE(batch > 0 && batch <= 65535, "sparse_mla_decode: invalid batch");
+  DSR_REQUIRE(k >= 0 && k <= 8192, "sparse_mla_decode: k %lld outside [0, 8192]", (long long)k);
+  DSR_REQUIRE(pool_blocks > 0 && table_stride > 0, "sparse_mla_decode: invalid pool/table");
+  DSR_REQUIRE(isfinite(scale) && scale > 0.f, "invalid attention scale");
+  DSR_REQUIRE(aligned16(q) && aligned16(kv_pool) && aligned16(swa),
+              "sparse_mla_decode: q, kv_pool and swa must be 16-byte aligned");
+  const size_t need = mla_workspace_bytes(batch, heads, k);
+  DSR_REQUIRE(workspace_bytes >= need, "sparse_mla_decode: workspace %zu < %zu bytes",
+              workspace_bytes, need);
+  const int tiles = mla_tiles(k);
+  const size_t parts = size_t(batch) * tiles * heads;
+  float* part_o = static_cast<float*>(workspace);
+  float* part_m = part_o + parts * kMlaDv;
+  float* part_l = part_m + parts;
+  int rc;
+  switch (heads) {
+    case 16:
+      rc = launch_mla<16>(q, kv_pool, pool_blocks, block_table, table_stride, visible, topk, k, swa,
+                          swa_len, scale, part_o, part_m, part_l, err, batch, heads, tiles, stream,
+                          pdl);
+      break;
+    case 32:
+      rc = launch_mla<32>(q, kv_pool, pool_blocks, block_table, table_stride, visible, topk, k, swa,
+                          swa_len, scale, part_o, part_m, part_l, err, batch, heads, tiles, stream,
+                          pdl);
+      break;
+    default:
+      rc = launch_mla<64>(q, kv_pool, pool_blocks, block_table, table_stride, visible, topk, k, swa,
+                          swa_len, scale, part_o, part_m, part_l, err, batch, heads, tiles, stream,
+                          pdl);
+      break;
+  }
+  if (rc != DSR_OK) return rc;
+  return launch_lse_combine(part_o, part_m, part_l, tiles, sink, out, nullptr, nullptr, err, batch,
+                            heads, kMlaDv, stream, pdl);
+}
+
+}  // namespace dsr
+
+extern "C" size_t dsr_mla_workspace_bytes(int64_t batch, int64_t heads, int64_t k) {
+  return dsr::mla_workspace_bytes(batch, heads, k);
+}
+
+extern "C" int dsr_sparse_mla_decode(const float* q, const uint16_t* kv_pool, int64_t pool_blocks,
+                                     const int32_t* block_table, int64_t table_stride,
+                                     const int32_t* visible, const int32_t* topk, int64_t k,
+                                     const uint16_t* swa, const int32_t* swa_len,
+                                     const float* sink, float scale, float* out, void* workspace,
+                                     size_t workspace_bytes, int32_t* err, int64_t batch,
+                                     int64_t heads, void* stream) {
+  dsr::clear_error();
+  return dsr::launch_mla_decode(q, kv_pool, pool_blocks, block_table, table_stride, visible, topk,
+                                k, swa, swa_len, sink, scale, out, workspace, workspace_bytes, err,
+                                batch, heads, dsr::as_stream(stream), false);
+}
+
+extern "C" int dsr_lse_combine(const float* part_o, const float* part_m, const float* part_l,
+                               int64_t parts, const float* sink, float* out, float* out_m,
+                               float* out_l, int32_t* err, int64_t batch, int64_t heads,
+                               int64_t dv, void* stream) {
+  dsr::clear_error();
+  return dsr::launch_lse_combine(part_o, part_m, part_l, parts, sink, out, out_m, out_l, err, batch,
+                                 heads, dv, dsr::as_stream(stream), false);
+}

@@ -1,0 +1,186 @@
+/*
+ * dsr_b200.h -- C ABI of the B200 (sm_100a) attention hot path of DeepSeekRPC.
+ *
+ * Every entry point takes plain device pointers, element counts and a
+ * cudaStream_t passed as `void*` (NULL = legacy default stream).  No entry point
+ * allocates device memory, synchronizes the stream or reads device data on the
+ * host.  Work is enqueued on `stream` only.
+ *
+ * Two error channels, as in the reference extension:
+ *   - host return value: DSR_OK, or a negative code for argument / shape / bound
+ *     violations (the reference raises them through TORCH_CHECK) and launch
+ *     failures; dsr_last_error() returns the message for the calling thread.
+ *   - device status word `err` (one int32 in device memory, zeroed by the
+ *     caller): data-dependent errors, first error wins via atomicCAS.  Codes 1..3
+ *     keep the reference meaning (native/operations.cu:44-158).
+ *
+ * Storage dtypes: BF16 values are passed as uint16_t bit patterns.
+ */
+#ifndef DSR_B200_H
+#define DSR_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- device status codes (written to err[0]) ---------------------------- */
+#define DSR_ERR_ID 1        /* invalid id, slot, block or visibility          */
+#define DSR_ERR_NONFINITE 2 /* non-finite input, score or output              */
+#define DSR_ERR_SCATTER 3   /* scatter bounds / duplicate / stale generation  */
+#define DSR_ERR_TIMEOUT 4   /* a bounded device-side wait gave up (new code)  */
+
+/* ---- host return codes --------------------------------------------------- */
+#define DSR_OK 0
+#define DSR_EINVAL (-1)  /* shape, dtype-size or bound violation             */
+#define DSR_ECUDA (-2)   /* CUDA runtime / launch failure                    */
+#define DSR_ENODEV (-3)  /* current device is not a compute-capability 10.x GPU */
+
+/* Fixed geometry of the paged decode path (DeepSeek V3.2/V4 sparse MLA). */
+#define DSR_BLOCK_TOKENS 64 /* tokens per paged pool block                   */
+#define DSR_INDEX_DIM 128   /* index-key width                               */
+#define DSR_KV_DIM 576      /* latent 512 + rope 64                          */
+#define DSR_V_DIM 512       /* value width = leading latent columns          */
+#define DSR_SWA_ROWS 128    /* sliding-window ring rows per sequence         */
+
+/* ABI generation; the reference module returns 2 from abi_version()
+ * (native/bindings.cpp:25). */
+int dsr_abi_version(void);
+
+/* Message of the last nonzero host return on this thread ("" if none). */
+const char* dsr_last_error(void);
+
+/* Returns DSR_OK when the current CUDA device is sm_100-class, else DSR_ENODEV. */
+int dsr_device_check(void);
+
+/* ===================== reference drop-in operations ======================= */
+
+/* Replaces ds_index_scores / index_kernel (native/operations.cu:84-123,199-212).
+ * q f32[rows,heads,128], keys bf16[capacity,128], weights f32[rows,heads],
+ * ids i32[rows,columns], visible i32[rows] -> out f32[rows,columns].
+ * out[r,c] = sum_h w[r,h]*max(q[r,h].keys[id],0); -inf for id==-1 or id>=visible[r].
+ * Bounds widened from the reference: heads <= 64 (was 32), columns < 2^31
+ * (was 8192), rows <= 65536 (was 4096). */
+int dsr_index_scores(const float* q, const uint16_t* keys, const float* weights,
+                     const int32_t* ids, const int32_t* visible, float* out, int32_t* err,
+                     int64_t rows, int64_t heads, int64_t columns, int64_t capacity,
+                     void* stream);
+
+/* Replaces ds_sparse_attention / sparse_kernel (native/operations.cu:30-82,180-197).
+ * q f32[rows,heads,width], window bf16[window_rows,width], source
+ * bf16[source_rows,width], ids i32[rows,selected], sink f32[heads] ->
+ * out f32[rows,heads,width]; online softmax whose initial state is (sink, 1, 0).
+ * Bounds widened: width <= 576 (was 512), window_rows <= 65536 (was 8192),
+ * source_rows < 2^31 (was 2^20), selected <= 65536 (was 4096). */
+int dsr_sparse_attention(const float* q, const uint16_t* window, const uint16_t* source,
+                         const int32_t* ids, const float* sink, float* out, int32_t* err,
+                         int64_t rows, int64_t heads, int64_t width, int64_t window_rows,
+                         int64_t source_rows, int64_t selected, float scale, void* stream);
+
+/* Replaces ds_scatter_slots / scatter_kernel (native/operations.cu:144-161,227-243).
+ * Generation-checked row scatter; does not modify `generations` (the caller
+ * bumps them, reference cache_pool.py:309).  Width bound widened to 576. */
+int dsr_scatter_slots(uint16_t* pool, const int64_t* generations, const int32_t* slots,
+                      const int64_t* expected, const uint16_t* values, int32_t* err,
+                      int64_t rows, int64_t width, int64_t capacity, void* stream);
+
+/* Replaces ds_engram_decode / engram_kernel (native/operations.cu:125-142,214-225).
+ * u8[rows,264] FP8-E4M3 x UE8M0 -> bf16[rows,256]. */
+int dsr_engram_decode(const uint8_t* encoded, uint16_t* out, int32_t* err, int64_t rows,
+                      void* stream);
+
+/* ========================= exact top-k selection ========================== */
+
+/* Replaces the streaming top-k of TiledIndexer._select + merge_ranked
+ * (src/deepseekrpc/index_selection.py:9-19,79-124).
+ * For each row r: among entries i < lengths[r] (and ids[r,i] >= 0 when `ids` is
+ * given) select the k largest scores; equal scores prefer the lower id; -0.0
+ * equals +0.0.  Output out_ids i32[rows,k]: the selected ids in ascending order,
+ * padded with -1.  Optional out_scores f32[rows,k] holds the matching scores
+ * (padding: -inf).  When `ids` is NULL the id of entry i is i + id_base.
+ * When `ids` is given, valid ids must increase along each row (any -1 entries
+ * are skipped).  k <= 8192; row_stride >= max length. */
+int dsr_topk_select(const float* scores, const int32_t* ids, const int32_t* lengths,
+                    int32_t* out_ids, float* out_scores, int32_t* err, int64_t rows,
+                    int64_t row_stride, int64_t k, int64_t id_base, void* stream);
+
+/* ======================== paged decode hot path =========================== */
+
+/* Lightning-indexer scores over a paged BF16 index-key pool, tcgen05 tensor cores.
+ * index_pool bf16[pool_blocks*64,128]; block_table i32[batch,table_stride]
+ * (physical block of logical block j = positions 64j..64j+63);
+ * visible i32[batch] keys per row (<= score_stride, else err 1); q f32[batch,heads,128]; weights
+ * f32[batch,heads]; heads in {16,32,64}.
+ * scores f32[batch,score_stride]: scores[b,p] for p < visible[b].
+ * Replaces TiledIndexer's per-tile index_scores calls (index_selection.py:94-107)
+ * for the dense (non-candidate) case. */
+int dsr_indexer_decode(const float* q, const float* weights, const uint16_t* index_pool,
+                       int64_t pool_blocks, const int32_t* block_table, int64_t table_stride,
+                       const int32_t* visible, float* scores, int64_t score_stride,
+                       int32_t* err, int64_t batch, int64_t heads, void* stream);
+
+/* Sparse MLA decode attention over the SWA ring plus top-k selected pool rows.
+ * q f32[batch,heads,576]; kv_pool bf16[pool_blocks*64,576]; block_table as above;
+ * topk i32[batch,k] logical positions (ascending, -1 padded), each < visible[b];
+ * swa bf16[batch,128,576] ring (row p%128 holds position p); swa_len i32[batch]
+ * valid window rows (<= 128); sink f32[heads]; heads in {16,32,64,128}.
+ * out f32[batch,heads,512] = softmax-with-sink weighted sum of the first 512
+ * columns of the selected rows (reference sparse_kernel with V = K, restricted
+ * to the value columns).  Scratch: workspace of dsr_mla_workspace_bytes(). */
+size_t dsr_mla_workspace_bytes(int64_t batch, int64_t heads, int64_t k);
+int dsr_sparse_mla_decode(const float* q, const uint16_t* kv_pool, int64_t pool_blocks,
+                          const int32_t* block_table, int64_t table_stride,
+                          const int32_t* visible, const int32_t* topk, int64_t k,
+                          const uint16_t* swa, const int32_t* swa_len, const float* sink,
+                          float scale, float* out, void* workspace, size_t workspace_bytes,
+                          int32_t* err, int64_t batch, int64_t heads, void* stream);
+
+/* Fused, generation-checked append of one KV row (576) and one index-key row
+ * (128) per sequence into the paged pools and the SWA ring.  Replaces the two
+ * DeviceRowPool.write calls of publish_source plus the SWA ring write
+ * (attention_state.py:183-192, cache_pool.py:289-313, vllm_attention.py:261).
+ * block_table i32[table_rows,table_stride]; seq i32[n] sequence of each new
+ * row (< table_rows); positions i32[n] its logical position;
+ * generations i64[pool_blocks*64] per physical row; expected i64[n].
+ * A row is written only if its physical row is in bounds, not repeated by an
+ * earlier row of the batch, generations[row]==expected[i] and both value rows
+ * are finite; then generations[row] = expected[i]+1.  Otherwise err = 3
+ * (bounds / duplicate / stale) or 2 (non-finite) and nothing of that row is
+ * written.  swa (bf16[table_rows,128,576], row p%128) may be NULL. */
+int dsr_append_kv_index(uint16_t* kv_pool, uint16_t* index_pool, int64_t* generations,
+                        int64_t pool_blocks, const int32_t* block_table, int64_t table_rows,
+                        int64_t table_stride, const int32_t* seq, const int32_t* positions,
+                        const int64_t* expected, const uint16_t* kv_values,
+                        const uint16_t* index_values, uint16_t* swa, int32_t* err, int64_t n,
+                        void* stream);
+
+/* Log-sum-exp combine of attention partials: for each (b,h) the T partials
+ * (m[b,t,h], l[b,t,h], o[b,t,h,:dv]) are merged; with a sink the result is
+ * normalised, out[b,h,:] = sum_t o_t e^{m_t-M} / (e^{sink_h-M} + sum_t l_t e^{m_t-M}),
+ * otherwise (out_m,out_l,out) receive the merged unnormalised partial. */
+int dsr_lse_combine(const float* part_o, const float* part_m, const float* part_l,
+                    int64_t parts, const float* sink, float* out, float* out_m, float* out_l,
+                    int32_t* err, int64_t batch, int64_t heads, int64_t dv, void* stream);
+
+/* One decode step: indexer -> exact top-k -> sparse MLA attention -> combine.
+ * Arguments as above; idx_q f32[batch,idx_heads,128], idx_w f32[batch,idx_heads];
+ * topk_out i32[batch,k] receives the selection; scores_out (nullable)
+ * f32[batch,score_stride].  Scratch: dsr_decode_workspace_bytes(). */
+size_t dsr_decode_workspace_bytes(int64_t batch, int64_t max_visible, int64_t heads,
+                                  int64_t k);
+int dsr_decode_step(const float* idx_q, const float* idx_w, int64_t idx_heads,
+                    const uint16_t* index_pool, const float* q, const uint16_t* kv_pool,
+                    int64_t heads, int64_t pool_blocks, const int32_t* block_table,
+                    int64_t table_stride, const int32_t* visible, int64_t max_visible,
+                    int64_t k, const uint16_t* swa, const int32_t* swa_len,
+                    const float* sink, float scale, float* out, int32_t* topk_out,
+                    float* scores_out, void* workspace, size_t workspace_bytes,
+                    int32_t* err, int64_t batch, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* DSR_B200_H */

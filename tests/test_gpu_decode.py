@@ -1,0 +1,131 @@
+"""Paged decode path on the B200 (indexer -> top-k -> sparse MLA) against the oracle.
+
+Tolerances: index scores within 1e-3 relative (measured
+against sum_h |w_h| |q_h.k|, the magnitude that bounds the rounding of a
+signed-weight sum); top-k bit-exact given identical fp32 scores; attention
+max abs error <= 2e-2 and mean abs error <= 2e-3.
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from _helpers import (assert_bf16_close, c_decode_step, c_indexer, c_mla, host, oracle_attention,
+                      oracle_scores, score_bound)
+from deepseekrpc_b200.workloads import CONFIGS, make_decode_inputs, small_config
+
+pytestmark = pytest.mark.gpu
+SCORE_RTOL = 1e-3
+
+
+def check_scores(h, scores, b):
+    n = int(h["visible"][b])
+    ref = oracle_scores(h, b)
+    bound = score_bound(h, b)
+    got = scores[b, :n]
+    assert np.all(np.isfinite(got))
+    err = np.abs(got.astype(np.float64) - ref)
+    assert np.all(err <= SCORE_RTOL * bound + 1e-6), f"max rel {np.max(err / (bound + 1e-30)):.2e}"
+    return ref
+
+
+@pytest.mark.parametrize("idx_heads", [64, 32, 16])
+def test_indexer_scores_ragged_batch(cuda, idx_heads):
+    cfg = small_config("cfg3", batch=4, idx_heads=idx_heads, seed=31)
+    inp, lengths = make_decode_inputs(cfg, lengths=[100, 4096, 9000, 70001])
+    scores, code = c_indexer(inp)
+    assert code == 0
+    h = host(inp)
+    s = scores.cpu().numpy()
+    for b in range(4):
+        check_scores(h, s, b)
+        assert np.all(np.isnan(s[b, lengths[b]:]))  # nothing written past visible
+
+
+def test_indexer_fp32_query_uses_hi_lo_split(cuda):
+    cfg = small_config("cfg2", context=20000, seed=32)
+    inp, _ = make_decode_inputs(cfg)
+    inp["idx_q"] = inp["idx_q"] + torch.randn_like(inp["idx_q"]) * 1e-3  # not BF16-representable
+    scores, code = c_indexer(inp)
+    assert code == 0
+    check_scores(host(inp), scores.cpu().numpy(), 0)
+
+
+def test_indexer_flags_bad_visibility_and_blocks(cuda):
+    cfg = small_config("cfg2", context=1000, seed=33)
+    inp, _ = make_decode_inputs(cfg)
+    bad = dict(inp)
+    bad["visible"] = inp["visible"] + 5000  # beyond the block table
+    _, code = c_indexer(bad)
+    assert code == 1
+    bad = dict(inp)
+    table = inp["block_table"].clone()
+    table[0, 3] = 10 ** 6
+    bad["block_table"] = table
+    _, code = c_indexer(bad)
+    assert code == 1
+
+
+@pytest.mark.parametrize("heads", [64, 16])
+def test_sparse_mla_against_oracle(cuda, heads):
+    cfg = small_config("cfg2", context=9000, heads=heads, seed=34)
+    inp, _ = make_decode_inputs(cfg)
+    h = host(inp)
+    rng = np.random.default_rng(34)
+    topk = np.full((1, 2048), -1, np.int32)
+    chosen = np.sort(rng.choice(9000, 1900, replace=False)).astype(np.int32)
+    topk[0, :1900] = chosen
+    out, code = c_mla(inp, torch.from_numpy(topk).cuda(), cfg.scale)
+    assert code == 0
+    assert_bf16_close(out.cpu().numpy()[0], oracle_attention(h, 0, topk[0], cfg.scale))
+
+
+def test_sparse_mla_short_window_and_empty_selection(cuda):
+    cfg = small_config("cfg2", context=37, seed=35)
+    inp, _ = make_decode_inputs(cfg)
+    h = host(inp)
+    topk = np.full((1, 2048), -1, np.int32)
+    out, code = c_mla(inp, torch.from_numpy(topk).cuda(), cfg.scale)
+    assert code == 0
+    assert_bf16_close(out.cpu().numpy()[0], oracle_attention(h, 0, topk[0], cfg.scale))
+    topk[0, :3] = [0, 36, 40]  # 40 >= visible -> code 1
+    _, code = c_mla(inp, torch.from_numpy(topk).cuda(), cfg.scale)
+    assert code == 1
+
+
+def run_step_and_check(cfg, lengths=None):
+    inp, lengths = make_decode_inputs(cfg, lengths=lengths)
+    out, topk, scores, code = c_decode_step(inp, cfg.topk, cfg.scale)
+    assert code == 0
+    h = host(inp)
+    s = scores.cpu().numpy()
+    t = topk.cpu().numpy()
+    o = out.cpu().numpy()
+    for b, n in enumerate(lengths):
+        ref_scores = check_scores(h, s, b)
+        # top-k: bit-exact against the reference ranking of the same fp32 scores
+        assert np.array_equal(t[b], oracle.tiled_topk(s[b, :n], cfg.topk))
+        # against the oracle's own scores the sets may differ only inside the rounding band
+        ref_topk = oracle.tiled_topk(ref_scores, cfg.topk)
+        diff = np.setxor1d(t[b][t[b] >= 0], ref_topk[ref_topk >= 0])
+        if len(diff):
+            threshold = np.sort(ref_scores)[::-1][min(cfg.topk, n) - 1]
+            band = SCORE_RTOL * score_bound(h, b)[diff] + 1e-6
+            assert np.all(np.abs(ref_scores[diff] - threshold) <= 2 * band)
+        assert_bf16_close(o[b], oracle_attention(h, b, t[b], cfg.scale))
+    return inp, lengths
+
+
+def test_decode_step_config1(cuda):
+    run_step_and_check(CONFIGS["cfg1"])
+
+
+def test_decode_step_config2_full_size(cuda):
+    run_step_and_check(CONFIGS["cfg2"])
+
+
+def test_decode_step_ragged_batch(cuda):
+    cfg = small_config("cfg3", batch=5, seed=36)
+    run_step_and_check(cfg, lengths=[1, 130, 2048, 9000, 70000])

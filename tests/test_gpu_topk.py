@@ -1,0 +1,91 @@
+"""Exact top-k on the B200: bit-exact against the reference's streaming merge (TiledIndexer)."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from _helpers import c_topk, dev
+
+pytestmark = pytest.mark.gpu
+
+
+def expected_rows(scores, lengths, k):
+    return np.stack([oracle.tiled_topk(scores[r, :n], k) for r, n in enumerate(lengths)])
+
+
+def test_topk_tie_fixture_at_decode_scale(cuda, golden):
+    g = golden("topk_ties")
+    scores = g["scores"][None]
+    out, code = c_topk(dev(scores), dev(np.array([scores.shape[1]], np.int32)), int(g["keep"]))
+    assert code == 0
+    assert np.array_equal(out.cpu().numpy()[0], g["expected"])
+
+
+def test_topk_ragged_rows_and_short_rows(cuda):
+    rng = np.random.default_rng(21)
+    lengths = [0, 1, 2047, 2048, 2049, 50000, 131072, 9000]
+    stride = 131072
+    scores = rng.normal(size=(len(lengths), stride)).astype(np.float32)
+    scores[7, :9000] = np.round(scores[7, :9000])  # heavy ties
+    out, code = c_topk(dev(scores), dev(np.array(lengths, np.int32)), 2048)
+    assert code == 0
+    assert np.array_equal(out.cpu().numpy(), expected_rows(scores, lengths, 2048))
+
+
+def test_topk_streaming_rows_beyond_shared_memory(cuda):
+    # 8 * 40960 keys fit in shared memory per cluster; longer rows stream from HBM
+    rng = np.random.default_rng(22)
+    n = 400000
+    scores = (np.round(rng.normal(size=(2, n)) * 8) / 8).astype(np.float32)
+    out, code = c_topk(dev(scores), dev(np.array([n, 333333], np.int32)), 2048)
+    assert code == 0
+    assert np.array_equal(out.cpu().numpy(), expected_rows(scores, [n, 333333], 2048))
+
+
+@pytest.mark.parametrize("k", [1, 13, 512, 4096])
+def test_topk_various_k(cuda, k):
+    rng = np.random.default_rng(23 + k)
+    scores = np.round(rng.normal(size=(3, 20000)) * 2).astype(np.float32)
+    lengths = [20000, 7, 15000]
+    out, code = c_topk(dev(scores), dev(np.array(lengths, np.int32)), k)
+    assert code == 0
+    assert np.array_equal(out.cpu().numpy(), expected_rows(scores, lengths, k))
+
+
+def test_topk_negative_zero_equals_positive_zero(cuda):
+    scores = np.array([[-0.0, 0.0, -0.0, 0.0, -1.0, 1.0]], np.float32)
+    out, code = c_topk(dev(scores), dev(np.array([6], np.int32)), 3)
+    assert code == 0
+    assert out.cpu().numpy().tolist() == [[0, 1, 5]]  # the two lowest ids among the zeros
+
+
+def test_topk_explicit_ids_skip_padding_and_return_scores(cuda):
+    rng = np.random.default_rng(24)
+    ranks, k = 4, 2048
+    scores = np.full((2, ranks * k), -np.inf, np.float32)
+    ids = np.full((2, ranks * k), -1, np.int32)
+    for row in range(2):
+        for r in range(ranks):
+            count = k if r != 2 else 1500
+            local = np.sort(rng.choice(65536, count, replace=False)) + r * 65536
+            ids[row, r * k:r * k + count] = local
+            scores[row, r * k:r * k + count] = np.round(rng.normal(size=count) * 3)
+    lengths = np.array([ranks * k] * 2, np.int32)
+    out, out_scores, code = c_topk(dev(scores), dev(lengths), k, ids=dev(ids), return_scores=True)
+    assert code == 0
+    for row in range(2):
+        valid = ids[row] >= 0
+        expected = oracle.tiled_topk(scores[row][valid], k, positions=ids[row][valid])
+        assert np.array_equal(out.cpu().numpy()[row], expected)
+        lookup = dict(zip(ids[row][valid].tolist(), scores[row][valid].tolist()))
+        assert out_scores.cpu().numpy()[row].tolist() == [lookup[i] for i in expected.tolist()]
+
+
+def test_topk_id_base_and_length_error(cuda):
+    scores = torch.arange(100, dtype=torch.float32, device="cuda")[None]
+    out, code = c_topk(scores, torch.tensor([100], dtype=torch.int32, device="cuda"), 4, id_base=1000)
+    assert code == 0 and out.tolist() == [[1096, 1097, 1098, 1099]]
+    out, code = c_topk(scores, torch.tensor([101], dtype=torch.int32, device="cuda"), 4)
+    assert code == 1 and out.tolist() == [[-1, -1, -1, -1]]
