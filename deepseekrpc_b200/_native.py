@@ -28,7 +28,9 @@ SIGNATURES = {
                                      c_int64, c_int64, c_float, _P]),
     "dsr_scatter_slots": (c_int, [_P, _P, _P, _P, _P, _P, c_int64, c_int64, c_int64, _P]),
     "dsr_engram_decode": (c_int, [_P, _P, _P, c_int64, _P]),
-    "dsr_topk_select": (c_int, [_P, _P, _P, _P, _P, _P, c_int64, c_int64, c_int64, c_int64, _P]),
+    "dsr_topk_workspace_bytes": (c_size_t, [c_int64, c_int64]),
+    "dsr_topk_select": (c_int, [_P, _P, _P, _P, _P, _P, c_int64, c_int64, c_int64, c_int64, _P, c_size_t,
+                                _P]),
     "dsr_indexer_decode": (c_int, [_P, _P, _P, c_int64, _P, c_int64, _P, _P, c_int64, _P, c_int64,
                                    c_int64, _P]),
     "dsr_mla_workspace_bytes": (c_size_t, [c_int64, c_int64, c_int64]),

@@ -15,7 +15,8 @@ inline int64_t round_up(int64_t x, int64_t m) { return (x + m - 1) / m * m; }
 extern "C" size_t dsr_decode_workspace_bytes(int64_t batch, int64_t max_visible, int64_t heads,
                                              int64_t k) {
   const int64_t stride = round_up(max_visible > 0 ? max_visible : 1, 64);
-  return size_t(batch) * size_t(stride) * 4 + dsr::mla_workspace_bytes(batch, heads, k) + 256;
+  return dsr::topk_workspace_bytes(batch, stride) + size_t(batch) * size_t(stride) * 4 +
+         dsr::mla_query_image_bytes(batch, heads) + dsr::mla_workspace_bytes(batch, heads, k) + 256;
 }
 
 extern "C" int dsr_decode_step(const float* idx_q, const float* idx_w, int64_t idx_heads,
@@ -36,18 +37,30 @@ extern "C" int dsr_decode_step(const float* idx_q, const float* idx_w, int64_t i
   const size_t need = dsr_decode_workspace_bytes(batch, max_visible, heads, k);
   DSR_REQUIRE(workspace_bytes >= need, "decode_step: workspace %zu < %zu bytes", workspace_bytes,
               need);
+  DSR_REQUIRE((reinterpret_cast<uintptr_t>(workspace) & 255u) == 0,
+              "decode_step: workspace must be 256-byte aligned");
   const int64_t stride = round_up(max_visible, 64);
-  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  // [top-k state (zero between calls) | scores | MLA query image | MLA partials]
+  uint8_t* topk_ws = static_cast<uint8_t*>(workspace);
+  const size_t topk_bytes = topk_workspace_bytes(batch, stride);
+  uint8_t* ws = topk_ws + topk_bytes;
+  workspace_bytes -= topk_bytes;
   float* scores = scores_out != nullptr ? scores_out : reinterpret_cast<float*>(ws);
-  uint8_t* mla_ws = ws + size_t(batch) * stride * 4;
-  const size_t mla_bytes = workspace_bytes - size_t(batch) * stride * 4;
+  uint16_t* q_img = reinterpret_cast<uint16_t*>(ws + size_t(batch) * stride * 4);
+  uint8_t* mla_ws = ws + size_t(batch) * stride * 4 + mla_query_image_bytes(batch, heads);
+  const size_t mla_bytes =
+      workspace_bytes - size_t(batch) * stride * 4 - mla_query_image_bytes(batch, heads);
   const cudaStream_t s = as_stream(stream);
+  // the indexer also converts the MLA query into the BF16 image the MLA kernel loads
+  // and builds the per-row score histograms the top-k kernel starts from
   int rc = launch_indexer_decode(idx_q, idx_w, index_pool, pool_blocks, block_table, table_stride,
-                                 visible, scores, stride, err, batch, idx_heads, s, false);
+                                 visible, scores, stride, err, batch, idx_heads, s, false, q, q_img,
+                                 heads, reinterpret_cast<uint32_t*>(topk_ws));
   if (rc != DSR_OK) return rc;
-  rc = launch_topk(scores, nullptr, visible, topk_out, nullptr, err, batch, stride, k, 0, s, true);
+  rc = launch_topk(scores, nullptr, visible, topk_out, nullptr, err, batch, stride, k, 0, topk_ws,
+                   topk_bytes, s, true, /*hist_ready=*/true);
   if (rc != DSR_OK) return rc;
   return launch_mla_decode(q, kv_pool, pool_blocks, block_table, table_stride, visible, topk_out, k,
                            swa, swa_len, sink, scale, out, mla_ws, mla_bytes, err, batch, heads, s,
-                           true);
+                           true, q_img);
 }

@@ -37,18 +37,27 @@ inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 
 // Launch helpers implemented by the kernel translation units.
 int launch_topk(const float* scores, const int32_t* ids, const int32_t* lengths, int32_t* out_ids,
                 float* out_scores, int32_t* err, int64_t rows, int64_t row_stride, int64_t k,
-                int64_t id_base, cudaStream_t stream, bool pdl);
+                int64_t id_base, void* workspace, size_t workspace_bytes, cudaStream_t stream,
+                bool pdl, bool hist_ready);
+// Top-k scratch; its first rows * 2048 uint32 are the per-row score histograms.
+size_t topk_workspace_bytes(int64_t rows, int64_t row_stride);
 int launch_indexer_decode(const float* q, const float* weights, const uint16_t* index_pool,
                           int64_t pool_blocks, const int32_t* block_table, int64_t table_stride,
                           const int32_t* visible, float* scores, int64_t score_stride,
                           int32_t* err, int64_t batch, int64_t heads, cudaStream_t stream,
-                          bool pdl);
+                          bool pdl, const float* mla_q = nullptr, uint16_t* mla_img = nullptr,
+                          int64_t mla_heads = 0, uint32_t* hist = nullptr);
+// Bytes of the BF16 MLA query image the indexer can emit for the MLA kernel.
+inline size_t mla_query_image_bytes(int64_t batch, int64_t heads) {
+  return size_t(batch) * size_t(heads) * DSR_KV_DIM * 2;
+}
 int launch_mla_decode(const float* q, const uint16_t* kv_pool, int64_t pool_blocks,
                       const int32_t* block_table, int64_t table_stride, const int32_t* visible,
                       const int32_t* topk, int64_t k, const uint16_t* swa,
                       const int32_t* swa_len, const float* sink, float scale, float* out,
                       void* workspace, size_t workspace_bytes, int32_t* err, int64_t batch,
-                      int64_t heads, cudaStream_t stream, bool pdl);
+                      int64_t heads, cudaStream_t stream, bool pdl,
+                      const uint16_t* q_img = nullptr);
 size_t mla_workspace_bytes(int64_t batch, int64_t heads, int64_t k);
 int launch_lse_combine(const float* part_o, const float* part_m, const float* part_l,
                        int64_t parts, const float* sink, float* out, float* out_m, float* out_l,

@@ -9,14 +9,16 @@
 // Kernel: persistent, one CTA per SM, tiles of 128 keys (two pool blocks).
 //   warp 0      TMA producer: two 64x64 boxes per pool block, 128-byte swizzle
 //   warp 1      TMEM allocator + single-thread tcgen05.mma issuer
-//   warps 2..5  epilogue: Q preparation, TMEM -> registers, ReLU, weighted
-//               head reduction, score store
+//   warps 2..9  epilogue, two warpgroups sharing every tile (each reduces half
+//               of the heads): Q preparation, TMEM -> registers, ReLU, weighted
+//               head reduction, score store, 11-bit score histogram for top-k
 // D[key, n] = K[key,:] . B[n,:] with B = [q_hi ; q_lo] (N = 2*heads rows), where
 // q_hi = bf16(q) and q_lo = bf16(q - q_hi): the two products summed in FP32
 // reproduce the FP32 query to ~2^-17 relative, so scores track the FP32
 // reference far inside the 1e-3 tolerance while the contraction runs on the
-// tensor cores.  Accumulators are double-buffered in TMEM so the epilogue of
-// tile i overlaps the MMA of tile i+1; smem stages are a 4-deep TMA ring.
+// tensor cores.  Four TMEM accumulators let the epilogue of tile i overlap the
+// MMAs of the next tiles; smem stages are a 4-deep TMA ring.  A BF16-exact
+// query (q_lo == 0, the FP8-valued reference query) contracts the q_hi rows only.
 #include "common.cuh"
 #include "host_common.h"
 
@@ -26,8 +28,10 @@ namespace {
 constexpr int kIxTile = 128;                 // keys per tile
 constexpr int kIxStages = 4;
 constexpr int kIxStageBytes = kIxTile * 256; // 128 keys x 128 bf16
-constexpr int kIxThreads = 192;
+constexpr int kIxThreads = 320;              // producer, MMA, 2 epilogue warpgroups
 constexpr int kIxMaxBatch = 1024;
+constexpr int kIxAcc = 4;                    // TMEM accumulators in flight
+constexpr int kIxHistBins = 2048;            // 11-bit score-key histogram for top-k
 
 template <int H>
 struct IxLayout {
@@ -36,13 +40,17 @@ struct IxLayout {
   static constexpr int kStagesOff = 0;
   static constexpr int kQOff = kIxStages * kIxStageBytes;
   static constexpr int kWOff = kQOff + 2 * kQSlotBytes;
-  static constexpr int kBarOff = kWOff + 2 * H * 4;
-  static constexpr int kNumBars = 2 * kIxStages + 8;
-  static constexpr int kMiscOff = kBarOff + kNumBars * 8;  // tmem slot, abort flag
-  static constexpr int kPrefixOff = kMiscOff + 16;
-  static constexpr int kBytes = kPrefixOff + (kIxMaxBatch + 1) * 4;
+  static constexpr int kXchOff = kWOff + 2 * H * 4;            // [2][128] partial scores
+  static constexpr int kHistOff = kXchOff + 2 * 128 * 4;       // [2048] u32
+  static constexpr int kBarOff = kHistOff + kIxHistBins * 4;
+  static constexpr int kNumBars = 2 * kIxStages + 2 * kIxAcc + 4;
+  static constexpr int kMiscOff = kBarOff + kNumBars * 8;  // tmem slot, abort flag, q_lo flags
+  static constexpr int kPrefixOff = kMiscOff + 32;
+  static constexpr int kVisOff = kPrefixOff + (kIxMaxBatch + 1) * 4;
+  static constexpr int kBytes = kVisOff + kIxMaxBatch * 4;
   static constexpr int kAlloc = kBytes + 1024;  // slack for 1024-byte alignment
-  static constexpr uint32_t kTmemCols = (2 * N <= 32) ? 32 : (2 * N <= 64 ? 64 : (2 * N <= 128 ? 128 : 256));
+  static constexpr uint32_t kTmemCols =
+      (kIxAcc * N <= 32) ? 32 : (kIxAcc * N <= 64 ? 64 : (kIxAcc * N <= 128 ? 128 : (kIxAcc * N <= 256 ? 256 : 512)));
 };
 
 __device__ __forceinline__ int find_row(const int* prefix, int batch, int t) {
@@ -55,15 +63,70 @@ __device__ __forceinline__ int find_row(const int* prefix, int batch, int t) {
   return lo;
 }
 
+// 32 lanes x 8 consecutive 32-bit TMEM columns
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t* r) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]),
+                 "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr));
+}
+template <int C>
+__device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, uint32_t* r) {
+  if constexpr (C == 8) {
+    tmem_ld8(taddr, r);
+  } else {
+#pragma unroll
+    for (int j = 0; j < C; j += 16) tmem_ld16(taddr + j, *reinterpret_cast<uint32_t(*)[16]>(r + j));
+  }
+}
+
+// The MLA query of the same decode step, FP32 [batch, heads, 576] -> BF16 in the
+// shared-memory image the sparse MLA kernel contracts against: per (sequence,
+// 64-head group) nine 64-column blocks of group_heads rows x 128 B, 128-byte
+// swizzled (dsr_mla_query_image_bytes()).  This CTA converts its share.
+__device__ __forceinline__ void mla_query_image(const float* __restrict__ q, uint16_t* __restrict__ img,
+                                                int batch, int heads, int tid, int nthreads) {
+  const int hg = heads < 64 ? heads : 64;
+  const int64_t total = int64_t(batch) * heads * (DSR_KV_DIM / 4);  // float4 units
+  const int64_t lo = total * blockIdx.x / gridDim.x, hi = total * (blockIdx.x + 1) / gridDim.x;
+  constexpr int kBatch = 8;
+  for (int64_t i0 = lo; i0 < hi; i0 += int64_t(nthreads) * kBatch) {
+    float4 v[kBatch];
+#pragma unroll
+    for (int j = 0; j < kBatch; ++j) {
+      const int64_t i = i0 + int64_t(j) * nthreads + tid;
+      if (i < hi) v[j] = __ldg(reinterpret_cast<const float4*>(q) + i);
+    }
+#pragma unroll
+    for (int j = 0; j < kBatch; ++j) {
+      const int64_t i = i0 + int64_t(j) * nthreads + tid;
+      if (i < hi) {
+        const int64_t bh = i / (DSR_KV_DIM / 4);
+        const int d = int(i % (DSR_KV_DIM / 4)) * 4;
+        const int h = int(bh % heads);
+        const int64_t g = (bh / heads) * (heads / hg) + h / hg;  // (sequence, head group)
+        uint8_t* base = reinterpret_cast<uint8_t*>(img) + (g * (DSR_KV_DIM / 64) + d / 64) * hg * 128;
+        const uint32_t w0 = __bfloat16_as_ushort(__float2bfloat16_rn(v[j].x)) |
+                            (uint32_t(__bfloat16_as_ushort(__float2bfloat16_rn(v[j].y))) << 16);
+        const uint32_t w1 = __bfloat16_as_ushort(__float2bfloat16_rn(v[j].z)) |
+                            (uint32_t(__bfloat16_as_ushort(__float2bfloat16_rn(v[j].w))) << 16);
+        *reinterpret_cast<uint2*>(base + sw128_offset(h % hg, d & 63)) = make_uint2(w0, w1);
+      }
+    }
+  }
+}
+
 template <int H>
 __global__ void __launch_bounds__(kIxThreads, 1)
     indexer_decode_kernel(const __grid_constant__ CUtensorMap kmap, const float* __restrict__ q,
                           const float* __restrict__ weights, const int32_t* __restrict__ block_table,
                           int64_t table_stride, const int32_t* __restrict__ visible,
                           int64_t pool_blocks, float* __restrict__ scores, int64_t score_stride,
-                          int32_t* err, int batch) {
+                          int32_t* err, int batch, const float* __restrict__ mla_q,
+                          uint16_t* __restrict__ mla_img, int mla_heads, uint32_t* __restrict__ hist) {
   using L = IxLayout<H>;
   constexpr int N = L::N;
+  constexpr int HH = H / 2;  // heads per epilogue warpgroup
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
@@ -72,13 +135,17 @@ __global__ void __launch_bounds__(kIxThreads, 1)
   uint64_t* full = bars;
   uint64_t* empty = bars + kIxStages;
   uint64_t* tfull = bars + 2 * kIxStages;
-  uint64_t* tempty = tfull + 2;
-  uint64_t* qfull = tfull + 4;
-  uint64_t* qempty = tfull + 6;
+  uint64_t* tempty = tfull + kIxAcc;
+  uint64_t* qfull = tempty + kIxAcc;
+  uint64_t* qempty = qfull + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kMiscOff);
   volatile int* abort = reinterpret_cast<volatile int*>(smem + L::kMiscOff + 4);
+  int* qlonz = reinterpret_cast<int*>(smem + L::kMiscOff + 8);  // [2] q_lo != 0 per slot
   int* prefix = reinterpret_cast<int*>(smem + L::kPrefixOff);
+  int* vis_s = reinterpret_cast<int*>(smem + L::kVisOff);  // validated visible counts
   float* wsm = reinterpret_cast<float*>(smem + L::kWOff);
+  float* xch = reinterpret_cast<float*>(smem + L::kXchOff);
+  uint32_t* hsm = reinterpret_cast<uint32_t*>(smem + L::kHistOff);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
@@ -87,10 +154,12 @@ __global__ void __launch_bounds__(kIxThreads, 1)
       mbar_init(&full[i], 1);
       mbar_init(&empty[i], 1);
     }
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < kIxAcc; ++i) {
       mbar_init(&tfull[i], 1);
-      mbar_init(&tempty[i], 128);
-      mbar_init(&qfull[i], 128);
+      mbar_init(&tempty[i], 256);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&qfull[i], 256);
       mbar_init(&qempty[i], 1);
     }
     *abort = 0;
@@ -101,9 +170,10 @@ __global__ void __launch_bounds__(kIxThreads, 1)
     tmem_alloc(tmem_slot, L::kTmemCols);
     tmem_relinquish();
   }
+  for (int i = threadIdx.x; i < kIxHistBins; i += kIxThreads) hsm[i] = 0u;
   pdl_wait();  // pool rows / visibility may come from the preceding append kernel
 
-  // tiles per row and their prefix (warp 0)
+  // validated visible counts, tiles per row and their prefix (warp 0)
   if (warp == 0) {
     const int per_lane = (batch + 31) / 32;
     const int b0 = lane * per_lane;
@@ -114,6 +184,7 @@ __global__ void __launch_bounds__(kIxThreads, 1)
         flag(err, DSR_ERR_ID);
         v = 0;
       }
+      vis_s[b] = v;
       local += (v + kIxTile - 1) / kIxTile;
     }
     int incl = local;
@@ -125,9 +196,7 @@ __global__ void __launch_bounds__(kIxThreads, 1)
     int run = incl - local;
     for (int b = b0; b < b0 + per_lane && b < batch; ++b) {
       prefix[b] = run;
-      int v = visible[b];
-      if (v < 0 || int64_t(v) > table_stride * 64 || int64_t(v) > score_stride) v = 0;
-      run += (v + kIxTile - 1) / kIxTile;
+      run += (vis_s[b] + kIxTile - 1) / kIxTile;
     }
     if (lane == 31) prefix[batch] = incl;
   }
@@ -140,37 +209,55 @@ __global__ void __launch_bounds__(kIxThreads, 1)
   const int t_lo = int((int64_t(total) * blockIdx.x) / gridDim.x);
   const int t_hi = int((int64_t(total) * (blockIdx.x + 1)) / gridDim.x);
 
+  if (t_lo >= t_hi && warp >= 2 && mla_q != nullptr)
+    mla_query_image(mla_q, mla_img, batch, mla_heads, threadIdx.x - 64, 256);
   if (t_lo < t_hi) {
     if (warp == 0) {
       // ------------------------------------------------------------ producer
-      if (lane == 0) {
-        int b = find_row(prefix, batch, t_lo);
-        for (int t = t_lo, s = 0; t < t_hi; ++t, ++s) {
-          while (t >= prefix[b + 1]) ++b;
+      // Block-table entries of 16 tiles are fetched by the 32 lanes at once
+      // (one load latency per 16 tiles); lane 0 then issues the TMA boxes.
+      for (int g0 = t_lo, s0 = 0; g0 < t_hi; g0 += 16, s0 += 16) {
+        const int t = g0 + (lane >> 1), blk = lane & 1;
+        int64_t pb = -1;  // -1: block beyond the visible keys, not loaded
+        if (t < t_hi) {
+          const int b = find_row(prefix, batch, t);
           const int tile = t - prefix[b];
-          const int vis = visible[b];  // validated by the prefix pass (row has tiles)
-          const int stage = s % kIxStages;
-          if (!mbar_wait(&empty[stage], ((s / kIxStages) & 1) ^ 1, abort, err)) break;
-          const int first = tile * kIxTile;
-          const int nblk = (vis - first) > 64 ? 2 : 1;
-          mbar_arrive_expect_tx(&full[stage], uint32_t(nblk) * 2u * 8192u);
-          const uint32_t dst = sbase + L::kStagesOff + stage * kIxStageBytes;
-          for (int blk = 0; blk < nblk; ++blk) {
-            int64_t pb = block_table[int64_t(b) * table_stride + tile * 2 + blk];
+          if (tile * kIxTile + blk * 64 < vis_s[b]) {
+            pb = block_table[int64_t(b) * table_stride + tile * 2 + blk];
             if (pb < 0 || pb >= pool_blocks) {
               flag(err, DSR_ERR_ID);
               pb = 0;
             }
-            for (int kh = 0; kh < 2; ++kh)
-              tma_load_2d(dst + kh * 16384 + blk * 8192, &kmap, &full[stage], kh * 64,
-                          int32_t(pb * 64));
           }
         }
+        bool ok = true;
+        for (int j = 0; j < 16 && g0 + j < t_hi; ++j) {
+          const int64_t pb0 = __shfl_sync(0xffffffffu, pb, 2 * j);
+          const int64_t pb1 = __shfl_sync(0xffffffffu, pb, 2 * j + 1);
+          if (lane == 0) {
+            const int s = s0 + j;
+            const int stage = s % kIxStages;
+            ok = mbar_wait(&empty[stage], ((s / kIxStages) & 1) ^ 1, abort, err);
+            if (ok) {
+              const int nblk = pb1 >= 0 ? 2 : 1;
+              mbar_arrive_expect_tx(&full[stage], uint32_t(nblk) * 2u * 8192u);
+              const uint32_t dst = sbase + L::kStagesOff + stage * kIxStageBytes;
+#pragma unroll
+              for (int kh = 0; kh < 2; ++kh) {
+                tma_load_2d(dst + kh * 16384, &kmap, &full[stage], kh * 64, int32_t(pb0 * 64));
+                if (nblk == 2)
+                  tma_load_2d(dst + kh * 16384 + 8192, &kmap, &full[stage], kh * 64, int32_t(pb1 * 64));
+              }
+            }
+          }
+          if (!__shfl_sync(0xffffffffu, ok ? 1 : 0, 0)) break;
+        }
+        if (*abort) break;
       }
     } else if (warp == 1) {
       // ----------------------------------------------------------- MMA issuer
       if (lane == 0) {
-        constexpr uint32_t idesc = umma_idesc_bf16(128, N, false, false);
+        uint32_t idesc = umma_idesc_bf16(128, N, false, false);
         int b = find_row(prefix, batch, t_lo);
         int rowseq = 0;
         for (int t = t_lo, s = 0; t < t_hi; ++t, ++s) {
@@ -181,11 +268,15 @@ __global__ void __launch_bounds__(kIxThreads, 1)
           const bool row_first = (t == t_lo) || (t == prefix[b]);
           const bool row_last = (t + 1 == t_hi) || (t + 1 == prefix[b + 1]);
           const int slot = rowseq & 1;
-          if (row_first && !mbar_wait(&qfull[slot], (rowseq >> 1) & 1, abort, err)) break;
+          if (row_first) {
+            if (!mbar_wait(&qfull[slot], (rowseq >> 1) & 1, abort, err)) break;
+            // a BF16-exact query has q_lo == 0: contract only the q_hi rows
+            idesc = umma_idesc_bf16(128, qlonz[slot] ? N : H, false, false);
+          }
           const int stage = s % kIxStages;
           if (!mbar_wait(&full[stage], (s / kIxStages) & 1, abort, err)) break;
-          const int acc = s & 1;
-          if (!mbar_wait(&tempty[acc], ((s >> 1) & 1) ^ 1, abort, err)) break;
+          const int acc = s % kIxAcc;
+          if (!mbar_wait(&tempty[acc], ((s / kIxAcc) & 1) ^ 1, abort, err)) break;
           tc_fence_after();
           const uint32_t a0 = sbase + L::kStagesOff + stage * kIxStageBytes;
           const uint32_t b0 = sbase + L::kQOff + slot * L::kQSlotBytes;
@@ -203,26 +294,37 @@ __global__ void __launch_bounds__(kIxThreads, 1)
       __syncwarp();
     } else {
       // ------------------------------------------------------------- epilogue
-      const int et = threadIdx.x - 64;  // 0..127
-      const int sp = warp & 3;          // TMEM sub-partition of this warp
+      // Two warpgroups share every tile: warpgroup g reduces heads [g*H/2, (g+1)*H/2).
+      const int et = threadIdx.x - 64;  // 0..255
+      const int wg = et >> 7;
+      const int row_in_tile = (warp & 3) * 32 + lane;  // TMEM lane of this thread
+      if (mla_q != nullptr) mla_query_image(mla_q, mla_img, batch, mla_heads, et, 256);
       int b = find_row(prefix, batch, t_lo);
       int rowseq = 0;
+      uint32_t lonz0 = 1, lonz1 = 1;  // q_lo != 0 for the row in slot 0 / 1
       // prepares Q (hi/lo bf16, 128-byte swizzled K-major) and weights of row rb into slot
       auto prepare = [&](int rb, int seq) -> bool {
         const int slot = seq & 1;
-        if (!mbar_wait(&qempty[slot], ((seq >> 1) & 1) ^ 1, abort, err)) return false;
+        // every epilogue thread reaches the barrier reduction below, aborted or not
+        const bool live = !*abort && mbar_wait(&qempty[slot], ((seq >> 1) & 1) ^ 1, abort, err);
         uint8_t* qs = smem + L::kQOff + slot * L::kQSlotBytes;
         const float4* src = reinterpret_cast<const float4*>(q + int64_t(rb) * H * 128);
-        for (int i = et; i < H * 32; i += 128) {  // float4 index
+        constexpr int kPer = H * 32 / 256;  // float4 per thread, all loads in flight at once
+        float4 xv[kPer];
+        uint32_t lo_any = 0;
+#pragma unroll
+        for (int j = 0; j < kPer; ++j) xv[j] = __ldg(src + et + j * 256);
+#pragma unroll
+        for (int j = 0; j < kPer && live; ++j) {
+          const int i = et + j * 256;
           const int h = i >> 5, d = (i & 31) * 4;
-          const float4 x = src[i];
-          const float xs[4] = {x.x, x.y, x.z, x.w};
+          const float xs[4] = {xv[j].x, xv[j].y, xv[j].z, xv[j].w};
           uint16_t hi[4], lo[4];
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const __nv_bfloat16 hb = __float2bfloat16_rn(xs[j]);
-            hi[j] = __bfloat16_as_ushort(hb);
-            lo[j] = __bfloat16_as_ushort(__float2bfloat16_rn(xs[j] - __bfloat162float(hb)));
+          for (int e = 0; e < 4; ++e) {
+            const __nv_bfloat16 hb = __float2bfloat16_rn(xs[e]);
+            hi[e] = __bfloat16_as_ushort(hb);
+            lo[e] = __bfloat16_as_ushort(__float2bfloat16_rn(xs[e] - __bfloat162float(hb)));
           }
           const int half = d >> 6, col = d & 63;
           uint8_t* base = qs + half * (N * 128);
@@ -230,15 +332,40 @@ __global__ void __launch_bounds__(kIxThreads, 1)
               make_uint2(hi[0] | (uint32_t(hi[1]) << 16), hi[2] | (uint32_t(hi[3]) << 16));
           *reinterpret_cast<uint2*>(base + sw128_offset(H + h, col)) =
               make_uint2(lo[0] | (uint32_t(lo[1]) << 16), lo[2] | (uint32_t(lo[3]) << 16));
+          lo_any |= (lo[0] | lo[1] | lo[2] | lo[3]) & 0x7fffu;
         }
-        for (int h = et; h < H; h += 128) wsm[slot * H + h] = weights[int64_t(rb) * H + h];
+        for (int h = et; h < H; h += 256) wsm[slot * H + h] = weights[int64_t(rb) * H + h];
+        uint32_t any;
+        asm volatile(
+            "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\t"
+            "bar.red.or.pred q, 2, 256, p;\n\tselp.u32 %0, 1, 0, q;\n\t}"
+            : "=r"(any)
+            : "r"(lo_any));
+        if (et == 0) qlonz[slot] = int(any);  // read by the MMA issuer after qfull
+        (slot ? lonz1 : lonz0) = any;
         fence_proxy_async_smem();
         mbar_arrive(&qfull[slot]);
-        return true;
+        return live;
       };
-      bool ok = prepare(b, 0);
-      for (int t = t_lo, s = 0; ok && t < t_hi; ++t, ++s) {
+      // flushes the CTA's score histogram of row rb into the row's global histogram
+      auto flush = [&](int rb) {
+        asm volatile("bar.sync 3, 256;" ::: "memory");
+        if (hist != nullptr)
+          for (int i = et; i < kIxHistBins; i += 256) {
+            const uint32_t v = hsm[i];
+            if (v) {
+              atomicAdd(hist + int64_t(rb) * kIxHistBins + i, v);
+              hsm[i] = 0u;
+            }
+          }
+        asm volatile("bar.sync 3, 256;" ::: "memory");
+      };
+      // Every epilogue thread walks every tile and reaches every named barrier;
+      // after an aborted wait it only skips the work (no early exit).
+      bool live = prepare(b, 0);
+      for (int t = t_lo, s = 0; t < t_hi; ++t, ++s) {
         if (t >= prefix[b + 1]) {  // next non-empty row
+          flush(b);
           while (t >= prefix[b + 1]) ++b;
           ++rowseq;
         }
@@ -246,36 +373,54 @@ __global__ void __launch_bounds__(kIxThreads, 1)
         if (t + 1 < t_hi && t + 1 == prefix[b + 1]) {
           int nb = b + 1;
           while (t + 1 >= prefix[nb + 1]) ++nb;
-          if (!prepare(nb, rowseq + 1)) break;
+          live = prepare(nb, rowseq + 1) && live;
         }
-        const int acc = s & 1;
-        if (!mbar_wait(&tfull[acc], (s >> 1) & 1, abort, err)) break;
-        tc_fence_after();
-        const float* w = wsm + (rowseq & 1) * H;
-        const uint32_t taddr = tmem_base + acc * N + (uint32_t(sp * 32) << 16);
+        const int acc = s % kIxAcc;
+        live = live && !*abort && mbar_wait(&tfull[acc], (s / kIxAcc) & 1, abort, err);
         float score = 0.f, check = 0.f;
+        if (live) {
+          tc_fence_after();
+          const float* w = wsm + (rowseq & 1) * H + wg * HH;
+          const uint32_t taddr = tmem_base + acc * N + wg * HH + (uint32_t((warp & 3) * 32) << 16);
+          if ((rowseq & 1) ? lonz1 : lonz0) {
+            uint32_t hi[HH], lo[HH];
+            tmem_ld_cols<HH>(taddr, hi);
+            tmem_ld_cols<HH>(taddr + H, lo);
+            tmem_wait_ld();
 #pragma unroll
-        for (int c = 0; c < H; c += 16) {
-          uint32_t hi[16], lo[16];
-          tmem_ld16(taddr + c, hi);
-          tmem_ld16(taddr + H + c, lo);
-          tmem_wait_ld();
+            for (int j = 0; j < HH; ++j) {
+              const float d = __uint_as_float(hi[j]) + __uint_as_float(lo[j]);
+              check += d;
+              score = fmaf(fmaxf(d, 0.f), w[j], score);
+            }
+          } else {
+            uint32_t hi[HH];
+            tmem_ld_cols<HH>(taddr, hi);
+            tmem_wait_ld();
 #pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            const float d = __uint_as_float(hi[j]) + __uint_as_float(lo[j]);
-            check += d;
-            score = fmaf(fmaxf(d, 0.f), w[c + j], score);
+            for (int j = 0; j < HH; ++j) {
+              const float d = __uint_as_float(hi[j]);
+              check += d;
+              score = fmaf(fmaxf(d, 0.f), w[j], score);
+            }
           }
+          tc_fence_before();
+          mbar_arrive(&tempty[acc]);
         }
-        tc_fence_before();
-        mbar_arrive(&tempty[acc]);
+        if (wg == 1) xch[(s & 1) * 128 + row_in_tile] = score;
         const int tile = t - prefix[b];
-        const int p = tile * kIxTile + sp * 32 + lane;
-        if (p < visible[b] && p < score_stride) {
-          if (!isfinite(score) || !isfinite(check)) flag(err, DSR_ERR_NONFINITE);
+        const int p = tile * kIxTile + row_in_tile;
+        if (live && p < vis_s[b] && !isfinite(check)) flag(err, DSR_ERR_NONFINITE);
+        asm volatile("bar.sync 3, 256;" ::: "memory");
+        if (live && wg == 0 && p < vis_s[b]) {
+          score += xch[(s & 1) * 128 + row_in_tile];
+          if (!isfinite(score)) flag(err, DSR_ERR_NONFINITE);
           scores[int64_t(b) * score_stride + p] = score;
+          // NaN ranks above +inf, as in the top-k kernel's key mapping
+          atomicAdd(&hsm[isnan(score) ? kIxHistBins - 1 : score_key(score) >> 21], 1u);
         }
       }
+      flush(b);
     }
   }
   pdl_launch_dependents();
@@ -291,6 +436,7 @@ template <int H>
 int launch_ix(const CUtensorMap& map, const float* q, const float* weights,
               const int32_t* block_table, int64_t table_stride, const int32_t* visible,
               int64_t pool_blocks, float* scores, int64_t score_stride, int32_t* err, int batch,
+              const float* mla_q, uint16_t* mla_img, int mla_heads, uint32_t* hist,
               cudaStream_t stream, bool pdl) {
   using L = IxLayout<H>;
   static bool configured = false;
@@ -312,7 +458,8 @@ int launch_ix(const CUtensorMap& map, const float* q, const float* weights,
   cfg.numAttrs = pdl ? 1 : 0;
   const cudaError_t e =
       cudaLaunchKernelEx(&cfg, indexer_decode_kernel<H>, map, q, weights, block_table, table_stride,
-                         visible, pool_blocks, scores, score_stride, err, batch);
+                         visible, pool_blocks, scores, score_stride, err, batch, mla_q, mla_img,
+                         mla_heads, hist);
   if (e != cudaSuccess) return fail(DSR_ECUDA, "indexer launch: %s", cudaGetErrorString(e));
   return DSR_OK;
 }
@@ -323,7 +470,12 @@ int launch_indexer_decode(const float* q, const float* weights, const uint16_t* 
                           int64_t pool_blocks, const int32_t* block_table, int64_t table_stride,
                           const int32_t* visible, float* scores, int64_t score_stride,
                           int32_t* err, int64_t batch, int64_t heads, cudaStream_t stream,
-                          bool pdl) {
+                          bool pdl, const float* mla_q, uint16_t* mla_img, int64_t mla_heads,
+                          uint32_t* hist) {
+  DSR_REQUIRE(mla_q == nullptr || (mla_img != nullptr && aligned16(mla_q) && aligned16(mla_img) &&
+                                   (mla_heads == 16 || mla_heads == 32 || mla_heads == 64 ||
+                                    mla_heads == 128)),
+              "indexer_decode: invalid MLA query image job");
   DSR_REQUIRE(q && weights && index_pool && block_table && visible && scores && err,
               "indexer_decode: null pointer");
   DSR_REQUIRE(heads == 16 || heads == 32 || heads == 64,
@@ -343,13 +495,13 @@ int launch_indexer_decode(const float* q, const float* weights, const uint16_t* 
   switch (heads) {
     case 16:
       return launch_ix<16>(map, q, weights, block_table, table_stride, visible, pool_blocks, scores,
-                           score_stride, err, int(batch), stream, pdl);
+                           score_stride, err, int(batch), mla_q, mla_img, int(mla_heads), hist, stream, pdl);
     case 32:
       return launch_ix<32>(map, q, weights, block_table, table_stride, visible, pool_blocks, scores,
-                           score_stride, err, int(batch), stream, pdl);
+                           score_stride, err, int(batch), mla_q, mla_img, int(mla_heads), hist, stream, pdl);
     default:
       return launch_ix<64>(map, q, weights, block_table, table_stride, visible, pool_blocks, scores,
-                           score_stride, err, int(batch), stream, pdl);
+                           score_stride, err, int(batch), mla_q, mla_img, int(mla_heads), hist, stream, pdl);
   }
 }
 
@@ -363,5 +515,5 @@ extern "C" int dsr_indexer_decode(const float* q, const float* weights, const ui
   dsr::clear_error();
   return dsr::launch_indexer_decode(q, weights, index_pool, pool_blocks, block_table, table_stride,
                                     visible, scores, score_stride, err, batch, heads,
-                                    dsr::as_stream(stream), false);
+                                    dsr::as_stream(stream), false, nullptr, nullptr, 0, nullptr);
 }

@@ -45,7 +45,7 @@ struct MlaLayout {
   static constexpr int kRedBytes = 2 * kTpk * HG * 4;
   static constexpr int kValidOff = kRedOff + kRedBytes;
   static constexpr int kBarOff = kValidOff + kMlaTile * 4;
-  static constexpr int kMiscOff = kBarOff + 4 * 8;
+  static constexpr int kMiscOff = kBarOff + 5 * 8;
   static constexpr int kBytes = kMiscOff + 16;
   static constexpr int kAlloc = kBytes + 1024;
   static constexpr uint32_t kTmemCols = 5 * HG <= 128 ? 128 : (5 * HG <= 256 ? 256 : 512);
@@ -60,7 +60,8 @@ __global__ void __launch_bounds__(kMlaThreads, 1)
                       const int32_t* __restrict__ topk, int k, const uint16_t* __restrict__ swa,
                       const int32_t* __restrict__ swa_len, float scale_log2,
                       float* __restrict__ part_o, float* __restrict__ part_m,
-                      float* __restrict__ part_l, int32_t* err, int heads) {
+                      float* __restrict__ part_l, int32_t* err, int heads,
+                      const uint16_t* __restrict__ q_img) {
   using L = MlaLayout<HG>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -71,6 +72,7 @@ __global__ void __launch_bounds__(kMlaThreads, 1)
   uint64_t* bar_s = bars + 1;   // S^T complete (commit)
   uint64_t* bar_p = bars + 2;   // P^T written (128 arrivals)
   uint64_t* bar_o = bars + 3;   // O^T complete (commit)
+  uint64_t* bar_q = bars + 4;   // BF16 query image landed (bulk copy)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kMiscOff);
   volatile int* abort = reinterpret_cast<volatile int*>(smem + L::kMiscOff + 4);
   int* valid = reinterpret_cast<int*>(smem + L::kValidOff);
@@ -86,6 +88,7 @@ __global__ void __launch_bounds__(kMlaThreads, 1)
     mbar_init(bar_s, 1);
     mbar_init(bar_p, 128);
     mbar_init(bar_o, 1);
+    mbar_init(bar_q, 1);
     *abort = 0;
     fence_barrier_init();
   }
@@ -100,11 +103,52 @@ __global__ void __launch_bounds__(kMlaThreads, 1)
   const uint32_t tmem_s = tmem_base;
   const uint32_t tmem_o = tmem_base + HG;
 
-  pdl_wait();  // top-k ids come from the preceding kernel
+  pdl_launch_dependents();  // the combine kernel may start its prologue early
 
   if (warp < 4) {
     const int t = threadIdx.x;  // key slot of this thread == TMEM lane
-    // ---- resolve the row of key t
+    if (q_img != nullptr) {
+      // ---- query: the preceding indexer kernel wrote the BF16 image; one bulk copy
+      pdl_wait();
+      if (t == 0) {
+        constexpr uint32_t kBytes = kMlaBlocks * HG * 128;
+        const uint16_t* src = q_img + (int64_t(b) * (heads / HG) + hg) * (kBytes / 2);
+        mbar_arrive_expect_tx(bar_q, kBytes);
+        bulk_load(sbase + L::kQOff, src, kBytes, bar_q);
+      }
+    } else {
+      // ---- query: FP32 -> BF16, 128-byte swizzled K-major, 9 column blocks of HG rows
+      // (8 float4 loads per thread in flight per batch)
+      const float4* qsrc = reinterpret_cast<const float4*>(q + (int64_t(b) * heads + h0) * kMlaD);
+      uint8_t* qs = smem + L::kQOff;
+      constexpr int kTotal = HG * (kMlaD / 4);
+      constexpr int kBatch = 8;
+      for (int i0 = 0; i0 < kTotal; i0 += 128 * kBatch) {
+        float4 xv[kBatch];
+#pragma unroll
+        for (int j = 0; j < kBatch; ++j) {
+          const int i = i0 + j * 128 + t;
+          if (i < kTotal) xv[j] = __ldg(qsrc + i);
+        }
+#pragma unroll
+        for (int j = 0; j < kBatch; ++j) {
+          const int i = i0 + j * 128 + t;
+          if (i < kTotal) {
+            const int h = i / (kMlaD / 4), d = (i % (kMlaD / 4)) * 4;
+            const float4 x = xv[j];
+            const uint32_t lo = __bfloat16_as_ushort(__float2bfloat16_rn(x.x)) |
+                                (uint32_t(__bfloat16_as_ushort(__float2bfloat16_rn(x.y))) << 16);
+            const uint32_t hi = __bfloat16_as_ushort(__float2bfloat16_rn(x.z)) |
+                                (uint32_t(__bfloat16_as_ushort(__float2bfloat16_rn(x.w))) << 16);
+            *reinterpret_cast<uint2*>(qs + (d >> 6) * (HG * 128) + sw128_offset(h, d & 63)) =
+                make_uint2(lo, hi);
+          }
+        }
+      }
+      if (t == 0) mbar_arrive(bar_q);
+      if (tile != 0) pdl_wait();
+    }
+    // ---- resolve the row of key t (top-k ids come from the preceding kernel)
     const uint16_t* src = nullptr;
     if (tile == 0) {
       int len = swa_len[b];
@@ -145,21 +189,6 @@ __global__ void __launch_bounds__(kMlaThreads, 1)
       }
     }
     cp_async_commit();
-    // ---- query: FP32 -> BF16, 128-byte swizzled K-major, 9 column blocks of HG rows
-    {
-      const float4* qsrc = reinterpret_cast<const float4*>(q + (int64_t(b) * heads + h0) * kMlaD);
-      uint8_t* qs = smem + L::kQOff;
-      for (int i = t; i < HG * (kMlaD / 4); i += 128) {
-        const int h = i / (kMlaD / 4), d = (i % (kMlaD / 4)) * 4;
-        const float4 x = qsrc[i];
-        const uint32_t lo = __bfloat16_as_ushort(__float2bfloat16_rn(x.x)) |
-                            (uint32_t(__bfloat16_as_ushort(__float2bfloat16_rn(x.y))) << 16);
-        const uint32_t hi = __bfloat16_as_ushort(__float2bfloat16_rn(x.z)) |
-                            (uint32_t(__bfloat16_as_ushort(__float2bfloat16_rn(x.w))) << 16);
-        *reinterpret_cast<uint2*>(qs + (d >> 6) * (HG * 128) + sw128_offset(h, d & 63)) =
-            make_uint2(lo, hi);
-      }
-    }
     cp_async_wait_all();
     fence_proxy_async_smem();
     mbar_arrive(bar_kv);
@@ -171,17 +200,15 @@ __global__ void __launch_bounds__(kMlaThreads, 1)
       tc_fence_after();
       const bool v = valid[t] != 0;
       const uint32_t taddr = tmem_s + (uint32_t(warp * 32) << 16);
+      uint32_t r[HG];
 #pragma unroll
-      for (int c = 0; c < HG; c += 16) {
-        uint32_t r[16];
-        tmem_ld16(taddr + c, r);
-        tmem_wait_ld();
+      for (int c = 0; c < HG; c += 16) tmem_ld16(taddr + c, *reinterpret_cast<uint32_t(*)[16]>(r + c));
+      tmem_wait_ld();
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          float s = __uint_as_float(r[j]) * scale_log2;
-          if (v && !isfinite(s)) flag(err, DSR_ERR_NONFINITE);
-          sT[(c + j) * L::kSPitch + t] = v ? s : -CUDART_INF_F;
-        }
+      for (int c = 0; c < HG; ++c) {
+        const float s = __uint_as_float(r[c]) * scale_log2;
+        if (v && !isfinite(s)) flag(err, DSR_ERR_NONFINITE);
+        sT[c * L::kSPitch + t] = v ? s : -CUDART_INF_F;
       }
     }
     asm volatile("bar.sync 1, 128;" ::: "memory");
@@ -235,19 +262,17 @@ __global__ void __launch_bounds__(kMlaThreads, 1)
       for (int c = 0; c < kMlaDv / 128; ++c) {
         const uint32_t taddr = tmem_o + c * HG + (uint32_t(warp * 32) << 16);
         const int d = c * 128 + t;
+        uint32_t r[HG];
 #pragma unroll
-        for (int hh = 0; hh < HG; hh += 16) {
-          uint32_t r[16];
-          tmem_ld16(taddr + hh, r);
-          tmem_wait_ld();
+        for (int hh = 0; hh < HG; hh += 16) tmem_ld16(taddr + hh, *reinterpret_cast<uint32_t(*)[16]>(r + hh));
+        tmem_wait_ld();
 #pragma unroll
-          for (int j = 0; j < 16; ++j) o[int64_t(hh + j) * kMlaDv + d] = __uint_as_float(r[j]);
-        }
+        for (int hh = 0; hh < HG; ++hh) o[int64_t(hh) * kMlaDv + d] = __uint_as_float(r[hh]);
       }
     }
   } else if (lane == 0) {
     // ------------------------------------------------------------ MMA issuer
-    if (mbar_wait(bar_kv, 0, abort, err)) {
+    if (mbar_wait(bar_kv, 0, abort, err) && mbar_wait(bar_q, 0, abort, err)) {
       tc_fence_after();
       constexpr uint32_t idesc_s = umma_idesc_bf16(128, HG, false, false);
 #pragma unroll 4
@@ -279,7 +304,6 @@ __global__ void __launch_bounds__(kMlaThreads, 1)
       }
     }
   }
-  pdl_launch_dependents();
   tc_fence_before();
   __syncthreads();
   if (warp == 4) {
@@ -297,40 +321,71 @@ __global__ void __launch_bounds__(128) lse_combine_kernel(
     const float* __restrict__ part_l, int parts, const float* __restrict__ sink,
     float* __restrict__ out, float* __restrict__ out_m, float* __restrict__ out_l, int32_t* err,
     int heads, int dv) {
+  extern __shared__ float wgt[];  // [parts] weights e^{m_t - M}
+  __shared__ float stat[2];       // M, 1 / L (or L)
   const int b = blockIdx.x, h = blockIdx.y;
   pdl_wait();
-  float M = -CUDART_INF_F;
-  float sk = 0.f;
-  if (sink != nullptr) {
-    sk = sink[h];
-    if (!isfinite(sk)) {
-      if (threadIdx.x == 0) flag(err, DSR_ERR_NONFINITE);
-      sk = 0.f;
+  const int64_t pbase = int64_t(b) * parts * heads + h;  // partial t at pbase + t * heads
+  if (threadIdx.x < 32) {
+    const int lane = threadIdx.x;
+    float sk = 0.f, M = -CUDART_INF_F;
+    if (sink != nullptr) {
+      sk = sink[h];
+      if (!isfinite(sk)) {
+        if (lane == 0) flag(err, DSR_ERR_NONFINITE);
+        sk = 0.f;
+      }
+      sk *= kLog2e;
+      M = sk;
     }
-    sk *= kLog2e;
-    M = sk;
-  }
-  for (int t = 0; t < parts; ++t) M = fmaxf(M, part_m[(int64_t(b) * parts + t) * heads + h]);
-  const float base = M == -CUDART_INF_F ? 0.f : M;
-  float Lsum = sink != nullptr ? exp2f(sk - base) : 0.f;
-  for (int t = 0; t < parts; ++t) {
-    const int64_t i = (int64_t(b) * parts + t) * heads + h;
-    Lsum += part_l[i] * exp2f(part_m[i] - base);
-  }
-  const float inv = sink != nullptr ? 1.f / Lsum : 1.f;
-  for (int d = threadIdx.x; d < dv; d += blockDim.x) {
-    float acc = 0.f;
-    for (int t = 0; t < parts; ++t) {
-      const int64_t i = (int64_t(b) * parts + t) * heads + h;
-      acc = fmaf(part_o[i * dv + d], exp2f(part_m[i] - base), acc);
+    for (int t = lane; t < parts; t += 32) M = fmaxf(M, part_m[pbase + int64_t(t) * heads]);
+#pragma unroll
+    for (int o = 16; o; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+    const float base = M == -CUDART_INF_F ? 0.f : M;
+    float lsum = 0.f;
+    for (int t = lane; t < parts; t += 32) {
+      const int64_t i = pbase + int64_t(t) * heads;
+      const float e = exp2f(part_m[i] - base);
+      wgt[t] = e;
+      lsum += part_l[i] * e;
     }
-    const float v = acc * inv;
-    if (!isfinite(v)) flag(err, DSR_ERR_NONFINITE);
-    out[(int64_t(b) * heads + h) * dv + d] = v;
+#pragma unroll
+    for (int o = 16; o; o >>= 1) lsum += __shfl_xor_sync(0xffffffffu, lsum, o);
+    if (lane == 0) {
+      if (sink != nullptr) lsum += exp2f(sk - base);
+      stat[0] = M;
+      stat[1] = lsum;
+    }
+  }
+  __syncthreads();
+  const float inv = sink != nullptr ? 1.f / stat[1] : 1.f;
+  // each thread owns 4 consecutive columns; the parts are read 8 at a time,
+  // all 8 float4 loads in flight before they are accumulated
+  for (int d = threadIdx.x * 4; d < dv; d += blockDim.x * 4) {
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int t0 = 0; t0 < parts; t0 += 8) {
+      float4 v[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        if (t0 + j < parts)
+          v[j] = __ldg(reinterpret_cast<const float4*>(part_o + (pbase + int64_t(t0 + j) * heads) * dv + d));
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        if (t0 + j < parts) {
+          const float w = wgt[t0 + j];
+          acc.x = fmaf(v[j].x, w, acc.x);
+          acc.y = fmaf(v[j].y, w, acc.y);
+          acc.z = fmaf(v[j].z, w, acc.z);
+          acc.w = fmaf(v[j].w, w, acc.w);
+        }
+    }
+    const float4 o = make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
+    if (!isfinite(o.x) || !isfinite(o.y) || !isfinite(o.z) || !isfinite(o.w)) flag(err, DSR_ERR_NONFINITE);
+    *reinterpret_cast<float4*>(out + (int64_t(b) * heads + h) * dv + d) = o;
   }
   if (sink == nullptr && threadIdx.x == 0) {
-    out_m[int64_t(b) * heads + h] = M;
-    out_l[int64_t(b) * heads + h] = Lsum;
+    out_m[int64_t(b) * heads + h] = stat[0];
+    out_l[int64_t(b) * heads + h] = stat[1];
   }
 }
 
@@ -339,7 +394,8 @@ int launch_mla(const float* q, const uint16_t* kv_pool, int64_t pool_blocks,
                const int32_t* block_table, int64_t table_stride, const int32_t* visible,
                const int32_t* topk, int64_t k, const uint16_t* swa, const int32_t* swa_len,
                float scale, float* part_o, float* part_m, float* part_l, int32_t* err,
-               int64_t batch, int64_t heads, int tiles, cudaStream_t stream, bool pdl) {
+               int64_t batch, int64_t heads, int tiles, cudaStream_t stream, bool pdl,
+               const uint16_t* q_img) {
   using L = MlaLayout<HG>;
   static bool configured = false;
   if (!configured) {
@@ -361,7 +417,7 @@ int launch_mla(const float* q, const uint16_t* kv_pool, int64_t pool_blocks,
   const cudaError_t e = cudaLaunchKernelEx(&cfg, mla_decode_kernel<HG>, q, kv_pool, pool_blocks,
                                            block_table, table_stride, visible, topk, int(k), swa,
                                            swa_len, scale * kLog2e, part_o, part_m, part_l, err,
-                                           int(heads));
+                                           int(heads), q_img);
   if (e != cudaSuccess) return fail(DSR_ECUDA, "mla launch: %s", cudaGetErrorString(e));
   return DSR_OK;
 }
@@ -383,11 +439,13 @@ int launch_lse_combine(const float* part_o, const float* part_m, const float* pa
   DSR_REQUIRE(sink != nullptr || (out_m != nullptr && out_l != nullptr),
               "lse_combine: an unnormalised combine needs out_m and out_l");
   DSR_REQUIRE(parts > 0 && parts <= 4096 && batch > 0 && batch <= 65535 && heads > 0 &&
-                  heads <= 65535 && dv > 0 && dv <= 4096,
-              "lse_combine: invalid shape");
+                  heads <= 65535 && dv > 0 && dv <= 4096 && dv % 4 == 0,
+              "lse_combine: invalid shape (dv must be a multiple of 4)");
+  DSR_REQUIRE(aligned16(part_o) && aligned16(out), "lse_combine: part_o and out must be 16-byte aligned");
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(unsigned(batch), unsigned(heads), 1);
   cfg.blockDim = dim3(128, 1, 1);
+  cfg.dynamicSmemBytes = size_t(parts) * 4;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -406,7 +464,8 @@ int launch_mla_decode(const float* q, const uint16_t* kv_pool, int64_t pool_bloc
                       const int32_t* topk, int64_t k, const uint16_t* swa,
                       const int32_t* swa_len, const float* sink, float scale, float* out,
                       void* workspace, size_t workspace_bytes, int32_t* err, int64_t batch,
-                      int64_t heads, cudaStream_t stream, bool pdl) {
+                      int64_t heads, cudaStream_t stream, bool pdl, const uint16_t* q_img) {
+  DSR_REQUIRE(q_img == nullptr || aligned16(q_img), "sparse_mla_decode: query image must be 16-byte aligned");
   DSR_REQUIRE(q && kv_pool && block_table && visible && topk && swa && swa_len && sink && out &&
                   err && workspace,
               "sparse_mla_decode: null pointer");
@@ -431,17 +490,17 @@ int launch_mla_decode(const float* q, const uint16_t* kv_pool, int64_t pool_bloc
     case 16:
       rc = launch_mla<16>(q, kv_pool, pool_blocks, block_table, table_stride, visible, topk, k, swa,
                           swa_len, scale, part_o, part_m, part_l, err, batch, heads, tiles, stream,
-                          pdl);
+                          pdl, q_img);
       break;
     case 32:
       rc = launch_mla<32>(q, kv_pool, pool_blocks, block_table, table_stride, visible, topk, k, swa,
                           swa_len, scale, part_o, part_m, part_l, err, batch, heads, tiles, stream,
-                          pdl);
+                          pdl, q_img);
       break;
     default:
       rc = launch_mla<64>(q, kv_pool, pool_blocks, block_table, table_stride, visible, topk, k, swa,
                           swa_len, scale, part_o, part_m, part_l, err, batch, heads, tiles, stream,
-                          pdl);
+                          pdl, q_img);
       break;
   }
   if (rc != DSR_OK) return rc;

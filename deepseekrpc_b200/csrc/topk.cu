@@ -6,310 +6,453 @@
 // then stable descending argsort by score), output sorted ascending and padded
 // with -1.
 //
-// Design: one thread-block cluster of 8 CTAs per row; CTA j owns the j-th
-// contiguous eighth of the row (kept in shared memory when it fits).  Scores
-// are mapped to order-preserving uint32 keys and the k-th largest key T is
-// found by an 11/11/10-bit radix select whose histograms are reduced across
-// the cluster through distributed shared memory.  The selected set is
-// {key > T} plus the first (in id order) `need` entries with key == T, which
-// reproduces the lower-id tie rule.  A warp-ballot ordered compaction then
-// writes the ids in ascending order.  No global scratch memory is used.
-#include <cooperative_groups.h>
-
+// Every entry gets a unique 63-bit composite key (u << 31) | (0x7fffffff - id),
+// u = order-preserving uint32 of the score (-0.0 == +0.0): "larger key" is
+// exactly "ranked earlier" under the reference rule, so the selected set is
+// {key >= K*} where K* is the k-th largest key.
+//
+// Design (no grid-wide barrier, no spinning):
+//   * a per-row 11-bit histogram of the score keys is built first, either by the
+//     indexer epilogue while it produces the scores, or by topk_hist_kernel;
+//   * topk_select_kernel spreads each row over many CTAs in 32-entry words.
+//     Every CTA finds the threshold bin from the row histogram, writes one
+//     bitmap word per 32 entries (bit set = key above the threshold bin) with a
+//     warp ballot, and appends its threshold-bin entries to the row's candidate
+//     list;
+//   * the last CTA to finish a row (atomic ticket after a fence) resolves K*
+//     among the candidates with local radix passes over the remaining 52 bits,
+//     sets their bits, converts the bitmap into the ascending id list and
+//     clears the row's histogram, ticket and candidate count for the next call.
+// Candidate-list overflow (heavily tied scores) falls back to the last CTA
+// resolving K* by scanning the whole row.  The workspace must be zero before
+// its first use; every completed call leaves it zero again.
 #include "common.cuh"
 #include "host_common.h"
 
 #include <math_constants.h>
 
-namespace cg = cooperative_groups;
-
 namespace dsr {
 namespace {
 
-constexpr int kTkCluster = 8;
-constexpr int kTkThreads = 512;
+constexpr int kTkThreads = 256;
 constexpr int kTkWarps = kTkThreads / 32;
-constexpr int kTkBins = 2048;
-constexpr int kTkResident = 40960;  // keys per CTA kept in shared memory (160 KiB)
+constexpr int kTkBins = 2048;      // level-0 digit: 11 bits
+constexpr int kTkCap = 8192;       // candidate entries per row
+constexpr int kTkLocalCap = 2048;  // candidate entries one CTA stages in shared memory
+constexpr int kTkLevels = 6;
+__constant__ int kTkShift[kTkLevels] = {52, 41, 31, 20, 10, 0};
+__constant__ int kTkBits[kTkLevels] = {11, 11, 10, 11, 10, 10};
+
+__device__ __forceinline__ uint64_t composite(uint32_t u, uint32_t lo) {
+  return (uint64_t(u) << 31) | uint64_t(lo);
+}
+
+struct TopkWs {
+  size_t hist, done, count, cand_key, cand_idx, bits, total;
+  int64_t words;  // bitmap words per row
+  __host__ __device__ TopkWs(int64_t rows, int64_t row_stride) {
+    words = (row_stride + 31) / 32;
+    hist = 0;                                                    // [rows][2048] u32
+    done = hist + size_t(rows) * kTkBins * 4;                    // [rows] u32 tickets
+    count = done + ((size_t(rows) * 4 + 255) / 256) * 256;       // [rows] u32 candidates
+    cand_key = count + ((size_t(rows) * 4 + 255) / 256) * 256;   // [rows][cap] u64 composite
+    cand_idx = cand_key + size_t(rows) * kTkCap * 8;             // [rows][cap] u32 entry index
+    bits = cand_idx + size_t(rows) * kTkCap * 4;                 // [rows][words] u32
+    total = bits + ((size_t(rows) * words * 4 + 255) / 256) * 256;
+  }
+};
 
 struct TopkShared {
-  uint32_t hist[2][kTkBins];
-  uint32_t slice[kTkBins / kTkCluster];
-  uint32_t slice_tot[kTkCluster];
-  uint32_t cta_gt[kTkCluster];
-  uint32_t cta_eq[kTkCluster];
-  uint32_t warp_take[kTkWarps];
-  uint32_t warp_off[kTkWarps];
-  uint32_t warp_gt[kTkWarps];
-  uint32_t warp_eq[kTkWarps];
-  uint32_t bcast[4];
+  uint32_t hist[kTkBins];
+  uint64_t lkey[kTkLocalCap];
+  uint32_t lidx[kTkLocalCap];
+  uint32_t scratch[2 * kTkWarps + 8];
+  uint32_t nlocal, base, last;
 };
 
 struct Select {
   uint32_t bin, above, total;
 };
 
-// Key of entry g of a row; 0 marks an absent entry (ids[g] < 0).  NaN sorts
-// above +inf as in a torch descending sort.  No finite or infinite score maps
-// to 0 (that would need the bit pattern 0xffffffff, a NaN).
-__device__ __forceinline__ uint32_t entry_key(const float* srow, const int32_t* irow, int64_t g) {
-  if (irow != nullptr && irow[g] < 0) return 0u;
-  const float s = srow[g];
+// Score key of entry i of a row; 0 marks an absent entry (ids[i] < 0).  NaN
+// sorts above +inf as in a torch descending sort; no score maps to 0.
+__device__ __forceinline__ uint32_t entry_key(const float* srow, const int32_t* irow, int64_t i) {
+  if (irow != nullptr && irow[i] < 0) return 0u;
+  const float s = srow[i];
   if (isnan(s)) return 0xffffffffu;
   return score_key(s);
 }
 
-__device__ __forceinline__ uint32_t warp_sum_u32(uint32_t v) {
+// Whole block: over h[0, nbins) (nbins in {1024, 2048}), the bin b with
+// count(bins > b) < need <= count(bins >= b).  Same result in every thread;
+// total < need (or need == 0) -> {0, total, total}.
+__device__ Select block_find_bin(const uint32_t* h, int nbins, uint32_t need, TopkShared& sh) {
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int bpt = nbins / kTkThreads;  // 8 or 4 bins per thread; thread 0 = top bins
+  const int top = nbins - tid * bpt;
+  uint32_t v[8], mine = 0;
 #pragma unroll
-  for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-  return v;
-}
-
-// Finds, over the cluster-wide histogram (sum of every CTA's `hist`), the bin b
-// such that count(bins > b) < need <= count(bins >= b).  Identical result in
-// every CTA.  total = number of keys in the histogram; when total < need the
-// result is {0, total, total}.
-__device__ Select cluster_select(cg::cluster_group& cluster, TopkShared& sh, uint32_t* hist,
-                                 int nbins, uint32_t need, unsigned rank) {
-  const int per = nbins / kTkCluster;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  cluster.sync();  // every CTA's histogram is complete
-  for (int b = threadIdx.x; b < per; b += blockDim.x) {
-    uint32_t s = 0;
+  for (int i = 0; i < 8; ++i) {
+    v[i] = i < bpt ? h[top - 1 - i] : 0u;
+    mine += v[i];
+  }
+  uint32_t incl = mine;
 #pragma unroll
-    for (int c = 0; c < kTkCluster; ++c) s += cluster.map_shared_rank(hist, c)[rank * per + b];
-    sh.slice[b] = s;
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t x = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += x;
   }
   __syncthreads();
-  if (warp == 0) {
-    uint32_t t = 0;
-    for (int b = lane; b < per; b += 32) t += sh.slice[b];
-    t = warp_sum_u32(t);
-    if (lane < kTkCluster) cluster.map_shared_rank(sh.slice_tot, lane)[rank] = t;
+  if (lane == 31) sh.scratch[warp] = incl;
+  __syncthreads();
+  uint32_t off = 0, total = 0;
+  for (int w = 0; w < kTkWarps; ++w) {
+    const uint32_t x = sh.scratch[w];
+    off += w < warp ? x : 0u;
+    total += x;
   }
-  cluster.sync();  // slice totals delivered; remote histogram reads finished
-  if (warp == 0) {
-    // lane 0 = highest slice
-    const uint32_t tot = lane < kTkCluster ? sh.slice_tot[kTkCluster - 1 - lane] : 0u;
-    uint32_t incl = tot;
+  incl += off;
+  const uint32_t excl = incl - mine;
+  if (need > 0 && total >= need && excl < need && incl >= need) {
+    uint32_t cum = excl;
+    int bin = top - 1;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      if (i < bpt) {
+        if (cum + v[i] >= need) {
+          bin = top - 1 - i;
+          break;
+        }
+        cum += v[i];
+      }
+    }
+    sh.scratch[kTkWarps] = uint32_t(bin);
+    sh.scratch[kTkWarps + 1] = cum;
+  }
+  __syncthreads();
+  if (need == 0 || total < need) return Select{0u, total, total};
+  return Select{sh.scratch[kTkWarps], sh.scratch[kTkWarps + 1], total};
+}
+
+// Word range [w0, w1) of CTA c over rows * words_per_row bitmap words.
+__device__ __forceinline__ void cta_words(int64_t total_words, uint32_t c, uint32_t n, int64_t& w0,
+                                          int64_t& w1) {
+  w0 = total_words * c / n;
+  w1 = total_words * (c + 1) / n;
+}
+// CTA owning word w (inverse of cta_words).
+__device__ __forceinline__ uint32_t word_owner(int64_t w, int64_t total_words, uint32_t n) {
+  int64_t c = w * int64_t(n) / total_words;
+  while (c + 1 < int64_t(n) && total_words * (c + 1) / n <= w) ++c;
+  while (c > 0 && total_words * c / n > w) --c;
+  return uint32_t(c);
+}
+
+__device__ __forceinline__ int64_t row_length(const int32_t* lengths, int64_t r, int64_t row_stride) {
+  const int64_t n = lengths[r];
+  return (n < 0 || n > row_stride) ? 0 : n;
+}
+
+// ---------------------------------------------------------------------------
+// Standalone histogram pass (the decode step gets it from the indexer).
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(kTkThreads) topk_hist_kernel(
+    const float* __restrict__ scores, const int32_t* __restrict__ ids,
+    const int32_t* __restrict__ lengths, int64_t rows, int64_t row_stride,
+    uint8_t* __restrict__ ws_base) {
+  __shared__ uint32_t hist[kTkBins];
+  const TopkWs L(rows, row_stride);
+  uint32_t* ghist = reinterpret_cast<uint32_t*>(ws_base + L.hist);
+  for (int i = threadIdx.x; i < kTkBins; i += kTkThreads) hist[i] = 0u;
+  pdl_launch_dependents();
+  pdl_wait();
+  int64_t w0, w1;
+  cta_words(rows * L.words, blockIdx.x, gridDim.x, w0, w1);
+  __syncthreads();
+  for (int64_t r = w0 / L.words; r < rows && r * L.words < w1; ++r) {
+    const int64_t n = row_length(lengths, r, row_stride);
+    const int64_t rb = r * L.words;
+    const int64_t e0 = (w0 > rb ? w0 - rb : 0) * 32;
+    int64_t e1 = ((w1 < rb + L.words ? w1 : rb + L.words) - rb) * 32;
+    if (e1 > n) e1 = n;
+    const float* srow = scores + r * row_stride;
+    const int32_t* irow = ids != nullptr ? ids + r * row_stride : nullptr;
+    constexpr int kBatch = 8;
+    for (int64_t i0 = e0; i0 < e1; i0 += int64_t(kTkThreads) * kBatch) {
+      uint32_t u[kBatch];
+#pragma unroll
+      for (int j = 0; j < kBatch; ++j) {
+        const int64_t i = i0 + j * kTkThreads + threadIdx.x;
+        u[j] = i < e1 ? entry_key(srow, irow, i) : 0u;
+      }
+#pragma unroll
+      for (int j = 0; j < kBatch; ++j)
+        if (u[j]) atomicAdd(&hist[u[j] >> 21], 1u);
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < kTkBins; i += kTkThreads) {
+      const uint32_t v = hist[i];
+      if (v) {
+        atomicAdd(ghist + r * kTkBins + i, v);
+        hist[i] = 0u;
+      }
+    }
+    __syncthreads();
+  }
+}
+
+// The k-th largest composite among `count` keys whose digits above `level` are
+// `prefix` (need = how many of them to take).  Whole block, shared histogram.
+template <typename KeyAt>
+__device__ uint64_t resolve_kstar(KeyAt key_at, int64_t count, uint64_t prefix, uint32_t need,
+                                  TopkShared& sh) {
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  int level = 1;
+  for (; level < kTkLevels; ++level) {
+    const int nb = 1 << kTkBits[level];
+    const int hs = kTkShift[level - 1];  // digits above this one are fixed by `prefix`
+    __syncthreads();
+    for (int i = tid; i < nb; i += kTkThreads) sh.hist[i] = 0u;
+    __syncthreads();
+    for (int64_t i = tid; i < count; i += kTkThreads) {
+      const uint64_t key = key_at(i);
+      if (key && (key >> hs) == (prefix >> hs))
+        atomicAdd(&sh.hist[uint32_t(key >> kTkShift[level]) & uint32_t(nb - 1)], 1u);
+    }
+    __syncthreads();
+    const Select r1 = block_find_bin(sh.hist, nb, need, sh);
+    need -= r1.above;
+    prefix |= uint64_t(r1.bin) << kTkShift[level];
+    if (sh.hist[r1.bin] == need) {  // the whole sub-bin is selected
+      ++level;
+      break;
+    }
+  }
+  // K* = smallest key matching the resolved digits
+  const int hs = kTkShift[level - 1];
+  uint64_t best = ~uint64_t(0);
+  for (int64_t i = tid; i < count; i += kTkThreads) {
+    const uint64_t key = key_at(i);
+    if (key && (key >> hs) == (prefix >> hs) && key < best) best = key;
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) {
+    const uint64_t other = __shfl_xor_sync(0xffffffffu, best, o);
+    best = other < best ? other : best;
+  }
+  __syncthreads();
+  if (lane == 0) {
+    sh.scratch[2 * warp] = uint32_t(best);
+    sh.scratch[2 * warp + 1] = uint32_t(best >> 32);
+  }
+  __syncthreads();
+  uint64_t kstar = ~uint64_t(0);
+  for (int w = 0; w < kTkWarps; ++w) {
+    const uint64_t v = (uint64_t(sh.scratch[2 * w + 1]) << 32) | sh.scratch[2 * w];
+    kstar = v < kstar ? v : kstar;
+  }
+  __syncthreads();
+  return kstar;
+}
+
+// ---------------------------------------------------------------------------
+// Selection: bitmap words + candidates per CTA, resolution by the last CTA.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(kTkThreads) topk_select_kernel(
+    const float* __restrict__ scores, const int32_t* __restrict__ ids,
+    const int32_t* __restrict__ lengths, int32_t* __restrict__ out_ids,
+    float* __restrict__ out_scores, int32_t* err, int64_t rows, int64_t row_stride, int k,
+    int64_t id_base, uint8_t* __restrict__ ws_base) {
+  __shared__ __align__(16) TopkShared sh;
+  const TopkWs L(rows, row_stride);
+  uint32_t* ghist = reinterpret_cast<uint32_t*>(ws_base + L.hist);
+  uint32_t* gdone = reinterpret_cast<uint32_t*>(ws_base + L.done);
+  uint32_t* gcount = reinterpret_cast<uint32_t*>(ws_base + L.count);
+  uint64_t* gkey = reinterpret_cast<uint64_t*>(ws_base + L.cand_key);
+  uint32_t* gidx = reinterpret_cast<uint32_t*>(ws_base + L.cand_idx);
+  uint32_t* gbits = reinterpret_cast<uint32_t*>(ws_base + L.bits);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const uint32_t cta = blockIdx.x, nctas = gridDim.x;
+  const int64_t total_words = rows * L.words;
+
+  pdl_launch_dependents();  // the consumer may start its prologue; it waits for our completion
+  pdl_wait();               // scores and histograms come from the preceding kernel
+  int64_t w0, w1;
+  cta_words(total_words, cta, nctas, w0, w1);
+
+  for (int64_t r = w0 / L.words; r < rows && r * L.words < w1; ++r) {
+    const int64_t rb = r * L.words;
+    const int64_t n = row_length(lengths, r, row_stride);
+    const int64_t a0 = w0 > rb ? w0 - rb : 0;                         // first word of the row
+    const int64_t a1 = (w1 < rb + L.words ? w1 : rb + L.words) - rb;  // end word of the row
+    const uint32_t first_cta = word_owner(rb, total_words, nctas);
+    const uint32_t touching = word_owner(rb + L.words - 1, total_words, nctas) - first_cta + 1;
+    if (cta == first_cta && tid == 0) {
+      const int32_t len = lengths[r];
+      if (len < 0 || len > row_stride) flag(err, DSR_ERR_ID);
+    }
+    const float* srow = scores + r * row_stride;
+    const int32_t* irow = ids != nullptr ? ids + r * row_stride : nullptr;
+    auto id_of = [&](int64_t i) -> int32_t {
+      return irow != nullptr ? irow[i] : int32_t(id_base + i);
+    };
+
+    // threshold bin of the row
+    for (int i = tid; i < kTkBins; i += kTkThreads) sh.hist[i] = ghist[r * kTkBins + i];
+    if (tid == 0) sh.nlocal = 0u;
+    __syncthreads();
+    const Select s0 = block_find_bin(sh.hist, kTkBins, uint32_t(k), sh);
+    const bool take_all = s0.total <= uint32_t(k);
+
+    // one warp per bitmap word: ballot of "above the threshold bin"
+    for (int64_t wd = a0 + warp; wd < a1; wd += kTkWarps) {
+      const int64_t i = wd * 32 + lane;
+      const uint32_t u = i < n ? entry_key(srow, irow, i) : 0u;
+      const uint32_t d = u >> 21;
+      const bool above = u != 0u && (take_all || d > s0.bin);
+      const bool cand = !take_all && u != 0u && d == s0.bin;
+      const unsigned word = __ballot_sync(0xffffffffu, above);
+      if (lane == 0) gbits[r * L.words + wd] = word;
+      const unsigned m = __ballot_sync(0xffffffffu, cand);
+      if (m) {
+        const int leader = __ffs(m) - 1;
+        uint32_t slot = 0;
+        if (lane == leader) slot = atomicAdd(&sh.nlocal, uint32_t(__popc(m)));
+        slot = __shfl_sync(0xffffffffu, slot, leader) + __popc(m & ((1u << lane) - 1u));
+        if (cand && slot < uint32_t(kTkLocalCap)) {
+          sh.lkey[slot] = composite(u, 0x7fffffffu - uint32_t(id_of(i)));
+          sh.lidx[slot] = uint32_t(i);
+        }
+      }
+    }
+    __syncthreads();
+    const uint32_t nl = sh.nlocal;
+    if (tid == 0) {
+      // an overflowing CTA forces the whole-row path through an oversized count
+      const uint32_t add = nl <= uint32_t(kTkLocalCap) ? nl : uint32_t(kTkCap) + 1u;
+      sh.base = add ? atomicAdd(gcount + r, add) : 0u;
+    }
+    __syncthreads();
+    for (uint32_t e = tid; e < nl && e < uint32_t(kTkLocalCap); e += kTkThreads) {
+      const uint32_t slot = sh.base + e;
+      if (slot < uint32_t(kTkCap)) {
+        gkey[r * kTkCap + slot] = sh.lkey[e];
+        gidx[r * kTkCap + slot] = sh.lidx[e];
+      }
+    }
+    // ticket: the last CTA of the row finishes it
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) sh.last = atomicAdd(gdone + r, 1u) == touching - 1 ? 1u : 0u;
+    __syncthreads();
+    if (!sh.last) continue;
+    __threadfence();
+
+    // other CTAs' words and candidates are read from L2 (__ldcg), never a stale L1 line
+    uint32_t* rbits = gbits + r * L.words;
+    const uint32_t count = __ldcg(gcount + r);
+    if (!take_all) {
+      const uint64_t prefix0 = uint64_t(s0.bin) << kTkShift[0];
+      const uint32_t need0 = uint32_t(k) - s0.above;
+      const bool whole_bin = sh.hist[s0.bin] == need0;  // every threshold-bin entry is selected
+      if (count <= uint32_t(kTkCap)) {
+        // ---- radix over the candidates' remaining digits
+        const uint64_t* ck = gkey + r * kTkCap;
+        const uint64_t kstar =
+            whole_bin ? 0ull
+                      : resolve_kstar([&](int64_t i) { return __ldcg(ck + i); }, count, prefix0, need0, sh);
+        for (uint32_t i = tid; i < count; i += kTkThreads)
+          if (__ldcg(ck + i) >= kstar) {
+            const uint32_t idx = __ldcg(gidx + r * kTkCap + i);
+            atomicOr(rbits + (idx >> 5), 1u << (idx & 31));
+          }
+      } else {
+        // ---- candidate overflow: resolve over the whole row, then mark its bin
+        auto row_key = [&](int64_t i) -> uint64_t {
+          const uint32_t u = entry_key(srow, irow, i);
+          return u ? composite(u, 0x7fffffffu - uint32_t(id_of(i))) : 0ull;
+        };
+        const uint64_t kstar = whole_bin ? 0ull : resolve_kstar(row_key, n, prefix0, need0, sh);
+        for (int64_t i = tid; i < n; i += kTkThreads) {
+          const uint32_t u = entry_key(srow, irow, i);
+          if (u && (u >> 21) == s0.bin && composite(u, 0x7fffffffu - uint32_t(id_of(i))) >= kstar)
+            atomicOr(rbits + (i >> 5), 1u << (i & 31));
+        }
+      }
+      __threadfence();
+      __syncthreads();
+    }
+
+    // ---- bitmap -> ascending ids (contiguous words per thread, block scan)
+    const int64_t nwords = (n + 31) / 32;
+    const int64_t per = (nwords + kTkThreads - 1) / kTkThreads;
+    const int64_t my0 = tid * per, my1 = my0 + per < nwords ? my0 + per : nwords;
+    uint32_t mine = 0;
+    for (int64_t wd = my0; wd < my1; ++wd) mine += __popc(__ldcg(rbits + wd));
+    uint32_t incl = mine;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
-      const uint32_t v = __shfl_up_sync(0xffffffffu, incl, o);
-      if (lane >= o) incl += v;
+      const uint32_t x = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += x;
     }
-    const uint32_t total = __shfl_sync(0xffffffffu, incl, 31);
-    Select r{0u, total, total};
-    if (total >= need && need > 0) {
-      const unsigned hit = __ballot_sync(0xffffffffu, incl >= need);
-      const int L = __ffs(hit) - 1;
-      const uint32_t above_slice = __shfl_sync(0xffffffffu, incl - tot, L);
-      const unsigned s = kTkCluster - 1 - L;
-      const uint32_t* rs = cluster.map_shared_rank(sh.slice, s);
-      const int bpl = per / 32;  // bins per lane (8 or 4)
-      // lane 0 covers the top bpl bins of the slice
-      const int top = per - lane * bpl;  // exclusive upper end
-      uint32_t mine = 0;
-      uint32_t vals[8];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        vals[i] = i < bpl ? rs[top - 1 - i] : 0u;
-        mine += vals[i];
-      }
-      uint32_t pin = mine;
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const uint32_t v = __shfl_up_sync(0xffffffffu, pin, o);
-        if (lane >= o) pin += v;
-      }
-      const unsigned hit2 = __ballot_sync(0xffffffffu, above_slice + pin >= need);
-      const int L2 = __ffs(hit2) - 1;
-      if (lane == L2) {
-        uint32_t cum = above_slice + pin - mine;
-        int bin = top - 1;
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          if (i < bpl) {
-            if (cum + vals[i] >= need) {
-              bin = top - 1 - i;
-              break;
-            }
-            cum += vals[i];
-          }
-        }
-        r.bin = s * per + bin;
-        r.above = cum;
-        r.total = total;
-        sh.bcast[0] = r.bin;
-        sh.bcast[1] = r.above;
-        sh.bcast[2] = r.total;
-      }
-    } else if (lane == 0) {
-      sh.bcast[0] = 0u;
-      sh.bcast[1] = total;
-      sh.bcast[2] = total;
-    }
-  }
-  __syncthreads();
-  return Select{sh.bcast[0], sh.bcast[1], sh.bcast[2]};
-}
-
-__global__ void __cluster_dims__(kTkCluster, 1, 1) __launch_bounds__(kTkThreads, 1)
-    topk_kernel(const float* __restrict__ scores, const int32_t* __restrict__ ids,
-                const int32_t* __restrict__ lengths, int32_t* __restrict__ out_ids,
-                float* __restrict__ out_scores, int32_t* err, int64_t row_stride, int k,
-                int64_t id_base, int64_t resident_cap) {
-  cg::cluster_group cluster = cg::this_cluster();
-  __shared__ TopkShared sh;
-  extern __shared__ uint32_t keys[];
-  const unsigned rank = cluster.block_rank();
-  const int64_t row = blockIdx.y;
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-
-  pdl_wait();  // scores may come from the preceding kernel
-
-  int64_t n = lengths[row];
-  if (n < 0 || n > row_stride) {
-    if (rank == 0 && tid == 0) flag(err, DSR_ERR_ID);
-    n = 0;
-  }
-  const int64_t chunk = (n + kTkCluster - 1) / kTkCluster;
-  const int64_t beg = rank * chunk;
-  const int64_t cnt = n > beg ? (n - beg < chunk ? n - beg : chunk) : 0;
-  const bool resident = chunk <= resident_cap;  // dynamic smem holds resident_cap keys
-  const float* srow = scores + row * row_stride + beg;
-  const int32_t* irow = ids != nullptr ? ids + row * row_stride + beg : nullptr;
-
-  auto key_at = [&](int64_t i) -> uint32_t {
-    return resident ? keys[i] : entry_key(srow, irow, i);
-  };
-
-  for (int i = tid; i < 2 * kTkBins; i += kTkThreads) (&sh.hist[0][0])[i] = 0u;
-  __syncthreads();
-
-  // pass 1: top 11 bits (load the chunk into shared memory when it fits)
-  for (int64_t i = tid; i < cnt; i += kTkThreads) {
-    const uint32_t u = entry_key(srow, irow, i);
-    if (resident) keys[i] = u;
-    if (u) atomicAdd(&sh.hist[0][u >> 21], 1u);
-  }
-  const Select s1 = cluster_select(cluster, sh, sh.hist[0], kTkBins, uint32_t(k), rank);
-  for (int i = tid; i < kTkBins; i += kTkThreads) sh.hist[0][i] = 0u;
-  const uint32_t total = s1.total;
-
-  uint32_t T = 0u, need = 0u;
-  if (total > uint32_t(k)) {
-    const uint32_t need1 = uint32_t(k) - s1.above;
-    const uint32_t p1 = s1.bin;
-    // pass 2: next 11 bits among keys whose top 11 bits equal p1
-    for (int64_t i = tid; i < cnt; i += kTkThreads) {
-      const uint32_t u = key_at(i);
-      if (u && (u >> 21) == p1) atomicAdd(&sh.hist[1][(u >> 10) & 2047u], 1u);
-    }
-    const Select s2 = cluster_select(cluster, sh, sh.hist[1], kTkBins, need1, rank);
-    const uint32_t need2 = need1 - s2.above;
-    const uint32_t p2 = (p1 << 11) | s2.bin;
-    // pass 3: last 10 bits
-    for (int64_t i = tid; i < cnt; i += kTkThreads) {
-      const uint32_t u = key_at(i);
-      if (u && (u >> 10) == p2) atomicAdd(&sh.hist[0][u & 1023u], 1u);
-    }
-    const Select s3 = cluster_select(cluster, sh, sh.hist[0], 1024, need2, rank);
-    need = need2 - s3.above;
-    T = (p2 << 10) | s3.bin;
-  }
-
-  // pass 4: per-warp counts of keys above T and equal to T (contiguous ranges)
-  const int64_t sub = (cnt + kTkWarps - 1) / kTkWarps;
-  const int64_t w_beg = warp * sub;
-  const int64_t w_end = (w_beg + sub < cnt) ? w_beg + sub : cnt;
-  {
-    uint32_t gt = 0, eq = 0;
-    for (int64_t i = w_beg + lane; i < w_end; i += 32) {
-      const uint32_t u = key_at(i);
-      gt += (u > T) ? 1u : 0u;
-      eq += (u != 0u && u == T) ? 1u : 0u;
-    }
-    gt = warp_sum_u32(gt);
-    eq = warp_sum_u32(eq);
-    if (lane == 0) {
-      sh.warp_gt[warp] = gt;
-      sh.warp_eq[warp] = eq;
-    }
-  }
-  __syncthreads();
-  if (tid < kTkCluster) {
-    uint32_t gt = 0, eq = 0;
+    __syncthreads();
+    if (lane == 31) sh.scratch[warp] = incl;
+    __syncthreads();
+    uint32_t pos = incl - mine, total = 0;
     for (int w = 0; w < kTkWarps; ++w) {
-      gt += sh.warp_gt[w];
-      eq += sh.warp_eq[w];
+      pos += w < warp ? sh.scratch[w] : 0u;
+      total += sh.scratch[w];
     }
-    cluster.map_shared_rank(sh.cta_gt, tid)[rank] = gt;
-    cluster.map_shared_rank(sh.cta_eq, tid)[rank] = eq;
-  }
-  cluster.sync();
-  if (tid == 0) {
-    uint32_t eq_before = 0, off = 0;
-    for (unsigned c = 0; c < rank; ++c) {
-      const uint32_t left = need > eq_before ? need - eq_before : 0u;
-      const uint32_t take = left < sh.cta_eq[c] ? left : sh.cta_eq[c];
-      off += sh.cta_gt[c] + take;
-      eq_before += sh.cta_eq[c];
-    }
-    for (int w = 0; w < kTkWarps; ++w) {
-      const uint32_t left = need > eq_before ? need - eq_before : 0u;
-      const uint32_t take = left < sh.warp_eq[w] ? left : sh.warp_eq[w];
-      sh.warp_take[w] = take;
-      sh.warp_off[w] = off;
-      off += sh.warp_gt[w] + take;
-      eq_before += sh.warp_eq[w];
-    }
-  }
-  __syncthreads();
-
-  // pass 5: ordered compaction, one warp per contiguous range
-  {
-    const uint32_t take = sh.warp_take[warp];
-    uint32_t pos = sh.warp_off[warp], eq_seen = 0;
-    int32_t* orow = out_ids + row * k;
-    float* osrow = out_scores != nullptr ? out_scores + row * k : nullptr;
-    const unsigned lt = (1u << lane) - 1u;
-    for (int64_t j = w_beg; j < w_end; j += 32) {
-      const int64_t i = j + lane;
-      const uint32_t u = i < w_end ? key_at(i) : 0u;
-      const bool eq = u != 0u && u == T;
-      const unsigned eqb = __ballot_sync(0xffffffffu, eq);
-      const uint32_t rank_eq = eq_seen + __popc(eqb & lt);
-      const bool pick = (u > T) || (eq && rank_eq < take);
-      const unsigned pb = __ballot_sync(0xffffffffu, pick);
-      if (pick) {
-        const uint32_t p = pos + __popc(pb & lt);
-        if (p < uint32_t(k)) {
-          orow[p] = irow != nullptr ? irow[i] : static_cast<int32_t>(id_base + beg + i);
-          if (osrow != nullptr) osrow[p] = srow[i];
+    int32_t* orow = out_ids + r * k;
+    float* osrow = out_scores != nullptr ? out_scores + r * k : nullptr;
+    for (int64_t wd = my0; wd < my1; ++wd) {
+      uint32_t word = __ldcg(rbits + wd);
+      while (word) {
+        const int bit = __ffs(word) - 1;
+        word &= word - 1;
+        const int64_t i = wd * 32 + bit;
+        if (pos < uint32_t(k)) {
+          orow[pos] = id_of(i);
+          if (osrow != nullptr) osrow[pos] = srow[i];
         }
+        ++pos;
       }
-      eq_seen += __popc(eqb);
-      pos += __popc(pb);
     }
-  }
-  // padding
-  if (rank == 0) {
     const uint32_t chosen = total < uint32_t(k) ? total : uint32_t(k);
     for (int p = int(chosen) + tid; p < k; p += kTkThreads) {
-      out_ids[row * k + p] = -1;
-      if (out_scores != nullptr) out_scores[row * k + p] = -CUDART_INF_F;
+      orow[p] = -1;
+      if (osrow != nullptr) osrow[p] = -CUDART_INF_F;
     }
+    // every CTA of the row is done with its state: clear it for the next call
+    for (int i = tid; i < kTkBins; i += kTkThreads) ghist[r * kTkBins + i] = 0u;
+    if (tid == 0) {
+      gcount[r] = 0u;
+      gdone[r] = 0u;
+    }
+    __syncthreads();
   }
-  pdl_launch_dependents();
-  cluster.sync();  // keep every CTA's shared memory alive until remote readers are done
+}
+
+int topk_ctas(int64_t rows, int64_t row_stride) {
+  const int64_t words = rows * ((row_stride + 31) / 32);
+  int64_t ctas = sm_count();
+  if (words < ctas * 4) ctas = (words + 3) / 4;  // at least 4 words (128 entries) per CTA
+  return int(ctas < 1 ? 1 : ctas);
 }
 
 }  // namespace
 
+size_t topk_workspace_bytes(int64_t rows, int64_t row_stride) {
+  return TopkWs(rows, row_stride).total;
+}
+
+// hist_ready: the per-row histograms in the workspace were already built (by the
+// indexer); otherwise topk_hist_kernel builds them first.
 int launch_topk(const float* scores, const int32_t* ids, const int32_t* lengths, int32_t* out_ids,
                 float* out_scores, int32_t* err, int64_t rows, int64_t row_stride, int64_t k,
-                int64_t id_base, cudaStream_t stream, bool pdl) {
-  DSR_REQUIRE(scores && lengths && out_ids && err, "topk_select: null pointer");
+                int64_t id_base, void* workspace, size_t workspace_bytes, cudaStream_t stream,
+                bool pdl, bool hist_ready) {
+  DSR_REQUIRE(scores && lengths && out_ids && err && workspace, "topk_select: null pointer");
   DSR_REQUIRE(rows > 0 && rows <= 65535, "topk_select: rows %lld outside [1, 65535]",
               (long long)rows);
   DSR_REQUIRE(k > 0 && k <= 8192, "topk_select: k %lld outside [1, 8192]", (long long)k);
@@ -317,37 +460,47 @@ int launch_topk(const float* scores, const int32_t* ids, const int32_t* lengths,
               "topk_select: invalid row stride");
   DSR_REQUIRE(id_base >= 0 && id_base + row_stride <= (int64_t(1) << 31),
               "topk_select: ids must fit int32");
-  static bool configured = false;
-  if (!configured) {
-    cudaFuncSetAttribute(topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         kTkResident * 4);
-    configured = true;
-  }
-  const int64_t chunk = (row_stride + kTkCluster - 1) / kTkCluster;
-  const size_t dyn = chunk <= kTkResident ? size_t(chunk) * 4 : 0;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(kTkCluster, unsigned(rows), 1);
-  cfg.blockDim = dim3(kTkThreads, 1, 1);
-  cfg.dynamicSmemBytes = dyn;
-  cfg.stream = stream;
+  const TopkWs L(rows, row_stride);
+  DSR_REQUIRE(workspace_bytes >= L.total, "topk_select: workspace %zu < %zu bytes",
+              workspace_bytes, L.total);
+  DSR_REQUIRE((reinterpret_cast<uintptr_t>(workspace) & 255u) == 0,
+              "topk_select: workspace must be 256-byte aligned");
+  const int ctas = topk_ctas(rows, row_stride);
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(unsigned(ctas), 1, 1);
+  cfg.blockDim = dim3(kTkThreads, 1, 1);
+  cfg.stream = stream;
   cfg.attrs = attr;
-  cfg.numAttrs = pdl ? 1 : 0;
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, topk_kernel, scores, ids, lengths, out_ids,
-                                           out_scores, err, row_stride, int(k), id_base,
-                                           int64_t(dyn / 4));
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  if (!hist_ready) {
+    cfg.numAttrs = pdl ? 1 : 0;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, topk_hist_kernel, scores, ids, lengths, rows,
+                                             row_stride, ws);
+    if (e != cudaSuccess) return fail(DSR_ECUDA, "topk histogram launch: %s", cudaGetErrorString(e));
+    cfg.numAttrs = 1;
+  } else {
+    cfg.numAttrs = pdl ? 1 : 0;
+  }
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, topk_select_kernel, scores, ids, lengths, out_ids,
+                                           out_scores, err, rows, row_stride, int(k), id_base, ws);
   if (e != cudaSuccess) return fail(DSR_ECUDA, "topk launch: %s", cudaGetErrorString(e));
   return DSR_OK;
 }
 
 }  // namespace dsr
 
+extern "C" size_t dsr_topk_workspace_bytes(int64_t rows, int64_t row_stride) {
+  return dsr::topk_workspace_bytes(rows, row_stride);
+}
+
 extern "C" int dsr_topk_select(const float* scores, const int32_t* ids, const int32_t* lengths,
                                int32_t* out_ids, float* out_scores, int32_t* err, int64_t rows,
-                               int64_t row_stride, int64_t k, int64_t id_base, void* stream) {
+                               int64_t row_stride, int64_t k, int64_t id_base, void* workspace,
+                               size_t workspace_bytes, void* stream) {
   dsr::clear_error();
   return dsr::launch_topk(scores, ids, lengths, out_ids, out_scores, err, rows, row_stride, k,
-                          id_base, dsr::as_stream(stream), false);
+                          id_base, workspace, workspace_bytes, dsr::as_stream(stream), false, false);
 }

@@ -143,10 +143,13 @@ std::vector<at::Tensor> ds_topk_select(at::Tensor scores, at::Tensor lengths, in
   auto out = at::empty({scores.size(0), k}, scores.options().dtype(at::kInt));
   at::Tensor out_scores = return_scores ? at::empty({scores.size(0), k}, scores.options()) : at::Tensor();
   auto error = status_like(scores);
+  const size_t ws_bytes = dsr_topk_workspace_bytes(scores.size(0), scores.size(1));
+  auto ws = at::zeros({int64_t(ws_bytes)}, scores.options().dtype(at::kByte));
   ok(dsr_topk_select(scores.data_ptr<float>(), ids ? ids->data_ptr<int32_t>() : nullptr,
                      lengths.data_ptr<int32_t>(), out.data_ptr<int32_t>(),
                      return_scores ? out_scores.data_ptr<float>() : nullptr, error.data_ptr<int32_t>(),
-                     scores.size(0), scores.size(1), k, id_base, current_stream()));
+                     scores.size(0), scores.size(1), k, id_base, ws.data_ptr(), ws_bytes,
+                     current_stream()));
   if (return_scores) return {out, error, out_scores};
   return {out, error};
 }
@@ -315,7 +318,7 @@ std::vector<at::Tensor> ds_decode_step(at::Tensor idx_q, at::Tensor idx_w, at::T
   const int64_t stride = (max_visible + 63) / 64 * 64;
   at::Tensor scores = return_scores ? at::empty({batch, stride}, q.options()) : at::Tensor();
   const size_t ws_bytes = dsr_decode_workspace_bytes(batch, max_visible, heads, k);
-  auto ws = at::empty({int64_t(ws_bytes)}, q.options().dtype(at::kByte));
+  auto ws = at::zeros({int64_t(ws_bytes)}, q.options().dtype(at::kByte));
   auto error = status_like(q);
   ok(dsr_decode_step(idx_q.data_ptr<float>(), idx_w.data_ptr<float>(), idx_q.size(1), bf16(index_pool),
                      q.data_ptr<float>(), bf16(kv_pool), heads, kv_pool.size(0) / 64,

@@ -101,10 +101,15 @@ int dsr_engram_decode(const uint8_t* encoded, uint16_t* out, int32_t* err, int64
  * padded with -1.  Optional out_scores f32[rows,k] holds the matching scores
  * (padding: -inf).  When `ids` is NULL the id of entry i is i + id_base.
  * When `ids` is given, valid ids must increase along each row (any -1 entries
- * are skipped).  k <= 8192; row_stride >= max length. */
+ * are skipped).  k <= 8192; row_stride >= max length.
+ * Scratch: dsr_topk_workspace_bytes(rows, row_stride) bytes, 256-byte aligned,
+ * zero before its first use; every completed call leaves it zero again.  Calls
+ * sharing a workspace must not overlap on the GPU. */
+size_t dsr_topk_workspace_bytes(int64_t rows, int64_t row_stride);
 int dsr_topk_select(const float* scores, const int32_t* ids, const int32_t* lengths,
                     int32_t* out_ids, float* out_scores, int32_t* err, int64_t rows,
-                    int64_t row_stride, int64_t k, int64_t id_base, void* stream);
+                    int64_t row_stride, int64_t k, int64_t id_base, void* workspace,
+                    size_t workspace_bytes, void* stream);
 
 /* ======================== paged decode hot path =========================== */
 
@@ -167,7 +172,9 @@ int dsr_lse_combine(const float* part_o, const float* part_m, const float* part_
 /* One decode step: indexer -> exact top-k -> sparse MLA attention -> combine.
  * Arguments as above; idx_q f32[batch,idx_heads,128], idx_w f32[batch,idx_heads];
  * topk_out i32[batch,k] receives the selection; scores_out (nullable)
- * f32[batch,score_stride].  Scratch: dsr_decode_workspace_bytes(). */
+ * f32[batch,score_stride].  Scratch: dsr_decode_workspace_bytes() bytes, 256-byte
+ * aligned, zero before its first use (every completed call leaves the parts
+ * that must start at zero cleared again); calls sharing it must not overlap. */
 size_t dsr_decode_workspace_bytes(int64_t batch, int64_t max_visible, int64_t heads,
                                   int64_t k);
 int dsr_decode_step(const float* idx_q, const float* idx_w, int64_t idx_heads,

@@ -67,8 +67,11 @@ def c_topk(scores, lengths, k, ids=None, id_base=0, return_scores=False):
     out = torch.empty((rows, k), dtype=torch.int32, device="cuda")
     out_s = torch.empty((rows, k), dtype=torch.float32, device="cuda") if return_scores else None
     err = status()
+    ws_bytes = _native.library().dsr_topk_workspace_bytes(rows, stride)
+    ws = torch.zeros(ws_bytes, dtype=torch.uint8, device="cuda")
     call("dsr_topk_select", ptr(scores), ptr(ids), ptr(lengths), ptr(out), ptr(out_s), ptr(err), rows,
-         stride, k, id_base, stream_handle())
+         stride, k, id_base, ptr(ws), ws_bytes, stream_handle())
+    c_topk.last_ws = ws
     code = finish(err)
     return (out, out_s, code) if return_scores else (out, code)
 
@@ -105,7 +108,7 @@ def c_decode_step(inp, k, scale, return_scores=True):
     stride = (max_visible + 63) // 64 * 64
     lib = _native.library()
     ws_bytes = lib.dsr_decode_workspace_bytes(b, max_visible, h, k)
-    ws = torch.empty(ws_bytes, dtype=torch.uint8, device="cuda")
+    ws = torch.zeros(ws_bytes, dtype=torch.uint8, device="cuda")
     out = torch.empty((b, h, 512), dtype=torch.float32, device="cuda")
     topk = torch.empty((b, k), dtype=torch.int32, device="cuda")
     scores = torch.full((b, stride), float("nan"), dtype=torch.float32, device="cuda") if return_scores else None

@@ -51,7 +51,7 @@ def test_torch_extension_keeps_reference_op_names():
     # engram rows beyond 1024
     lambda n: n.dsr_engram_decode(1, 1, 1, 1025, None),
     # top-k k beyond 8192
-    lambda n: n.dsr_topk_select(1, None, 1, 1, None, 1, 1, 16, 8193, 0, None),
+    lambda n: n.dsr_topk_select(1, None, 1, 1, None, 1, 1, 16, 8193, 0, 256, 1 << 20, None),
     # indexer heads not in {16,32,64}
     lambda n: n.dsr_indexer_decode(16, 16, 16, 1, 1, 1, 1, 1, 64, 1, 1, 48, None),
     # null pointers

@@ -35,13 +35,31 @@ def test_topk_ragged_rows_and_short_rows(cuda):
 
 
 def test_topk_streaming_rows_beyond_shared_memory(cuda):
-    # 8 * 40960 keys fit in shared memory per cluster; longer rows stream from HBM
+    # rows longer than the clusters' shared memory are re-read from HBM on each pass
     rng = np.random.default_rng(22)
-    n = 400000
+    n = 700000
     scores = (np.round(rng.normal(size=(2, n)) * 8) / 8).astype(np.float32)
-    out, code = c_topk(dev(scores), dev(np.array([n, 333333], np.int32)), 2048)
+    out, code = c_topk(dev(scores), dev(np.array([n, 600001], np.int32)), 2048)
     assert code == 0
-    assert np.array_equal(out.cpu().numpy(), expected_rows(scores, [n, 333333], 2048))
+    assert np.array_equal(out.cpu().numpy(), expected_rows(scores, [n, 600001], 2048))
+
+
+def test_topk_threshold_bin_overflow_takes_cluster_radix_path(cuda):
+    # more than 8192 entries share the threshold bin: all-equal scores, and a row
+    # where 20000 entries tie exactly at the threshold value
+    rng = np.random.default_rng(25)
+    n = 60000
+    scores = np.zeros((3, n), np.float32)
+    scores[1] = rng.normal(size=n).astype(np.float32)
+    scores[1, rng.choice(n, 20000, replace=False)] = 1.5
+    scores[1, :100] = 9.0
+    scores[2] = -0.0
+    scores[2, 5::7] = 0.0
+    lengths = [n, n, 50000]
+    out, code = c_topk(dev(scores), dev(np.array(lengths, np.int32)), 2048)
+    assert code == 0
+    assert np.array_equal(out.cpu().numpy(), expected_rows(scores, lengths, 2048))
+    assert out.cpu().numpy()[0].tolist() == list(range(2048))
 
 
 @pytest.mark.parametrize("k", [1, 13, 512, 4096])
