@@ -31,6 +31,8 @@ SIGNATURES = {
     "dsr_topk_workspace_bytes": (c_size_t, [c_int64, c_int64]),
     "dsr_topk_select": (c_int, [_P, _P, _P, _P, _P, _P, c_int64, c_int64, c_int64, c_int64, _P, c_size_t,
                                 _P]),
+    "dsr_topk_select_noalloc": (c_int, [_P, _P, _P, _P, _P, _P, c_int64, c_int64, c_int64, c_int64,
+                                        _P]),
     "dsr_indexer_decode": (c_int, [_P, _P, _P, c_int64, _P, c_int64, _P, _P, c_int64, _P, c_int64,
                                    c_int64, _P]),
     "dsr_mla_workspace_bytes": (c_size_t, [c_int64, c_int64, c_int64]),

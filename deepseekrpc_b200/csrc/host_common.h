@@ -41,6 +41,8 @@ int launch_topk(const float* scores, const int32_t* ids, const int32_t* lengths,
                 bool pdl, bool hist_ready);
 // Top-k scratch; its first rows * 2048 uint32 are the per-row score histograms.
 size_t topk_workspace_bytes(int64_t rows, int64_t row_stride);
+// Leading bytes of that scratch (histograms, tickets, counts) that must be zero at launch.
+size_t topk_zeroed_prefix_bytes(int64_t rows, int64_t row_stride);
 int launch_indexer_decode(const float* q, const float* weights, const uint16_t* index_pool,
                           int64_t pool_blocks, const int32_t* block_table, int64_t table_stride,
                           const int32_t* visible, float* scores, int64_t score_stride,

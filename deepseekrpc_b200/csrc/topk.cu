@@ -446,6 +446,10 @@ size_t topk_workspace_bytes(int64_t rows, int64_t row_stride) {
   return TopkWs(rows, row_stride).total;
 }
 
+size_t topk_zeroed_prefix_bytes(int64_t rows, int64_t row_stride) {
+  return TopkWs(rows, row_stride).cand_key;
+}
+
 // hist_ready: the per-row histograms in the workspace were already built (by the
 // indexer); otherwise topk_hist_kernel builds them first.
 int launch_topk(const float* scores, const int32_t* ids, const int32_t* lengths, int32_t* out_ids,

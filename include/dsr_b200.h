@@ -111,6 +111,24 @@ int dsr_topk_select(const float* scores, const int32_t* ids, const int32_t* leng
                     int64_t row_stride, int64_t k, int64_t id_base, void* workspace,
                     size_t workspace_bytes, void* stream);
 
+/* Allocation-free variant of dsr_topk_select.  No reference counterpart: it
+ * serves hosts that cannot hand the library device memory per call.  Same
+ * arguments, validation and results as dsr_topk_select, minus the workspace.
+ * Scratch is a fixed DSR_TOPK_NOALLOC_BYTES array inside this library (one per
+ * device); calls with dsr_topk_workspace_bytes(rows, row_stride) above it are
+ * refused with DSR_EINVAL before any CUDA call (e.g. 8 rows x 131072 entries
+ * fit, 16 rows x 131072 do not).  Nothing is allocated: the first call on a
+ * device resolves the array's address (cudaGetSymbolAddress), so make that
+ * first call outside any stream capture; each call clears the zero-initialised
+ * part of the scratch with cudaMemsetAsync on `stream` before its kernels.
+ * All calls on one device share the scratch: calls that overlap on the GPU
+ * (different streams, or threads without ordering) race and must be
+ * serialised by the caller. */
+#define DSR_TOPK_NOALLOC_BYTES (1u << 20)
+int dsr_topk_select_noalloc(const float* scores, const int32_t* ids, const int32_t* lengths,
+                            int32_t* out_ids, float* out_scores, int32_t* err, int64_t rows,
+                            int64_t row_stride, int64_t k, int64_t id_base, void* stream);
+
 /* ======================== paged decode hot path =========================== */
 
 /* Lightning-indexer scores over a paged BF16 index-key pool, tcgen05 tensor cores.
