@@ -6,26 +6,30 @@
 // then stable descending argsort by score), output sorted ascending and padded
 // with -1.
 //
-// Every entry gets a unique 63-bit composite key (u << 31) | (0x7fffffff - id),
-// u = order-preserving uint32 of the score (-0.0 == +0.0): "larger key" is
-// exactly "ranked earlier" under the reference rule, so the selected set is
-// {key >= K*} where K* is the k-th largest key.
+// Every entry gets a unique 63-bit rank key (u << 31) | (0x7fffffff - id),
+// u = order-preserving uint32 of the score (-0.0 == +0.0, NaN above +inf):
+// "larger key" is exactly "ranked earlier" under the reference rule, so the
+// selected set is {key >= K*} where K* is the k-th largest key.  Digit 0 of a
+// key is u >> 21 (11 bits), digit 1 is the next 11 bits of u.
 //
-// Design (no grid-wide barrier, no spinning):
-//   * a per-row 11-bit histogram of the score keys is built first, either by the
-//     indexer epilogue while it produces the scores, or by topk_hist_kernel;
-//   * topk_select_kernel spreads each row over many CTAs in 32-entry words.
-//     Every CTA finds the threshold bin from the row histogram, writes one
-//     bitmap word per 32 entries (bit set = key above the threshold bin) with a
-//     warp ballot, and appends its threshold-bin entries to the row's candidate
-//     list;
-//   * the last CTA to finish a row (atomic ticket after a fence) resolves K*
-//     among the candidates with local radix passes over the remaining 52 bits,
-//     sets their bits, converts the bitmap into the ascending id list and
-//     clears the row's histogram, ticket and candidate count for the next call.
-// Candidate-list overflow (heavily tied scores) falls back to the last CTA
-// resolving K* by scanning the whole row.  The workspace must be zero before
-// its first use; every completed call leaves it zero again.
+// Design (no grid-wide barrier, no spinning), one launch:
+//   * a per-row histogram of digit 0 is built first, by the indexer epilogue
+//     while it produces the scores, or by topk_hist_kernel;
+//   * topk_select_kernel spreads each row over the CTAs in 32-entry words.
+//     Every CTA finds the threshold bin of digit 0 from the row histogram,
+//     stages its entries at or above that bin (compacted, in entry order, as
+//     (raw score bits << 31 | 0x7fffffff - id) records) in the row's staging
+//     area, counts the digit 1 of its threshold-bin entries into a second row
+//     histogram, and takes a ticket;
+//   * the CTA that takes the last ticket of a row reads the digit-1 histogram,
+//     ranks only the entries that share both digits with K* (usually a handful,
+//     in shared memory), then walks the staged records in entry order, keeps the
+//     selected ones with ballots, 4096 records per chunk, writes ids and scores,
+//     and clears the row's histograms and ticket for the next call.
+// When more than kTkRankCap entries share K*'s two digits (massively tied
+// scores) the last CTA ranks them over the whole row instead.  The workspace
+// must be zero before its first use; every completed call leaves its zeroed
+// part zero again.
 #include "common.cuh"
 #include "host_common.h"
 
@@ -36,9 +40,11 @@ namespace {
 
 constexpr int kTkThreads = 256;
 constexpr int kTkWarps = kTkThreads / 32;
-constexpr int kTkBins = 2048;      // level-0 digit: 11 bits
-constexpr int kTkCap = 8192;       // candidate entries per row
-constexpr int kTkLocalCap = 2048;  // candidate entries one CTA stages in shared memory
+constexpr int kTkBins = 2048;      // digits 0 and 1: 11 bits each
+constexpr int kTkMaxCtas = 256;    // CTAs of one launch (one staged-count slot each; fits uint8)
+constexpr int kTkPer = 4;          // entries per thread per staging chunk (strided)
+constexpr int kTkRegs = 16;        // staged records per thread per output chunk (strided)
+constexpr int kTkRankCap = 2048;   // entries ranked in shared memory
 constexpr int kTkLevels = 6;
 __constant__ int kTkShift[kTkLevels] = {52, 41, 31, 20, 10, 0};
 __constant__ int kTkBits[kTkLevels] = {11, 11, 10, 11, 10, 10};
@@ -47,40 +53,46 @@ __device__ __forceinline__ uint64_t composite(uint32_t u, uint32_t lo) {
   return (uint64_t(u) << 31) | uint64_t(lo);
 }
 
+// Order-preserving key of raw fp32 bits; NaN (any payload) above +inf.
+__device__ __forceinline__ uint32_t rank_u(uint32_t raw) {
+  if ((raw & 0x7fffffffu) > 0x7f800000u) return 0xffffffffu;
+  return score_key(__uint_as_float(raw));
+}
+
 struct TopkWs {
-  size_t hist, done, count, cand_key, cand_idx, bits, total;
-  int64_t words;  // bitmap words per row
+  size_t hist, hist1, done, cnt, stage, total;
+  int64_t words;  // 32-entry words per row
   __host__ __device__ TopkWs(int64_t rows, int64_t row_stride) {
     words = (row_stride + 31) / 32;
-    hist = 0;                                                    // [rows][2048] u32
-    done = hist + size_t(rows) * kTkBins * 4;                    // [rows] u32 tickets
-    count = done + ((size_t(rows) * 4 + 255) / 256) * 256;       // [rows] u32 candidates
-    cand_key = count + ((size_t(rows) * 4 + 255) / 256) * 256;   // [rows][cap] u64 composite
-    cand_idx = cand_key + size_t(rows) * kTkCap * 8;             // [rows][cap] u32 entry index
-    bits = cand_idx + size_t(rows) * kTkCap * 4;                 // [rows][words] u32
-    total = bits + ((size_t(rows) * words * 4 + 255) / 256) * 256;
+    hist = 0;                                                    // [rows][2048] u32 digit 0
+    hist1 = hist + size_t(rows) * kTkBins * 4;                   // [rows][2048] u32 digit 1 of the threshold bin
+    done = hist1 + size_t(rows) * kTkBins * 4;                   // [rows] u32 tickets
+    cnt = done + ((size_t(rows) * 4 + 255) / 256) * 256;         // [rows][256] u32 staged per CTA
+    stage = cnt + size_t(rows) * kTkMaxCtas * 4;                 // [rows][row_stride] u64 records
+    total = stage + ((size_t(rows) * size_t(row_stride) * 8 + 255) / 256) * 256;
   }
 };
 
 struct TopkShared {
   uint32_t hist[kTkBins];
-  uint64_t lkey[kTkLocalCap];
-  uint32_t lidx[kTkLocalCap];
+  uint64_t rank[kTkRankCap];
+  uint32_t pre[kTkMaxCtas + 1];  // exclusive prefix of staged counts per slot
+  uint32_t e0s[kTkMaxCtas];      // first entry of each slot's range in the row
+  uint32_t tot[kTkPer][kTkWarps];
+  uint32_t tot16[kTkRegs][kTkWarps];
+  uint8_t map[kTkThreads * kTkRegs];  // chunk position -> slot
   uint32_t scratch[2 * kTkWarps + 8];
-  uint32_t nlocal, base, last;
+  uint32_t nrank, last;
 };
 
 struct Select {
   uint32_t bin, above, total;
 };
 
-// Score key of entry i of a row; 0 marks an absent entry (ids[i] < 0).  NaN
-// sorts above +inf as in a torch descending sort; no score maps to 0.
+// Score key of entry i of a row; 0 marks an absent entry (ids[i] < 0).
 __device__ __forceinline__ uint32_t entry_key(const float* srow, const int32_t* irow, int64_t i) {
   if (irow != nullptr && irow[i] < 0) return 0u;
-  const float s = srow[i];
-  if (isnan(s)) return 0xffffffffu;
-  return score_key(s);
+  return rank_u(__float_as_uint(srow[i]));
 }
 
 // Whole block: over h[0, nbins) (nbins in {1024, 2048}), the bin b with
@@ -134,7 +146,28 @@ __device__ Select block_find_bin(const uint32_t* h, int nbins, uint32_t need, To
   return Select{sh.scratch[kTkWarps], sh.scratch[kTkWarps + 1], total};
 }
 
-// Word range [w0, w1) of CTA c over rows * words_per_row bitmap words.
+// Exclusive block scan of one value per thread; `total` = the block's sum.
+__device__ __forceinline__ uint32_t block_excl_scan(uint32_t v, uint32_t& total, TopkShared& sh) {
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  uint32_t incl = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t x = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += x;
+  }
+  __syncthreads();
+  if (lane == 31) sh.scratch[warp] = incl;
+  __syncthreads();
+  uint32_t off = 0;
+  total = 0;
+  for (int w = 0; w < kTkWarps; ++w) {
+    off += w < warp ? sh.scratch[w] : 0u;
+    total += sh.scratch[w];
+  }
+  return off + incl - v;
+}
+
+// Word range [w0, w1) of CTA c over rows * words_per_row words.
 __device__ __forceinline__ void cta_words(int64_t total_words, uint32_t c, uint32_t n, int64_t& w0,
                                           int64_t& w1) {
   w0 = total_words * c / n;
@@ -201,13 +234,12 @@ __global__ void __launch_bounds__(kTkThreads) topk_hist_kernel(
   }
 }
 
-// The k-th largest composite among `count` keys whose digits above `level` are
-// `prefix` (need = how many of them to take).  Whole block, shared histogram.
+// The need-th largest rank key among the `count` keys whose digits above
+// `level` equal those of `prefix`.  Whole block, shared histogram.
 template <typename KeyAt>
 __device__ uint64_t resolve_kstar(KeyAt key_at, int64_t count, uint64_t prefix, uint32_t need,
-                                  TopkShared& sh) {
+                                  int level, TopkShared& sh) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  int level = 1;
   for (; level < kTkLevels; ++level) {
     const int nb = 1 << kTkBits[level];
     const int hs = kTkShift[level - 1];  // digits above this one are fixed by `prefix`
@@ -255,8 +287,13 @@ __device__ uint64_t resolve_kstar(KeyAt key_at, int64_t count, uint64_t prefix, 
   return kstar;
 }
 
+// Staged record -> rank key.
+__device__ __forceinline__ uint64_t record_key(uint64_t rec) {
+  return composite(rank_u(uint32_t(rec >> 31)), uint32_t(rec) & 0x7fffffffu);
+}
+
 // ---------------------------------------------------------------------------
-// Selection: bitmap words + candidates per CTA, resolution by the last CTA.
+// Selection: staging by every CTA, resolution and output by the row's last CTA.
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(kTkThreads) topk_select_kernel(
     const float* __restrict__ scores, const int32_t* __restrict__ ids,
@@ -266,11 +303,10 @@ __global__ void __launch_bounds__(kTkThreads) topk_select_kernel(
   __shared__ __align__(16) TopkShared sh;
   const TopkWs L(rows, row_stride);
   uint32_t* ghist = reinterpret_cast<uint32_t*>(ws_base + L.hist);
+  uint32_t* ghist1 = reinterpret_cast<uint32_t*>(ws_base + L.hist1);
   uint32_t* gdone = reinterpret_cast<uint32_t*>(ws_base + L.done);
-  uint32_t* gcount = reinterpret_cast<uint32_t*>(ws_base + L.count);
-  uint64_t* gkey = reinterpret_cast<uint64_t*>(ws_base + L.cand_key);
-  uint32_t* gidx = reinterpret_cast<uint32_t*>(ws_base + L.cand_idx);
-  uint32_t* gbits = reinterpret_cast<uint32_t*>(ws_base + L.bits);
+  uint32_t* gcnt = reinterpret_cast<uint32_t*>(ws_base + L.cnt);
+  uint64_t* gstage = reinterpret_cast<uint64_t*>(ws_base + L.stage);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const uint32_t cta = blockIdx.x, nctas = gridDim.x;
   const int64_t total_words = rows * L.words;
@@ -285,6 +321,8 @@ __global__ void __launch_bounds__(kTkThreads) topk_select_kernel(
     const int64_t n = row_length(lengths, r, row_stride);
     const int64_t a0 = w0 > rb ? w0 - rb : 0;                         // first word of the row
     const int64_t a1 = (w1 < rb + L.words ? w1 : rb + L.words) - rb;  // end word of the row
+    const int64_t e0 = a0 * 32;
+    const int64_t e1 = a1 * 32 < n ? a1 * 32 : n;  // this CTA's entries [e0, e1)
     const uint32_t first_cta = word_owner(rb, total_words, nctas);
     const uint32_t touching = word_owner(rb + L.words - 1, total_words, nctas) - first_cta + 1;
     if (cta == first_cta && tid == 0) {
@@ -293,54 +331,70 @@ __global__ void __launch_bounds__(kTkThreads) topk_select_kernel(
     }
     const float* srow = scores + r * row_stride;
     const int32_t* irow = ids != nullptr ? ids + r * row_stride : nullptr;
-    auto id_of = [&](int64_t i) -> int32_t {
-      return irow != nullptr ? irow[i] : int32_t(id_base + i);
-    };
+    uint32_t* h0row = ghist + r * kTkBins;
+    uint32_t* h1row = ghist1 + r * kTkBins;
+    uint64_t* srec = gstage + r * row_stride;
 
-    // threshold bin of the row
-    for (int i = tid; i < kTkBins; i += kTkThreads) sh.hist[i] = ghist[r * kTkBins + i];
-    if (tid == 0) sh.nlocal = 0u;
+    // ---- row histogram and the first chunk of scores, loaded together
+    uint32_t hv[kTkBins / kTkThreads];
+#pragma unroll
+    for (int j = 0; j < kTkBins / kTkThreads; ++j) hv[j] = h0row[j * kTkThreads + tid];
+    uint32_t raw[kTkPer];
+    int32_t idv[kTkPer];
+    auto load_chunk = [&](int64_t c0) {
+#pragma unroll
+      for (int j = 0; j < kTkPer; ++j) {
+        const int64_t i = c0 + j * kTkThreads + tid;
+        const bool in = i < e1;
+        raw[j] = in ? __float_as_uint(srow[i]) : 0u;
+        idv[j] = in ? (irow != nullptr ? irow[i] : int32_t(id_base + i)) : -1;
+      }
+    };
+    load_chunk(e0);
+#pragma unroll
+    for (int j = 0; j < kTkBins / kTkThreads; ++j) sh.hist[j * kTkThreads + tid] = hv[j];
     __syncthreads();
     const Select s0 = block_find_bin(sh.hist, kTkBins, uint32_t(k), sh);
     const bool take_all = s0.total <= uint32_t(k);
+    const uint32_t need0 = uint32_t(k) - s0.above;
+    const bool whole_bin = take_all || sh.hist[s0.bin] == need0;  // no entry left to rank
 
-    // one warp per bitmap word: ballot of "above the threshold bin"
-    for (int64_t wd = a0 + warp; wd < a1; wd += kTkWarps) {
-      const int64_t i = wd * 32 + lane;
-      const uint32_t u = i < n ? entry_key(srow, irow, i) : 0u;
-      const uint32_t d = u >> 21;
-      const bool above = u != 0u && (take_all || d > s0.bin);
-      const bool cand = !take_all && u != 0u && d == s0.bin;
-      const unsigned word = __ballot_sync(0xffffffffu, above);
-      if (lane == 0) gbits[r * L.words + wd] = word;
-      const unsigned m = __ballot_sync(0xffffffffu, cand);
-      if (m) {
-        const int leader = __ffs(m) - 1;
-        uint32_t slot = 0;
-        if (lane == leader) slot = atomicAdd(&sh.nlocal, uint32_t(__popc(m)));
-        slot = __shfl_sync(0xffffffffu, slot, leader) + __popc(m & ((1u << lane) - 1u));
-        if (cand && slot < uint32_t(kTkLocalCap)) {
-          sh.lkey[slot] = composite(u, 0x7fffffffu - uint32_t(id_of(i)));
-          sh.lidx[slot] = uint32_t(i);
+    // ---- stage entries at or above the threshold bin, compacted in entry order
+    uint32_t staged = 0;  // block-uniform running count
+    for (int64_t c0 = e0; c0 < e1; c0 += int64_t(kTkThreads) * kTkPer) {
+      if (c0 != e0) load_chunk(c0);
+      bool keep[kTkPer];
+      unsigned bal[kTkPer];
+#pragma unroll
+      for (int j = 0; j < kTkPer; ++j) {
+        const uint32_t d0 = rank_u(raw[j]) >> 21;
+        keep[j] = idv[j] >= 0 && (take_all || d0 >= s0.bin);
+        if (keep[j] && !whole_bin && d0 == s0.bin)
+          atomicAdd(h1row + ((rank_u(raw[j]) >> 10) & (kTkBins - 1)), 1u);
+        bal[j] = __ballot_sync(0xffffffffu, keep[j]);
+        if (lane == 0) sh.tot[j][warp] = __popc(bal[j]);
+      }
+      __syncthreads();
+      uint32_t base = staged;
+#pragma unroll
+      for (int j = 0; j < kTkPer; ++j) {
+        uint32_t before = 0, all = 0;
+        for (int w = 0; w < kTkWarps; ++w) {
+          before += w < warp ? sh.tot[j][w] : 0u;
+          all += sh.tot[j][w];
         }
+        if (keep[j]) {
+          const uint32_t pos = base + before + __popc(bal[j] & ((1u << lane) - 1u));
+          srec[e0 + pos] = (uint64_t(raw[j]) << 31) | uint64_t(0x7fffffffu - uint32_t(idv[j]));
+        }
+        base += all;
       }
+      staged = base;
+      __syncthreads();  // sh.tot is reused by the next chunk
     }
-    __syncthreads();
-    const uint32_t nl = sh.nlocal;
-    if (tid == 0) {
-      // an overflowing CTA forces the whole-row path through an oversized count
-      const uint32_t add = nl <= uint32_t(kTkLocalCap) ? nl : uint32_t(kTkCap) + 1u;
-      sh.base = add ? atomicAdd(gcount + r, add) : 0u;
-    }
-    __syncthreads();
-    for (uint32_t e = tid; e < nl && e < uint32_t(kTkLocalCap); e += kTkThreads) {
-      const uint32_t slot = sh.base + e;
-      if (slot < uint32_t(kTkCap)) {
-        gkey[r * kTkCap + slot] = sh.lkey[e];
-        gidx[r * kTkCap + slot] = sh.lidx[e];
-      }
-    }
-    // ticket: the last CTA of the row finishes it
+    if (tid == 0) gcnt[r * kTkMaxCtas + (cta - first_cta)] = staged;
+
+    // ---- ticket: the last CTA of the row finishes it
     __threadfence();
     __syncthreads();
     if (tid == 0) sh.last = atomicAdd(gdone + r, 1u) == touching - 1 ? 1u : 0u;
@@ -348,87 +402,149 @@ __global__ void __launch_bounds__(kTkThreads) topk_select_kernel(
     if (!sh.last) continue;
     __threadfence();
 
-    // other CTAs' words and candidates are read from L2 (__ldcg), never a stale L1 line
-    uint32_t* rbits = gbits + r * L.words;
-    const uint32_t count = __ldcg(gcount + r);
-    if (!take_all) {
-      const uint64_t prefix0 = uint64_t(s0.bin) << kTkShift[0];
-      const uint32_t need0 = uint32_t(k) - s0.above;
-      const bool whole_bin = sh.hist[s0.bin] == need0;  // every threshold-bin entry is selected
-      if (count <= uint32_t(kTkCap)) {
-        // ---- radix over the candidates' remaining digits
-        const uint64_t* ck = gkey + r * kTkCap;
-        const uint64_t kstar =
-            whole_bin ? 0ull
-                      : resolve_kstar([&](int64_t i) { return __ldcg(ck + i); }, count, prefix0, need0, sh);
-        for (uint32_t i = tid; i < count; i += kTkThreads)
-          if (__ldcg(ck + i) >= kstar) {
-            const uint32_t idx = __ldcg(gidx + r * kTkCap + i);
-            atomicOr(rbits + (idx >> 5), 1u << (idx & 31));
+    // other CTAs' counts, records and digit-1 counts are read from L2 (__ldcg)
+    uint32_t h1v[kTkBins / kTkThreads];
+    if (!whole_bin) {
+#pragma unroll
+      for (int j = 0; j < kTkBins / kTkThreads; ++j) h1v[j] = __ldcg(h1row + j * kTkThreads + tid);
+    }
+    const uint32_t my_cnt = uint32_t(tid) < touching ? __ldcg(gcnt + r * kTkMaxCtas + tid) : 0u;
+    if (uint32_t(tid) < touching) {
+      int64_t cw0, cw1;
+      cta_words(total_words, first_cta + tid, nctas, cw0, cw1);
+      sh.e0s[tid] = uint32_t((cw0 > rb ? cw0 - rb : 0) * 32);
+    }
+    uint32_t total_staged = 0;
+    const uint32_t my_pre = block_excl_scan(my_cnt, total_staged, sh);
+    sh.pre[tid] = my_pre;
+    if (tid == 0) sh.pre[touching] = total_staged;
+    // (slots >= touching are never searched: pre[touching] bounds every walk)
+
+    // digit 1 of K*
+    uint32_t bin1 = 0, need1 = 0;
+    bool sub_all = true;  // every threshold-bin entry with digit 1 == bin1 is selected
+    if (!whole_bin) {
+#pragma unroll
+      for (int j = 0; j < kTkBins / kTkThreads; ++j) sh.hist[j * kTkThreads + tid] = h1v[j];
+      __syncthreads();
+      const Select s1 = block_find_bin(sh.hist, kTkBins, need0, sh);
+      bin1 = s1.bin;
+      need1 = need0 - s1.above;
+      sub_all = need1 == sh.hist[s1.bin];
+    }
+    if (tid == 0) sh.nrank = 0u;
+    __syncthreads();
+
+    // records f = c0 + j * kTkThreads + tid of the row's staged sequence: a
+    // shared map gives every position of the chunk its slot, so consecutive
+    // threads load consecutive records and write consecutive outputs
+    constexpr uint32_t kChunk = uint32_t(kTkThreads) * kTkRegs;
+    uint64_t rec[kTkRegs];
+    uint32_t loaded_c0 = 0xffffffffu;  // block-uniform
+    auto load_records = [&](uint32_t c0) {
+      if (loaded_c0 == c0) return;
+      loaded_c0 = c0;
+      __syncthreads();  // readers of the previous chunk's map are done
+      if (uint32_t(tid) < touching) {
+        const uint32_t b = sh.pre[tid], e = sh.pre[tid + 1];
+        const uint32_t lo = b > c0 ? b : c0, hi = e < c0 + kChunk ? e : c0 + kChunk;
+        for (uint32_t f = lo; f < hi; ++f) sh.map[f - c0] = uint8_t(tid);
+      }
+      __syncthreads();
+#pragma unroll
+      for (int j = 0; j < kTkRegs; ++j) {
+        const uint32_t f = c0 + j * kTkThreads + tid;
+        if (f < total_staged) {
+          const uint32_t slot = sh.map[f - c0];
+          rec[j] = __ldcg(srec + sh.e0s[slot] + (f - sh.pre[slot]));
+        } else {
+          rec[j] = 0ull;
+        }
+      }
+    };
+    const uint64_t prefix1 = (uint64_t(s0.bin) << kTkShift[0]) | (uint64_t(bin1) << kTkShift[1]);
+    auto shares_two_digits = [&](uint64_t key) { return (key >> kTkShift[1]) == (prefix1 >> kTkShift[1]); };
+
+    // ---- rank the entries that share K*'s two digits
+    uint64_t kstar = prefix1;  // with sub_all: every key with those digits qualifies
+    if (!sub_all) {
+      for (uint32_t c0 = 0; c0 < total_staged; c0 += kChunk) {
+        load_records(c0);
+#pragma unroll
+        for (int j = 0; j < kTkRegs; ++j) {
+          const uint32_t f = c0 + j * kTkThreads + tid;
+          const uint64_t key = record_key(rec[j]);
+          if (f < total_staged && shares_two_digits(key)) {
+            const uint32_t slot = atomicAdd(&sh.nrank, 1u);
+            if (slot < uint32_t(kTkRankCap)) sh.rank[slot] = key;
           }
+        }
+      }
+      __syncthreads();
+      const uint32_t nr = sh.nrank;
+      if (nr <= uint32_t(kTkRankCap)) {
+        kstar = resolve_kstar([&](int64_t i) { return sh.rank[i]; }, nr, prefix1, need1, 2, sh);
       } else {
-        // ---- candidate overflow: resolve over the whole row, then mark its bin
         auto row_key = [&](int64_t i) -> uint64_t {
           const uint32_t u = entry_key(srow, irow, i);
-          return u ? composite(u, 0x7fffffffu - uint32_t(id_of(i))) : 0ull;
+          const int32_t id = irow != nullptr ? irow[i] : int32_t(id_base + i);
+          return u ? composite(u, 0x7fffffffu - uint32_t(id)) : 0ull;
         };
-        const uint64_t kstar = whole_bin ? 0ull : resolve_kstar(row_key, n, prefix0, need0, sh);
-        for (int64_t i = tid; i < n; i += kTkThreads) {
-          const uint32_t u = entry_key(srow, irow, i);
-          if (u && (u >> 21) == s0.bin && composite(u, 0x7fffffffu - uint32_t(id_of(i))) >= kstar)
-            atomicOr(rbits + (i >> 5), 1u << (i & 31));
-        }
+        kstar = resolve_kstar(row_key, n, prefix1, need1, 2, sh);
       }
-      __threadfence();
-      __syncthreads();
     }
 
-    // ---- bitmap -> ascending ids (contiguous words per thread, block scan)
-    const int64_t nwords = (n + 31) / 32;
-    const int64_t per = (nwords + kTkThreads - 1) / kTkThreads;
-    const int64_t my0 = tid * per, my1 = my0 + per < nwords ? my0 + per : nwords;
-    uint32_t mine = 0;
-    for (int64_t wd = my0; wd < my1; ++wd) mine += __popc(__ldcg(rbits + wd));
-    uint32_t incl = mine;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const uint32_t x = __shfl_up_sync(0xffffffffu, incl, o);
-      if (lane >= o) incl += x;
-    }
-    __syncthreads();
-    if (lane == 31) sh.scratch[warp] = incl;
-    __syncthreads();
-    uint32_t pos = incl - mine, total = 0;
-    for (int w = 0; w < kTkWarps; ++w) {
-      pos += w < warp ? sh.scratch[w] : 0u;
-      total += sh.scratch[w];
-    }
+    // ---- keep the selected records in entry order and write them out
     int32_t* orow = out_ids + r * k;
     float* osrow = out_scores != nullptr ? out_scores + r * k : nullptr;
-    for (int64_t wd = my0; wd < my1; ++wd) {
-      uint32_t word = __ldcg(rbits + wd);
-      while (word) {
-        const int bit = __ffs(word) - 1;
-        word &= word - 1;
-        const int64_t i = wd * 32 + bit;
-        if (pos < uint32_t(k)) {
-          orow[pos] = id_of(i);
-          if (osrow != nullptr) osrow[pos] = srow[i];
-        }
-        ++pos;
+    uint32_t written = 0;  // block-uniform
+    for (uint32_t c0 = 0; c0 < total_staged && written < uint32_t(k); c0 += kChunk) {
+      load_records(c0);  // the rank pass already holds a single chunk
+      unsigned bal[kTkRegs];
+#pragma unroll
+      for (int j = 0; j < kTkRegs; ++j) {
+        const uint32_t f = c0 + j * kTkThreads + tid;
+        const uint64_t key = record_key(rec[j]);
+        const bool keep = f < total_staged &&
+                          (whole_bin || uint32_t(key >> kTkShift[0]) > s0.bin || key >= kstar);
+        bal[j] = __ballot_sync(0xffffffffu, keep);
+        if (lane == 0) sh.tot16[j][warp] = __popc(bal[j]);
       }
+      __syncthreads();
+      uint32_t base = written;
+#pragma unroll
+      for (int j = 0; j < kTkRegs; ++j) {
+        uint32_t before = 0, all = 0;
+#pragma unroll
+        for (int w = 0; w < kTkWarps; ++w) {
+          const uint32_t t = sh.tot16[j][w];
+          before += w < warp ? t : 0u;
+          all += t;
+        }
+        if ((bal[j] >> lane) & 1u) {
+          const uint32_t pos = base + before + __popc(bal[j] & ((1u << lane) - 1u));
+          if (pos < uint32_t(k)) {
+            orow[pos] = int32_t(0x7fffffffu - (uint32_t(rec[j]) & 0x7fffffffu));
+            if (osrow != nullptr) osrow[pos] = __uint_as_float(uint32_t(rec[j] >> 31));
+          }
+        }
+        base += all;
+      }
+      written = base;
+      __syncthreads();  // sh.tot16 is reused by the next chunk
     }
-    const uint32_t chosen = total < uint32_t(k) ? total : uint32_t(k);
+    const uint32_t chosen = written < uint32_t(k) ? written : uint32_t(k);
     for (int p = int(chosen) + tid; p < k; p += kTkThreads) {
       orow[p] = -1;
       if (osrow != nullptr) osrow[p] = -CUDART_INF_F;
     }
     // every CTA of the row is done with its state: clear it for the next call
-    for (int i = tid; i < kTkBins; i += kTkThreads) ghist[r * kTkBins + i] = 0u;
-    if (tid == 0) {
-      gcount[r] = 0u;
-      gdone[r] = 0u;
+#pragma unroll
+    for (int j = 0; j < kTkBins / kTkThreads; ++j) {
+      h0row[j * kTkThreads + tid] = 0u;
+      h1row[j * kTkThreads + tid] = 0u;
     }
+    if (tid == 0) gdone[r] = 0u;
     __syncthreads();
   }
 }
@@ -436,6 +552,7 @@ __global__ void __launch_bounds__(kTkThreads) topk_select_kernel(
 int topk_ctas(int64_t rows, int64_t row_stride) {
   const int64_t words = rows * ((row_stride + 31) / 32);
   int64_t ctas = sm_count();
+  if (ctas > kTkMaxCtas) ctas = kTkMaxCtas;
   if (words < ctas * 4) ctas = (words + 3) / 4;  // at least 4 words (128 entries) per CTA
   return int(ctas < 1 ? 1 : ctas);
 }
@@ -447,7 +564,7 @@ size_t topk_workspace_bytes(int64_t rows, int64_t row_stride) {
 }
 
 size_t topk_zeroed_prefix_bytes(int64_t rows, int64_t row_stride) {
-  return TopkWs(rows, row_stride).cand_key;
+  return TopkWs(rows, row_stride).cnt;
 }
 
 // hist_ready: the per-row histograms in the workspace were already built (by the

@@ -124,7 +124,7 @@ int dsr_topk_select(const float* scores, const int32_t* ids, const int32_t* leng
  * All calls on one device share the scratch: calls that overlap on the GPU
  * (different streams, or threads without ordering) race and must be
  * serialised by the caller. */
-#define DSR_TOPK_NOALLOC_BYTES (1u << 20)
+#define DSR_TOPK_NOALLOC_BYTES (16u << 20)
 int dsr_topk_select_noalloc(const float* scores, const int32_t* ids, const int32_t* lengths,
                             int32_t* out_ids, float* out_scores, int32_t* err, int64_t rows,
                             int64_t row_stride, int64_t k, int64_t id_base, void* stream);

@@ -107,3 +107,31 @@ def test_topk_id_base_and_length_error(cuda):
     assert code == 0 and out.tolist() == [[1096, 1097, 1098, 1099]]
     out, code = c_topk(scores, torch.tensor([101], dtype=torch.int32, device="cuda"), 4)
     assert code == 1 and out.tolist() == [[-1, -1, -1, -1]]
+
+
+def test_topk_each_resolution_path(cuda):
+    # rows built so the threshold bin is resolved by each route: ranked among staged
+    # candidates, ranked over the candidate list (digit-1 bin too big to stage), whole
+    # threshold bin selected, whole digit-1 bin selected, candidate-list overflow
+    rng = np.random.default_rng(26)
+    n, k = 60000, 2048
+    scores = (rng.normal(size=(5, n)) * 0.05).astype(np.float32)
+    layouts = [
+        [],                                              # staged ranking (plain normal scores)
+        [(1000, 2.0), (3000, 1.0)],                      # 3000 tied in one digit-1 bin
+        [(2048, 5.0)],                                   # the threshold bin is exactly k
+        [(300, 3.0), (500, 1.125), (1248, 1.0625), (1000, 1.0)],  # cut at a digit-1 bin edge
+        [(500, 4.0), (12000, 1.0)],                      # more candidates than the list holds
+    ]
+    for row, layout in enumerate(layouts):
+        pos = rng.permutation(n)
+        start = 0
+        for count, value in layout:
+            scores[row, pos[start:start + count]] = value
+            start += count
+    if not layouts[0]:
+        scores[0] = rng.normal(size=n).astype(np.float32)
+    lengths = [n] * 5
+    out, code = c_topk(dev(scores), dev(np.array(lengths, np.int32)), k)
+    assert code == 0
+    assert np.array_equal(out.cpu().numpy(), expected_rows(scores, lengths, k))

@@ -15,7 +15,7 @@ from _helpers import c_topk, dev, finish, status
 from deepseekrpc_b200 import _native
 from deepseekrpc_b200._native import ptr, stream_handle
 
-SCRATCH_BYTES = 1 << 20  # DSR_TOPK_NOALLOC_BYTES
+SCRATCH_BYTES = 16 << 20  # DSR_TOPK_NOALLOC_BYTES
 
 
 def c_topk_noalloc(scores, lengths, k, ids=None, id_base=0):
