@@ -1,0 +1,53 @@
+"""Few eager decode steps through the C ABI, for profiler captures.
+
+    python -m deepseekrpc_b200.profile_step [--config cfg2] [--steps 4]
+
+Runs `steps` decode steps (indexer -> top-k -> sparse MLA -> LSE combine, four
+kernel launches each) of one BASELINE config on cuda:0 without CUDA graphs, so
+that a profiler sees each kernel launch on its own, then checks the device
+status.  Inputs are drawn on the GPU (seeded) and stay resident; one pool
+replica, so a profiler's cache flush between replays makes each captured launch
+read its pools from DRAM.
+"""
+from __future__ import annotations
+
+import argparse
+import sys
+
+import torch
+
+from deepseekrpc_b200 import _native
+from deepseekrpc_b200.workloads import CONFIGS, make_decode_inputs
+
+
+def main(argv=None) -> int:
+    parser = argparse.ArgumentParser(description=__doc__)
+    parser.add_argument("--config", default="cfg2", choices=sorted(CONFIGS))
+    parser.add_argument("--steps", type=int, default=4)
+    args = parser.parse_args(argv)
+    cfg = CONFIGS[args.config]
+    torch.cuda.set_device(0)
+    inp, lengths = make_decode_inputs(cfg, device="cuda:0", gen_device="cuda")
+    lib = _native.library()
+    batch, max_visible = len(lengths), max(lengths)
+    ws_bytes = lib.dsr_decode_workspace_bytes(batch, max_visible, cfg.heads, cfg.topk)
+    ws = torch.zeros(ws_bytes, dtype=torch.uint8, device="cuda:0")
+    out = torch.empty((batch, cfg.heads, 512), device="cuda:0")
+    topk = torch.empty((batch, cfg.topk), dtype=torch.int32, device="cuda:0")
+    err = torch.zeros(1, dtype=torch.int32, device="cuda:0")
+    for _ in range(args.steps):
+        _native.call("dsr_decode_step", inp["idx_q"].data_ptr(), inp["idx_w"].data_ptr(), cfg.idx_heads,
+                     inp["index_pool"].data_ptr(), inp["q"].data_ptr(), inp["kv_pool"].data_ptr(), cfg.heads,
+                     inp["kv_pool"].shape[0] // 64, inp["block_table"].data_ptr(), inp["block_table"].shape[1],
+                     inp["visible"].data_ptr(), max_visible, cfg.topk, inp["swa"].data_ptr(),
+                     inp["swa_len"].data_ptr(), inp["sink"].data_ptr(), cfg.scale, out.data_ptr(),
+                     topk.data_ptr(), None, ws.data_ptr(), ws_bytes, err.data_ptr(), batch,
+                     _native.stream_handle())
+    torch.cuda.synchronize()
+    status = int(err.item())
+    print(f"{args.steps} decode steps of {cfg.name}: device status {status}")
+    return 0 if status == 0 else 1
+
+
+if __name__ == "__main__":
+    sys.exit(main())
