@@ -59,7 +59,8 @@ int launch_mla_decode(const float* q, const uint16_t* kv_pool, int64_t pool_bloc
                       const int32_t* swa_len, const float* sink, float scale, float* out,
                       void* workspace, size_t workspace_bytes, int32_t* err, int64_t batch,
                       int64_t heads, cudaStream_t stream, bool pdl,
-                      const uint16_t* q_img = nullptr);
+                      const uint16_t* q_img = nullptr, int64_t id_base = 0,
+                      bool partial = false, float* out_m = nullptr, float* out_l = nullptr);
 size_t mla_workspace_bytes(int64_t batch, int64_t heads, int64_t k);
 int launch_lse_combine(const float* part_o, const float* part_m, const float* part_l,
                        int64_t parts, const float* sink, float* out, float* out_m, float* out_l,

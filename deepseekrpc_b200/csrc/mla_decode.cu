@@ -61,7 +61,7 @@ __global__ void __launch_bounds__(kMlaThreads, 1)
                       const int32_t* __restrict__ swa_len, float scale_log2,
                       float* __restrict__ part_o, float* __restrict__ part_m,
                       float* __restrict__ part_l, int32_t* err, int heads,
-                      const uint16_t* __restrict__ q_img) {
+                      const uint16_t* __restrict__ q_img, int64_t id_base, int foreign_ok) {
   using L = MlaLayout<HG>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -162,12 +162,17 @@ __global__ void __launch_bounds__(kMlaThreads, 1)
       if (idx < k) {
         const int id = topk[int64_t(b) * k + idx];
         if (id != -1) {
-          if (id < 0 || id >= visible[b]) {
+          // position id lives in this pool at local row id - id_base; with
+          // foreign_ok, ids owned by another shard are skipped, not errors
+          const int64_t local = int64_t(id) - id_base;
+          if (id < 0) {
             flag(err, DSR_ERR_ID);
+          } else if (local < 0 || local >= visible[b]) {
+            if (!foreign_ok) flag(err, DSR_ERR_ID);
           } else {
-            const int64_t blk = block_table[int64_t(b) * table_stride + (id >> 6)];
+            const int64_t blk = block_table[int64_t(b) * table_stride + (local >> 6)];
             if (blk < 0 || blk >= pool_blocks) flag(err, DSR_ERR_ID);
-            else src = kv_pool + (blk * 64 + (id & 63)) * kMlaD;
+            else src = kv_pool + (blk * 64 + (local & 63)) * kMlaD;
           }
         }
       }
@@ -395,7 +400,7 @@ int launch_mla(const float* q, const uint16_t* kv_pool, int64_t pool_blocks,
                const int32_t* topk, int64_t k, const uint16_t* swa, const int32_t* swa_len,
                float scale, float* part_o, float* part_m, float* part_l, int32_t* err,
                int64_t batch, int64_t heads, int tiles, cudaStream_t stream, bool pdl,
-               const uint16_t* q_img) {
+               const uint16_t* q_img, int64_t id_base, bool foreign_ok) {
   using L = MlaLayout<HG>;
   static bool configured = false;
   if (!configured) {
@@ -417,7 +422,7 @@ int launch_mla(const float* q, const uint16_t* kv_pool, int64_t pool_blocks,
   const cudaError_t e = cudaLaunchKernelEx(&cfg, mla_decode_kernel<HG>, q, kv_pool, pool_blocks,
                                            block_table, table_stride, visible, topk, int(k), swa,
                                            swa_len, scale * kLog2e, part_o, part_m, part_l, err,
-                                           int(heads), q_img);
+                                           int(heads), q_img, id_base, int(foreign_ok));
   if (e != cudaSuccess) return fail(DSR_ECUDA, "mla launch: %s", cudaGetErrorString(e));
   return DSR_OK;
 }
@@ -464,11 +469,15 @@ int launch_mla_decode(const float* q, const uint16_t* kv_pool, int64_t pool_bloc
                       const int32_t* topk, int64_t k, const uint16_t* swa,
                       const int32_t* swa_len, const float* sink, float scale, float* out,
                       void* workspace, size_t workspace_bytes, int32_t* err, int64_t batch,
-                      int64_t heads, cudaStream_t stream, bool pdl, const uint16_t* q_img) {
+                      int64_t heads, cudaStream_t stream, bool pdl, const uint16_t* q_img,
+                      int64_t id_base, bool partial, float* out_m, float* out_l) {
   DSR_REQUIRE(q_img == nullptr || aligned16(q_img), "sparse_mla_decode: query image must be 16-byte aligned");
-  DSR_REQUIRE(q && kv_pool && block_table && visible && topk && swa && swa_len && sink && out &&
-                  err && workspace,
+  DSR_REQUIRE(q && kv_pool && block_table && visible && topk && swa && swa_len && out && err &&
+                  workspace,
               "sparse_mla_decode: null pointer");
+  DSR_REQUIRE(partial ? (sink == nullptr && out_m != nullptr && out_l != nullptr) : sink != nullptr,
+              "sparse_mla_decode: a sink (full) or out_m and out_l (partial) are required");
+  DSR_REQUIRE(id_base >= 0 && id_base < (int64_t(1) << 31), "sparse_mla_decode: invalid id base");
   DSR_REQUIRE(heads == 16 || heads == 32 || heads == 64 || heads == 128,
               "sparse_mla_decode: heads %lld not in {16,32,64,128}", (long long)heads);
   DSR_REQUIRE(batch > 0 && batch <= 65535, "sparse_mla_decode: invalid batch");
@@ -490,21 +499,21 @@ int launch_mla_decode(const float* q, const uint16_t* kv_pool, int64_t pool_bloc
     case 16:
       rc = launch_mla<16>(q, kv_pool, pool_blocks, block_table, table_stride, visible, topk, k, swa,
                           swa_len, scale, part_o, part_m, part_l, err, batch, heads, tiles, stream,
-                          pdl, q_img);
+                          pdl, q_img, id_base, partial);
       break;
     case 32:
       rc = launch_mla<32>(q, kv_pool, pool_blocks, block_table, table_stride, visible, topk, k, swa,
                           swa_len, scale, part_o, part_m, part_l, err, batch, heads, tiles, stream,
-                          pdl, q_img);
+                          pdl, q_img, id_base, partial);
       break;
     default:
       rc = launch_mla<64>(q, kv_pool, pool_blocks, block_table, table_stride, visible, topk, k, swa,
                           swa_len, scale, part_o, part_m, part_l, err, batch, heads, tiles, stream,
-                          pdl, q_img);
+                          pdl, q_img, id_base, partial);
       break;
   }
   if (rc != DSR_OK) return rc;
-  return launch_lse_combine(part_o, part_m, part_l, tiles, sink, out, nullptr, nullptr, err, batch,
+  return launch_lse_combine(part_o, part_m, part_l, tiles, sink, out, out_m, out_l, err, batch,
                             heads, kMlaDv, stream, pdl);
 }
 
@@ -525,6 +534,20 @@ extern "C" int dsr_sparse_mla_decode(const float* q, const uint16_t* kv_pool, in
   return dsr::launch_mla_decode(q, kv_pool, pool_blocks, block_table, table_stride, visible, topk,
                                 k, swa, swa_len, sink, scale, out, workspace, workspace_bytes, err,
                                 batch, heads, dsr::as_stream(stream), false);
+}
+
+extern "C" int dsr_sparse_mla_partial(const float* q, const uint16_t* kv_pool, int64_t pool_blocks,
+                                      const int32_t* block_table, int64_t table_stride,
+                                      const int32_t* visible, const int32_t* topk, int64_t k,
+                                      int64_t id_base, const uint16_t* swa, const int32_t* swa_len,
+                                      float scale, float* out_o, float* out_m, float* out_l,
+                                      void* workspace, size_t workspace_bytes, int32_t* err,
+                                      int64_t batch, int64_t heads, void* stream) {
+  dsr::clear_error();
+  return dsr::launch_mla_decode(q, kv_pool, pool_blocks, block_table, table_stride, visible, topk,
+                                k, swa, swa_len, nullptr, scale, out_o, workspace, workspace_bytes,
+                                err, batch, heads, dsr::as_stream(stream), false, nullptr, id_base,
+                                true, out_m, out_l);
 }
 
 extern "C" int dsr_lse_combine(const float* part_o, const float* part_m, const float* part_l,

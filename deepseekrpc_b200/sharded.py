@@ -1,0 +1,348 @@
+"""Sequence-sharded sparse-attention decode across the GPUs of one node.
+
+One process per GPU (torch.distributed, NCCL).  Rank r of G owns the logical
+positions [r*S, (r+1)*S) of every sequence, S = the shard span (a multiple of
+the 64-token block), in its own index-key and KV pools; the SWA rows live on
+the rank that owns each sequence's tail.  A decode step is
+
+  1. local indexer scores over the owned positions, local exact top-k with
+     global ids (id_base = r*S), scores returned with the ids;
+  2. one all-gather of the (score, id) lists; every rank merges the G lists
+     into the exact global top-k with the same tie rule (the union of the local
+     top-k sets holds the global top-k under that total order), so every rank
+     holds the same selection without a second exchange;
+  3. local sparse-MLA partial (m, l, o) over the selected rows it owns (plus the
+     SWA rows on the tail owner), without the sink;
+  4. one all-gather of the partials and a log-sum-exp combine that adds the
+     sink exactly once.
+
+There is no reference counterpart (the reference decodes on one GPU); the
+single-GPU semantics it must reproduce are TiledIndexer.select
+(index_selection.py:79-124) followed by sparse_attention with the sink
+(native/operations.cu:30-82).
+
+The exchange/layout helpers are plain torch and run on any backend (the CPU
+tests use gloo); the per-rank compute goes through the C ABI and needs the
+built library and a B200.
+"""
+from __future__ import annotations
+
+import json
+import os
+import time
+from dataclasses import dataclass
+
+import torch
+import torch.distributed as dist
+
+from . import _native
+from .workloads import BLOCK, INDEX_DIM, KV_DIM, SWA_ROWS, V_DIM, CONFIGS
+
+# ----------------------------------------------------------------- planning
+
+
+@dataclass(frozen=True)
+class ShardPlan:
+    """Position ownership of rank `rank` out of `world` for a batch of sequences."""
+
+    world: int
+    rank: int
+    lengths: tuple  # visible positions of each sequence (the query sits at L-1)
+
+    @property
+    def span(self) -> int:
+        """Positions per shard: the longest sequence's blocks split evenly."""
+        blocks = (max(self.lengths) + BLOCK - 1) // BLOCK
+        return ((blocks + self.world - 1) // self.world) * BLOCK
+
+    @property
+    def id_base(self) -> int:
+        return self.rank * self.span
+
+    def local_visible(self) -> list[int]:
+        """Owned visible positions of each sequence: [id_base, id_base + n)."""
+        base, span = self.id_base, self.span
+        return [max(0, min(n - base, span)) for n in self.lengths]
+
+    def owns_tail(self, b: int) -> bool:
+        """The rank holding position L_b - 1 also holds that sequence's SWA rows."""
+        n = self.lengths[b]
+        return n > 0 and self.id_base <= n - 1 < self.id_base + self.span
+
+    def local_swa_len(self) -> list[int]:
+        return [min(SWA_ROWS, n) if self.owns_tail(b) else 0 for b, n in enumerate(self.lengths)]
+
+    def local_blocks(self) -> int:
+        return self.span // BLOCK
+
+
+def local_block_table(full_table: torch.Tensor, plan: ShardPlan) -> torch.Tensor:
+    """Columns of a global block table owned by `plan` (block j of the shard = global
+    block id_base/64 + j), padded with -1 past the table's end."""
+    first = plan.id_base // BLOCK
+    cols = plan.local_blocks()
+    out = torch.full((full_table.shape[0], cols), -1, dtype=torch.int32, device=full_table.device)
+    take = max(0, min(cols, full_table.shape[1] - first))
+    if take:
+        out[:, :take] = full_table[:, first:first + take]
+    return out.contiguous()
+
+
+# ------------------------------------------------------------ exchange layouts
+
+
+def pack_topk(scores: torch.Tensor, ids: torch.Tensor) -> torch.Tensor:
+    """[2, B, k] int32: the local scores (bit pattern) and their global ids."""
+    return torch.stack((scores.contiguous().view(torch.int32), ids.contiguous()))
+
+
+def unpack_gathered_topk(gathered: torch.Tensor, world: int):
+    """[G*2, B, k] (rank-major all-gather of pack_topk) -> scores f32[B, G*k], ids i32[B, G*k].
+
+    Ranks own increasing position ranges and each list is ascending, so along a
+    row the ids increase: the form the top-k merge (explicit-id mode) requires."""
+    g = gathered.view(world, 2, gathered.shape[-2], gathered.shape[-1])
+    b, k = g.shape[2], g.shape[3]
+    scores = g[:, 0].permute(1, 0, 2).reshape(b, world * k).contiguous().view(torch.float32)
+    ids = g[:, 1].permute(1, 0, 2).reshape(b, world * k).contiguous()
+    return scores, ids
+
+
+def pack_partials(o: torch.Tensor, m: torch.Tensor, l: torch.Tensor) -> torch.Tensor:
+    """f32 [B*H*(512+2)]: o, then m, then l of this rank's partial."""
+    return torch.cat((o.reshape(-1), m.reshape(-1), l.reshape(-1)))
+
+
+def unpack_gathered_partials(gathered: torch.Tensor, world: int, batch: int, heads: int):
+    """Rank-major gathered partials -> o f32[G, B*H, 512], m f32[G, B*H], l f32[G, B*H].
+
+    Laid out so that dsr_lse_combine with batch=1 and heads=B*H merges the G
+    partials of every (b, h) (partial t of pair j at t*B*H + j)."""
+    bh = batch * heads
+    g = gathered.view(world, bh * (V_DIM + 2))
+    o = g[:, :bh * V_DIM].reshape(world, bh, V_DIM).contiguous()
+    m = g[:, bh * V_DIM:bh * (V_DIM + 1)].contiguous()
+    l = g[:, bh * (V_DIM + 1):].contiguous()
+    return o, m, l
+
+
+def all_gather(tensor: torch.Tensor, group=None) -> torch.Tensor:
+    """Rank-major concatenation along a new leading dimension (flattened into dim 0)."""
+    world = dist.get_world_size(group)
+    out = torch.empty((world * tensor.shape[0],) + tuple(tensor.shape[1:]), dtype=tensor.dtype,
+                      device=tensor.device)
+    dist.all_gather_into_tensor(out, tensor.contiguous(), group=group)
+    return out
+
+
+# ------------------------------------------------------------- per-rank step
+
+
+class ShardedDecoder:
+    """Buffers and C-ABI calls of one rank's sharded decode step."""
+
+    def __init__(self, plan: ShardPlan, heads: int, idx_heads: int, topk: int, scale: float,
+                 sink: torch.Tensor, device):
+        self.plan, self.heads, self.idx_heads, self.k, self.scale = plan, heads, idx_heads, topk, scale
+        self.lib = _native.library()
+        B = len(plan.lengths)
+        self.batch = B
+        self.span = plan.span
+        dev = torch.device(device)
+        self.visible = torch.tensor(plan.local_visible(), dtype=torch.int32, device=dev)
+        self.swa_len = torch.tensor(plan.local_swa_len(), dtype=torch.int32, device=dev)
+        self.merge_len = torch.full((B,), plan.world * topk, dtype=torch.int32, device=dev)
+        self.scores = torch.empty((B, self.span), device=dev)
+        self.local_ids = torch.empty((B, topk), dtype=torch.int32, device=dev)
+        self.local_scores = torch.empty((B, topk), device=dev)
+        self.ids = torch.empty((B, topk), dtype=torch.int32, device=dev)
+        self.topk_bytes = self.lib.dsr_topk_workspace_bytes(B, max(self.span, plan.world * topk))
+        self.topk_ws = torch.zeros(self.topk_bytes, dtype=torch.uint8, device=dev)
+        self.mla_bytes = self.lib.dsr_mla_workspace_bytes(B, heads, topk)
+        self.mla_ws = torch.zeros(self.mla_bytes, dtype=torch.uint8, device=dev)
+        self.o = torch.empty((B, heads, V_DIM), device=dev)
+        self.m = torch.empty((B, heads), device=dev)
+        self.l = torch.empty((B, heads), device=dev)
+        self.out = torch.empty((B, heads, V_DIM), device=dev)
+        self.sink_bh = sink.float().repeat(B).contiguous().to(dev)  # sink of pair (b, h) at b*H + h
+        self.err = torch.zeros(1, dtype=torch.int32, device=dev)
+
+    # the three phases, so a single-GPU emulation can run them shard by shard
+    def select_local(self, idx_q, idx_w, index_pool, block_table, stream=None):
+        s = _native.stream_handle(stream)
+        p = _native.ptr
+        _native.call("dsr_indexer_decode", p(idx_q), p(idx_w), p(index_pool), index_pool.shape[0] // BLOCK,
+                     p(block_table), block_table.shape[1], p(self.visible), p(self.scores), self.span,
+                     p(self.err), self.batch, self.idx_heads, s)
+        _native.call("dsr_topk_select", p(self.scores), None, p(self.visible), p(self.local_ids),
+                     p(self.local_scores), p(self.err), self.batch, self.span, self.k, self.plan.id_base,
+                     p(self.topk_ws), self.topk_bytes, s)
+        return pack_topk(self.local_scores, self.local_ids)
+
+    def merge(self, gathered, stream=None):
+        scores_all, ids_all = unpack_gathered_topk(gathered, self.plan.world)
+        p = _native.ptr
+        _native.call("dsr_topk_select", p(scores_all), p(ids_all), p(self.merge_len), p(self.ids), None,
+                     p(self.err), self.batch, scores_all.shape[1], self.k, 0, p(self.topk_ws),
+                     self.topk_bytes, _native.stream_handle(stream))
+        return self.ids
+
+    def attend_local(self, q, kv_pool, block_table, swa, stream=None):
+        p = _native.ptr
+        _native.call("dsr_sparse_mla_partial", p(q), p(kv_pool), kv_pool.shape[0] // BLOCK, p(block_table),
+                     block_table.shape[1], p(self.visible), p(self.ids), self.k, self.plan.id_base, p(swa),
+                     p(self.swa_len), float(self.scale), p(self.o), p(self.m), p(self.l), p(self.mla_ws),
+                     self.mla_bytes, p(self.err), self.batch, self.heads, _native.stream_handle(stream))
+        return pack_partials(self.o, self.m, self.l)
+
+    def combine(self, gathered, stream=None):
+        o, m, l = unpack_gathered_partials(gathered, self.plan.world, self.batch, self.heads)
+        p = _native.ptr
+        _native.call("dsr_lse_combine", p(o), p(m), p(l), self.plan.world, p(self.sink_bh), p(self.out), None,
+                     None, p(self.err), 1, self.batch * self.heads, V_DIM, _native.stream_handle(stream))
+        return self.out
+
+    def step(self, inputs, group=None, stream=None):
+        """One full decode step with the two all-gathers; returns out f32[B, H, 512]."""
+        packed = self.select_local(inputs["idx_q"], inputs["idx_w"], inputs["index_pool"],
+                                   inputs["block_table"], stream)
+        self.merge(all_gather(packed, group), stream)
+        partial = self.attend_local(inputs["q"], inputs["kv_pool"], inputs["block_table"], inputs["swa"], stream)
+        return self.combine(all_gather(partial, group), stream)
+
+
+# ------------------------------------------------------------------ inputs
+
+
+def make_shard_inputs(cfg, plan: ShardPlan, device, seed_offset: int = 0):
+    """Seeded synthetic inputs of one rank: its own paged pools for the owned
+    positions of every sequence (blocks laid out by a seeded permutation), the
+    queries (identical on every rank: drawn from the config seed) and, on the
+    tail owner, the SWA rows."""
+    dev = torch.device(device)
+    gq = torch.Generator(device=dev)
+    gq.manual_seed(cfg.seed)
+    B = len(plan.lengths)
+    idx_q = torch.randn((B, cfg.idx_heads, INDEX_DIM), generator=gq, device=dev).to(torch.bfloat16).float()
+    idx_w = torch.randn((B, cfg.idx_heads), generator=gq, device=dev) * cfg.weight_scale
+    q = torch.randn((B, cfg.heads, KV_DIM), generator=gq, device=dev).to(torch.bfloat16).float()
+    sink = torch.randn((cfg.heads,), generator=gq, device=dev)
+    g = torch.Generator(device=dev)
+    g.manual_seed(cfg.seed * 1000003 + 7919 * (plan.rank + 1) + seed_offset)
+    local = plan.local_visible()
+    blocks = [(n + BLOCK - 1) // BLOCK for n in local]
+    total = max(1, sum(blocks))
+    index_pool = torch.randn((total * BLOCK, INDEX_DIM), generator=g, device=dev).to(torch.bfloat16)
+    kv_pool = torch.randn((total * BLOCK, KV_DIM), generator=g, device=dev).to(torch.bfloat16)
+    swa = torch.randn((B, SWA_ROWS, KV_DIM), generator=g, device=dev).to(torch.bfloat16)
+    perm = torch.randperm(total, generator=g, device=dev).to(torch.int32).cpu()
+    table = torch.full((B, plan.local_blocks()), -1, dtype=torch.int32)
+    start = 0
+    for b, nb in enumerate(blocks):
+        table[b, :nb] = perm[start:start + nb]
+        start += nb
+    return dict(idx_q=idx_q.contiguous(), idx_w=idx_w.float().contiguous(), q=q.contiguous(),
+                sink=sink.float().contiguous(), index_pool=index_pool.contiguous(), kv_pool=kv_pool.contiguous(),
+                swa=swa.contiguous(), block_table=table.to(dev).contiguous())
+
+
+# ------------------------------------------------------------------- bench
+
+
+def _timed_steps(fn, steps, stream, dev, group=None) -> float:
+    """ms per step: CUDA events on `stream` around `steps` calls, barrier and
+    synchronize on both sides, max over ranks."""
+    dist.barrier(group)
+    torch.cuda.synchronize()
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        start.record(stream)
+        for i in range(steps):
+            fn(i)
+        end.record(stream)
+    end.synchronize()
+    torch.cuda.synchronize()
+    dist.barrier(group)
+    ms = torch.tensor([start.elapsed_time(end) / steps], device=dev)
+    dist.all_reduce(ms, op=dist.ReduceOp.MAX, group=group)
+    return float(ms.item())
+
+
+# kernels of this library launched per sharded step: indexer, local top-k
+# (histogram + select), merge top-k (histogram + select), MLA partial (tiles +
+# in-shard combine), cross-shard combine
+LAUNCHES_PER_STEP = 8
+
+
+def bench_main(args, metric: str) -> None:
+    """bench.py --gpus N under torch.distributed.run: config 5 sharded over N ranks.
+
+    `value` = µs per decode step of the whole job (4 sequences x 1,048,576
+    positions, fixed as N grows: strong scaling), max over ranks of CUDA-event
+    time around K steps, barrier + synchronize on both sides.  `e2e` repeats the
+    steps with each rank's query inputs copied from pinned host memory and the
+    attention output copied back inside the timed region."""
+    from datetime import timedelta
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", str(args.gpus)))
+    local_rank = int(os.environ.get("LOCAL_RANK", str(rank)))
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    try:
+        cfg = CONFIGS["cfg5"]
+        plan = ShardPlan(world, rank, tuple([cfg.context] * cfg.batch))
+        inputs = make_shard_inputs(cfg, plan, dev)
+        dec = ShardedDecoder(plan, cfg.heads, cfg.idx_heads, cfg.topk, cfg.scale, inputs["sink"], dev)
+        stream = torch.cuda.Stream(device=dev)
+        with torch.cuda.stream(stream):
+            for _ in range(args.warmup):
+                dec.step(inputs, stream=stream)
+        torch.cuda.synchronize()
+        assert int(dec.err.item()) == 0, f"rank {rank}: device status {int(dec.err.item())}"
+        step_ms = _timed_steps(lambda i: dec.step(inputs, stream=stream), args.steps, stream, dev)
+
+        # end to end: query inputs host -> device, output device -> host, every step
+        names = ("idx_q", "idx_w", "q")
+        sizes = [inputs[n].numel() for n in names]
+        h_in = torch.empty(sum(sizes), pin_memory=True)
+        h_in.copy_(torch.cat([inputs[n].reshape(-1).cpu() for n in names]))
+        d_in = torch.empty(sum(sizes), device=dev)
+        staged = dict(inputs)
+        off = 0
+        for n, size in zip(names, sizes):
+            staged[n] = d_in[off:off + size].view(inputs[n].shape)
+            off += size
+        h_out = torch.empty(tuple(dec.out.shape), pin_memory=True)
+
+        def e2e_step(_):
+            d_in.copy_(h_in, non_blocking=True)
+            out = dec.step(staged, stream=stream)
+            h_out.copy_(out, non_blocking=True)
+
+        with torch.cuda.stream(stream):
+            for i in range(3):
+                e2e_step(i)
+        e2e_ms = _timed_steps(e2e_step, args.steps, stream, dev)
+        assert int(dec.err.item()) == 0
+        if rank == 0:
+            from .workloads import algorithmic_bytes
+            total_bytes = algorithmic_bytes(list(plan.lengths), cfg.heads, cfg.topk, cfg.idx_heads)
+            print(json.dumps({
+                "metric": metric, "value": round(step_ms * 1e3, 3), "unit": "us", "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(step_ms, 6),
+                "higher_is_better": False, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+                "data": "synthetic (seeded N(0,1), BF16 pools per rank)",
+                "config": {"workload": cfg.name + f", sharded over {world} GPUs", "batch": cfg.batch,
+                           "context": cfg.context, "topk": cfg.topk, "heads": cfg.heads,
+                           "l2": "inputs larger than L2 on every rank", "parallelism": f"sequence shards x{world}"},
+                "step_hbm": {"bytes": total_bytes,
+                             "achieved_gbs": round(total_bytes / (step_ms * 1e-3) / 1e9, 1)},
+                "e2e": {"value": round(e2e_ms * 1e3, 3), "unit": "us",
+                        "h2d_bytes_per_step": world * h_in.numel() * 4,
+                        "d2h_bytes_per_step": world * h_out.numel() * 4},
+                "gpu_launches": LAUNCHES_PER_STEP * args.steps,
+            }))
+    finally:
+        dist.destroy_process_group()

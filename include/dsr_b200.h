@@ -160,6 +160,24 @@ int dsr_sparse_mla_decode(const float* q, const uint16_t* kv_pool, int64_t pool_
                           float scale, float* out, void* workspace, size_t workspace_bytes,
                           int32_t* err, int64_t batch, int64_t heads, void* stream);
 
+/* Sparse MLA partial over ONE position shard, for sequence-sharded decode.
+ * The pools, block table and swa hold this shard's positions
+ * [id_base, id_base + visible[b]) (id_base a multiple of 64); topk holds the
+ * GLOBAL selection (ids ascending, -1 padded): ids outside the shard are
+ * skipped, not errors.  Outputs the unnormalised merged partial of the shard,
+ * without the sink: out_o f32[batch,heads,512] = sum_i 2^{s_i - m} v_i,
+ * out_m f32[batch,heads] = m (max of s_i, base-2 units: s_i = log2(e) * scale * q.k_i),
+ * out_l f32[batch,heads] = sum_i 2^{s_i - m}; an empty shard gives m = -inf,
+ * l = 0, o = 0.  dsr_lse_combine over the shards' partials with the sink
+ * gives the full attention output.  Scratch: dsr_mla_workspace_bytes(). */
+int dsr_sparse_mla_partial(const float* q, const uint16_t* kv_pool, int64_t pool_blocks,
+                           const int32_t* block_table, int64_t table_stride,
+                           const int32_t* visible, const int32_t* topk, int64_t k,
+                           int64_t id_base, const uint16_t* swa, const int32_t* swa_len,
+                           float scale, float* out_o, float* out_m, float* out_l,
+                           void* workspace, size_t workspace_bytes, int32_t* err,
+                           int64_t batch, int64_t heads, void* stream);
+
 /* Fused, generation-checked append of one KV row (576) and one index-key row
  * (128) per sequence into the paged pools and the SWA ring.  Replaces the two
  * DeviceRowPool.write calls of publish_source plus the SWA ring write
@@ -180,8 +198,9 @@ int dsr_append_kv_index(uint16_t* kv_pool, uint16_t* index_pool, int64_t* genera
                         void* stream);
 
 /* Log-sum-exp combine of attention partials: for each (b,h) the T partials
- * (m[b,t,h], l[b,t,h], o[b,t,h,:dv]) are merged; with a sink the result is
- * normalised, out[b,h,:] = sum_t o_t e^{m_t-M} / (e^{sink_h-M} + sum_t l_t e^{m_t-M}),
+ * (m[b,t,h], l[b,t,h], o[b,t,h,:dv]), m in base-2 units, are merged; with a
+ * sink (natural-log units) the result is normalised,
+ * out[b,h,:] = sum_t o_t 2^{m_t-M} / (2^{log2(e) sink_h - M} + sum_t l_t 2^{m_t-M}),
  * otherwise (out_m,out_l,out) receive the merged unnormalised partial. */
 int dsr_lse_combine(const float* part_o, const float* part_m, const float* part_l,
                     int64_t parts, const float* sink, float* out, float* out_m, float* out_l,
