@@ -373,6 +373,13 @@ def run_single(args):
                "sample": f"{samples} full config-2 decode steps (oracle/ops.py decode_step, numpy float32), "
                          "median"}
 
+    # config 5 through the sharded code on this one GPU: the N=1 point of the
+    # 1/2/4/8 scaling series that `--gpus N` reports for config 5
+    scaling_base = None
+    if not args.no_scaling_base:
+        from deepseekrpc_b200 import sharded
+        scaling_base = sharded.single_gpu_base(max(3, min(K, 200)), 3, dev)
+
     result = {
         "metric": METRIC, "value": round(step_ms * 1e3, 3), "unit": "us", "n_gpus": 1, "steps": K,
         "warmup": W, "ms_per_step": round(step_ms, 6), "higher_is_better": False, "scaling": "strong",
@@ -395,6 +402,7 @@ def run_single(args):
         "gpu_launches": KERNELS_PER_STEP * K,
         "breakdown": dict(breakdown, indexer_us=round(ix_ms * 1e3, 3)),
         "clocks": clocks,
+        "scaling_base": scaling_base,
     }
     print(json.dumps(result))
 
@@ -442,6 +450,8 @@ def main(argv=None):
     parser.add_argument("--soak", type=float, default=1.0, help="seconds of untimed warm-up load")
     parser.add_argument("--cpu-budget", type=float, default=15.0)
     parser.add_argument("--no-cpu-baseline", action="store_true")
+    parser.add_argument("--no-scaling-base", action="store_true",
+                        help="skip the 1-GPU config-5 point of the scaling series")
     args = parser.parse_args(argv)
     if args.warmup < 3:
         parser.error("--warmup must be >= 3")

@@ -98,6 +98,16 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   }
 }
 
+// After an abort: waits (bounded, ignoring the abort flag) for a barrier that
+// TMA copies complete, so that no copy lands in shared memory after the CTA exits.
+__device__ __forceinline__ bool mbar_drain(uint64_t* bar, uint32_t parity) {
+  const uint64_t start = global_ns();
+  for (uint32_t spin = 0;; ++spin) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((spin & 63u) == 63u && global_ns() - start > kWaitNs) return false;
+  }
+}
+
 // ---------------------------------------------------------------------------
 // proxy fences
 // ---------------------------------------------------------------------------
@@ -108,7 +118,7 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
 }
 
 // ---------------------------------------------------------------------------
-// TMA (no multicast anywhere in this library)
+// TMA: every load lands in the issuing CTA's own shared memory
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void tma_prefetch_desc(const void* tmap) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tmap)) : "memory");
@@ -119,6 +129,19 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const void* tmap, uint
       "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
       " [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
       "l"(reinterpret_cast<uint64_t>(tmap)), "r"(smem_u32(bar)), "r"(x), "r"(y)
+      : "memory");
+}
+// Row gather: four rows (y0..y3) of one box-wide column slab starting at column
+// x, from a tensor map whose box is one row high; 4 x box bytes land at dst
+// (128-byte aligned), swizzled like a tiled load to that address.  Rows outside
+// the tensor read the fill value (zero).
+__device__ __forceinline__ void tma_gather4(uint32_t dst, const void* tmap, uint64_t* bar, int32_t x,
+                                            int32_t y0, int32_t y1, int32_t y2, int32_t y3) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6, %7}], [%2];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(smem_u32(bar)), "r"(x), "r"(y0), "r"(y1), "r"(y2),
+      "r"(y3)
       : "memory");
 }
 // 1-D bulk copy global -> shared (addresses 16-byte aligned, bytes % 16 == 0).

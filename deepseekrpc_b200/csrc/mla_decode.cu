@@ -9,7 +9,7 @@
 //
 // mla_decode_kernel: grid (tiles, batch, head groups); one CTA handles one
 // 128-row tile (tile 0 = SWA window, tiles 1.. = consecutive 128 top-k ids).
-//   warps 0..3  gather the 128 rows (cp.async, 128-byte swizzle), convert the
+//   warps 0..3  gather the 128 rows (TMA 4-row gathers, 128-byte swizzle), convert the
 //               FP32 query to BF16, softmax of the tile, partial output store
 //   warp 4      TMEM allocator + tcgen05.mma issuer
 //   S^T[key, h]  = K[key,:576] . Q[h,:576]          (M=128 keys, N=heads)
@@ -54,7 +54,9 @@ struct MlaLayout {
 
 template <int HG>
 __global__ void __launch_bounds__(kMlaThreads, 1)
-    mla_decode_kernel(const float* __restrict__ q, const uint16_t* __restrict__ kv_pool,
+    mla_decode_kernel(const __grid_constant__ CUtensorMap kv_map,
+                      const __grid_constant__ CUtensorMap swa_map,
+                      const float* __restrict__ q, const uint16_t* __restrict__ kv_pool,
                       int64_t pool_blocks, const int32_t* __restrict__ block_table,
                       int64_t table_stride, const int32_t* __restrict__ visible,
                       const int32_t* __restrict__ topk, int k, const uint16_t* __restrict__ swa,
@@ -68,11 +70,11 @@ __global__ void __launch_bounds__(kMlaThreads, 1)
                                              ~uintptr_t(1023));
   const uint32_t sbase = smem_u32(smem);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBarOff);
-  uint64_t* bar_kv = bars + 0;  // rows gathered + Q converted (128 arrivals)
+  uint64_t* bar_kv = bars + 0;  // rows gathered (TMA transaction bytes + 1 arrival)
   uint64_t* bar_s = bars + 1;   // S^T complete (commit)
   uint64_t* bar_p = bars + 2;   // P^T written (128 arrivals)
   uint64_t* bar_o = bars + 3;   // O^T complete (commit)
-  uint64_t* bar_q = bars + 4;   // BF16 query image landed (bulk copy)
+  uint64_t* bar_q = bars + 4;   // BF16 query in place (bulk copy, or converted in-kernel)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kMiscOff);
   volatile int* abort = reinterpret_cast<volatile int*>(smem + L::kMiscOff + 4);
   int* valid = reinterpret_cast<int*>(smem + L::kValidOff);
@@ -84,11 +86,12 @@ __global__ void __launch_bounds__(kMlaThreads, 1)
   const int h0 = hg * HG;
 
   if (threadIdx.x == 0) {
-    mbar_init(bar_kv, 128);
+    tma_prefetch_desc(blockIdx.x == 0 ? &swa_map : &kv_map);
+    mbar_init(bar_kv, 1);
     mbar_init(bar_s, 1);
     mbar_init(bar_p, 128);
     mbar_init(bar_o, 1);
-    mbar_init(bar_q, 1);
+    mbar_init(bar_q, q_img != nullptr ? 1 : 128);  // bulk copy, or 128 converting threads
     *abort = 0;
     fence_barrier_init();
   }
@@ -111,10 +114,20 @@ __global__ void __launch_bounds__(kMlaThreads, 1)
       // ---- query: the preceding indexer kernel wrote the BF16 image; one bulk copy
       pdl_wait();
       if (t == 0) {
+        // image groups hold GI = min(heads, 64) heads: [9 blocks][GI rows][128 B];
+        // this CTA's HG rows start at a multiple of 16 rows (swizzle phase kept)
         constexpr uint32_t kBytes = kMlaBlocks * HG * 128;
-        const uint16_t* src = q_img + (int64_t(b) * (heads / HG) + hg) * (kBytes / 2);
+        const int gi = heads < 64 ? heads : 64;
+        const uint8_t* img = reinterpret_cast<const uint8_t*>(q_img) +
+                             ((int64_t(b) * (heads / gi) + h0 / gi) * kMlaBlocks * gi + h0 % gi) * 128;
         mbar_arrive_expect_tx(bar_q, kBytes);
-        bulk_load(sbase + L::kQOff, src, kBytes, bar_q);
+        if (gi == HG) {
+          bulk_load(sbase + L::kQOff, img, kBytes, bar_q);
+        } else {
+#pragma unroll 1
+          for (int c = 0; c < kMlaBlocks; ++c)
+            bulk_load(sbase + L::kQOff + c * (HG * 128), img + int64_t(c) * gi * 128, HG * 128, bar_q);
+        }
       }
     } else {
       // ---- query: FP32 -> BF16, 128-byte swizzled K-major, 9 column blocks of HG rows
@@ -145,18 +158,21 @@ __global__ void __launch_bounds__(kMlaThreads, 1)
           }
         }
       }
-      if (t == 0) mbar_arrive(bar_q);
+      fence_proxy_async_smem();  // generic-proxy writes become visible to the MMA
+      mbar_arrive(bar_q);
       if (tile != 0) pdl_wait();
     }
-    // ---- resolve the row of key t (top-k ids come from the preceding kernel)
-    const uint16_t* src = nullptr;
+    // ---- resolve the row of key t (top-k ids come from the preceding kernel);
+    // rows past the tensor (the OOB sentinel) are zero-filled by the gather
+    const int32_t oob = tile == 0 ? int32_t(gridDim.y) * DSR_SWA_ROWS : int32_t(pool_blocks * 64);
+    int32_t row = oob;
     if (tile == 0) {
       int len = swa_len[b];
       if (len < 0 || len > DSR_SWA_ROWS) {
         if (t == 0) flag(err, DSR_ERR_ID);
         len = 0;
       }
-      if (t < len) src = swa + (int64_t(b) * DSR_SWA_ROWS + t) * kMlaD;
+      if (t < len) row = b * DSR_SWA_ROWS + t;
     } else {
       const int idx = (tile - 1) * kMlaTile + t;
       if (idx < k) {
@@ -172,31 +188,29 @@ __global__ void __launch_bounds__(kMlaThreads, 1)
           } else {
             const int64_t blk = block_table[int64_t(b) * table_stride + (local >> 6)];
             if (blk < 0 || blk >= pool_blocks) flag(err, DSR_ERR_ID);
-            else src = kv_pool + (blk * 64 + (local & 63)) * kMlaD;
+            else row = int32_t(blk * 64 + (local & 63));
           }
         }
       }
     }
-    valid[t] = src != nullptr;
-    // ---- gather: warp w copies rows 32w..32w+31, one row at a time (coalesced)
-    const uint64_t my_src = reinterpret_cast<uint64_t>(src);
-    for (int i = 0; i < 32; ++i) {
-      const int r = warp * 32 + i;
-      const uint64_t rs = __shfl_sync(0xffffffffu, my_src, i);
-      for (int j = lane; j < 72; j += 32) {
-        const int c = j >> 3, ch = j & 7;
-        const uint32_t dst = sbase + L::kKvOff + c * 16384 + r * 128 + ((ch ^ (r & 7)) << 4);
-        if (rs != 0) {
-          cp_async16(dst, reinterpret_cast<const uint16_t*>(rs) + j * 8);
-        } else {
-          asm volatile("st.shared.v4.u32 [%0], {%1,%1,%1,%1};" ::"r"(dst), "r"(0u) : "memory");
-        }
-      }
+    valid[t] = row != oob;
+    // ---- gather: 4-row TMA gathers of 64-column slabs into the 9 swizzled
+    // column blocks; warp w issues the 8 x 9 gathers of its rows 32w..32w+31
+    if (t == 0) mbar_arrive_expect_tx(bar_kv, uint32_t(kMlaBlocks) * kMlaTile * 128);
+    const CUtensorMap* map = tile == 0 ? &swa_map : &kv_map;
+#pragma unroll
+    for (int i = 0; i < 3; ++i) {
+      const int j = lane + 32 * i;
+      const int jj = j < 8 * kMlaBlocks ? j : 0;
+      const int g = jj / kMlaBlocks, c = jj - g * kMlaBlocks;
+      const int32_t r0 = __shfl_sync(0xffffffffu, row, 4 * g);
+      const int32_t r1 = __shfl_sync(0xffffffffu, row, 4 * g + 1);
+      const int32_t r2 = __shfl_sync(0xffffffffu, row, 4 * g + 2);
+      const int32_t r3 = __shfl_sync(0xffffffffu, row, 4 * g + 3);
+      if (j < 8 * kMlaBlocks)
+        tma_gather4(sbase + L::kKvOff + c * 16384 + (warp * 32 + 4 * g) * 128, map, bar_kv, c * 64,
+                    r0, r1, r2, r3);
     }
-    cp_async_commit();
-    cp_async_wait_all();
-    fence_proxy_async_smem();
-    mbar_arrive(bar_kv);
 
     // ---- scores of key t for the HG heads -> transposed fp32 buffer (query region)
     bool ok = mbar_wait(bar_s, 0, abort, err);
@@ -311,6 +325,11 @@ __global__ void __launch_bounds__(kMlaThreads, 1)
   }
   tc_fence_before();
   __syncthreads();
+  if (*abort && threadIdx.x == 0) {
+    // a wait gave up: let the row gathers and the query copy land before exit
+    mbar_drain(bar_kv, 0);
+    if (q_img != nullptr) mbar_drain(bar_q, 0);
+  }
   if (warp == 4) {
     tc_fence_after();
     tmem_dealloc(tmem_base, L::kTmemCols);
@@ -409,6 +428,12 @@ int launch_mla(const float* q, const uint16_t* kv_pool, int64_t pool_blocks,
     if (e != cudaSuccess) return fail(DSR_ECUDA, "mla smem attribute: %s", cudaGetErrorString(e));
     configured = true;
   }
+  // row-gather tensor maps: one-row boxes of 64 columns over the pool and the SWA rows
+  CUtensorMap kv_map, swa_map;
+  int rc = encode_tmap_bf16_2d(&kv_map, kv_pool, kMlaD, uint64_t(pool_blocks) * 64, 64, 1);
+  if (rc != DSR_OK) return rc;
+  rc = encode_tmap_bf16_2d(&swa_map, swa, kMlaD, uint64_t(batch) * DSR_SWA_ROWS, 64, 1);
+  if (rc != DSR_OK) return rc;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(unsigned(tiles), unsigned(batch), unsigned(heads / HG));
   cfg.blockDim = dim3(kMlaThreads, 1, 1);
@@ -419,7 +444,8 @@ int launch_mla(const float* q, const uint16_t* kv_pool, int64_t pool_blocks,
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, mla_decode_kernel<HG>, q, kv_pool, pool_blocks,
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, mla_decode_kernel<HG>, kv_map, swa_map, q, kv_pool,
+                                           pool_blocks,
                                            block_table, table_stride, visible, topk, int(k), swa,
                                            swa_len, scale * kLog2e, part_o, part_m, part_l, err,
                                            int(heads), q_img, id_base, int(foreign_ok));
@@ -482,7 +508,9 @@ int launch_mla_decode(const float* q, const uint16_t* kv_pool, int64_t pool_bloc
               "sparse_mla_decode: heads %lld not in {16,32,64,128}", (long long)heads);
   DSR_REQUIRE(batch > 0 && batch <= 65535, "sparse_mla_decode: invalid batch");
   DSR_REQUIRE(k >= 0 && k <= 8192, "sparse_mla_decode: k %lld outside [0, 8192]", (long long)k);
-  DSR_REQUIRE(pool_blocks > 0 && table_stride > 0, "sparse_mla_decode: invalid pool/table");
+  DSR_REQUIRE(pool_blocks > 0 && pool_blocks * 64 < (int64_t(1) << 31) && table_stride > 0,
+              "sparse_mla_decode: invalid pool/table (pool rows must fit int32)");
+  DSR_REQUIRE(batch * DSR_SWA_ROWS < (int64_t(1) << 31), "sparse_mla_decode: too many SWA rows");
   DSR_REQUIRE(isfinite(scale) && scale > 0.f, "invalid attention scale");
   DSR_REQUIRE(aligned16(q) && aligned16(kv_pool) && aligned16(swa),
               "sparse_mla_decode: q, kv_pool and swa must be 16-byte aligned");
@@ -494,8 +522,12 @@ int launch_mla_decode(const float* q, const uint16_t* kv_pool, int64_t pool_bloc
   float* part_o = static_cast<float*>(workspace);
   float* part_m = part_o + parts * kMlaDv;
   float* part_l = part_m + parts;
+  // heads per CTA: the largest group (<= 64) whose grid still fits one wave of
+  // CTAs; smaller groups re-gather the same rows (L2 hits) to use more SMs
+  int hg = heads < 64 ? int(heads) : 64;
+  while (hg > 16 && batch * tiles * (heads / (hg / 2)) <= sm_count()) hg /= 2;
   int rc;
-  switch (heads) {
+  switch (hg) {
     case 16:
       rc = launch_mla<16>(q, kv_pool, pool_blocks, block_table, table_stride, visible, topk, k, swa,
                           swa_len, scale, part_o, part_m, part_l, err, batch, heads, tiles, stream,

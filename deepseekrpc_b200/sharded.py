@@ -269,6 +269,44 @@ def _timed_steps(fn, steps, stream, dev, group=None) -> float:
     return float(ms.item())
 
 
+def single_gpu_base(steps: int, warmup: int, device) -> dict:
+    """Config 5 on ONE GPU through the same sharded code (one shard, no
+    collectives): the 1-GPU point of the 1/2/4/8 strong-scaling series."""
+    cfg = CONFIGS["cfg5"]
+    dev = torch.device(device)
+    plan = ShardPlan(1, 0, tuple([cfg.context] * cfg.batch))
+    inputs = make_shard_inputs(cfg, plan, dev)
+    dec = ShardedDecoder(plan, cfg.heads, cfg.idx_heads, cfg.topk, cfg.scale, inputs["sink"], dev)
+    stream = torch.cuda.Stream(device=dev)
+
+    def step(_):
+        packed = dec.select_local(inputs["idx_q"], inputs["idx_w"], inputs["index_pool"], inputs["block_table"],
+                                  stream)
+        dec.merge(packed, stream)
+        partial = dec.attend_local(inputs["q"], inputs["kv_pool"], inputs["block_table"], inputs["swa"], stream)
+        dec.combine(partial, stream)
+
+    with torch.cuda.stream(stream):
+        for i in range(warmup):
+            step(i)
+    torch.cuda.synchronize()
+    assert int(dec.err.item()) == 0, f"device status {int(dec.err.item())}"
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        start.record(stream)
+        for i in range(steps):
+            step(i)
+        end.record(stream)
+    end.synchronize()
+    ms = start.elapsed_time(end) / steps
+    del inputs, dec
+    torch.cuda.empty_cache()
+    return {"workload": cfg.name + ", one shard on 1 GPU", "value": round(ms * 1e3, 3), "unit": "us",
+            "steps": steps, "note": "1-GPU point of the config-5 scaling series (bench.py --gpus N>1 "
+                                    "runs config 5 sharded over N ranks)"}
+
+
 # kernels of this library launched per sharded step: indexer, local top-k
 # (histogram + select), merge top-k (histogram + select), MLA partial (tiles +
 # in-shard combine), cross-shard combine
