@@ -35,6 +35,8 @@ SIGNATURES = {
                                         _P]),
     "dsr_indexer_decode": (c_int, [_P, _P, _P, c_int64, _P, c_int64, _P, _P, c_int64, _P, c_int64,
                                    c_int64, _P]),
+    "dsr_indexer_prefill": (c_int, [_P, _P, _P, c_int64, _P, c_int64, _P, _P, c_int64, _P, c_int64,
+                                    c_int64, _P]),
     "dsr_mla_workspace_bytes": (c_size_t, [c_int64, c_int64, c_int64]),
     "dsr_sparse_mla_decode": (c_int, [_P, _P, c_int64, _P, c_int64, _P, _P, c_int64, _P, _P, _P,
                                       c_float, _P, _P, c_size_t, _P, c_int64, c_int64, _P]),

@@ -49,6 +49,10 @@ int launch_indexer_decode(const float* q, const float* weights, const uint16_t* 
                           int32_t* err, int64_t batch, int64_t heads, cudaStream_t stream,
                           bool pdl, const float* mla_q = nullptr, uint16_t* mla_img = nullptr,
                           int64_t mla_heads = 0, uint32_t* hist = nullptr);
+int launch_indexer_prefill(const float* q, const float* weights, const uint16_t* index_pool,
+                           int64_t pool_blocks, const int32_t* block_table, int64_t table_stride,
+                           const int32_t* visible, float* scores, int64_t score_stride, int32_t* err,
+                           int64_t queries, int64_t heads, cudaStream_t stream);
 // Bytes of the BF16 MLA query image the indexer can emit for the MLA kernel.
 inline size_t mla_query_image_bytes(int64_t batch, int64_t heads) {
   return size_t(batch) * size_t(heads) * DSR_KV_DIM * 2;

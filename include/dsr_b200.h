@@ -144,6 +144,22 @@ int dsr_indexer_decode(const float* q, const float* weights, const uint16_t* ind
                        const int32_t* visible, float* scores, int64_t score_stride,
                        int32_t* err, int64_t batch, int64_t heads, void* stream);
 
+/* Lightning-indexer scores of a chunk of prefill queries against ONE sequence,
+ * as a tcgen05 GEMM: each 128-key tile is contracted against a group of 128/heads
+ * queries at once.  q f32[queries,heads,128]; weights f32[queries,heads];
+ * index_pool and paging as above, block_table i32[table_len] the sequence's
+ * blocks; visible i32[queries] keys query t sees (causal: its position + 1,
+ * <= score_stride and <= table_len*64, else err 1); heads in {32,64}.
+ * scores f32[queries,score_stride]: scores[t,p] for p < visible[t].  Queries
+ * whose FP32 values are not BF16-exact are contracted as bf16(q) plus the
+ * bf16 residual.  Replaces TiledIndexer's per-row tiles for prefill rows
+ * (index_selection.py:79-107); the per-query top-k runs on the scores with
+ * dsr_topk_select. */
+int dsr_indexer_prefill(const float* q, const float* weights, const uint16_t* index_pool,
+                        int64_t pool_blocks, const int32_t* block_table, int64_t table_len,
+                        const int32_t* visible, float* scores, int64_t score_stride, int32_t* err,
+                        int64_t queries, int64_t heads, void* stream);
+
 /* Sparse MLA decode attention over the SWA ring plus top-k selected pool rows.
  * q f32[batch,heads,576]; kv_pool bf16[pool_blocks*64,576]; block_table as above;
  * topk i32[batch,k] logical positions (ascending, -1 padded), each < visible[b];
