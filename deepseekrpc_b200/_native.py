@@ -42,6 +42,12 @@ SIGNATURES = {
                                       c_float, _P, _P, c_size_t, _P, c_int64, c_int64, _P]),
     "dsr_sparse_mla_partial": (c_int, [_P, _P, c_int64, _P, c_int64, _P, _P, c_int64, c_int64, _P, _P,
                                        c_float, _P, _P, _P, _P, c_size_t, _P, c_int64, c_int64, _P]),
+    "dsr_indexer_topk_workspace_bytes": (c_size_t, [c_int64, c_int64]),
+    "dsr_indexer_topk_decode": (c_int, [_P, _P, c_int64, _P, c_int64, _P, c_int64, _P, c_int64, c_int64,
+                                        c_int64, _P, _P, _P, _P, c_size_t, _P, c_int64, _P]),
+    "dsr_topk_merge_workspace_bytes": (c_size_t, [c_int64, c_int64, c_int64]),
+    "dsr_topk_merge_lists": (c_int, [_P, c_int64, c_int64, c_int64, _P, _P, c_size_t, _P, _P]),
+    "dsr_lse_combine_packed": (c_int, [_P, c_int64, _P, _P, _P, c_int64, c_int64, _P]),
     "dsr_append_kv_index": (c_int, [_P, _P, _P, c_int64, _P, c_int64, c_int64, _P, _P, _P, _P, _P,
                                     _P, _P, c_int64, _P]),
     "dsr_lse_combine": (c_int, [_P, _P, _P, c_int64, _P, _P, _P, _P, _P, c_int64, c_int64, c_int64,

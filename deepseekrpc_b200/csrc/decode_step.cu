@@ -64,3 +64,44 @@ extern "C" int dsr_decode_step(const float* idx_q, const float* idx_w, int64_t i
                            swa, swa_len, sink, scale, out, mla_ws, mla_bytes, err, batch, heads, s,
                            true, q_img);
 }
+
+// Indexer scores -> exact top-k with the scores of the chosen entries, the
+// indexer's histogram handed to the top-k kernel and the two launches chained by
+// programmatic dependent launch (the per-shard selection of sequence-sharded
+// decode, and the dense TiledIndexer.select of index_selection.py:79-124).
+extern "C" size_t dsr_indexer_topk_workspace_bytes(int64_t batch, int64_t max_visible) {
+  const int64_t stride = round_up(max_visible > 0 ? max_visible : 1, 64);
+  return dsr::topk_workspace_bytes(batch, stride) + size_t(batch) * size_t(stride) * 4 + 256;
+}
+
+extern "C" int dsr_indexer_topk_decode(const float* idx_q, const float* idx_w, int64_t idx_heads,
+                                       const uint16_t* index_pool, int64_t pool_blocks,
+                                       const int32_t* block_table, int64_t table_stride,
+                                       const int32_t* visible, int64_t max_visible, int64_t k,
+                                       int64_t id_base, int32_t* out_ids, float* out_scores,
+                                       float* scores_out, void* workspace, size_t workspace_bytes,
+                                       int32_t* err, int64_t batch, void* stream) {
+  using namespace dsr;
+  clear_error();
+  DSR_REQUIRE(workspace != nullptr, "indexer_topk: workspace is required");
+  DSR_REQUIRE(max_visible > 0 && max_visible <= table_stride * 64,
+              "indexer_topk: max_visible %lld outside [1, table capacity %lld]",
+              (long long)max_visible, (long long)(table_stride * 64));
+  const size_t need = dsr_indexer_topk_workspace_bytes(batch, max_visible);
+  DSR_REQUIRE(workspace_bytes >= need, "indexer_topk: workspace %zu < %zu bytes", workspace_bytes,
+              need);
+  DSR_REQUIRE((reinterpret_cast<uintptr_t>(workspace) & 255u) == 0,
+              "indexer_topk: workspace must be 256-byte aligned");
+  const int64_t stride = round_up(max_visible, 64);
+  uint8_t* topk_ws = static_cast<uint8_t*>(workspace);
+  const size_t topk_bytes = topk_workspace_bytes(batch, stride);
+  float* scores =
+      scores_out != nullptr ? scores_out : reinterpret_cast<float*>(topk_ws + topk_bytes);
+  const cudaStream_t s = as_stream(stream);
+  int rc = launch_indexer_decode(idx_q, idx_w, index_pool, pool_blocks, block_table, table_stride,
+                                 visible, scores, stride, err, batch, idx_heads, s, false, nullptr,
+                                 nullptr, 0, reinterpret_cast<uint32_t*>(topk_ws));
+  if (rc != DSR_OK) return rc;
+  return launch_topk(scores, nullptr, visible, out_ids, out_scores, err, batch, stride, k, id_base,
+                     topk_ws, topk_bytes, s, true, /*hist_ready=*/true);
+}

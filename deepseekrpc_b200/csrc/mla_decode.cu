@@ -337,6 +337,60 @@ __global__ void __launch_bounds__(kMlaThreads, 1)
 }
 
 // ---------------------------------------------------------------------------
+// Combine of per-shard partials in their exchange layout: packed f32
+// [world][o (B*H*512) | m (B*H) | l (B*H)], one (b, h) per CTA; the sink enters
+// once.  out[b,h,:] = sum_w o_w 2^{m_w-M} / (2^{log2(e) sink_h - M} + sum_w l_w 2^{m_w-M}).
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(128) lse_combine_packed_kernel(
+    const float* __restrict__ packed, int world, const float* __restrict__ sink,
+    float* __restrict__ out, int32_t* err, int heads) {
+  __shared__ float wgt[64];
+  __shared__ float stat[2];
+  const int b = blockIdx.x, h = blockIdx.y;
+  const int64_t bh = int64_t(gridDim.x) * heads, pair = int64_t(b) * heads + h;
+  const int64_t span = bh * (kMlaDv + 2);  // floats per shard
+  pdl_wait();
+  if (threadIdx.x < 32) {
+    const int lane = threadIdx.x;
+    float sk = sink[h];
+    if (!isfinite(sk)) {
+      if (lane == 0) flag(err, DSR_ERR_NONFINITE);
+      sk = 0.f;
+    }
+    sk *= kLog2e;
+    float M = sk;
+    for (int w = lane; w < world; w += 32) M = fmaxf(M, packed[w * span + bh * kMlaDv + pair]);
+#pragma unroll
+    for (int o = 16; o; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+    float lsum = 0.f;
+    for (int w = lane; w < world; w += 32) {
+      const float e = exp2f(packed[w * span + bh * kMlaDv + pair] - M);
+      wgt[w] = e;
+      lsum += packed[w * span + bh * (kMlaDv + 1) + pair] * e;
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) lsum += __shfl_xor_sync(0xffffffffu, lsum, o);
+    if (lane == 0) stat[0] = 1.f / (lsum + exp2f(sk - M));
+  }
+  __syncthreads();
+  const float inv = stat[0];
+  for (int d = threadIdx.x * 4; d < kMlaDv; d += blockDim.x * 4) {
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int w = 0; w < world; ++w) {
+      const float4 v = __ldg(reinterpret_cast<const float4*>(packed + w * span + pair * kMlaDv + d));
+      const float e = wgt[w];
+      acc.x = fmaf(v.x, e, acc.x);
+      acc.y = fmaf(v.y, e, acc.y);
+      acc.z = fmaf(v.z, e, acc.z);
+      acc.w = fmaf(v.w, e, acc.w);
+    }
+    const float4 o = make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
+    if (!isfinite(o.x) || !isfinite(o.y) || !isfinite(o.z) || !isfinite(o.w)) flag(err, DSR_ERR_NONFINITE);
+    *reinterpret_cast<float4*>(out + pair * kMlaDv + d) = o;
+  }
+}
+
+// ---------------------------------------------------------------------------
 // LSE combine.  m in log2 units; with a sink (natural-log units, converted
 // here) the output is normalised, otherwise the merged partial is returned.
 // ---------------------------------------------------------------------------
@@ -580,6 +634,22 @@ extern "C" int dsr_sparse_mla_partial(const float* q, const uint16_t* kv_pool, i
                                 k, swa, swa_len, nullptr, scale, out_o, workspace, workspace_bytes,
                                 err, batch, heads, dsr::as_stream(stream), false, nullptr, id_base,
                                 true, out_m, out_l);
+}
+
+extern "C" int dsr_lse_combine_packed(const float* packed, int64_t world, const float* sink,
+                                      float* out, int32_t* err, int64_t batch, int64_t heads,
+                                      void* stream) {
+  dsr::clear_error();
+  DSR_REQUIRE(packed && sink && out && err, "lse_combine_packed: null pointer");
+  DSR_REQUIRE(world > 0 && world <= 64 && batch > 0 && batch <= 65535 && heads > 0 && heads <= 1024 &&
+                  (batch * heads) % 2 == 0,
+              "lse_combine_packed: invalid shape (batch * heads must be even)");
+  DSR_REQUIRE(dsr::aligned16(packed) && dsr::aligned16(out),
+              "lse_combine_packed: packed and out must be 16-byte aligned");
+  dsr::lse_combine_packed_kernel<<<dim3(unsigned(batch), unsigned(heads), 1), 128, 0,
+                                   dsr::as_stream(stream)>>>(packed, int(world), sink, out, err,
+                                                             int(heads));
+  return dsr::launch_status("lse_combine_packed launch");
 }
 
 extern "C" int dsr_lse_combine(const float* part_o, const float* part_m, const float* part_l,

@@ -611,7 +611,79 @@ int launch_topk(const float* scores, const int32_t* ids, const int32_t* lengths,
   return DSR_OK;
 }
 
+// ---------------------------------------------------------------------------
+// Merge of per-shard ranked lists: lists i32[world][2][rows][k] (per shard: the
+// scores' bit patterns, then their global ids, -1 padded; a shard's ids increase
+// and shard w's ids lie below shard w+1's) -> rows of world*k (score, id) pairs
+// in id order, then the exact top-k of each row.
+// ---------------------------------------------------------------------------
+namespace {
+__global__ void __launch_bounds__(256) merge_gather_kernel(const int32_t* __restrict__ lists,
+                                                           int world, int rows, int k,
+                                                           float* __restrict__ scores,
+                                                           int32_t* __restrict__ ids,
+                                                           int32_t* __restrict__ lengths) {
+  const int64_t total = int64_t(world) * rows * k;
+  for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += int64_t(gridDim.x) * blockDim.x) {
+    const int j = int(i % k);
+    const int64_t wr = i / k;
+    const int r = int(wr % rows), w = int(wr / rows);
+    const int32_t* src = lists + (int64_t(w) * 2 * rows + r) * k + j;
+    const int64_t dst = int64_t(r) * world * k + int64_t(w) * k + j;
+    scores[dst] = __int_as_float(src[0]);
+    ids[dst] = src[int64_t(rows) * k];
+  }
+  if (blockIdx.x == 0)
+    for (int r = threadIdx.x; r < rows; r += blockDim.x) lengths[r] = world * k;
+  pdl_launch_dependents();
+}
+}  // namespace
+
+size_t topk_merge_workspace_bytes(int64_t rows, int64_t world, int64_t k) {
+  const int64_t n = world * k;
+  return topk_workspace_bytes(rows, n) + ((size_t(rows) * n * 8 + size_t(rows) * 4 + 255) / 256) * 256;
+}
+
+int launch_topk_merge(const int32_t* lists, int64_t world, int64_t rows, int64_t k,
+                      int32_t* out_ids, void* workspace, size_t workspace_bytes, int32_t* err,
+                      cudaStream_t stream) {
+  DSR_REQUIRE(lists && out_ids && err && workspace, "topk_merge: null pointer");
+  DSR_REQUIRE(world > 0 && world <= 64 && rows > 0 && rows <= 65535 && k > 0 && k <= 8192,
+              "topk_merge: invalid shape");
+  DSR_REQUIRE(workspace_bytes >= topk_merge_workspace_bytes(rows, world, k),
+              "topk_merge: workspace too small");
+  DSR_REQUIRE((reinterpret_cast<uintptr_t>(workspace) & 255u) == 0,
+              "topk_merge: workspace must be 256-byte aligned");
+  const int64_t n = world * k;
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  const size_t tk = topk_workspace_bytes(rows, n);
+  float* scores = reinterpret_cast<float*>(ws + tk);
+  int32_t* ids = reinterpret_cast<int32_t*>(scores + rows * n);
+  int32_t* lengths = ids + rows * n;
+  const int64_t total = rows * n;
+  const int blocks = int((total + 255) / 256 < 4 * sm_count() ? (total + 255) / 256 : 4 * sm_count());
+  merge_gather_kernel<<<blocks, 256, 0, stream>>>(lists, int(world), int(rows), int(k), scores, ids,
+                                                  lengths);
+  const int rc = launch_status("topk_merge gather launch");
+  if (rc != DSR_OK) return rc;
+  return launch_topk(scores, ids, lengths, out_ids, nullptr, err, rows, n, k, 0, ws, tk, stream,
+                     true, false);
+}
+
 }  // namespace dsr
+
+extern "C" size_t dsr_topk_merge_workspace_bytes(int64_t rows, int64_t world, int64_t k) {
+  return dsr::topk_merge_workspace_bytes(rows, world, k);
+}
+
+extern "C" int dsr_topk_merge_lists(const int32_t* lists, int64_t world, int64_t rows, int64_t k,
+                                    int32_t* out_ids, void* workspace, size_t workspace_bytes,
+                                    int32_t* err, void* stream) {
+  dsr::clear_error();
+  return dsr::launch_topk_merge(lists, world, rows, k, out_ids, workspace, workspace_bytes, err,
+                                dsr::as_stream(stream));
+}
 
 extern "C" size_t dsr_topk_workspace_bytes(int64_t rows, int64_t row_stride) {
   return dsr::topk_workspace_bytes(rows, row_stride);

@@ -89,18 +89,18 @@ def local_block_table(full_table: torch.Tensor, plan: ShardPlan) -> torch.Tensor
 
 
 # ------------------------------------------------------------ exchange layouts
+#
+# Send buffers are written in place by the kernels and all-gathered rank-major:
+#   top-k lists: i32 [2][B][k] per rank (the scores' bit patterns, then the
+#                global ids, -1 padded) -> gathered [G*2][B][k], read by
+#                dsr_topk_merge_lists;
+#   partials:    f32 [o (B*H*512) | m (B*H) | l (B*H)] per rank -> gathered
+#                [G][...], read by dsr_lse_combine_packed.
+# The two decoders below restate those layouts on the host (tests, inspection).
 
 
-def pack_topk(scores: torch.Tensor, ids: torch.Tensor) -> torch.Tensor:
-    """[2, B, k] int32: the local scores (bit pattern) and their global ids."""
-    return torch.stack((scores.contiguous().view(torch.int32), ids.contiguous()))
-
-
-def unpack_gathered_topk(gathered: torch.Tensor, world: int):
-    """[G*2, B, k] (rank-major all-gather of pack_topk) -> scores f32[B, G*k], ids i32[B, G*k].
-
-    Ranks own increasing position ranges and each list is ascending, so along a
-    row the ids increase: the form the top-k merge (explicit-id mode) requires."""
+def gathered_lists(gathered: torch.Tensor, world: int):
+    """Gathered top-k lists -> scores f32[B, G*k], ids i32[B, G*k], ids increasing along a row."""
     g = gathered.view(world, 2, gathered.shape[-2], gathered.shape[-1])
     b, k = g.shape[2], g.shape[3]
     scores = g[:, 0].permute(1, 0, 2).reshape(b, world * k).contiguous().view(torch.float32)
@@ -108,26 +108,16 @@ def unpack_gathered_topk(gathered: torch.Tensor, world: int):
     return scores, ids
 
 
-def pack_partials(o: torch.Tensor, m: torch.Tensor, l: torch.Tensor) -> torch.Tensor:
-    """f32 [B*H*(512+2)]: o, then m, then l of this rank's partial."""
-    return torch.cat((o.reshape(-1), m.reshape(-1), l.reshape(-1)))
-
-
-def unpack_gathered_partials(gathered: torch.Tensor, world: int, batch: int, heads: int):
-    """Rank-major gathered partials -> o f32[G, B*H, 512], m f32[G, B*H], l f32[G, B*H].
-
-    Laid out so that dsr_lse_combine with batch=1 and heads=B*H merges the G
-    partials of every (b, h) (partial t of pair j at t*B*H + j)."""
+def gathered_partials(gathered: torch.Tensor, world: int, batch: int, heads: int):
+    """Gathered partials -> o f32[G, B*H, 512], m f32[G, B*H], l f32[G, B*H] (base-2 m)."""
     bh = batch * heads
     g = gathered.view(world, bh * (V_DIM + 2))
-    o = g[:, :bh * V_DIM].reshape(world, bh, V_DIM).contiguous()
-    m = g[:, bh * V_DIM:bh * (V_DIM + 1)].contiguous()
-    l = g[:, bh * (V_DIM + 1):].contiguous()
-    return o, m, l
+    return (g[:, :bh * V_DIM].reshape(world, bh, V_DIM), g[:, bh * V_DIM:bh * (V_DIM + 1)],
+            g[:, bh * (V_DIM + 1):])
 
 
 def all_gather(tensor: torch.Tensor, group=None) -> torch.Tensor:
-    """Rank-major concatenation along a new leading dimension (flattened into dim 0)."""
+    """Rank-major concatenation along dim 0."""
     world = dist.get_world_size(group)
     out = torch.empty((world * tensor.shape[0],) + tuple(tensor.shape[1:]), dtype=tensor.dtype,
                       device=tensor.device)
@@ -151,62 +141,60 @@ class ShardedDecoder:
         dev = torch.device(device)
         self.visible = torch.tensor(plan.local_visible(), dtype=torch.int32, device=dev)
         self.swa_len = torch.tensor(plan.local_swa_len(), dtype=torch.int32, device=dev)
-        self.merge_len = torch.full((B,), plan.world * topk, dtype=torch.int32, device=dev)
-        self.scores = torch.empty((B, self.span), device=dev)
-        self.local_ids = torch.empty((B, topk), dtype=torch.int32, device=dev)
-        self.local_scores = torch.empty((B, topk), device=dev)
+        self.send_lists = torch.empty((2, B, topk), dtype=torch.int32, device=dev)
+        self.ix_bytes = self.lib.dsr_indexer_topk_workspace_bytes(B, self.span)
+        self.ix_ws = torch.zeros(self.ix_bytes, dtype=torch.uint8, device=dev)
+        self.merge_bytes = self.lib.dsr_topk_merge_workspace_bytes(B, plan.world, topk)
+        self.merge_ws = torch.zeros(self.merge_bytes, dtype=torch.uint8, device=dev)
         self.ids = torch.empty((B, topk), dtype=torch.int32, device=dev)
-        self.topk_bytes = self.lib.dsr_topk_workspace_bytes(B, max(self.span, plan.world * topk))
-        self.topk_ws = torch.zeros(self.topk_bytes, dtype=torch.uint8, device=dev)
         self.mla_bytes = self.lib.dsr_mla_workspace_bytes(B, heads, topk)
         self.mla_ws = torch.zeros(self.mla_bytes, dtype=torch.uint8, device=dev)
-        self.o = torch.empty((B, heads, V_DIM), device=dev)
-        self.m = torch.empty((B, heads), device=dev)
-        self.l = torch.empty((B, heads), device=dev)
+        bh = B * heads
+        self.send_partial = torch.empty(bh * (V_DIM + 2), device=dev)
+        self.o = self.send_partial[:bh * V_DIM]
+        self.m = self.send_partial[bh * V_DIM:bh * (V_DIM + 1)]
+        self.l = self.send_partial[bh * (V_DIM + 1):]
         self.out = torch.empty((B, heads, V_DIM), device=dev)
-        self.sink_bh = sink.float().repeat(B).contiguous().to(dev)  # sink of pair (b, h) at b*H + h
+        self.sink = sink.float().contiguous().to(dev)
         self.err = torch.zeros(1, dtype=torch.int32, device=dev)
 
-    # the three phases, so a single-GPU emulation can run them shard by shard
+    # the phases, so a single-GPU emulation can run them shard by shard
     def select_local(self, idx_q, idx_w, index_pool, block_table, stream=None):
-        s = _native.stream_handle(stream)
+        """Local indexer + exact top-k (global ids and scores) into the send buffer."""
         p = _native.ptr
-        _native.call("dsr_indexer_decode", p(idx_q), p(idx_w), p(index_pool), index_pool.shape[0] // BLOCK,
-                     p(block_table), block_table.shape[1], p(self.visible), p(self.scores), self.span,
-                     p(self.err), self.batch, self.idx_heads, s)
-        _native.call("dsr_topk_select", p(self.scores), None, p(self.visible), p(self.local_ids),
-                     p(self.local_scores), p(self.err), self.batch, self.span, self.k, self.plan.id_base,
-                     p(self.topk_ws), self.topk_bytes, s)
-        return pack_topk(self.local_scores, self.local_ids)
+        _native.call("dsr_indexer_topk_decode", p(idx_q), p(idx_w), self.idx_heads, p(index_pool),
+                     index_pool.shape[0] // BLOCK, p(block_table), block_table.shape[1], p(self.visible),
+                     self.span, self.k, self.plan.id_base, p(self.send_lists[1]), p(self.send_lists[0]), None,
+                     p(self.ix_ws), self.ix_bytes, p(self.err), self.batch, _native.stream_handle(stream))
+        return self.send_lists
 
     def merge(self, gathered, stream=None):
-        scores_all, ids_all = unpack_gathered_topk(gathered, self.plan.world)
+        """Exact global top-k from the gathered lists (identical on every rank)."""
         p = _native.ptr
-        _native.call("dsr_topk_select", p(scores_all), p(ids_all), p(self.merge_len), p(self.ids), None,
-                     p(self.err), self.batch, scores_all.shape[1], self.k, 0, p(self.topk_ws),
-                     self.topk_bytes, _native.stream_handle(stream))
+        _native.call("dsr_topk_merge_lists", p(gathered), self.plan.world, self.batch, self.k, p(self.ids),
+                     p(self.merge_ws), self.merge_bytes, p(self.err), _native.stream_handle(stream))
         return self.ids
 
     def attend_local(self, q, kv_pool, block_table, swa, stream=None):
+        """This rank's unnormalised partial (o, m, l) into the send buffer."""
         p = _native.ptr
         _native.call("dsr_sparse_mla_partial", p(q), p(kv_pool), kv_pool.shape[0] // BLOCK, p(block_table),
                      block_table.shape[1], p(self.visible), p(self.ids), self.k, self.plan.id_base, p(swa),
                      p(self.swa_len), float(self.scale), p(self.o), p(self.m), p(self.l), p(self.mla_ws),
                      self.mla_bytes, p(self.err), self.batch, self.heads, _native.stream_handle(stream))
-        return pack_partials(self.o, self.m, self.l)
+        return self.send_partial
 
     def combine(self, gathered, stream=None):
-        o, m, l = unpack_gathered_partials(gathered, self.plan.world, self.batch, self.heads)
         p = _native.ptr
-        _native.call("dsr_lse_combine", p(o), p(m), p(l), self.plan.world, p(self.sink_bh), p(self.out), None,
-                     None, p(self.err), 1, self.batch * self.heads, V_DIM, _native.stream_handle(stream))
+        _native.call("dsr_lse_combine_packed", p(gathered), self.plan.world, p(self.sink), p(self.out),
+                     p(self.err), self.batch, self.heads, _native.stream_handle(stream))
         return self.out
 
     def step(self, inputs, group=None, stream=None):
         """One full decode step with the two all-gathers; returns out f32[B, H, 512]."""
-        packed = self.select_local(inputs["idx_q"], inputs["idx_w"], inputs["index_pool"],
-                                   inputs["block_table"], stream)
-        self.merge(all_gather(packed, group), stream)
+        lists = self.select_local(inputs["idx_q"], inputs["idx_w"], inputs["index_pool"],
+                                  inputs["block_table"], stream)
+        self.merge(all_gather(lists, group), stream)
         partial = self.attend_local(inputs["q"], inputs["kv_pool"], inputs["block_table"], inputs["swa"], stream)
         return self.combine(all_gather(partial, group), stream)
 
@@ -247,6 +235,22 @@ def make_shard_inputs(cfg, plan: ShardPlan, device, seed_offset: int = 0):
 
 
 # ------------------------------------------------------------------- bench
+
+
+def _capture(fn, stream):
+    """fn() captured as a CUDA graph on `stream` (all ranks together), or None."""
+    torch.cuda.synchronize()
+    dist.barrier()
+    graph = torch.cuda.CUDAGraph()
+    try:
+        with torch.cuda.graph(graph, stream=stream):
+            fn()
+    except RuntimeError:
+        graph = None
+    ok = torch.tensor([1 if graph is not None else 0], device=torch.cuda.current_device())
+    dist.all_reduce(ok, op=dist.ReduceOp.MIN)  # the same choice on every rank
+    torch.cuda.synchronize()
+    return graph if int(ok.item()) == 1 else None
 
 
 def _timed_steps(fn, steps, stream, dev, group=None) -> float:
@@ -291,12 +295,17 @@ def single_gpu_base(steps: int, warmup: int, device) -> dict:
             step(i)
     torch.cuda.synchronize()
     assert int(dec.err.item()) == 0, f"device status {int(dec.err.item())}"
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        step(0)
+    torch.cuda.synchronize()
     start = torch.cuda.Event(enable_timing=True)
     end = torch.cuda.Event(enable_timing=True)
     with torch.cuda.stream(stream):
+        graph.replay()
         start.record(stream)
         for i in range(steps):
-            step(i)
+            graph.replay()
         end.record(stream)
     end.synchronize()
     ms = start.elapsed_time(end) / steps
@@ -307,9 +316,9 @@ def single_gpu_base(steps: int, warmup: int, device) -> dict:
                                     "runs config 5 sharded over N ranks)"}
 
 
-# kernels of this library launched per sharded step: indexer, local top-k
-# (histogram + select), merge top-k (histogram + select), MLA partial (tiles +
-# in-shard combine), cross-shard combine
+# kernels of this library launched per sharded step: indexer, local top-k,
+# list gather + histogram + top-k of the merge, MLA partial (tiles + in-shard
+# combine), cross-shard combine
 LAUNCHES_PER_STEP = 8
 
 
@@ -339,7 +348,12 @@ def bench_main(args, metric: str) -> None:
                 dec.step(inputs, stream=stream)
         torch.cuda.synchronize()
         assert int(dec.err.item()) == 0, f"rank {rank}: device status {int(dec.err.item())}"
-        step_ms = _timed_steps(lambda i: dec.step(inputs, stream=stream), args.steps, stream, dev)
+        # one step (kernels and both NCCL all-gathers) as a CUDA graph; every rank
+        # captures, so the collectives line up; eager steps if capture is refused
+        graph = _capture(lambda: dec.step(inputs, stream=stream), stream)
+        run = (lambda i: graph.replay()) if graph is not None else (lambda i: dec.step(inputs, stream=stream))
+        step_ms = _timed_steps(run, args.steps, stream, dev)
+        run_graphed = graph is not None
 
         # end to end: query inputs host -> device, output device -> host, every step
         names = ("idx_q", "idx_w", "q")
@@ -362,8 +376,12 @@ def bench_main(args, metric: str) -> None:
         with torch.cuda.stream(stream):
             for i in range(3):
                 e2e_step(i)
-        e2e_ms = _timed_steps(e2e_step, args.steps, stream, dev)
+        e2e_graph = _capture(lambda: e2e_step(0), stream)
+        e2e_run = (lambda i: e2e_graph.replay()) if e2e_graph is not None else e2e_step
+        e2e_ms = _timed_steps(e2e_run, args.steps, stream, dev)
+        torch.cuda.synchronize()
         assert int(dec.err.item()) == 0
+        graph = e2e_graph = None  # graphs holding NCCL work go before the process group
         if rank == 0:
             from .workloads import algorithmic_bytes
             total_bytes = algorithmic_bytes(list(plan.lengths), cfg.heads, cfg.topk, cfg.idx_heads)
@@ -381,6 +399,7 @@ def bench_main(args, metric: str) -> None:
                         "h2d_bytes_per_step": world * h_in.numel() * 4,
                         "d2h_bytes_per_step": world * h_out.numel() * 4},
                 "gpu_launches": LAUNCHES_PER_STEP * args.steps,
+                "mode": "cuda graph per step" if run_graphed else "eager launches",
             }))
     finally:
         dist.destroy_process_group()

@@ -194,6 +194,46 @@ int dsr_sparse_mla_partial(const float* q, const uint16_t* kv_pool, int64_t pool
                            void* workspace, size_t workspace_bytes, int32_t* err,
                            int64_t batch, int64_t heads, void* stream);
 
+/* ===================== sequence-sharded decode (multi-GPU) ===================
+ * Rank r of G holds positions [id_base, id_base + visible[b]) of every sequence
+ * in its own pools.  Per step: dsr_indexer_topk_decode (local scores and top-k
+ * with global ids and their scores) -> all-gather of the packed lists ->
+ * dsr_topk_merge_lists (exact global top-k, same on every rank) ->
+ * dsr_sparse_mla_partial (this rank's partial over its selected rows) ->
+ * all-gather of the packed partials -> dsr_lse_combine_packed.  No reference
+ * counterpart (the reference decodes on one GPU). */
+
+/* Indexer scores -> exact top-k, chained on the device: out_ids i32[batch,k]
+ * (id_base + position, ascending, -1 padded), out_scores (nullable)
+ * f32[batch,k] their scores (-inf padding), scores_out (nullable)
+ * f32[batch, round_up(max_visible,64)].  Arguments otherwise as
+ * dsr_indexer_decode / dsr_topk_select.  Scratch as dsr_decode_step's. */
+size_t dsr_indexer_topk_workspace_bytes(int64_t batch, int64_t max_visible);
+int dsr_indexer_topk_decode(const float* idx_q, const float* idx_w, int64_t idx_heads,
+                            const uint16_t* index_pool, int64_t pool_blocks,
+                            const int32_t* block_table, int64_t table_stride,
+                            const int32_t* visible, int64_t max_visible, int64_t k,
+                            int64_t id_base, int32_t* out_ids, float* out_scores,
+                            float* scores_out, void* workspace, size_t workspace_bytes,
+                            int32_t* err, int64_t batch, void* stream);
+
+/* Exact top-k of the union of per-shard ranked lists.  lists i32[world][2][rows][k]:
+ * per shard the scores' bit patterns, then their ids (-1 padded); within a shard
+ * ids increase, and every id of shard w is below every id of shard w+1.
+ * out_ids i32[rows,k] ascending, -1 padded.  Scratch:
+ * dsr_topk_merge_workspace_bytes(), 256-byte aligned, zero before first use. */
+size_t dsr_topk_merge_workspace_bytes(int64_t rows, int64_t world, int64_t k);
+int dsr_topk_merge_lists(const int32_t* lists, int64_t world, int64_t rows, int64_t k,
+                         int32_t* out_ids, void* workspace, size_t workspace_bytes, int32_t* err,
+                         void* stream);
+
+/* Combine of the shards' partials in their exchange layout: packed
+ * f32[world][o (batch*heads*512) | m (batch*heads) | l (batch*heads)] as written
+ * by dsr_sparse_mla_partial into one buffer per rank; out f32[batch,heads,512]
+ * with the sink counted once.  batch*heads must be even. */
+int dsr_lse_combine_packed(const float* packed, int64_t world, const float* sink, float* out,
+                           int32_t* err, int64_t batch, int64_t heads, void* stream);
+
 /* Fused, generation-checked append of one KV row (576) and one index-key row
  * (128) per sequence into the paged pools and the SWA ring.  Replaces the two
  * DeviceRowPool.write calls of publish_source plus the SWA ring write

@@ -13,8 +13,8 @@ import torch.distributed as dist
 import torch.multiprocessing as mp
 
 import oracle
-from deepseekrpc_b200.sharded import (ShardPlan, all_gather, local_block_table, pack_partials, pack_topk,
-                                      unpack_gathered_partials, unpack_gathered_topk)
+from deepseekrpc_b200.sharded import (ShardPlan, all_gather, gathered_lists, gathered_partials,
+                                      local_block_table)
 
 
 @pytest.mark.parametrize("world", [1, 2, 3, 8])
@@ -47,7 +47,7 @@ def _free_port():
 
 
 def _local_topk(scores_full, plan, k):
-    """What each rank's dsr_topk_select returns: the shard's top-k with global ids and scores."""
+    """What each rank's dsr_indexer_topk_decode returns: the shard's top-k with global ids and scores."""
     batch = scores_full.shape[0]
     ids = np.full((batch, k), -1, np.int32)
     scores = np.full((batch, k), -np.inf, np.float32)
@@ -87,8 +87,9 @@ def _exchange_worker(rank, world, port, failures):
 
         # step 2: exchange of the local lists, merge to the exact global top-k
         sc, ids = _local_topk(scores_full, plan, k)
-        s_all, i_all = unpack_gathered_topk(all_gather(pack_topk(torch.from_numpy(sc), torch.from_numpy(ids))),
-                                            world)
+        # the send buffer dsr_indexer_topk_decode fills: [scores' bits ; ids]
+        send = torch.stack((torch.from_numpy(sc).view(torch.int32), torch.from_numpy(ids)))
+        s_all, i_all = gathered_lists(all_gather(send), world)
         assert s_all.shape == (batch, world * k) and i_all.shape == (batch, world * k)
         merged = []
         for b, n in enumerate(lengths):
@@ -110,9 +111,10 @@ def _exchange_worker(rank, world, port, failures):
             rows = np.concatenate([swa[b, :swa_len[b]], kv[b, mine]])
             mb, lb, ob = _partial(q[b], rows, scale)
             m[b], l[b], o[b] = mb, lb, ob
-        po, pm, pl = unpack_gathered_partials(
-            all_gather(pack_partials(torch.from_numpy(o), torch.from_numpy(m), torch.from_numpy(l))),
-            world, batch, heads)
+        # the send buffer dsr_sparse_mla_partial fills: [o | m | l]
+        send = torch.cat((torch.from_numpy(o).reshape(-1), torch.from_numpy(m).reshape(-1),
+                          torch.from_numpy(l).reshape(-1)))
+        po, pm, pl = gathered_partials(all_gather(send), world, batch, heads)
         po, pm, pl = po.double().numpy(), pm.double().numpy(), pl.double().numpy()
         sk = np.tile(sink, batch).astype(np.float64) * np.log2(np.e)  # sink of pair (b, h) at b*H + h
         M = np.maximum(pm.max(axis=0), sk)
