@@ -399,11 +399,20 @@ __global__ void __launch_bounds__(128) lse_combine_kernel(
     const float* __restrict__ part_l, int parts, const float* __restrict__ sink,
     float* __restrict__ out, float* __restrict__ out_m, float* __restrict__ out_l, int32_t* err,
     int heads, int dv) {
-  extern __shared__ float wgt[];  // [parts] weights e^{m_t - M}
-  __shared__ float stat[2];       // M, 1 / L (or L)
+  constexpr int kInFlight = 24;   // partials whose columns a thread holds at once
+  extern __shared__ float wgt[];  // [parts] weights 2^{m_t - M}
+  __shared__ float stat[2];       // M, L
   const int b = blockIdx.x, h = blockIdx.y;
   pdl_wait();
   const int64_t pbase = int64_t(b) * parts * heads + h;  // partial t at pbase + t * heads
+  // the columns of the first kInFlight partials are requested before the weights
+  // exist, so the statistics and the values arrive in one memory round trip
+  const int d0 = threadIdx.x * 4;
+  float4 v[kInFlight];
+#pragma unroll
+  for (int j = 0; j < kInFlight; ++j)
+    if (j < parts && d0 < dv)
+      v[j] = __ldg(reinterpret_cast<const float4*>(part_o + (pbase + int64_t(j) * heads) * dv + d0));
   if (threadIdx.x < 32) {
     const int lane = threadIdx.x;
     float sk = 0.f, M = -CUDART_INF_F;
@@ -416,12 +425,30 @@ __global__ void __launch_bounds__(128) lse_combine_kernel(
       sk *= kLog2e;
       M = sk;
     }
-    for (int t = lane; t < parts; t += 32) M = fmaxf(M, part_m[pbase + int64_t(t) * heads]);
+    float mv[4], lv[4];  // up to 128 partials, loaded together
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int t = lane + 32 * j;
+      mv[j] = t < parts ? part_m[pbase + int64_t(t) * heads] : -CUDART_INF_F;
+      lv[j] = t < parts ? part_l[pbase + int64_t(t) * heads] : 0.f;
+    }
+    for (int t = lane + 128; t < parts; t += 32) M = fmaxf(M, part_m[pbase + int64_t(t) * heads]);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) M = fmaxf(M, mv[j]);
 #pragma unroll
     for (int o = 16; o; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
     const float base = M == -CUDART_INF_F ? 0.f : M;
     float lsum = 0.f;
-    for (int t = lane; t < parts; t += 32) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int t = lane + 32 * j;
+      if (t < parts) {
+        const float e = exp2f(mv[j] - base);
+        wgt[t] = e;
+        lsum += lv[j] * e;
+      }
+    }
+    for (int t = lane + 128; t < parts; t += 32) {
       const int64_t i = pbase + int64_t(t) * heads;
       const float e = exp2f(part_m[i] - base);
       wgt[t] = e;
@@ -437,24 +464,34 @@ __global__ void __launch_bounds__(128) lse_combine_kernel(
   }
   __syncthreads();
   const float inv = sink != nullptr ? 1.f / stat[1] : 1.f;
-  // each thread owns 4 consecutive columns; the parts are read 8 at a time,
-  // all 8 float4 loads in flight before they are accumulated
-  for (int d = threadIdx.x * 4; d < dv; d += blockDim.x * 4) {
+  for (int d = d0; d < dv; d += blockDim.x * 4) {
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int t0 = 0; t0 < parts; t0 += 8) {
-      float4 v[8];
+    if (d == d0) {
 #pragma unroll
-      for (int j = 0; j < 8; ++j)
-        if (t0 + j < parts)
-          v[j] = __ldg(reinterpret_cast<const float4*>(part_o + (pbase + int64_t(t0 + j) * heads) * dv + d));
-#pragma unroll
-      for (int j = 0; j < 8; ++j)
-        if (t0 + j < parts) {
-          const float w = wgt[t0 + j];
+      for (int j = 0; j < kInFlight; ++j)
+        if (j < parts) {
+          const float w = wgt[j];
           acc.x = fmaf(v[j].x, w, acc.x);
           acc.y = fmaf(v[j].y, w, acc.y);
           acc.z = fmaf(v[j].z, w, acc.z);
           acc.w = fmaf(v[j].w, w, acc.w);
+        }
+    }
+    // columns past the first group, and partials past kInFlight, 8 loads at a time
+    for (int t0 = d == d0 ? kInFlight : 0; t0 < parts; t0 += 8) {
+      float4 u[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        if (t0 + j < parts)
+          u[j] = __ldg(reinterpret_cast<const float4*>(part_o + (pbase + int64_t(t0 + j) * heads) * dv + d));
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        if (t0 + j < parts) {
+          const float w = wgt[t0 + j];
+          acc.x = fmaf(u[j].x, w, acc.x);
+          acc.y = fmaf(u[j].y, w, acc.y);
+          acc.z = fmaf(u[j].z, w, acc.z);
+          acc.w = fmaf(u[j].w, w, acc.w);
         }
     }
     const float4 o = make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
