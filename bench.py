@@ -313,6 +313,76 @@ def prefill_leg(dev, reps=5):
             "note": "scores materialised (4.36 GB, not counted as algorithmic); top-k over 512-row launches"}
 
 
+# --------------------------------------------------------- batched (config 3)
+def batched_leg(dev, steps=50):
+    """Config 3: 32 sequences of seeded ragged lengths in [8192, 65536] over one
+    shared paged pool; each step appends one token per sequence (KV + index +
+    SWA rows, generation-checked) and then decodes all 32."""
+    import torch
+    from deepseekrpc_b200 import _native
+    from deepseekrpc_b200.workloads import CONFIGS, algorithmic_bytes, make_decode_inputs
+    cfg = CONFIGS["cfg3"]
+    inp, lengths = make_decode_inputs(cfg, device=dev, gen_device="cuda")
+    B, L = len(lengths), max(lengths)
+    lib = _native.library()
+    rows = inp["kv_pool"].shape[0]
+    generations = torch.zeros(rows, dtype=torch.int64, device=dev)
+    seq = torch.arange(B, dtype=torch.int32, device=dev)
+    positions = (inp["visible"] - 1).contiguous()
+    expected = torch.zeros(B, dtype=torch.int64, device=dev)
+    gen = torch.Generator(device=dev).manual_seed(9)
+    kv_new = torch.randn((B, 576), generator=gen, device=dev).to(torch.bfloat16)
+    ix_new = torch.randn((B, 128), generator=gen, device=dev).to(torch.bfloat16)
+    ws_bytes = lib.dsr_decode_workspace_bytes(B, L, cfg.heads, cfg.topk)
+    ws = torch.zeros(ws_bytes, dtype=torch.uint8, device=dev)
+    out = torch.empty((B, cfg.heads, 512), device=dev)
+    topk = torch.empty((B, cfg.topk), dtype=torch.int32, device=dev)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    stream = torch.cuda.Stream(device=dev)
+
+    def step():
+        s = _native.stream_handle(stream)
+        _native.call("dsr_append_kv_index", inp["kv_pool"].data_ptr(), inp["index_pool"].data_ptr(),
+                     generations.data_ptr(), rows // 64, inp["block_table"].data_ptr(), B,
+                     inp["block_table"].shape[1], seq.data_ptr(), positions.data_ptr(), expected.data_ptr(),
+                     kv_new.data_ptr(), ix_new.data_ptr(), inp["swa"].data_ptr(), err.data_ptr(), B, s)
+        expected.add_(1)  # the rows' generation after this append
+        _native.call("dsr_decode_step", inp["idx_q"].data_ptr(), inp["idx_w"].data_ptr(), cfg.idx_heads,
+                     inp["index_pool"].data_ptr(), inp["q"].data_ptr(), inp["kv_pool"].data_ptr(), cfg.heads,
+                     rows // 64, inp["block_table"].data_ptr(), inp["block_table"].shape[1],
+                     inp["visible"].data_ptr(), L, cfg.topk, inp["swa"].data_ptr(), inp["swa_len"].data_ptr(),
+                     inp["sink"].data_ptr(), cfg.scale, out.data_ptr(), topk.data_ptr(), None, ws.data_ptr(),
+                     ws_bytes, err.data_ptr(), B, s)
+
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            step()
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0, f"batched device status {int(err.item())}"
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        step()
+    torch.cuda.synchronize()
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        graph.replay()
+        start.record(stream)
+        for _ in range(steps):
+            graph.replay()
+        end.record(stream)
+    end.synchronize()
+    ms = start.elapsed_time(end) / steps
+    assert int(err.item()) == 0, f"batched device status {int(err.item())}"
+    nbytes = algorithmic_bytes(lengths, cfg.heads, cfg.topk, cfg.idx_heads) + B * (576 + 128) * 2 * 2
+    hbm, _, peak_kind = peaks()
+    return {"workload": cfg.name + ", append 1 token per sequence + decode", "value": round(ms * 1e3, 2),
+            "unit": "us per batched step", "context_total": int(sum(lengths)), "bytes": nbytes,
+            "achieved_gbs": round(nbytes / (ms * 1e-3) / 1e9, 1),
+            "frac": round(nbytes / (ms * 1e-3) / 1e9 / hbm, 4), "peak_kind": f"{peak_kind} HBM",
+            "steps": steps, "mode": "cuda graph per step (append, generation bump, decode)"}
+
+
 # ---------------------------------------------------------------- single GPU
 def run_single(args):
     import torch
@@ -450,6 +520,7 @@ def run_single(args):
         scaling_base = sharded.single_gpu_base(max(3, min(K, 200)), 3, dev)
 
     prefill = None if args.no_prefill else prefill_leg(dev)
+    batched = None if args.no_batched else batched_leg(dev)
 
     result = {
         "metric": METRIC, "value": round(step_ms * 1e3, 3), "unit": "us", "n_gpus": 1, "steps": K,
@@ -475,6 +546,7 @@ def run_single(args):
         "clocks": clocks,
         "scaling_base": scaling_base,
         "prefill": prefill,
+        "batched": batched,
     }
     print(json.dumps(result))
 
@@ -525,6 +597,7 @@ def main(argv=None):
     parser.add_argument("--no-scaling-base", action="store_true",
                         help="skip the 1-GPU config-5 point of the scaling series")
     parser.add_argument("--no-prefill", action="store_true", help="skip the config-4 prefill indexer leg")
+    parser.add_argument("--no-batched", action="store_true", help="skip the config-3 batched decode leg")
     args = parser.parse_args(argv)
     if args.warmup < 3:
         parser.error("--warmup must be >= 3")
