@@ -37,6 +37,11 @@ SIGNATURES = {
                                    c_int64, _P]),
     "dsr_indexer_prefill": (c_int, [_P, _P, _P, c_int64, _P, c_int64, _P, _P, c_int64, _P, c_int64,
                                     c_int64, _P]),
+    "dsr_candidate_blocks_workspace_bytes": (c_size_t, [c_int64, c_int64, c_int64]),
+    "dsr_candidate_blocks": (c_int, [_P, _P, c_int64, c_int64, c_int64, _P, _P, c_size_t, _P, _P]),
+    "dsr_candidate_select_workspace_bytes": (c_size_t, [c_int64, c_int64]),
+    "dsr_candidate_select": (c_int, [_P, _P, c_int64, _P, c_int64, _P, c_int64, _P, _P, c_int64, c_int64,
+                                     _P, _P, c_size_t, _P, c_int64, _P]),
     "dsr_mla_workspace_bytes": (c_size_t, [c_int64, c_int64, c_int64]),
     "dsr_sparse_mla_decode": (c_int, [_P, _P, c_int64, _P, c_int64, _P, _P, c_int64, _P, _P, _P,
                                       c_float, _P, _P, c_size_t, _P, c_int64, c_int64, _P]),

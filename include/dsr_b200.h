@@ -160,6 +160,29 @@ int dsr_indexer_prefill(const float* q, const float* weights, const uint16_t* in
                         const int32_t* visible, float* scores, int64_t score_stride, int32_t* err,
                         int64_t queries, int64_t heads, void* stream);
 
+/* Candidate-block mode of TiledIndexer (index_selection.py:62-90,108-123).
+ * dsr_candidate_blocks: from a dense indexer's scores f32[rows,score_stride]
+ * (entries < visible[r]), block scores = max over 8 consecutive positions (NaN
+ * propagates), the block of position visible-1 pinned to +inf, and the `keep`
+ * best blocks (ties: lower block id) -> out_blocks i32[rows,keep] ascending,
+ * -1 padded.  dsr_candidate_select: a later indexer scores only the positions
+ * of candidate_blocks i32[rows,ncand] (ascending, -1 padded, each block below
+ * ceil(visible/8), at least one for a nonempty row; else status 1 and nothing
+ * selected) below visible[r] and returns its top-k positions out_ids
+ * i32[rows,k] ascending, -1 padded.  Scratch: the *_workspace_bytes() sizes,
+ * 256-byte aligned, zero before first use. */
+size_t dsr_candidate_blocks_workspace_bytes(int64_t rows, int64_t score_stride, int64_t keep);
+int dsr_candidate_blocks(const float* scores, const int32_t* visible, int64_t rows,
+                         int64_t score_stride, int64_t keep, int32_t* out_blocks, void* workspace,
+                         size_t workspace_bytes, int32_t* err, void* stream);
+size_t dsr_candidate_select_workspace_bytes(int64_t rows, int64_t ncand);
+int dsr_candidate_select(const float* idx_q, const float* idx_w, int64_t idx_heads,
+                         const uint16_t* index_pool, int64_t pool_blocks,
+                         const int32_t* block_table, int64_t table_stride, const int32_t* visible,
+                         const int32_t* candidate_blocks, int64_t ncand, int64_t k,
+                         int32_t* out_ids, void* workspace, size_t workspace_bytes, int32_t* err,
+                         int64_t rows, void* stream);
+
 /* Sparse MLA decode attention over the SWA ring plus top-k selected pool rows.
  * q f32[batch,heads,576]; kv_pool bf16[pool_blocks*64,576]; block_table as above;
  * topk i32[batch,k] logical positions (ascending, -1 padded), each < visible[b];

@@ -119,6 +119,54 @@ def tiled_topk(scores_row, keep, *, tile_rows=8192, positions=None):
     return out
 
 
+# ------------------------------------------------------ candidate blocks (a2)
+def candidate_blocks(scores_row, visible, keep=2048, *, tile_rows=8192):
+    """TiledIndexer._select's candidate production (index_selection.py:108-119) for one row.
+
+    Per tile of tile_rows positions, the scores (padded with -inf to a multiple
+    of 8) are max-reduced over blocks of 8 positions, the block holding position
+    visible-1 is pinned to +inf, and the blocks are ranked with merge_ranked
+    (keep); the chosen block ids come back sorted ascending, -1 padded to `keep`.
+    """
+    scores_row = np.asarray(scores_row, np.float32)[:visible]
+    best_s = np.empty(0, np.float32)
+    best_i = np.empty(0, np.int64)
+    for start in range(0, visible, tile_rows):
+        tile = scores_row[start:start + tile_rows]
+        if len(tile) % 8:
+            tile = np.concatenate([tile, np.full(8 - len(tile) % 8, -np.inf, np.float32)])
+        blocks = tile.reshape(-1, 8)
+        reduced = np.where(np.isnan(blocks).any(axis=1), np.float32(np.nan), blocks.max(axis=1)).astype(np.float32)
+        ids = np.arange(start // 8, start // 8 + len(reduced), dtype=np.int64)
+        reduced[ids == (visible - 1) // 8] = np.inf
+        best_s, best_i = merge_ranked(best_s, best_i, reduced, ids, keep=keep)
+    out = np.full(keep, -1, np.int32)
+    chosen = np.sort(best_i).astype(np.int32)
+    out[:len(chosen)] = chosen
+    return out
+
+
+def candidate_positions(blocks_row, visible):
+    """Logical positions a candidate-restricted indexer scores (index_selection.py:62-90):
+    every position of each listed block (ascending, -1 padded) below `visible`.
+    Raises OracleError where the reference raises ValidationError: blocks not
+    strictly increasing, a block after padding, a block past the visible keys,
+    or no position at all for a nonempty query."""
+    last, padded, positions = -1, False, []
+    for block in blocks_row:
+        block = int(block)
+        if block == -1:
+            padded = True
+            continue
+        if padded or block <= last or not 0 <= block < (visible + 7) // 8:
+            raise OracleError("candidate blocks are stale, duplicated or out of order")
+        last = block
+        positions.extend(range(block * 8, min(block * 8 + 8, visible)))
+    if visible and not positions:
+        raise OracleError("a nonempty index query has no published candidate blocks")
+    return np.asarray(positions, np.int64)
+
+
 # --------------------------------------------------------------- scatter (a6)
 def scatter_slots(pool_bits, generations, slots, expected, value_bits):
     """native/operations.cu:144-161 (scatter_kernel) semantics on bf16 bit arrays.

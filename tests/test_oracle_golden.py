@@ -108,3 +108,29 @@ def test_bf16_round_trip_is_round_to_nearest_even():
     back = oracle.bf16_bits_to_f32(b)
     assert back[0] == 1.0 and back[1] == 1.0 and back[2] == np.float32(1.0 + 2 ** -7)
     assert back[3] == -2.5 and np.isinf(back[6])
+
+
+def test_candidate_restriction_matches_the_reference_known_answer():
+    # the reference self-test's candidate lists and visibility (gpu_selftest.py:232-243):
+    # a restricted selection scores every position of the listed blocks below visible
+    blocks = [[2, 30, 64], [0, 127, 128], [3, 14, 80]]
+    for row, visible in enumerate([513, 1025, 1025]):
+        listed = np.array(blocks[row] + [-1] * 2045, np.int32)
+        expected = [p for b in blocks[row] for p in range(b * 8, min(b * 8 + 8, visible))]
+        assert oracle.candidate_positions(listed, visible).tolist() == expected
+
+
+@pytest.mark.parametrize("listed,visible", [([3, 3], 64), ([5, 2], 64), ([-1, 4], 64), ([8], 64), ([-1], 10)])
+def test_candidate_lists_are_validated_like_the_reference(listed, visible):
+    with pytest.raises(OracleError):
+        oracle.candidate_positions(np.array(listed, np.int32), visible)
+
+
+def test_candidate_blocks_pin_the_newest_block_and_rank_by_block_max():
+    scores = np.array([5, 1, 1, 1, 1, 1, 1, 1,   0, 0, 0, 9, 0, 0, 0, 0,   2, 2, 2, 2, 2, 2, 2, 2,
+                       7, 7, -1], np.float32)
+    # block maxima 5, 9, 2 and the partial newest block (pinned): keep 2 -> blocks 1 and 3
+    assert oracle.candidate_blocks(scores, len(scores), keep=2).tolist() == [1, 3]
+    # ties at equal block maxima go to the lower block id
+    tied = np.zeros(32, np.float32)
+    assert oracle.candidate_blocks(tied, 32, keep=2).tolist() == [0, 3]
