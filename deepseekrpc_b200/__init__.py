@@ -1,11 +1,11 @@
 """B200-native (sm_100a) implementation of DeepSeekRPC's attention hot path.
 
 Layers:
-  include/dsr_b200.h / libdsr_b200.so   C ABI over the hand-written kernels
+  include/dsr_b200.h / libdsr_b200.so   C ABI over the hand-written kernels (_native: ctypes)
   deepseekrpc_cuda (torch extension)    the reference module's op names on that ABI
-  cuda_ops, cache_pool, index_selection host-side mirrors of the reference modules
-  paged                                 paged pools + the fused decode step
+  cuda_ops, index_selection             host-side mirrors of the reference modules
   sharded                               sequence sharding across GPUs (NCCL)
+  workloads, profile_step               seeded BASELINE-config inputs, profiler driver
 """
 from __future__ import annotations
 
