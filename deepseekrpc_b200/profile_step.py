@@ -24,7 +24,11 @@ def main(argv=None) -> int:
     parser = argparse.ArgumentParser(description=__doc__)
     parser.add_argument("--config", default="cfg2", choices=sorted(CONFIGS))
     parser.add_argument("--steps", type=int, default=4)
+    parser.add_argument("--prefill", type=int, nargs=2, metavar=("QUERIES", "CONTEXT"),
+                        help="instead: the prefill indexer GEMM, QUERIES causal queries ending at CONTEXT keys")
     args = parser.parse_args(argv)
+    if args.prefill:
+        return prefill(*args.prefill, args.steps)
     cfg = CONFIGS[args.config]
     torch.cuda.set_device(0)
     inp, lengths = make_decode_inputs(cfg, device="cuda:0", gen_device="cuda")
@@ -46,6 +50,28 @@ def main(argv=None) -> int:
     torch.cuda.synchronize()
     status = int(err.item())
     print(f"{args.steps} decode steps of {cfg.name}: device status {status}")
+    return 0 if status == 0 else 1
+
+
+def prefill(queries: int, context: int, steps: int) -> int:
+    """`steps` launches of the prefill indexer (64 heads) on one seeded sequence."""
+    from .workloads import small_config
+    torch.cuda.set_device(0)
+    inp, _ = make_decode_inputs(small_config("cfg2"), device="cuda:0", gen_device="cuda", lengths=[context])
+    pool, table = inp["index_pool"], inp["block_table"][0].contiguous()
+    gen = torch.Generator(device="cuda:0").manual_seed(4)
+    q = torch.randn((queries, 64, 128), generator=gen, device="cuda:0").to(torch.bfloat16).float()
+    w = torch.randn((queries, 64), generator=gen, device="cuda:0")
+    visible = torch.arange(context - queries + 1, context + 1, dtype=torch.int32, device="cuda:0")
+    scores = torch.empty((queries, context), device="cuda:0")
+    err = torch.zeros(1, dtype=torch.int32, device="cuda:0")
+    for _ in range(steps):
+        _native.call("dsr_indexer_prefill", q.data_ptr(), w.data_ptr(), pool.data_ptr(), pool.shape[0] // 64,
+                     table.data_ptr(), table.shape[0], visible.data_ptr(), scores.data_ptr(), context,
+                     err.data_ptr(), queries, 64, _native.stream_handle())
+    torch.cuda.synchronize()
+    status = int(err.item())
+    print(f"{steps} prefill indexer launches, {queries} queries x {context} keys: device status {status}")
     return 0 if status == 0 else 1
 
 
