@@ -12,24 +12,28 @@
 // selected set is {key >= K*} where K* is the k-th largest key.  Digit 0 of a
 // key is u >> 21 (11 bits), digit 1 is the next 11 bits of u.
 //
-// Design (no grid-wide barrier, no spinning), one launch:
+// Design (no grid-wide barrier), one launch:
 //   * a per-row histogram of digit 0 is built first, by the indexer epilogue
 //     while it produces the scores, or by topk_hist_kernel;
 //   * topk_select_kernel spreads each row over the CTAs in 32-entry words.
-//     Every CTA finds the threshold bin of digit 0 from the row histogram,
-//     stages its entries at or above that bin (compacted, in entry order, as
-//     (raw score bits << 31 | 0x7fffffff - id) records) in the row's staging
+//     Every CTA streams its range through a ring of bulk copies into shared
+//     memory (kTkStages chunks in flight), finds the threshold bin of digit 0
+//     from the row histogram, stages its entries at or above that bin
+//     (compacted, in entry order, as (raw score bits << 31 | 0x7fffffff - id)
+//     records, the count padded to even with a 0 record) in the row's staging
 //     area, counts the digit 1 of its threshold-bin entries into a second row
 //     histogram, and takes a ticket;
-//   * the CTA that takes the last ticket of a row reads the digit-1 histogram,
-//     ranks only the entries that share both digits with K* (usually a handful,
-//     in shared memory), then walks the staged records in entry order, keeps the
-//     selected ones with ballots, 4096 records per chunk, writes ids and scores,
-//     and clears the row's histograms and ticket for the next call.
-// When more than kTkRankCap entries share K*'s two digits (massively tied
-// scores) the last CTA ranks them over the whole row instead.  The workspace
-// must be zero before its first use; every completed call leaves its zeroed
-// part zero again.
+//   * the CTA that takes the last ticket of a row copies all staged records
+//     into shared memory at once (16-byte cp.async), reads the digit-1
+//     histogram, ranks the few entries that share both digits with K* pairwise,
+//     and writes the selected ids (and scores) through one block scan of
+//     per-thread counts; then it clears the row's histograms and ticket.
+// More than kTkRankCap entries sharing K*'s two digits (massively tied scores)
+// are ranked over the whole row; more than kTkRecCap staged records are walked
+// from L2 in chunks.  The workspace must be zero before its first use; every
+// completed call leaves its zeroed part zero again.  A bounded wait that gives
+// up (a copy that never lands) sets DSR_ERR_TIMEOUT; the workspace must then be
+// zeroed again.
 #include "common.cuh"
 #include "host_common.h"
 
@@ -42,7 +46,14 @@ constexpr int kTkThreads = 256;
 constexpr int kTkWarps = kTkThreads / 32;
 constexpr int kTkBins = 2048;      // digits 0 and 1: 11 bits each
 constexpr int kTkMaxCtas = 256;    // CTAs of one launch (one staged-count slot each; fits uint8)
-constexpr int kTkPer = 4;          // entries per thread per staging chunk (strided)
+constexpr int kTkVec = 8;          // 4-entry runs per thread per histogram batch
+constexpr int kTkChunk = kTkThreads * 4 * kTkVec;  // entries per histogram batch
+constexpr int kTkPer = 8;          // consecutive entries per thread per staging chunk
+constexpr int kTkCh = kTkThreads * kTkPer;         // entries per staging chunk
+constexpr int kTkStages = 4;       // staging chunks in flight (bulk copies)
+constexpr int kTkRecCap = 16384;   // staged records the last CTA holds in shared memory
+constexpr size_t kTkDynSmem = size_t(kTkRecCap) * 8;  // the copy ring, then the records
+static_assert(kTkDynSmem >= size_t(kTkStages) * kTkCh * 8, "copy ring (scores and ids) fits");
 constexpr int kTkRegs = 16;        // staged records per thread per output chunk (strided)
 constexpr int kTkRankCap = 2048;   // entries ranked in shared memory
 constexpr int kTkLevels = 6;
@@ -61,15 +72,17 @@ __device__ __forceinline__ uint32_t rank_u(uint32_t raw) {
 
 struct TopkWs {
   size_t hist, hist1, done, cnt, stage, total;
-  int64_t words;  // 32-entry words per row
+  int64_t words;    // 32-entry words per row
+  int64_t sstride;  // staged records per row (row_stride rounded up to even)
   __host__ __device__ TopkWs(int64_t rows, int64_t row_stride) {
     words = (row_stride + 31) / 32;
+    sstride = (row_stride + 1) & ~int64_t(1);
     hist = 0;                                                    // [rows][2048] u32 digit 0
     hist1 = hist + size_t(rows) * kTkBins * 4;                   // [rows][2048] u32 digit 1 of the threshold bin
     done = hist1 + size_t(rows) * kTkBins * 4;                   // [rows] u32 tickets
     cnt = done + ((size_t(rows) * 4 + 255) / 256) * 256;         // [rows][256] u32 staged per CTA
-    stage = cnt + size_t(rows) * kTkMaxCtas * 4;                 // [rows][row_stride] u64 records
-    total = stage + ((size_t(rows) * size_t(row_stride) * 8 + 255) / 256) * 256;
+    stage = cnt + size_t(rows) * kTkMaxCtas * 4;                 // [rows][sstride] u64 records
+    total = stage + ((size_t(rows) * size_t(sstride) * 8 + 255) / 256) * 256;
   }
 };
 
@@ -78,11 +91,14 @@ struct TopkShared {
   uint64_t rank[kTkRankCap];
   uint32_t pre[kTkMaxCtas + 1];  // exclusive prefix of staged counts per slot
   uint32_t e0s[kTkMaxCtas];      // first entry of each slot's range in the row
-  uint32_t tot[kTkPer][kTkWarps];
+  uint32_t tot[2][kTkWarps];      // per-warp staged counts, by chunk parity
   uint32_t tot16[kTkRegs][kTkWarps];
   uint8_t map[kTkThreads * kTkRegs];  // chunk position -> slot
   uint32_t scratch[2 * kTkWarps + 8];
+  uint64_t full[kTkStages];      // copy ring: chunk landed
+  uint64_t kstar;
   uint32_t nrank, last;
+  int abort;
 };
 
 struct Select {
@@ -189,18 +205,29 @@ __device__ __forceinline__ int64_t row_length(const int32_t* lengths, int64_t r,
 // ---------------------------------------------------------------------------
 // Standalone histogram pass (the decode step gets it from the indexer).
 // ---------------------------------------------------------------------------
+// Scores cluster in few digit-0 bins, so on long ranges every warp counts into a
+// histogram of its own (kTkWarps * kTkBins words of dynamic shared memory):
+// same-bin updates from different warps would serialise on one shared word.
+// Short ranges share one histogram (less to clear and flush).
+constexpr size_t kTkHistSmem = size_t(kTkWarps) * kTkBins * 4;
+constexpr int64_t kTkHistSplit = 16384;  // entries per CTA from which the warps split
+
+template <bool kIds>
 __global__ void __launch_bounds__(kTkThreads) topk_hist_kernel(
     const float* __restrict__ scores, const int32_t* __restrict__ ids,
     const int32_t* __restrict__ lengths, int64_t rows, int64_t row_stride,
     uint8_t* __restrict__ ws_base) {
-  __shared__ uint32_t hist[kTkBins];
+  extern __shared__ uint32_t whist[];  // [kTkWarps][kTkBins]
   const TopkWs L(rows, row_stride);
   uint32_t* ghist = reinterpret_cast<uint32_t*>(ws_base + L.hist);
-  for (int i = threadIdx.x; i < kTkBins; i += kTkThreads) hist[i] = 0u;
-  pdl_launch_dependents();
-  pdl_wait();
+  const int tid = threadIdx.x, warp = tid >> 5;
   int64_t w0, w1;
   cta_words(rows * L.words, blockIdx.x, gridDim.x, w0, w1);
+  const int copies = (w1 - w0) * 32 >= kTkHistSplit ? kTkWarps : 1;
+  uint32_t* hist = whist + (warp % copies) * kTkBins;
+  for (int i = tid; i < copies * kTkBins; i += kTkThreads) whist[i] = 0u;
+  pdl_launch_dependents();
+  pdl_wait();
   __syncthreads();
   for (int64_t r = w0 / L.words; r < rows && r * L.words < w1; ++r) {
     const int64_t n = row_length(lengths, r, row_stride);
@@ -209,26 +236,42 @@ __global__ void __launch_bounds__(kTkThreads) topk_hist_kernel(
     int64_t e1 = ((w1 < rb + L.words ? w1 : rb + L.words) - rb) * 32;
     if (e1 > n) e1 = n;
     const float* srow = scores + r * row_stride;
-    const int32_t* irow = ids != nullptr ? ids + r * row_stride : nullptr;
-    constexpr int kBatch = 8;
-    for (int64_t i0 = e0; i0 < e1; i0 += int64_t(kTkThreads) * kBatch) {
-      uint32_t u[kBatch];
+    const int32_t* irow = kIds ? ids + r * row_stride : nullptr;
+    const bool vec = (reinterpret_cast<uintptr_t>(srow) & 15u) == 0 &&
+                     (!kIds || (reinterpret_cast<uintptr_t>(irow) & 15u) == 0);
+    for (int64_t c0 = e0; c0 < e1; c0 += kTkChunk) {
+      uint32_t u[4 * kTkVec];
 #pragma unroll
-      for (int j = 0; j < kBatch; ++j) {
-        const int64_t i = i0 + j * kTkThreads + threadIdx.x;
-        u[j] = i < e1 ? entry_key(srow, irow, i) : 0u;
+      for (int v = 0; v < kTkVec; ++v) {
+        const int64_t i = c0 + int64_t(v) * 4 * kTkThreads + 4 * tid;
+        if (vec && i + 3 < e1) {
+          const uint4 s4 = *reinterpret_cast<const uint4*>(srow + i);
+          u[4 * v] = rank_u(s4.x), u[4 * v + 1] = rank_u(s4.y);
+          u[4 * v + 2] = rank_u(s4.z), u[4 * v + 3] = rank_u(s4.w);
+          if (kIds) {
+            const int4 i4 = *reinterpret_cast<const int4*>(irow + i);
+            if (i4.x < 0) u[4 * v] = 0u;
+            if (i4.y < 0) u[4 * v + 1] = 0u;
+            if (i4.z < 0) u[4 * v + 2] = 0u;
+            if (i4.w < 0) u[4 * v + 3] = 0u;
+          }
+        } else {
+#pragma unroll
+          for (int q = 0; q < 4; ++q) u[4 * v + q] = i + q < e1 ? entry_key(srow, irow, i + q) : 0u;
+        }
       }
 #pragma unroll
-      for (int j = 0; j < kBatch; ++j)
+      for (int j = 0; j < 4 * kTkVec; ++j)
         if (u[j]) atomicAdd(&hist[u[j] >> 21], 1u);
     }
     __syncthreads();
-    for (int i = threadIdx.x; i < kTkBins; i += kTkThreads) {
-      const uint32_t v = hist[i];
-      if (v) {
-        atomicAdd(ghist + r * kTkBins + i, v);
-        hist[i] = 0u;
+    for (int i = tid; i < kTkBins; i += kTkThreads) {
+      uint32_t v = 0;
+      for (int w = 0; w < copies; ++w) {
+        v += whist[w * kTkBins + i];
+        whist[w * kTkBins + i] = 0u;
       }
+      if (v) atomicAdd(ghist + r * kTkBins + i, v);
     }
     __syncthreads();
   }
@@ -295,12 +338,14 @@ __device__ __forceinline__ uint64_t record_key(uint64_t rec) {
 // ---------------------------------------------------------------------------
 // Selection: staging by every CTA, resolution and output by the row's last CTA.
 // ---------------------------------------------------------------------------
+template <bool kIds>
 __global__ void __launch_bounds__(kTkThreads) topk_select_kernel(
     const float* __restrict__ scores, const int32_t* __restrict__ ids,
     const int32_t* __restrict__ lengths, int32_t* __restrict__ out_ids,
     float* __restrict__ out_scores, int32_t* err, int64_t rows, int64_t row_stride, int k,
     int64_t id_base, uint8_t* __restrict__ ws_base) {
   __shared__ __align__(16) TopkShared sh;
+  extern __shared__ __align__(128) uint8_t dyn[];  // copy ring, later the row's staged records
   const TopkWs L(rows, row_stride);
   uint32_t* ghist = reinterpret_cast<uint32_t*>(ws_base + L.hist);
   uint32_t* ghist1 = reinterpret_cast<uint32_t*>(ws_base + L.hist1);
@@ -310,11 +355,18 @@ __global__ void __launch_bounds__(kTkThreads) topk_select_kernel(
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const uint32_t cta = blockIdx.x, nctas = gridDim.x;
   const int64_t total_words = rows * L.words;
+  if (tid == 0) {
+    for (int s = 0; s < kTkStages; ++s) mbar_init(&sh.full[s], 1);
+    sh.abort = 0;
+    fence_barrier_init();
+  }
+  __syncthreads();
 
   pdl_launch_dependents();  // the consumer may start its prologue; it waits for our completion
   pdl_wait();               // scores and histograms come from the preceding kernel
   int64_t w0, w1;
   cta_words(total_words, cta, nctas, w0, w1);
+  uint32_t issued = 0;  // chunks this CTA has put on the copy ring (stage = n % kTkStages)
 
   for (int64_t r = w0 / L.words; r < rows && r * L.words < w1; ++r) {
     const int64_t rb = r * L.words;
@@ -330,27 +382,39 @@ __global__ void __launch_bounds__(kTkThreads) topk_select_kernel(
       if (len < 0 || len > row_stride) flag(err, DSR_ERR_ID);
     }
     const float* srow = scores + r * row_stride;
-    const int32_t* irow = ids != nullptr ? ids + r * row_stride : nullptr;
+    const int32_t* irow = kIds ? ids + r * row_stride : nullptr;
     uint32_t* h0row = ghist + r * kTkBins;
     uint32_t* h1row = ghist1 + r * kTkBins;
-    uint64_t* srec = gstage + r * row_stride;
+    uint64_t* srec = gstage + r * L.sstride;
 
-    // ---- row histogram and the first chunk of scores, loaded together
+    // ---- chunks of kTkCh entries: thread tid takes the kTkPer consecutive
+    // entries c0 + kTkPer * tid + q.  Aligned rows stream through a ring of
+    // kTkStages bulk copies into shared memory (one elected thread issues them);
+    // others are read with plain loads.
+    const bool ring = (row_stride & 3) == 0 && (reinterpret_cast<uintptr_t>(srow) & 15u) == 0 &&
+                      (!kIds || (reinterpret_cast<uintptr_t>(irow) & 15u) == 0);
+    const int64_t nch = e1 > e0 ? (e1 - e0 + kTkCh - 1) / kTkCh : 0;
+    const uint32_t first = issued;
+    auto issue = [&](int64_t c) {  // elected thread: chunk c of the row onto its stage
+      const uint32_t st = (first + uint32_t(c)) % kTkStages;
+      const int64_t c0 = e0 + c * kTkCh;
+      const int64_t cnt = ((e1 - c0 < kTkCh ? e1 - c0 : kTkCh) + 3) & ~int64_t(3);  // stays in the row
+      const uint32_t bytes = uint32_t(cnt) * 4u;
+      mbar_arrive_expect_tx(&sh.full[st], kIds ? 2u * bytes : bytes);
+      bulk_load(smem_u32(dyn + size_t(st) * kTkCh * 4), srow + c0, bytes, &sh.full[st]);
+      if (kIds)
+        bulk_load(smem_u32(dyn + size_t(kTkStages + st) * kTkCh * 4), irow + c0, bytes, &sh.full[st]);
+    };
+    if (ring && tid == 0) {
+      fence_proxy_async_smem();  // the records of a previous row were written through the generic proxy
+      for (int64_t c = 0; c < nch && c < kTkStages; ++c) issue(c);
+    }
+    if (ring) issued += uint32_t(nch);
+
+    // ---- row histogram -> threshold bin of digit 0
     uint32_t hv[kTkBins / kTkThreads];
 #pragma unroll
     for (int j = 0; j < kTkBins / kTkThreads; ++j) hv[j] = h0row[j * kTkThreads + tid];
-    uint32_t raw[kTkPer];
-    int32_t idv[kTkPer];
-    auto load_chunk = [&](int64_t c0) {
-#pragma unroll
-      for (int j = 0; j < kTkPer; ++j) {
-        const int64_t i = c0 + j * kTkThreads + tid;
-        const bool in = i < e1;
-        raw[j] = in ? __float_as_uint(srow[i]) : 0u;
-        idv[j] = in ? (irow != nullptr ? irow[i] : int32_t(id_base + i)) : -1;
-      }
-    };
-    load_chunk(e0);
 #pragma unroll
     for (int j = 0; j < kTkBins / kTkThreads; ++j) sh.hist[j * kTkThreads + tid] = hv[j];
     __syncthreads();
@@ -361,36 +425,88 @@ __global__ void __launch_bounds__(kTkThreads) topk_select_kernel(
 
     // ---- stage entries at or above the threshold bin, compacted in entry order
     uint32_t staged = 0;  // block-uniform running count
-    for (int64_t c0 = e0; c0 < e1; c0 += int64_t(kTkThreads) * kTkPer) {
-      if (c0 != e0) load_chunk(c0);
-      bool keep[kTkPer];
-      unsigned bal[kTkPer];
+    int64_t c = 0;
+    bool aborted = false;
+    for (; c < nch; ++c) {
+      const int64_t i = e0 + c * kTkCh + int64_t(kTkPer) * tid;
+      uint32_t raw[kTkPer];
+      int32_t idv[kTkPer];
+      bool ok = true;
+      if (ring) {
+        const uint32_t n_ = first + uint32_t(c);
+        ok = mbar_wait(&sh.full[n_ % kTkStages], (n_ / kTkStages) & 1u, &sh.abort, err);
+        const uint8_t* stage = dyn + size_t(n_ % kTkStages) * kTkCh * 4 + size_t(kTkPer) * 4 * tid;
 #pragma unroll
-      for (int j = 0; j < kTkPer; ++j) {
-        const uint32_t d0 = rank_u(raw[j]) >> 21;
-        keep[j] = idv[j] >= 0 && (take_all || d0 >= s0.bin);
-        if (keep[j] && !whole_bin && d0 == s0.bin)
-          atomicAdd(h1row + ((rank_u(raw[j]) >> 10) & (kTkBins - 1)), 1u);
-        bal[j] = __ballot_sync(0xffffffffu, keep[j]);
-        if (lane == 0) sh.tot[j][warp] = __popc(bal[j]);
-      }
-      __syncthreads();
-      uint32_t base = staged;
+        for (int v = 0; v < kTkPer / 4; ++v) {
+          const uint4 x = reinterpret_cast<const uint4*>(stage)[v];
+          raw[4 * v] = x.x, raw[4 * v + 1] = x.y, raw[4 * v + 2] = x.z, raw[4 * v + 3] = x.w;
+          if (kIds) {
+            const int4 y = reinterpret_cast<const int4*>(stage + size_t(kTkStages) * kTkCh * 4)[v];
+            idv[4 * v] = y.x, idv[4 * v + 1] = y.y, idv[4 * v + 2] = y.z, idv[4 * v + 3] = y.w;
+          }
+        }
+      } else {
 #pragma unroll
-      for (int j = 0; j < kTkPer; ++j) {
-        uint32_t before = 0, all = 0;
-        for (int w = 0; w < kTkWarps; ++w) {
-          before += w < warp ? sh.tot[j][w] : 0u;
-          all += sh.tot[j][w];
+        for (int q = 0; q < kTkPer; ++q) {
+          const bool in = i + q < e1;
+          raw[q] = in ? __float_as_uint(srow[i + q]) : 0u;
+          if (kIds) idv[q] = in ? irow[i + q] : -1;
         }
-        if (keep[j]) {
-          const uint32_t pos = base + before + __popc(bal[j] & ((1u << lane) - 1u));
-          srec[e0 + pos] = (uint64_t(raw[j]) << 31) | uint64_t(0x7fffffffu - uint32_t(idv[j]));
-        }
-        base += all;
       }
-      staged = base;
-      __syncthreads();  // sh.tot is reused by the next chunk
+      uint32_t mask = 0;
+#pragma unroll
+      for (int q = 0; q < kTkPer; ++q) {
+        const uint32_t u = rank_u(raw[q]);
+        const bool present = ok && i + q < e1 && (!kIds || idv[q] >= 0);
+        const bool keep = present && (take_all || (u >> 21) >= s0.bin);
+        if (kIds && present && idv[q] == 0x7fffffff) flag(err, DSR_ERR_ID);  // reserved for the pad record
+        if (keep && !whole_bin && (u >> 21) == s0.bin) atomicAdd(h1row + ((u >> 10) & (kTkBins - 1)), 1u);
+        mask |= uint32_t(keep) << q;
+      }
+      const uint32_t cnt = __popc(mask);
+      uint32_t incl = cnt;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += y;
+      }
+      if (lane == 31) sh.tot[c & 1][warp] = incl;
+      if (__syncthreads_or(!ok)) {  // a copy never landed: every thread leaves together
+        aborted = true;
+        break;
+      }
+      if (ring && tid == 0 && c + kTkStages < nch) issue(c + kTkStages);  // this stage is consumed
+      uint32_t before = 0, all = 0;
+#pragma unroll
+      for (int w = 0; w < kTkWarps; ++w) {
+        const uint32_t t = sh.tot[c & 1][w];
+        before += w < warp ? t : 0u;
+        all += t;
+      }
+      uint32_t pos = staged + before + incl - cnt;
+#pragma unroll
+      for (int q = 0; q < kTkPer; ++q)
+        if ((mask >> q) & 1u) {
+          const uint32_t id = kIds ? uint32_t(idv[q]) : uint32_t(id_base + i + q);
+          srec[e0 + pos] = (uint64_t(raw[q]) << 31) | uint64_t(0x7fffffffu - id);
+          ++pos;
+        }
+      staged += all;
+    }
+    if (aborted) {
+      // wait (bounded) for the copies still in flight, then leave; the status is set
+      if (ring && tid == 0)
+        for (int64_t d = c; d < nch && d < c + kTkStages; ++d) {
+          const uint32_t n_ = first + uint32_t(d);
+          mbar_drain(&sh.full[n_ % kTkStages], (n_ / kTkStages) & 1u);
+        }
+      return;
+    }
+    // an even count keeps every CTA's records 16-byte aligned for the last CTA's
+    // copies; the pad record is 0, which no entry produces (ids < 2^31 - 1)
+    if (staged & 1u) {
+      if (tid == 0) srec[e0 + staged] = 0ull;
+      ++staged;
     }
     if (tid == 0) gcnt[r * kTkMaxCtas + (cta - first_cta)] = staged;
 
@@ -402,7 +518,7 @@ __global__ void __launch_bounds__(kTkThreads) topk_select_kernel(
     if (!sh.last) continue;
     __threadfence();
 
-    // other CTAs' counts, records and digit-1 counts are read from L2 (__ldcg)
+    // other CTAs' counts, records and digit-1 counts are read from L2 (__ldcg, cp.async.cg)
     uint32_t h1v[kTkBins / kTkThreads];
     if (!whole_bin) {
 #pragma unroll
@@ -419,8 +535,22 @@ __global__ void __launch_bounds__(kTkThreads) topk_select_kernel(
     sh.pre[tid] = my_pre;
     if (tid == 0) sh.pre[touching] = total_staged;
     // (slots >= touching are never searched: pre[touching] bounds every walk)
+    __syncthreads();
 
-    // digit 1 of K*
+    // ---- up to kTkRecCap records: all of them into shared memory at once,
+    // every warp copying whole slots in 16-byte pieces (counts are even)
+    const bool in_smem = total_staged <= uint32_t(kTkRecCap);
+    uint64_t* recs = reinterpret_cast<uint64_t*>(dyn);
+    if (in_smem) {
+      for (uint32_t sl = warp; sl < touching; sl += kTkWarps) {
+        const uint32_t b = sh.pre[sl], e = sh.pre[sl + 1];
+        const uint64_t* src = srec + sh.e0s[sl];
+        for (uint32_t f = b + 2 * lane; f < e; f += 64) cp_async16(smem_u32(recs + f), src + (f - b));
+      }
+      cp_async_commit();
+    }
+
+    // digit 1 of K* (while the copies fly)
     uint32_t bin1 = 0, need1 = 0;
     bool sub_all = true;  // every threshold-bin entry with digit 1 == bin1 is selected
     if (!whole_bin) {
@@ -432,108 +562,166 @@ __global__ void __launch_bounds__(kTkThreads) topk_select_kernel(
       need1 = need0 - s1.above;
       sub_all = need1 == sh.hist[s1.bin];
     }
-    if (tid == 0) sh.nrank = 0u;
-    __syncthreads();
-
-    // records f = c0 + j * kTkThreads + tid of the row's staged sequence: a
-    // shared map gives every position of the chunk its slot, so consecutive
-    // threads load consecutive records and write consecutive outputs
-    constexpr uint32_t kChunk = uint32_t(kTkThreads) * kTkRegs;
-    uint64_t rec[kTkRegs];
-    uint32_t loaded_c0 = 0xffffffffu;  // block-uniform
-    auto load_records = [&](uint32_t c0) {
-      if (loaded_c0 == c0) return;
-      loaded_c0 = c0;
-      __syncthreads();  // readers of the previous chunk's map are done
-      if (uint32_t(tid) < touching) {
-        const uint32_t b = sh.pre[tid], e = sh.pre[tid + 1];
-        const uint32_t lo = b > c0 ? b : c0, hi = e < c0 + kChunk ? e : c0 + kChunk;
-        for (uint32_t f = lo; f < hi; ++f) sh.map[f - c0] = uint8_t(tid);
-      }
-      __syncthreads();
-#pragma unroll
-      for (int j = 0; j < kTkRegs; ++j) {
-        const uint32_t f = c0 + j * kTkThreads + tid;
-        if (f < total_staged) {
-          const uint32_t slot = sh.map[f - c0];
-          rec[j] = __ldcg(srec + sh.e0s[slot] + (f - sh.pre[slot]));
-        } else {
-          rec[j] = 0ull;
-        }
-      }
-    };
     const uint64_t prefix1 = (uint64_t(s0.bin) << kTkShift[0]) | (uint64_t(bin1) << kTkShift[1]);
+    if (tid == 0) {
+      sh.nrank = 0u;
+      sh.kstar = prefix1;
+    }
     auto shares_two_digits = [&](uint64_t key) { return (key >> kTkShift[1]) == (prefix1 >> kTkShift[1]); };
-
-    // ---- rank the entries that share K*'s two digits
+    auto selected = [&](uint64_t rec, uint64_t kstar) {
+      const uint64_t key = record_key(rec);
+      return rec != 0ull && (whole_bin || uint32_t(key >> kTkShift[0]) > s0.bin || key >= kstar);
+    };
+    int32_t* orow = out_ids + r * k;
+    float* osrow = out_scores != nullptr ? out_scores + r * k : nullptr;
     uint64_t kstar = prefix1;  // with sub_all: every key with those digits qualifies
-    if (!sub_all) {
-      for (uint32_t c0 = 0; c0 < total_staged; c0 += kChunk) {
-        load_records(c0);
-#pragma unroll
-        for (int j = 0; j < kTkRegs; ++j) {
-          const uint32_t f = c0 + j * kTkThreads + tid;
-          const uint64_t key = record_key(rec[j]);
-          if (f < total_staged && shares_two_digits(key)) {
+    uint32_t chosen = 0;
+
+    if (in_smem) {
+      cp_async_wait_all();
+      __syncthreads();
+      // thread tid owns the contiguous records [f0, f1)
+      const uint32_t per = (total_staged + kTkThreads - 1) / kTkThreads;
+      const uint32_t f0 = tid * per < total_staged ? tid * per : total_staged;
+      const uint32_t f1 = f0 + per < total_staged ? f0 + per : total_staged;
+      if (!sub_all) {
+        // ---- rank the entries that share K*'s two digits
+        for (uint32_t f = f0; f < f1; ++f) {
+          const uint64_t rec = recs[f];
+          const uint64_t key = record_key(rec);
+          if (rec != 0ull && shares_two_digits(key)) {
             const uint32_t slot = atomicAdd(&sh.nrank, 1u);
             if (slot < uint32_t(kTkRankCap)) sh.rank[slot] = key;
           }
         }
-      }
-      __syncthreads();
-      const uint32_t nr = sh.nrank;
-      if (nr <= uint32_t(kTkRankCap)) {
-        kstar = resolve_kstar([&](int64_t i) { return sh.rank[i]; }, nr, prefix1, need1, 2, sh);
-      } else {
-        auto row_key = [&](int64_t i) -> uint64_t {
-          const uint32_t u = entry_key(srow, irow, i);
-          const int32_t id = irow != nullptr ? irow[i] : int32_t(id_base + i);
-          return u ? composite(u, 0x7fffffffu - uint32_t(id)) : 0ull;
-        };
-        kstar = resolve_kstar(row_key, n, prefix1, need1, 2, sh);
-      }
-    }
-
-    // ---- keep the selected records in entry order and write them out
-    int32_t* orow = out_ids + r * k;
-    float* osrow = out_scores != nullptr ? out_scores + r * k : nullptr;
-    uint32_t written = 0;  // block-uniform
-    for (uint32_t c0 = 0; c0 < total_staged && written < uint32_t(k); c0 += kChunk) {
-      load_records(c0);  // the rank pass already holds a single chunk
-      unsigned bal[kTkRegs];
-#pragma unroll
-      for (int j = 0; j < kTkRegs; ++j) {
-        const uint32_t f = c0 + j * kTkThreads + tid;
-        const uint64_t key = record_key(rec[j]);
-        const bool keep = f < total_staged &&
-                          (whole_bin || uint32_t(key >> kTkShift[0]) > s0.bin || key >= kstar);
-        bal[j] = __ballot_sync(0xffffffffu, keep);
-        if (lane == 0) sh.tot16[j][warp] = __popc(bal[j]);
-      }
-      __syncthreads();
-      uint32_t base = written;
-#pragma unroll
-      for (int j = 0; j < kTkRegs; ++j) {
-        uint32_t before = 0, all = 0;
-#pragma unroll
-        for (int w = 0; w < kTkWarps; ++w) {
-          const uint32_t t = sh.tot16[j][w];
-          before += w < warp ? t : 0u;
-          all += t;
+        __syncthreads();
+        const uint32_t nr = sh.nrank;
+        if (nr <= uint32_t(kTkThreads)) {
+          // keys are unique: exactly one candidate has need1 - 1 candidates above it
+          if (uint32_t(tid) < nr) {
+            const uint64_t mine = sh.rank[tid];
+            uint32_t above = 0;
+            for (uint32_t j = 0; j < nr; ++j) above += sh.rank[j] > mine ? 1u : 0u;
+            if (above == need1 - 1) sh.kstar = mine;
+          }
+          __syncthreads();
+          kstar = sh.kstar;
+        } else if (nr <= uint32_t(kTkRankCap)) {
+          kstar = resolve_kstar([&](int64_t j) { return sh.rank[j]; }, nr, prefix1, need1, 2, sh);
+        } else {
+          auto row_key = [&](int64_t j) -> uint64_t {
+            const uint32_t u = entry_key(srow, irow, j);
+            const int32_t id = kIds ? irow[j] : int32_t(id_base + j);
+            return u ? composite(u, 0x7fffffffu - uint32_t(id)) : 0ull;
+          };
+          kstar = resolve_kstar(row_key, n, prefix1, need1, 2, sh);
         }
-        if ((bal[j] >> lane) & 1u) {
-          const uint32_t pos = base + before + __popc(bal[j] & ((1u << lane) - 1u));
+      }
+      // ---- ordered output: one block scan of the per-thread counts
+      uint32_t mine = 0;
+      for (uint32_t f = f0; f < f1; ++f) mine += selected(recs[f], kstar) ? 1u : 0u;
+      uint32_t total_sel = 0;
+      uint32_t pos = block_excl_scan(mine, total_sel, sh);
+      for (uint32_t f = f0; f < f1; ++f) {
+        const uint64_t rec = recs[f];
+        if (selected(rec, kstar)) {
           if (pos < uint32_t(k)) {
-            orow[pos] = int32_t(0x7fffffffu - (uint32_t(rec[j]) & 0x7fffffffu));
-            if (osrow != nullptr) osrow[pos] = __uint_as_float(uint32_t(rec[j] >> 31));
+            orow[pos] = int32_t(0x7fffffffu - (uint32_t(rec) & 0x7fffffffu));
+            if (osrow != nullptr) osrow[pos] = __uint_as_float(uint32_t(rec >> 31));
+          }
+          ++pos;
+        }
+      }
+      chosen = total_sel < uint32_t(k) ? total_sel : uint32_t(k);
+    } else {
+      // ---- more records than shared memory holds (massively tied scores): walk
+      // them from L2 in chunks; a shared map gives every position of a chunk its
+      // slot, so consecutive threads load consecutive records
+      constexpr uint32_t kChunk = uint32_t(kTkThreads) * kTkRegs;
+      uint64_t rec[kTkRegs];
+      uint32_t loaded_c0 = 0xffffffffu;  // block-uniform
+      auto load_records = [&](uint32_t c0) {
+        if (loaded_c0 == c0) return;
+        loaded_c0 = c0;
+        __syncthreads();  // readers of the previous chunk's map are done
+        if (uint32_t(tid) < touching) {
+          const uint32_t b = sh.pre[tid], e = sh.pre[tid + 1];
+          const uint32_t lo = b > c0 ? b : c0, hi = e < c0 + kChunk ? e : c0 + kChunk;
+          for (uint32_t f = lo; f < hi; ++f) sh.map[f - c0] = uint8_t(tid);
+        }
+        __syncthreads();
+#pragma unroll
+        for (int j = 0; j < kTkRegs; ++j) {
+          const uint32_t f = c0 + j * kTkThreads + tid;
+          if (f < total_staged) {
+            const uint32_t slot = sh.map[f - c0];
+            rec[j] = __ldcg(srec + sh.e0s[slot] + (f - sh.pre[slot]));
+          } else {
+            rec[j] = 0ull;
           }
         }
-        base += all;
+      };
+      if (!sub_all) {
+        __syncthreads();  // sh.nrank
+        for (uint32_t c0 = 0; c0 < total_staged; c0 += kChunk) {
+          load_records(c0);
+#pragma unroll
+          for (int j = 0; j < kTkRegs; ++j) {
+            const uint64_t key = record_key(rec[j]);
+            if (rec[j] != 0ull && shares_two_digits(key)) {
+              const uint32_t slot = atomicAdd(&sh.nrank, 1u);
+              if (slot < uint32_t(kTkRankCap)) sh.rank[slot] = key;
+            }
+          }
+        }
+        __syncthreads();
+        const uint32_t nr = sh.nrank;
+        if (nr <= uint32_t(kTkRankCap)) {
+          kstar = resolve_kstar([&](int64_t j) { return sh.rank[j]; }, nr, prefix1, need1, 2, sh);
+        } else {
+          auto row_key = [&](int64_t j) -> uint64_t {
+            const uint32_t u = entry_key(srow, irow, j);
+            const int32_t id = kIds ? irow[j] : int32_t(id_base + j);
+            return u ? composite(u, 0x7fffffffu - uint32_t(id)) : 0ull;
+          };
+          kstar = resolve_kstar(row_key, n, prefix1, need1, 2, sh);
+        }
       }
-      written = base;
-      __syncthreads();  // sh.tot16 is reused by the next chunk
+      // ---- keep the selected records in entry order and write them out
+      uint32_t written = 0;  // block-uniform
+      for (uint32_t c0 = 0; c0 < total_staged && written < uint32_t(k); c0 += kChunk) {
+        load_records(c0);  // the rank pass already holds a single chunk
+        unsigned bal[kTkRegs];
+#pragma unroll
+        for (int j = 0; j < kTkRegs; ++j) {
+          bal[j] = __ballot_sync(0xffffffffu, selected(rec[j], kstar));
+          if (lane == 0) sh.tot16[j][warp] = __popc(bal[j]);
+        }
+        __syncthreads();
+        uint32_t base = written;
+#pragma unroll
+        for (int j = 0; j < kTkRegs; ++j) {
+          uint32_t before = 0, all = 0;
+#pragma unroll
+          for (int w = 0; w < kTkWarps; ++w) {
+            const uint32_t t = sh.tot16[j][w];
+            before += w < warp ? t : 0u;
+            all += t;
+          }
+          if ((bal[j] >> lane) & 1u) {
+            const uint32_t pos = base + before + __popc(bal[j] & ((1u << lane) - 1u));
+            if (pos < uint32_t(k)) {
+              orow[pos] = int32_t(0x7fffffffu - (uint32_t(rec[j]) & 0x7fffffffu));
+              if (osrow != nullptr) osrow[pos] = __uint_as_float(uint32_t(rec[j] >> 31));
+            }
+          }
+          base += all;
+        }
+        written = base;
+        __syncthreads();  // sh.tot16 is reused by the next chunk
+      }
+      chosen = written < uint32_t(k) ? written : uint32_t(k);
     }
-    const uint32_t chosen = written < uint32_t(k) ? written : uint32_t(k);
     for (int p = int(chosen) + tid; p < k; p += kTkThreads) {
       orow[p] = -1;
       if (osrow != nullptr) osrow[p] = -CUDART_INF_F;
@@ -545,7 +733,7 @@ __global__ void __launch_bounds__(kTkThreads) topk_select_kernel(
       h1row[j * kTkThreads + tid] = 0u;
     }
     if (tid == 0) gdone[r] = 0u;
-    __syncthreads();
+    __syncthreads();  // the record area and the ring are reused by the next row
   }
 }
 
@@ -579,8 +767,8 @@ int launch_topk(const float* scores, const int32_t* ids, const int32_t* lengths,
   DSR_REQUIRE(k > 0 && k <= 8192, "topk_select: k %lld outside [1, 8192]", (long long)k);
   DSR_REQUIRE(row_stride > 0 && row_stride <= (int64_t(1) << 31) - 1,
               "topk_select: invalid row stride");
-  DSR_REQUIRE(id_base >= 0 && id_base + row_stride <= (int64_t(1) << 31),
-              "topk_select: ids must fit int32");
+  DSR_REQUIRE(id_base >= 0 && id_base + row_stride < (int64_t(1) << 31) - 1,
+              "topk_select: ids must be below 2^31 - 1");
   const TopkWs L(rows, row_stride);
   DSR_REQUIRE(workspace_bytes >= L.total, "topk_select: workspace %zu < %zu bytes",
               workspace_bytes, L.total);
@@ -597,16 +785,45 @@ int launch_topk(const float* scores, const int32_t* ids, const int32_t* lengths,
   cfg.attrs = attr;
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   if (!hist_ready) {
+    static bool configured = false;
+    if (!configured) {
+      cudaError_t e = cudaFuncSetAttribute(topk_hist_kernel<true>,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize, int(kTkHistSmem));
+      if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(topk_hist_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 int(kTkHistSmem));
+      if (e != cudaSuccess) return fail(DSR_ECUDA, "topk histogram smem attribute: %s", cudaGetErrorString(e));
+      configured = true;
+    }
     cfg.numAttrs = pdl ? 1 : 0;
-    const cudaError_t e = cudaLaunchKernelEx(&cfg, topk_hist_kernel, scores, ids, lengths, rows,
-                                             row_stride, ws);
+    cfg.dynamicSmemBytes = kTkHistSmem;
+    const cudaError_t e =
+        ids != nullptr
+            ? cudaLaunchKernelEx(&cfg, topk_hist_kernel<true>, scores, ids, lengths, rows, row_stride, ws)
+            : cudaLaunchKernelEx(&cfg, topk_hist_kernel<false>, scores, ids, lengths, rows, row_stride, ws);
+    cfg.dynamicSmemBytes = 0;
     if (e != cudaSuccess) return fail(DSR_ECUDA, "topk histogram launch: %s", cudaGetErrorString(e));
     cfg.numAttrs = 1;
   } else {
     cfg.numAttrs = pdl ? 1 : 0;
   }
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, topk_select_kernel, scores, ids, lengths, out_ids,
-                                           out_scores, err, rows, row_stride, int(k), id_base, ws);
+  static bool select_configured = false;
+  if (!select_configured) {
+    cudaError_t e = cudaFuncSetAttribute(topk_select_kernel<true>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, int(kTkDynSmem));
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(topk_select_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               int(kTkDynSmem));
+    if (e != cudaSuccess) return fail(DSR_ECUDA, "topk smem attribute: %s", cudaGetErrorString(e));
+    select_configured = true;
+  }
+  cfg.dynamicSmemBytes = kTkDynSmem;
+  const cudaError_t e =
+      ids != nullptr
+          ? cudaLaunchKernelEx(&cfg, topk_select_kernel<true>, scores, ids, lengths, out_ids,
+                               out_scores, err, rows, row_stride, int(k), id_base, ws)
+          : cudaLaunchKernelEx(&cfg, topk_select_kernel<false>, scores, ids, lengths, out_ids,
+                               out_scores, err, rows, row_stride, int(k), id_base, ws);
   if (e != cudaSuccess) return fail(DSR_ECUDA, "topk launch: %s", cudaGetErrorString(e));
   return DSR_OK;
 }
@@ -638,6 +855,233 @@ __global__ void __launch_bounds__(256) merge_gather_kernel(const int32_t* __rest
     for (int r = threadIdx.x; r < rows; r += blockDim.x) lengths[r] = world * k;
   pdl_launch_dependents();
 }
+
+// Rows of at most kMgThreads * kMgMaxPer entries are merged by one CTA each:
+// the rank keys stay in registers, a radix select narrows the key range on a
+// shared histogram (warp-aggregated counts), and the selected entries leave in
+// entry order, which is id order, through one ordered compaction.  No global
+// atomics, no staging, one launch.
+constexpr int kMgThreads = 1024;
+constexpr int kMgWarps = kMgThreads / 32;
+constexpr int kMgMaxPer = 16;
+constexpr int kMgRankCap = 128;  // bin size ranked directly
+
+// Whole block of kMgThreads: over h[0, nb) (nb in {1024, 2048}) the bin b with
+// count(bins > b) < need <= count(bins >= b); returns b, sets `above`.
+__device__ uint32_t merge_find_bin(const uint32_t* h, int nb, uint32_t need, uint32_t& above,
+                                   uint32_t* wsum, uint32_t* result) {
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int bpt = nb / kMgThreads;  // 1 or 2; thread 0 holds the top bins
+  const int top = nb - tid * bpt;
+  const uint32_t v0 = h[top - 1], v1 = bpt == 2 ? h[top - 2] : 0u;
+  const uint32_t mine = v0 + v1;
+  uint32_t incl = mine;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t x = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += x;
+  }
+  if (lane == 31) wsum[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    uint32_t s = wsum[lane];
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t x = __shfl_up_sync(0xffffffffu, s, o);
+      if (lane >= o) s += x;
+    }
+    wsum[lane] = s - wsum[lane];  // exclusive warp offsets
+  }
+  __syncthreads();
+  incl += wsum[warp];
+  const uint32_t excl = incl - mine;
+  if (excl < need && incl >= need) {
+    const bool first = excl + v0 >= need;
+    result[0] = uint32_t(first ? top - 1 : top - 2);
+    result[1] = first ? excl : excl + v0;
+  }
+  __syncthreads();
+  above = result[1];
+  return result[0];
+}
+
+template <int E>
+__global__ void __launch_bounds__(kMgThreads) merge_select_kernel(const int32_t* __restrict__ lists,
+                                                                  int world, int rows, int k,
+                                                                  int32_t* __restrict__ out_ids) {
+  __shared__ uint32_t hist[kTkBins];
+  __shared__ uint32_t wsum[kMgWarps];
+  __shared__ uint64_t wmin[kMgWarps], wmax[kMgWarps];
+  __shared__ uint64_t cand[kMgRankCap];
+  __shared__ uint64_t kstar_s;
+  __shared__ uint32_t result[2], ncand;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int r = blockIdx.x;
+  const int n = world * k;
+  pdl_launch_dependents();
+  pdl_wait();  // the lists come from the preceding exchange
+
+  // thread tid holds the E consecutive entries e0 + j of the row's world * k
+  // (entry e is entry e % k of shard e / k, so entry order is id order); every
+  // load is issued before any is used
+  const int e0 = tid * E;
+  uint32_t raw[E];
+  int32_t idv[E];
+  const bool vec = E >= 4 && k % E == 0 && (reinterpret_cast<uintptr_t>(lists) & 15u) == 0;
+  if (vec) {  // the run lies inside one shard and starts on a 16-byte boundary
+    const int ec = e0 < n ? e0 : 0;
+    const int w = ec / k;
+    const int32_t* src = lists + (int64_t(w) * 2 * rows + r) * k + (ec - w * k);
+#pragma unroll
+    for (int v = 0; v < E / 4; ++v) {
+      const int4 a = __ldg(reinterpret_cast<const int4*>(src) + v);
+      const int4 b = __ldg(reinterpret_cast<const int4*>(src + int64_t(rows) * k) + v);
+      raw[4 * v] = uint32_t(a.x), raw[4 * v + 1] = uint32_t(a.y);
+      raw[4 * v + 2] = uint32_t(a.z), raw[4 * v + 3] = uint32_t(a.w);
+      idv[4 * v] = b.x, idv[4 * v + 1] = b.y, idv[4 * v + 2] = b.z, idv[4 * v + 3] = b.w;
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < E; ++j) {
+      const int e = e0 + j < n ? e0 + j : n - 1;
+      const int w = e / k;
+      const int32_t* src = lists + (int64_t(w) * 2 * rows + r) * k + (e - w * k);
+      raw[j] = uint32_t(__ldg(src));
+      idv[j] = __ldg(src + int64_t(rows) * k);
+    }
+  }
+  uint64_t key[E];
+  uint32_t mine = 0;
+  uint64_t kmin = ~0ull, kmax = 0ull;
+#pragma unroll
+  for (int j = 0; j < E; ++j) {
+    const bool present = e0 + j < n && idv[j] >= 0;
+    key[j] = present ? composite(rank_u(raw[j]), 0x7fffffffu - uint32_t(idv[j])) : 0ull;
+    if (present) {
+      ++mine;
+      kmin = key[j] < kmin ? key[j] : kmin;
+      kmax = key[j] > kmax ? key[j] : kmax;
+    }
+  }
+  // present entries in the row and the range of their keys
+#pragma unroll
+  for (int o = 16; o; o >>= 1) {
+    mine += __shfl_xor_sync(0xffffffffu, mine, o);
+    const uint64_t a = __shfl_xor_sync(0xffffffffu, kmin, o), b = __shfl_xor_sync(0xffffffffu, kmax, o);
+    kmin = a < kmin ? a : kmin;
+    kmax = b > kmax ? b : kmax;
+  }
+  if (lane == 0) {
+    wsum[warp] = mine;
+    wmin[warp] = kmin;
+    wmax[warp] = kmax;
+  }
+  __syncthreads();
+  uint32_t present = wsum[lane];
+  kmin = wmin[lane];
+  kmax = wmax[lane];
+#pragma unroll
+  for (int o = 16; o; o >>= 1) {
+    present += __shfl_xor_sync(0xffffffffu, present, o);
+    const uint64_t a = __shfl_xor_sync(0xffffffffu, kmin, o), b = __shfl_xor_sync(0xffffffffu, kmax, o);
+    kmin = a < kmin ? a : kmin;
+    kmax = b > kmax ? b : kmax;
+  }
+  __syncthreads();
+
+  // radix select over the remaining key range [lo, lo + span], 2048 equal bins a
+  // level (the merged lists hold each shard's best scores only, so fixed float
+  // digits would pile them into a few bins); selected = {key >= thr}
+  uint64_t thr = 1ull;  // take_all: every present key (key > 0) passes
+  if (present > uint32_t(k)) {
+    uint32_t need = uint32_t(k);
+    uint64_t lo = kmin, span = kmax - kmin;
+    for (int level = 0; level < 8; ++level) {
+      const int bits = span ? 64 - __clzll(static_cast<long long>(span)) : 0;
+      const int sh = bits > 11 ? bits - 11 : 0;
+      for (int i = tid; i < kTkBins; i += kMgThreads) hist[i] = 0u;
+      __syncthreads();
+#pragma unroll
+      for (int j = 0; j < E; ++j)
+        if (key[j] >= lo && key[j] - lo <= span) atomicAdd(&hist[uint32_t((key[j] - lo) >> sh)], 1u);
+      __syncthreads();
+      uint32_t above;
+      const uint32_t b = merge_find_bin(hist, kTkBins, need, above, wsum, result);
+      need -= above;
+      thr = lo + (uint64_t(b) << sh);
+      const uint32_t inbin = hist[b];
+      if (tid == 0) ncand = 0u;
+      __syncthreads();  // hist is cleared by the next level
+      if (inbin == need || sh == 0) break;  // the whole sub-range is selected
+      const uint64_t width = (uint64_t(1) << sh) - 1;
+      span = span - (uint64_t(b) << sh) < width ? span - (uint64_t(b) << sh) : width;
+      lo = thr;
+      if (inbin <= uint32_t(kMgRankCap)) {
+        // few keys left in the bin: K* is the one with need - 1 of them above it
+#pragma unroll
+        for (int j = 0; j < E; ++j)
+          if (key[j] >= lo && key[j] - lo <= span) cand[atomicAdd(&ncand, 1u)] = key[j];
+        __syncthreads();
+        if (uint32_t(tid) < inbin) {
+          const uint64_t mine = cand[tid];
+          uint32_t more = 0;
+          for (uint32_t j = 0; j < inbin; ++j) more += cand[j] > mine ? 1u : 0u;
+          if (more == need - 1) kstar_s = mine;
+        }
+        __syncthreads();
+        thr = kstar_s;
+        break;
+      }
+    }
+  }
+
+  // ordered compaction: one block scan of the per-thread counts
+  uint32_t mask = 0;
+#pragma unroll
+  for (int j = 0; j < E; ++j) mask |= uint32_t(key[j] != 0ull && key[j] >= thr) << j;
+  const uint32_t c = __popc(mask);
+  uint32_t incl = c;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t x = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += x;
+  }
+  if (lane == 31) wsum[warp] = incl;
+  __syncthreads();
+  uint32_t wv = wsum[lane], wincl = wv;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t x = __shfl_up_sync(0xffffffffu, wincl, o);
+    if (lane >= o) wincl += x;
+  }
+  const uint32_t total = __shfl_sync(0xffffffffu, wincl, 31);
+  uint32_t pos = __shfl_sync(0xffffffffu, wincl - wv, warp) + incl - c;
+  int32_t* orow = out_ids + int64_t(r) * k;
+#pragma unroll
+  for (int j = 0; j < E; ++j)
+    if ((mask >> j) & 1u) {
+      if (pos < uint32_t(k)) orow[pos] = int32_t(0x7fffffffu - (uint32_t(key[j]) & 0x7fffffffu));
+      ++pos;
+    }
+  for (int p = int(total < uint32_t(k) ? total : uint32_t(k)) + tid; p < k; p += kMgThreads) orow[p] = -1;
+}
+
+template <int E>
+int launch_merge_select(const int32_t* lists, int world, int rows, int k, int32_t* out_ids,
+                        cudaStream_t stream) {
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(unsigned(rows), 1, 1);
+  cfg.blockDim = dim3(kMgThreads, 1, 1);
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, merge_select_kernel<E>, lists, world, rows, k, out_ids);
+  if (e != cudaSuccess) return fail(DSR_ECUDA, "topk_merge launch: %s", cudaGetErrorString(e));
+  return DSR_OK;
+}
 }  // namespace
 
 size_t topk_merge_workspace_bytes(int64_t rows, int64_t world, int64_t k) {
@@ -656,6 +1100,14 @@ int launch_topk_merge(const int32_t* lists, int64_t world, int64_t rows, int64_t
   DSR_REQUIRE((reinterpret_cast<uintptr_t>(workspace) & 255u) == 0,
               "topk_merge: workspace must be 256-byte aligned");
   const int64_t n = world * k;
+  if (n <= int64_t(kMgThreads) * kMgMaxPer) {
+    const int per = int((n + kMgThreads - 1) / kMgThreads);
+    if (per <= 1) return launch_merge_select<1>(lists, int(world), int(rows), int(k), out_ids, stream);
+    if (per <= 2) return launch_merge_select<2>(lists, int(world), int(rows), int(k), out_ids, stream);
+    if (per <= 4) return launch_merge_select<4>(lists, int(world), int(rows), int(k), out_ids, stream);
+    if (per <= 8) return launch_merge_select<8>(lists, int(world), int(rows), int(k), out_ids, stream);
+    return launch_merge_select<16>(lists, int(world), int(rows), int(k), out_ids, stream);
+  }
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   const size_t tk = topk_workspace_bytes(rows, n);
   float* scores = reinterpret_cast<float*>(ws + tk);

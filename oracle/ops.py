@@ -90,11 +90,15 @@ def merge_ranked(scores, ids, new_scores, new_ids, *, keep):
     """index_selection.py:9-19: exact streaming ranking, lower ids break ties.
 
     Stable argsort by id, then stable descending argsort by score (-0.0 == +0.0).
+    torch's descending sort ranks NaN above +inf; numpy's would rank it last, so
+    NaN is ordered by a leading key of its own.
     """
     scores = np.concatenate([np.asarray(scores, np.float32), np.asarray(new_scores, np.float32)])
     ids = np.concatenate([np.asarray(ids, np.int64), np.asarray(new_ids, np.int64)])
     order = np.argsort(ids, kind="stable")
-    order = order[np.argsort(-scores[order], kind="stable")[:keep]]
+    s = scores[order]
+    nan = np.isnan(s)
+    order = order[np.lexsort((np.where(nan, np.float32(0), -s), ~nan))[:keep]]
     return scores[order], ids[order]
 
 

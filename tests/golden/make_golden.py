@@ -119,6 +119,11 @@ def main(argv=None):
     s, i = merge_ranked(torch.empty(0), torch.empty(0, dtype=torch.int64),
                         torch.tensor([9., 8., 7., float("inf")]), torch.arange(4), keep=2)
     merge["pinned_ids"] = i.numpy()
+    # NaN scores: torch's descending sort ranks them above +inf
+    nan_values = np.array([1., np.nan, np.inf, -0.0, np.nan, -np.inf, 0.0, 2., np.inf, 0.0], np.float32)
+    s, i = merge_ranked(torch.empty(0), torch.empty(0, dtype=torch.int64), torch.from_numpy(nan_values),
+                        torch.arange(len(nan_values)), keep=8)
+    merge["nan_values"], merge["nan_ids"] = nan_values, i.numpy()
     out["merge_ranked"] = merge
 
     # 7. tie-heavy top-2048 over 131072 scores through 8192-wide tiles (TiledIndexer merge)

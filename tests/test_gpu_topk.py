@@ -34,8 +34,8 @@ def test_topk_ragged_rows_and_short_rows(cuda):
     assert np.array_equal(out.cpu().numpy(), expected_rows(scores, lengths, 2048))
 
 
-def test_topk_streaming_rows_beyond_shared_memory(cuda):
-    # rows longer than the clusters' shared memory are re-read from HBM on each pass
+def test_topk_long_rows_stream_through_the_copy_ring(cuda):
+    # rows of several chunks per CTA: the bulk-copy ring wraps many times
     rng = np.random.default_rng(22)
     n = 700000
     scores = (np.round(rng.normal(size=(2, n)) * 8) / 8).astype(np.float32)
@@ -44,7 +44,7 @@ def test_topk_streaming_rows_beyond_shared_memory(cuda):
     assert np.array_equal(out.cpu().numpy(), expected_rows(scores, [n, 600001], 2048))
 
 
-def test_topk_threshold_bin_overflow_takes_cluster_radix_path(cuda):
+def test_topk_threshold_bin_overflow_ranks_over_the_row(cuda):
     # more than 8192 entries share the threshold bin: all-equal scores, and a row
     # where 20000 entries tie exactly at the threshold value
     rng = np.random.default_rng(25)
@@ -110,18 +110,23 @@ def test_topk_id_base_and_length_error(cuda):
 
 
 def test_topk_each_resolution_path(cuda):
-    # rows built so the threshold bin is resolved by each route: ranked among staged
-    # candidates, ranked over the candidate list (digit-1 bin too big to stage), whole
-    # threshold bin selected, whole digit-1 bin selected, candidate-list overflow
+    # rows built so the threshold bin is resolved by each route: a few candidates
+    # ranked pairwise, a candidate list ranked digit by digit, candidates beyond the
+    # list ranked over the row, whole threshold bin selected, whole digit-1 bin
+    # selected; and staged records beyond the last CTA's shared memory (walked from
+    # L2) with a short and an overflowing candidate list
     rng = np.random.default_rng(26)
     n, k = 60000, 2048
-    scores = (rng.normal(size=(5, n)) * 0.05).astype(np.float32)
+    scores = (rng.normal(size=(8, n)) * 0.05).astype(np.float32)
     layouts = [
-        [],                                              # staged ranking (plain normal scores)
+        [],                                              # pairwise ranking (plain normal scores)
         [(1000, 2.0), (3000, 1.0)],                      # 3000 tied in one digit-1 bin
         [(2048, 5.0)],                                   # the threshold bin is exactly k
         [(300, 3.0), (500, 1.125), (1248, 1.0625), (1000, 1.0)],  # cut at a digit-1 bin edge
         [(500, 4.0), (12000, 1.0)],                      # more candidates than the list holds
+        [(1500, 2.0), (1000, 1.0)],                      # 1000 candidates: ranked digit by digit
+        [(100, 2.0), (20000, 1.0)],                      # 20100 staged, 20000 candidates
+        [],                                              # 18000 staged in one digit-0 bin
     ]
     for row, layout in enumerate(layouts):
         pos = rng.permutation(n)
@@ -129,9 +134,43 @@ def test_topk_each_resolution_path(cuda):
         for count, value in layout:
             scores[row, pos[start:start + count]] = value
             start += count
-    if not layouts[0]:
-        scores[0] = rng.normal(size=n).astype(np.float32)
-    lengths = [n] * 5
+    scores[0] = rng.normal(size=n).astype(np.float32)
+    scores[7, rng.permutation(n)[:18000]] = rng.uniform(1.0, 1.25, 18000).astype(np.float32)
+    lengths = [n] * 8
     out, code = c_topk(dev(scores), dev(np.array(lengths, np.int32)), k)
     assert code == 0
     assert np.array_equal(out.cpu().numpy(), expected_rows(scores, lengths, k))
+
+
+def test_topk_ranks_nan_above_infinity(cuda):
+    # torch's descending sort (the reference's merge_ranked) puts NaN first
+    rng = np.random.default_rng(29)
+    n = 40000
+    scores = rng.normal(size=(2, n)).astype(np.float32)
+    scores[0, rng.choice(n, 700, replace=False)] = np.nan
+    scores[0, rng.choice(n, 900, replace=False)] = np.inf
+    scores[1, rng.choice(n, 3000, replace=False)] = np.nan  # more NaN than k
+    scores[1, :50] = -np.inf
+    out, code = c_topk(dev(scores), dev(np.array([n, n - 7], np.int32)), 2048)
+    assert code == 0
+    assert np.array_equal(out.cpu().numpy(), expected_rows(scores, [n, n - 7], 2048))
+
+
+def test_topk_rows_not_16_byte_aligned(cuda):
+    # an odd row stride leaves rows off 16-byte boundaries: plain loads, same result
+    rng = np.random.default_rng(30)
+    stride = 50001
+    scores = np.round(rng.normal(size=(5, stride)) * 4).astype(np.float32)
+    lengths = [stride, 50000, 3, 33333, 0]
+    out, code = c_topk(dev(scores), dev(np.array(lengths, np.int32)), 2048)
+    assert code == 0
+    assert np.array_equal(out.cpu().numpy(), expected_rows(scores, lengths, 2048))
+    # valid ids increase along a row (the entry point's contract)
+    ids = np.stack([np.sort(rng.choice(200000, stride, replace=False)).astype(np.int32) for _ in range(5)])
+    ids[:, ::17] = -1
+    out, code = c_topk(dev(scores), dev(np.array(lengths, np.int32)), 2048, ids=dev(ids))
+    assert code == 0
+    for row, m in enumerate(lengths):
+        valid = ids[row, :m] >= 0
+        expected = oracle.tiled_topk(scores[row, :m][valid], 2048, positions=ids[row, :m][valid])
+        assert np.array_equal(out.cpu().numpy()[row], expected)

@@ -24,6 +24,10 @@ def test_merge_ranked_matches_the_reference_outputs(golden):
             start += count
         assert ids.tolist() == g[f"ids_{name}"].tolist()
         assert np.array_equal(scores.numpy(), g[f"scores_{name}"])
+    nan_values = torch.from_numpy(g["nan_values"])
+    _, ids = merge_ranked(torch.empty(0), torch.empty(0, dtype=torch.int64), nan_values,
+                          torch.arange(len(nan_values)), keep=8)
+    assert ids.tolist() == g["nan_ids"].tolist()
 
 
 @pytest.mark.parametrize("kwargs", [dict(tile_rows=12), dict(tile_rows=4), dict(tile_rows=16384), dict(keep=0),

@@ -47,6 +47,9 @@ def test_merge_ranked_tie_rule_matches_reference(golden):
     _, ids = oracle.merge_ranked(np.empty(0, np.float32), np.empty(0, np.int64),
                                  np.array([9., 8., 7., np.inf], np.float32), np.arange(4), keep=2)
     assert ids.tolist() == g["pinned_ids"].tolist() == [3, 0]
+    _, ids = oracle.merge_ranked(np.empty(0, np.float32), np.empty(0, np.int64), g["nan_values"],
+                                 np.arange(len(g["nan_values"])), keep=8)
+    assert ids.tolist() == g["nan_ids"].tolist() == [1, 4, 2, 8, 7, 0, 3, 6]
 
 
 def test_tiled_topk_ties_match_reference_at_decode_scale(golden):
