@@ -131,6 +131,13 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const void* tmap, uint
       "l"(reinterpret_cast<uint64_t>(tmap)), "r"(smem_u32(bar)), "r"(x), "r"(y)
       : "memory");
 }
+// L2 prefetch of the box a 2D tiled load at (x, y) would fetch (no shared memory).
+__device__ __forceinline__ void tma_prefetch_2d(const void* tmap, int32_t x, int32_t y) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(
+                   reinterpret_cast<uint64_t>(tmap)),
+               "r"(x), "r"(y)
+               : "memory");
+}
 // Row gather: four rows (y0..y3) of one box-wide column slab starting at column
 // x, from a tensor map whose box is one row high; 4 x box bytes land at dst
 // (128-byte aligned), swizzled like a tiled load to that address.  Rows outside

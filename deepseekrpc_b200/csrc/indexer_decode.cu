@@ -149,32 +149,30 @@ __global__ void __launch_bounds__(kIxThreads, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
-  if (threadIdx.x == 0) {
-    for (int i = 0; i < kIxStages; ++i) {
-      mbar_init(&full[i], 1);
-      mbar_init(&empty[i], 1);
-    }
-    for (int i = 0; i < kIxAcc; ++i) {
-      mbar_init(&tfull[i], 1);
-      mbar_init(&tempty[i], 256);
-    }
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&qfull[i], 256);
-      mbar_init(&qempty[i], 1);
-    }
-    *abort = 0;
-    fence_barrier_init();
-    tma_prefetch_desc(&kmap);
-  }
-  if (warp == 1) {
-    tmem_alloc(tmem_slot, L::kTmemCols);
-    tmem_relinquish();
-  }
-  for (int i = threadIdx.x; i < kIxHistBins; i += kIxThreads) hsm[i] = 0u;
-  pdl_wait();  // pool rows / visibility may come from the preceding append kernel
-
-  // validated visible counts, tiles per row and their prefix (warp 0)
+  // Start-up: the producer warp goes first to memory (visibility, tile prefix,
+  // then block-table entries and the first tiles) and only arrives at the
+  // start-up barrier; the MMA warp allocates TMEM, the epilogue clears the
+  // histogram, and both wait there for the prefix.
   if (warp == 0) {
+    if (lane == 0) {
+      for (int i = 0; i < kIxStages; ++i) {
+        mbar_init(&full[i], 1);
+        mbar_init(&empty[i], 1);
+      }
+      for (int i = 0; i < kIxAcc; ++i) {
+        mbar_init(&tfull[i], 1);
+        mbar_init(&tempty[i], 256);
+      }
+      for (int i = 0; i < 2; ++i) {
+        mbar_init(&qfull[i], 256);
+        mbar_init(&qempty[i], 1);
+      }
+      *abort = 0;
+      fence_barrier_init();
+      tma_prefetch_desc(&kmap);
+    }
+    pdl_wait();  // pool rows / visibility may come from the preceding append kernel
+    // validated visible counts, tiles per row and their prefix
     const int per_lane = (batch + 31) / 32;
     const int b0 = lane * per_lane;
     int local = 0;
@@ -199,11 +197,21 @@ __global__ void __launch_bounds__(kIxThreads, 1)
       run += (vis_s[b] + kIxTile - 1) / kIxTile;
     }
     if (lane == 31) prefix[batch] = incl;
+    __syncwarp();
+    asm volatile("bar.arrive 1, %0;" ::"n"(kIxThreads) : "memory");
+  } else {
+    if (warp == 1) {
+      tmem_alloc(tmem_slot, L::kTmemCols);
+      tmem_relinquish();
+    } else {
+      for (int i = threadIdx.x - 64; i < kIxHistBins; i += kIxThreads - 64) hsm[i] = 0u;
+    }
+    tc_fence_before();
+    pdl_wait();
+    asm volatile("bar.sync 1, %0;" ::"n"(kIxThreads) : "memory");
+    tc_fence_after();
   }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem_base = *tmem_slot;
+  const uint32_t tmem_base = warp == 0 ? 0u : *tmem_slot;  // the producer never reads TMEM
 
   const int total = prefix[batch];
   const int t_lo = int((int64_t(total) * blockIdx.x) / gridDim.x);
@@ -298,7 +306,6 @@ __global__ void __launch_bounds__(kIxThreads, 1)
       const int et = threadIdx.x - 64;  // 0..255
       const int wg = et >> 7;
       const int row_in_tile = (warp & 3) * 32 + lane;  // TMEM lane of this thread
-      if (mla_q != nullptr) mla_query_image(mla_q, mla_img, batch, mla_heads, et, 256);
       int b = find_row(prefix, batch, t_lo);
       int rowseq = 0;
       uint32_t lonz0 = 1, lonz1 = 1;  // q_lo != 0 for the row in slot 0 / 1
@@ -363,6 +370,8 @@ __global__ void __launch_bounds__(kIxThreads, 1)
       // Every epilogue thread walks every tile and reaches every named barrier;
       // after an aborted wait it only skips the work (no early exit).
       bool live = prepare(b, 0);
+      // this CTA's share of the MLA query image, after the first row's query
+      if (mla_q != nullptr) mla_query_image(mla_q, mla_img, batch, mla_heads, et, 256);
       for (int t = t_lo, s = 0; t < t_hi; ++t, ++s) {
         if (t >= prefix[b + 1]) {  // next non-empty row
           flush(b);

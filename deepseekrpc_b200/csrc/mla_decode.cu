@@ -45,7 +45,7 @@ struct MlaLayout {
   static constexpr int kRedBytes = 2 * kTpk * HG * 4;
   static constexpr int kValidOff = kRedOff + kRedBytes;
   static constexpr int kBarOff = kValidOff + kMlaTile * 4;
-  static constexpr int kMiscOff = kBarOff + 5 * 8;
+  static constexpr int kMiscOff = kBarOff + (4 + kMlaBlocks) * 8;
   static constexpr int kBytes = kMiscOff + 16;
   static constexpr int kAlloc = kBytes + 1024;
   static constexpr uint32_t kTmemCols = 5 * HG <= 128 ? 128 : (5 * HG <= 256 ? 256 : 512);
@@ -70,11 +70,11 @@ __global__ void __launch_bounds__(kMlaThreads, 1)
                                              ~uintptr_t(1023));
   const uint32_t sbase = smem_u32(smem);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBarOff);
-  uint64_t* bar_kv = bars + 0;  // rows gathered (TMA transaction bytes + 1 arrival)
-  uint64_t* bar_s = bars + 1;   // S^T complete (commit)
-  uint64_t* bar_p = bars + 2;   // P^T written (128 arrivals)
-  uint64_t* bar_o = bars + 3;   // O^T complete (commit)
-  uint64_t* bar_q = bars + 4;   // BF16 query in place (bulk copy, or converted in-kernel)
+  uint64_t* bar_s = bars + 0;   // S^T complete (commit)
+  uint64_t* bar_p = bars + 1;   // P^T written (128 arrivals)
+  uint64_t* bar_o = bars + 2;   // O^T complete (commit)
+  uint64_t* bar_q = bars + 3;   // BF16 query in place (bulk copy, or converted in-kernel)
+  uint64_t* bar_kv = bars + 4;  // [9] column block c of the rows gathered (TMA bytes + 1 arrival)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kMiscOff);
   volatile int* abort = reinterpret_cast<volatile int*>(smem + L::kMiscOff + 4);
   int* valid = reinterpret_cast<int*>(smem + L::kValidOff);
@@ -87,7 +87,7 @@ __global__ void __launch_bounds__(kMlaThreads, 1)
 
   if (threadIdx.x == 0) {
     tma_prefetch_desc(blockIdx.x == 0 ? &swa_map : &kv_map);
-    mbar_init(bar_kv, 1);
+    for (int c = 0; c < kMlaBlocks; ++c) mbar_init(bar_kv + c, 1);
     mbar_init(bar_s, 1);
     mbar_init(bar_p, 128);
     mbar_init(bar_o, 1);
@@ -196,19 +196,22 @@ __global__ void __launch_bounds__(kMlaThreads, 1)
     valid[t] = row != oob;
     // ---- gather: 4-row TMA gathers of 64-column slabs into the 9 swizzled
     // column blocks; warp w issues the 8 x 9 gathers of its rows 32w..32w+31
-    if (t == 0) mbar_arrive_expect_tx(bar_kv, uint32_t(kMlaBlocks) * kMlaTile * 128);
+    if (t == 0)
+      for (int c = 0; c < kMlaBlocks; ++c) mbar_arrive_expect_tx(bar_kv + c, kMlaTile * 128);
     const CUtensorMap* map = tile == 0 ? &swa_map : &kv_map;
+    // column-block major: every warp issues block 0 of its 8 row groups first, so the
+    // score MMA can start on block 0 while the later blocks are still in flight
 #pragma unroll
     for (int i = 0; i < 3; ++i) {
       const int j = lane + 32 * i;
       const int jj = j < 8 * kMlaBlocks ? j : 0;
-      const int g = jj / kMlaBlocks, c = jj - g * kMlaBlocks;
+      const int c = jj >> 3, g = jj & 7;
       const int32_t r0 = __shfl_sync(0xffffffffu, row, 4 * g);
       const int32_t r1 = __shfl_sync(0xffffffffu, row, 4 * g + 1);
       const int32_t r2 = __shfl_sync(0xffffffffu, row, 4 * g + 2);
       const int32_t r3 = __shfl_sync(0xffffffffu, row, 4 * g + 3);
       if (j < 8 * kMlaBlocks)
-        tma_gather4(sbase + L::kKvOff + c * 16384 + (warp * 32 + 4 * g) * 128, map, bar_kv, c * 64,
+        tma_gather4(sbase + L::kKvOff + c * 16384 + (warp * 32 + 4 * g) * 128, map, bar_kv + c, c * 64,
                     r0, r1, r2, r3);
     }
 
@@ -291,24 +294,31 @@ __global__ void __launch_bounds__(kMlaThreads, 1)
     }
   } else if (lane == 0) {
     // ------------------------------------------------------------ MMA issuer
-    if (mbar_wait(bar_kv, 0, abort, err) && mbar_wait(bar_q, 0, abort, err)) {
+    // S^T column block by column block, each as soon as its rows have landed
+    bool ready = mbar_wait(bar_q, 0, abort, err);
+    constexpr uint32_t idesc_s = umma_idesc_bf16(128, HG, false, false);
+#pragma unroll 1
+    for (int c = 0; c < kMlaBlocks && ready; ++c) {
+      ready = mbar_wait(bar_kv + c, 0, abort, err);
+      if (!ready) break;
       tc_fence_after();
-      constexpr uint32_t idesc_s = umma_idesc_bf16(128, HG, false, false);
-#pragma unroll 4
-      for (int kk = 0; kk < kMlaD / 16; ++kk) {
-        const int c = kk >> 2, sub = kk & 3;
+#pragma unroll
+      for (int sub = 0; sub < 4; ++sub) {
         const uint64_t ad = umma_desc_sw128(sbase + L::kKvOff + c * 16384 + sub * 32, 16, 1024);
         const uint64_t bd = umma_desc_sw128(sbase + L::kQOff + c * (HG * 128) + sub * 32, 16, 1024);
-        umma_bf16(tmem_s, ad, bd, idesc_s, kk > 0 ? 1u : 0u);
+        umma_bf16(tmem_s, ad, bd, idesc_s, (c | sub) != 0 ? 1u : 0u);
       }
+    }
+    if (ready) {
       umma_commit(bar_s);
       if (mbar_wait(bar_p, 0, abort, err)) {
         tc_fence_after();
         constexpr uint32_t idesc_o = umma_idesc_bf16(128, HG, true, false);
+        // the four 128-column accumulators interleaved: consecutive MMAs are independent
 #pragma unroll 1
-        for (int c = 0; c < kMlaDv / 128; ++c) {
+        for (int ks = 0; ks < kMlaTile / 16; ++ks) {
 #pragma unroll
-          for (int ks = 0; ks < kMlaTile / 16; ++ks) {
+          for (int c = 0; c < kMlaDv / 128; ++c) {
             // A = V^T (MN-major): 128 value columns = two 64-column blocks (LBO), 16 keys
             const uint64_t ad =
                 umma_desc_sw128(sbase + L::kKvOff + (2 * c) * 16384 + ks * 2048, 16384, 1024);
@@ -327,7 +337,7 @@ __global__ void __launch_bounds__(kMlaThreads, 1)
   __syncthreads();
   if (*abort && threadIdx.x == 0) {
     // a wait gave up: let the row gathers and the query copy land before exit
-    mbar_drain(bar_kv, 0);
+    for (int c = 0; c < kMlaBlocks; ++c) mbar_drain(bar_kv + c, 0);
     if (q_img != nullptr) mbar_drain(bar_q, 0);
   }
   if (warp == 4) {

@@ -42,19 +42,24 @@
 namespace dsr {
 namespace {
 
-constexpr int kTkThreads = 256;
+constexpr int kTkThreads = 512;   // selection CTA
 constexpr int kTkWarps = kTkThreads / 32;
 constexpr int kTkBins = 2048;      // digits 0 and 1: 11 bits each
 constexpr int kTkMaxCtas = 256;    // CTAs of one launch (one staged-count slot each; fits uint8)
+constexpr int kHsThreads = 256;   // histogram CTA
+constexpr int kHsWarps = kHsThreads / 32;
 constexpr int kTkVec = 8;          // 4-entry runs per thread per histogram batch
-constexpr int kTkChunk = kTkThreads * 4 * kTkVec;  // entries per histogram batch
-constexpr int kTkPer = 8;          // consecutive entries per thread per staging chunk
+constexpr int kTkChunk = kHsThreads * 4 * kTkVec;  // entries per histogram batch
+constexpr int kTkPer = 4;          // consecutive entries per thread per staging chunk
 constexpr int kTkCh = kTkThreads * kTkPer;         // entries per staging chunk
 constexpr int kTkStages = 4;       // staging chunks in flight (bulk copies)
-constexpr int kTkRecCap = 16384;   // staged records the last CTA holds in shared memory
-constexpr size_t kTkDynSmem = size_t(kTkRecCap) * 8;  // the copy ring, then the records
-static_assert(kTkDynSmem >= size_t(kTkStages) * kTkCh * 8, "copy ring (scores and ids) fits");
-constexpr int kTkRegs = 16;        // staged records per thread per output chunk (strided)
+constexpr int kTkRecCap = 15 * kTkThreads;  // staged records the last CTA holds in shared memory
+constexpr int kTkRun = kTkRecCap / kTkThreads;  // records per thread there (at most; odd)
+constexpr size_t kTkDynSmem = size_t(kTkStages) * kTkCh * 8;  // the copy ring, then the records
+static_assert(kTkDynSmem >= size_t(kTkRecCap) * 8, "records fit the ring's space");
+static_assert(kTkRun % 2 == 1 && kTkRun <= 32, "odd run, one mask word");
+static_assert(kTkMaxCtas <= kTkThreads, "one thread per slot");
+constexpr int kTkRegs = 8;         // staged records per thread per output chunk (strided)
 constexpr int kTkRankCap = 2048;   // entries ranked in shared memory
 constexpr int kTkLevels = 6;
 __constant__ int kTkShift[kTkLevels] = {52, 41, 31, 20, 10, 0};
@@ -89,13 +94,14 @@ struct TopkWs {
 struct TopkShared {
   uint32_t hist[kTkBins];
   uint64_t rank[kTkRankCap];
-  uint32_t pre[kTkMaxCtas + 1];  // exclusive prefix of staged counts per slot
+  uint32_t pre[kTkThreads + 1];  // exclusive prefix of staged counts per slot
   uint32_t e0s[kTkMaxCtas];      // first entry of each slot's range in the row
   uint32_t tot[2][kTkWarps];      // per-warp staged counts, by chunk parity
   uint32_t tot16[kTkRegs][kTkWarps];
   uint8_t map[kTkThreads * kTkRegs];  // chunk position -> slot
   uint32_t scratch[2 * kTkWarps + 8];
   uint64_t full[kTkStages];      // copy ring: chunk landed
+  uint64_t recbar;               // last CTA: the row's staged records landed
   uint64_t kstar;
   uint32_t nrank, last;
   int abort;
@@ -114,9 +120,9 @@ __device__ __forceinline__ uint32_t entry_key(const float* srow, const int32_t* 
 // Whole block: over h[0, nbins) (nbins in {1024, 2048}), the bin b with
 // count(bins > b) < need <= count(bins >= b).  Same result in every thread;
 // total < need (or need == 0) -> {0, total, total}.
-__device__ Select block_find_bin(const uint32_t* h, int nbins, uint32_t need, TopkShared& sh) {
+__device__ __noinline__ Select block_find_bin(const uint32_t* h, int nbins, uint32_t need, TopkShared& sh) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int bpt = nbins / kTkThreads;  // 8 or 4 bins per thread; thread 0 = top bins
+  const int bpt = nbins / kTkThreads;  // 4 or 2 bins per thread; thread 0 = top bins
   const int top = nbins - tid * bpt;
   uint32_t v[8], mine = 0;
 #pragma unroll
@@ -163,7 +169,7 @@ __device__ Select block_find_bin(const uint32_t* h, int nbins, uint32_t need, To
 }
 
 // Exclusive block scan of one value per thread; `total` = the block's sum.
-__device__ __forceinline__ uint32_t block_excl_scan(uint32_t v, uint32_t& total, TopkShared& sh) {
+__device__ __noinline__ uint32_t block_excl_scan(uint32_t v, uint32_t& total, TopkShared& sh) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   uint32_t incl = v;
 #pragma unroll
@@ -206,26 +212,26 @@ __device__ __forceinline__ int64_t row_length(const int32_t* lengths, int64_t r,
 // Standalone histogram pass (the decode step gets it from the indexer).
 // ---------------------------------------------------------------------------
 // Scores cluster in few digit-0 bins, so on long ranges every warp counts into a
-// histogram of its own (kTkWarps * kTkBins words of dynamic shared memory):
+// histogram of its own (kHsWarps * kTkBins words of dynamic shared memory):
 // same-bin updates from different warps would serialise on one shared word.
 // Short ranges share one histogram (less to clear and flush).
-constexpr size_t kTkHistSmem = size_t(kTkWarps) * kTkBins * 4;
+constexpr size_t kTkHistSmem = size_t(kHsWarps) * kTkBins * 4;
 constexpr int64_t kTkHistSplit = 16384;  // entries per CTA from which the warps split
 
 template <bool kIds>
-__global__ void __launch_bounds__(kTkThreads) topk_hist_kernel(
+__global__ void __launch_bounds__(kHsThreads) topk_hist_kernel(
     const float* __restrict__ scores, const int32_t* __restrict__ ids,
     const int32_t* __restrict__ lengths, int64_t rows, int64_t row_stride,
     uint8_t* __restrict__ ws_base) {
-  extern __shared__ uint32_t whist[];  // [kTkWarps][kTkBins]
+  extern __shared__ uint32_t whist[];  // [kHsWarps][kTkBins]
   const TopkWs L(rows, row_stride);
   uint32_t* ghist = reinterpret_cast<uint32_t*>(ws_base + L.hist);
   const int tid = threadIdx.x, warp = tid >> 5;
   int64_t w0, w1;
   cta_words(rows * L.words, blockIdx.x, gridDim.x, w0, w1);
-  const int copies = (w1 - w0) * 32 >= kTkHistSplit ? kTkWarps : 1;
+  const int copies = (w1 - w0) * 32 >= kTkHistSplit ? kHsWarps : 1;
   uint32_t* hist = whist + (warp % copies) * kTkBins;
-  for (int i = tid; i < copies * kTkBins; i += kTkThreads) whist[i] = 0u;
+  for (int i = tid; i < copies * kTkBins; i += kHsThreads) whist[i] = 0u;
   pdl_launch_dependents();
   pdl_wait();
   __syncthreads();
@@ -243,7 +249,7 @@ __global__ void __launch_bounds__(kTkThreads) topk_hist_kernel(
       uint32_t u[4 * kTkVec];
 #pragma unroll
       for (int v = 0; v < kTkVec; ++v) {
-        const int64_t i = c0 + int64_t(v) * 4 * kTkThreads + 4 * tid;
+        const int64_t i = c0 + int64_t(v) * 4 * kHsThreads + 4 * tid;
         if (vec && i + 3 < e1) {
           const uint4 s4 = *reinterpret_cast<const uint4*>(srow + i);
           u[4 * v] = rank_u(s4.x), u[4 * v + 1] = rank_u(s4.y);
@@ -265,7 +271,7 @@ __global__ void __launch_bounds__(kTkThreads) topk_hist_kernel(
         if (u[j]) atomicAdd(&hist[u[j] >> 21], 1u);
     }
     __syncthreads();
-    for (int i = tid; i < kTkBins; i += kTkThreads) {
+    for (int i = tid; i < kTkBins; i += kHsThreads) {
       uint32_t v = 0;
       for (int w = 0; w < copies; ++w) {
         v += whist[w * kTkBins + i];
@@ -330,6 +336,13 @@ __device__ uint64_t resolve_kstar(KeyAt key_at, int64_t count, uint64_t prefix, 
   return kstar;
 }
 
+// Ticket: returns the old value; acq_rel at gpu scope.
+__device__ __forceinline__ uint32_t ticket_add(uint32_t* p) {
+  uint32_t old;
+  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(old) : "l"(p) : "memory");
+  return old;
+}
+
 // Staged record -> rank key.
 __device__ __forceinline__ uint64_t record_key(uint64_t rec) {
   return composite(rank_u(uint32_t(rec >> 31)), uint32_t(rec) & 0x7fffffffu);
@@ -357,6 +370,7 @@ __global__ void __launch_bounds__(kTkThreads) topk_select_kernel(
   const int64_t total_words = rows * L.words;
   if (tid == 0) {
     for (int s = 0; s < kTkStages; ++s) mbar_init(&sh.full[s], 1);
+    mbar_init(&sh.recbar, 1);
     sh.abort = 0;
     fence_barrier_init();
   }
@@ -366,7 +380,8 @@ __global__ void __launch_bounds__(kTkThreads) topk_select_kernel(
   pdl_wait();               // scores and histograms come from the preceding kernel
   int64_t w0, w1;
   cta_words(total_words, cta, nctas, w0, w1);
-  uint32_t issued = 0;  // chunks this CTA has put on the copy ring (stage = n % kTkStages)
+  uint32_t issued = 0;    // chunks this CTA has put on the copy ring (stage = n % kTkStages)
+  uint32_t recphase = 0;  // rows whose records this CTA gathered (phase of sh.recbar)
 
   for (int64_t r = w0 / L.words; r < rows && r * L.words < w1; ++r) {
     const int64_t rb = r * L.words;
@@ -510,13 +525,13 @@ __global__ void __launch_bounds__(kTkThreads) topk_select_kernel(
     }
     if (tid == 0) gcnt[r * kTkMaxCtas + (cta - first_cta)] = staged;
 
-    // ---- ticket: the last CTA of the row finishes it
-    __threadfence();
+    // ---- ticket: the last CTA of the row finishes it.  The barrier orders every
+    // thread's records and counts before thread 0's acq_rel ticket (cumulative at
+    // gpu scope); the last CTA's acquire and barrier order its reads after all.
     __syncthreads();
-    if (tid == 0) sh.last = atomicAdd(gdone + r, 1u) == touching - 1 ? 1u : 0u;
+    if (tid == 0) sh.last = ticket_add(gdone + r) == touching - 1 ? 1u : 0u;
     __syncthreads();
     if (!sh.last) continue;
-    __threadfence();
 
     // other CTAs' counts, records and digit-1 counts are read from L2 (__ldcg, cp.async.cg)
     uint32_t h1v[kTkBins / kTkThreads];
@@ -542,12 +557,18 @@ __global__ void __launch_bounds__(kTkThreads) topk_select_kernel(
     const bool in_smem = total_staged <= uint32_t(kTkRecCap);
     uint64_t* recs = reinterpret_cast<uint64_t*>(dyn);
     if (in_smem) {
-      for (uint32_t sl = warp; sl < touching; sl += kTkWarps) {
-        const uint32_t b = sh.pre[sl], e = sh.pre[sl + 1];
-        const uint64_t* src = srec + sh.e0s[sl];
-        for (uint32_t f = b + 2 * lane; f < e; f += 64) cp_async16(smem_u32(recs + f), src + (f - b));
+      // thread tid copies slot tid with one bulk copy; the barrier expects the
+      // row's bytes before any copy is issued (fence: the area was last written
+      // through the generic proxy)
+      if (tid == 0) {
+        fence_proxy_async_smem();
+        mbar_arrive_expect_tx(&sh.recbar, total_staged * 8u);
       }
-      cp_async_commit();
+      __syncthreads();
+      if (uint32_t(tid) < touching) {
+        const uint32_t b = sh.pre[tid], e = sh.pre[tid + 1];
+        if (e > b) bulk_load(smem_u32(recs + b), srec + sh.e0s[tid], (e - b) * 8u, &sh.recbar);
+      }
     }
 
     // digit 1 of K* (while the copies fly)
@@ -578,22 +599,36 @@ __global__ void __launch_bounds__(kTkThreads) topk_select_kernel(
     uint32_t chosen = 0;
 
     if (in_smem) {
-      cp_async_wait_all();
-      __syncthreads();
-      // thread tid owns the contiguous records [f0, f1)
-      const uint32_t per = (total_staged + kTkThreads - 1) / kTkThreads;
+      const bool landed = mbar_wait(&sh.recbar, recphase & 1u, &sh.abort, err);
+      ++recphase;
+      if (__syncthreads_or(!landed)) {
+        if (tid == 0) mbar_drain(&sh.recbar, (recphase - 1) & 1u);
+        return;  // the status is set
+      }
+      // thread tid owns the contiguous records [f0, f0 + held); an odd run length
+      // keeps the 8-byte shared reads of a warp on distinct banks.  The passes are
+      // short loops: this code runs once per row on a cold instruction cache.
+      const uint32_t per = ((total_staged + kTkThreads - 1) / kTkThreads) | 1u;
       const uint32_t f0 = tid * per < total_staged ? tid * per : total_staged;
-      const uint32_t f1 = f0 + per < total_staged ? f0 + per : total_staged;
-      if (!sub_all) {
-        // ---- rank the entries that share K*'s two digits
-        for (uint32_t f = f0; f < f1; ++f) {
-          const uint64_t rec = recs[f];
-          const uint64_t key = record_key(rec);
-          if (rec != 0ull && shares_two_digits(key)) {
-            const uint32_t slot = atomicAdd(&sh.nrank, 1u);
-            if (slot < uint32_t(kTkRankCap)) sh.rank[slot] = key;
-          }
+      const uint32_t held = total_staged - f0 < per ? total_staged - f0 : per;
+      // one pass: records surely selected (above K*'s two digits) and candidates
+      // (sharing them); candidates join the rank list
+      uint32_t sure = 0, cand = 0;
+      const uint32_t p01 = uint32_t(prefix1 >> kTkShift[1]);
+#pragma unroll 3
+      for (uint32_t j = 0; j < held; ++j) {
+        const uint64_t rec = recs[f0 + j];
+        const uint32_t d01 = rank_u(uint32_t(rec >> 31)) >> 10;  // K*'s two digits: u >> 10
+        const bool is_cand = rec != 0ull && !whole_bin && d01 == p01;
+        sure |= uint32_t(rec != 0ull && (whole_bin || d01 > p01)) << j;
+        cand |= uint32_t(is_cand) << j;
+        if (is_cand && !sub_all) {
+          const uint32_t slot = atomicAdd(&sh.nrank, 1u);
+          if (slot < uint32_t(kTkRankCap)) sh.rank[slot] = record_key(rec);
         }
+      }
+      if (!sub_all) {
+        // ---- K* among the candidates
         __syncthreads();
         const uint32_t nr = sh.nrank;
         if (nr <= uint32_t(kTkThreads)) {
@@ -617,20 +652,49 @@ __global__ void __launch_bounds__(kTkThreads) topk_select_kernel(
           kstar = resolve_kstar(row_key, n, prefix1, need1, 2, sh);
         }
       }
-      // ---- ordered output: one block scan of the per-thread counts
-      uint32_t mine = 0;
-      for (uint32_t f = f0; f < f1; ++f) mine += selected(recs[f], kstar) ? 1u : 0u;
+      // ---- ordered output: one block scan of the per-thread counts; the ids (and
+      // scores) are gathered in shared memory, then leave in 16-byte stores
+      uint32_t mask = sure;
+      for (uint32_t c = cand; c; c &= c - 1) {
+        const uint32_t j = __ffs(c) - 1;
+        if (record_key(recs[f0 + j]) >= kstar) mask |= 1u << j;
+      }
       uint32_t total_sel = 0;
-      uint32_t pos = block_excl_scan(mine, total_sel, sh);
-      for (uint32_t f = f0; f < f1; ++f) {
-        const uint64_t rec = recs[f];
-        if (selected(rec, kstar)) {
-          if (pos < uint32_t(k)) {
-            orow[pos] = int32_t(0x7fffffffu - (uint32_t(rec) & 0x7fffffffu));
-            if (osrow != nullptr) osrow[pos] = __uint_as_float(uint32_t(rec >> 31));
+      uint32_t pos = block_excl_scan(__popc(mask), total_sel, sh);
+      const bool gather = k <= (osrow != nullptr ? kTkRankCap : 2 * kTkRankCap) && (k & 3) == 0 &&
+                          (reinterpret_cast<uintptr_t>(orow) & 15u) == 0 &&
+                          (reinterpret_cast<uintptr_t>(osrow) & 15u) == 0;
+      int32_t* gid = reinterpret_cast<int32_t*>(sh.rank);
+      float* gsc = reinterpret_cast<float*>(sh.rank) + k;
+      while (mask) {
+        const uint32_t j = __ffs(mask) - 1;
+        mask &= mask - 1;
+        if (pos < uint32_t(k)) {
+          const uint64_t rec = recs[f0 + j];
+          const int32_t id = int32_t(0x7fffffffu - (uint32_t(rec) & 0x7fffffffu));
+          const float sc = __uint_as_float(uint32_t(rec >> 31));
+          if (gather) {
+            gid[pos] = id;
+            if (osrow != nullptr) gsc[pos] = sc;
+          } else {
+            orow[pos] = id;
+            if (osrow != nullptr) osrow[pos] = sc;
           }
-          ++pos;
         }
+        ++pos;
+      }
+      if (gather) {
+        const uint32_t got = total_sel < uint32_t(k) ? total_sel : uint32_t(k);
+        for (uint32_t p = got + tid; p < uint32_t(k); p += kTkThreads) {
+          gid[p] = -1;
+          if (osrow != nullptr) gsc[p] = -CUDART_INF_F;
+        }
+        __syncthreads();
+        for (int p = 4 * tid; p < k; p += 4 * kTkThreads) {
+          *reinterpret_cast<int4*>(orow + p) = *reinterpret_cast<const int4*>(gid + p);
+          if (osrow != nullptr) *reinterpret_cast<float4*>(osrow + p) = *reinterpret_cast<const float4*>(gsc + p);
+        }
+        total_sel = uint32_t(k);  // the padding is written
       }
       chosen = total_sel < uint32_t(k) ? total_sel : uint32_t(k);
     } else {
@@ -797,11 +861,13 @@ int launch_topk(const float* scores, const int32_t* ids, const int32_t* lengths,
     }
     cfg.numAttrs = pdl ? 1 : 0;
     cfg.dynamicSmemBytes = kTkHistSmem;
+    cfg.blockDim = dim3(kHsThreads, 1, 1);
     const cudaError_t e =
         ids != nullptr
             ? cudaLaunchKernelEx(&cfg, topk_hist_kernel<true>, scores, ids, lengths, rows, row_stride, ws)
             : cudaLaunchKernelEx(&cfg, topk_hist_kernel<false>, scores, ids, lengths, rows, row_stride, ws);
     cfg.dynamicSmemBytes = 0;
+    cfg.blockDim = dim3(kTkThreads, 1, 1);
     if (e != cudaSuccess) return fail(DSR_ECUDA, "topk histogram launch: %s", cudaGetErrorString(e));
     cfg.numAttrs = 1;
   } else {
