@@ -53,13 +53,17 @@ constexpr int kTkChunk = kHsThreads * 4 * kTkVec;  // entries per histogram batc
 constexpr int kTkPer = 4;          // consecutive entries per thread per staging chunk
 constexpr int kTkCh = kTkThreads * kTkPer;         // entries per staging chunk
 constexpr int kTkStages = 4;       // staging chunks in flight (bulk copies)
-constexpr int kTkRecCap = 15 * kTkThreads;  // staged records the last CTA holds in shared memory
+// staged records the last CTA holds in shared memory: a threshold bin spans up to a
+// quarter octave of scores, which for normal-like scores of 2^20-entry rows is
+// about 11K records above the bin's lower edge
+constexpr int kTkRecCap = 31 * kTkThreads;
 constexpr int kTkRun = kTkRecCap / kTkThreads;  // records per thread there (at most; odd)
-constexpr size_t kTkDynSmem = size_t(kTkStages) * kTkCh * 8;  // the copy ring, then the records
-static_assert(kTkDynSmem >= size_t(kTkRecCap) * 8, "records fit the ring's space");
+constexpr size_t kTkDynSmem = size_t(kTkRecCap) * 8;  // the copy ring, then the records
+static_assert(kTkDynSmem >= size_t(kTkStages) * kTkCh * 8, "the copy ring fits the records' space");
 static_assert(kTkRun % 2 == 1 && kTkRun <= 32, "odd run, one mask word");
 static_assert(kTkMaxCtas <= kTkThreads, "one thread per slot");
 constexpr int kTkRegs = 8;         // staged records per thread per output chunk (strided)
+constexpr int kTkRowGroup = 32;    // rows staged before their finishing (one bit each)
 constexpr int kTkRankCap = 2048;   // entries ranked in shared memory
 constexpr int kTkLevels = 6;
 __constant__ int kTkShift[kTkLevels] = {52, 41, 31, 20, 10, 0};
@@ -103,6 +107,7 @@ struct TopkShared {
   uint64_t full[kTkStages];      // copy ring: chunk landed
   uint64_t recbar;               // last CTA: the row's staged records landed
   uint64_t kstar;
+  uint32_t rbin[kTkRowGroup], rneed[kTkRowGroup], rwhole[kTkRowGroup];  // rows this CTA finishes
   uint32_t nrank, last;
   int abort;
 };
@@ -383,421 +388,452 @@ __global__ void __launch_bounds__(kTkThreads) topk_select_kernel(
   uint32_t issued = 0;    // chunks this CTA has put on the copy ring (stage = n % kTkStages)
   uint32_t recphase = 0;  // rows whose records this CTA gathered (phase of sh.recbar)
 
-  for (int64_t r = w0 / L.words; r < rows && r * L.words < w1; ++r) {
-    const int64_t rb = r * L.words;
-    const int64_t n = row_length(lengths, r, row_stride);
-    const int64_t a0 = w0 > rb ? w0 - rb : 0;                         // first word of the row
-    const int64_t a1 = (w1 < rb + L.words ? w1 : rb + L.words) - rb;  // end word of the row
-    const int64_t e0 = a0 * 32;
-    const int64_t e1 = a1 * 32 < n ? a1 * 32 : n;  // this CTA's entries [e0, e1)
-    const uint32_t first_cta = word_owner(rb, total_words, nctas);
-    const uint32_t touching = word_owner(rb + L.words - 1, total_words, nctas) - first_cta + 1;
-    if (cta == first_cta && tid == 0) {
-      const int32_t len = lengths[r];
-      if (len < 0 || len > row_stride) flag(err, DSR_ERR_ID);
-    }
-    const float* srow = scores + r * row_stride;
-    const int32_t* irow = kIds ? ids + r * row_stride : nullptr;
-    uint32_t* h0row = ghist + r * kTkBins;
-    uint32_t* h1row = ghist1 + r * kTkBins;
-    uint64_t* srec = gstage + r * L.sstride;
-
-    // ---- chunks of kTkCh entries: thread tid takes the kTkPer consecutive
-    // entries c0 + kTkPer * tid + q.  Aligned rows stream through a ring of
-    // kTkStages bulk copies into shared memory (one elected thread issues them);
-    // others are read with plain loads.
-    const bool ring = (row_stride & 3) == 0 && (reinterpret_cast<uintptr_t>(srow) & 15u) == 0 &&
-                      (!kIds || (reinterpret_cast<uintptr_t>(irow) & 15u) == 0);
-    const int64_t nch = e1 > e0 ? (e1 - e0 + kTkCh - 1) / kTkCh : 0;
-    const uint32_t first = issued;
-    auto issue = [&](int64_t c) {  // elected thread: chunk c of the row onto its stage
-      const uint32_t st = (first + uint32_t(c)) % kTkStages;
-      const int64_t c0 = e0 + c * kTkCh;
-      const int64_t cnt = ((e1 - c0 < kTkCh ? e1 - c0 : kTkCh) + 3) & ~int64_t(3);  // stays in the row
-      const uint32_t bytes = uint32_t(cnt) * 4u;
-      mbar_arrive_expect_tx(&sh.full[st], kIds ? 2u * bytes : bytes);
-      bulk_load(smem_u32(dyn + size_t(st) * kTkCh * 4), srow + c0, bytes, &sh.full[st]);
-      if (kIds)
-        bulk_load(smem_u32(dyn + size_t(kTkStages + st) * kTkCh * 4), irow + c0, bytes, &sh.full[st]);
-    };
-    if (ring && tid == 0) {
-      fence_proxy_async_smem();  // the records of a previous row were written through the generic proxy
-      for (int64_t c = 0; c < nch && c < kTkStages; ++c) issue(c);
-    }
-    if (ring) issued += uint32_t(nch);
-
-    // ---- row histogram -> threshold bin of digit 0
-    uint32_t hv[kTkBins / kTkThreads];
-#pragma unroll
-    for (int j = 0; j < kTkBins / kTkThreads; ++j) hv[j] = h0row[j * kTkThreads + tid];
-#pragma unroll
-    for (int j = 0; j < kTkBins / kTkThreads; ++j) sh.hist[j * kTkThreads + tid] = hv[j];
-    __syncthreads();
-    const Select s0 = block_find_bin(sh.hist, kTkBins, uint32_t(k), sh);
-    const bool take_all = s0.total <= uint32_t(k);
-    const uint32_t need0 = uint32_t(k) - s0.above;
-    const bool whole_bin = take_all || sh.hist[s0.bin] == need0;  // no entry left to rank
-
-    // ---- stage entries at or above the threshold bin, compacted in entry order
-    uint32_t staged = 0;  // block-uniform running count
-    int64_t c = 0;
-    bool aborted = false;
-    for (; c < nch; ++c) {
-      const int64_t i = e0 + c * kTkCh + int64_t(kTkPer) * tid;
-      uint32_t raw[kTkPer];
-      int32_t idv[kTkPer];
-      bool ok = true;
-      if (ring) {
-        const uint32_t n_ = first + uint32_t(c);
-        ok = mbar_wait(&sh.full[n_ % kTkStages], (n_ / kTkStages) & 1u, &sh.abort, err);
-        const uint8_t* stage = dyn + size_t(n_ % kTkStages) * kTkCh * 4 + size_t(kTkPer) * 4 * tid;
-#pragma unroll
-        for (int v = 0; v < kTkPer / 4; ++v) {
-          const uint4 x = reinterpret_cast<const uint4*>(stage)[v];
-          raw[4 * v] = x.x, raw[4 * v + 1] = x.y, raw[4 * v + 2] = x.z, raw[4 * v + 3] = x.w;
-          if (kIds) {
-            const int4 y = reinterpret_cast<const int4*>(stage + size_t(kTkStages) * kTkCh * 4)[v];
-            idv[4 * v] = y.x, idv[4 * v + 1] = y.y, idv[4 * v + 2] = y.z, idv[4 * v + 3] = y.w;
-          }
-        }
-      } else {
-#pragma unroll
-        for (int q = 0; q < kTkPer; ++q) {
-          const bool in = i + q < e1;
-          raw[q] = in ? __float_as_uint(srow[i + q]) : 0u;
-          if (kIds) idv[q] = in ? irow[i + q] : -1;
-        }
+  const int64_t r_first = w0 / L.words;
+  const int64_t r_end = (w1 + L.words - 1) / L.words < rows ? (w1 + L.words - 1) / L.words : rows;
+  for (int64_t rg = r_first; rg < r_end; rg += kTkRowGroup) {
+    const int64_t rg_end = rg + kTkRowGroup < r_end ? rg + kTkRowGroup : r_end;
+    uint32_t won = 0;  // rows of the group whose last ticket this CTA took
+    // ---- every row of the group is staged first: finishing one row never
+    // delays this CTA's share of the next
+    for (int64_t r = rg; r < rg_end; ++r) {
+      const int64_t rb = r * L.words;
+      const int64_t n = row_length(lengths, r, row_stride);
+      const int64_t a0 = w0 > rb ? w0 - rb : 0;                         // first word of the row
+      const int64_t a1 = (w1 < rb + L.words ? w1 : rb + L.words) - rb;  // end word of the row
+      const int64_t e0 = a0 * 32;
+      const int64_t e1 = a1 * 32 < n ? a1 * 32 : n;  // this CTA's entries [e0, e1)
+      const uint32_t first_cta = word_owner(rb, total_words, nctas);
+      const uint32_t touching = word_owner(rb + L.words - 1, total_words, nctas) - first_cta + 1;
+      if (cta == first_cta && tid == 0) {
+        const int32_t len = lengths[r];
+        if (len < 0 || len > row_stride) flag(err, DSR_ERR_ID);
       }
-      uint32_t mask = 0;
-#pragma unroll
-      for (int q = 0; q < kTkPer; ++q) {
-        const uint32_t u = rank_u(raw[q]);
-        const bool present = ok && i + q < e1 && (!kIds || idv[q] >= 0);
-        const bool keep = present && (take_all || (u >> 21) >= s0.bin);
-        if (kIds && present && idv[q] == 0x7fffffff) flag(err, DSR_ERR_ID);  // reserved for the pad record
-        if (keep && !whole_bin && (u >> 21) == s0.bin) atomicAdd(h1row + ((u >> 10) & (kTkBins - 1)), 1u);
-        mask |= uint32_t(keep) << q;
-      }
-      const uint32_t cnt = __popc(mask);
-      uint32_t incl = cnt;
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
-        if (lane >= o) incl += y;
-      }
-      if (lane == 31) sh.tot[c & 1][warp] = incl;
-      if (__syncthreads_or(!ok)) {  // a copy never landed: every thread leaves together
-        aborted = true;
-        break;
-      }
-      if (ring && tid == 0 && c + kTkStages < nch) issue(c + kTkStages);  // this stage is consumed
-      uint32_t before = 0, all = 0;
-#pragma unroll
-      for (int w = 0; w < kTkWarps; ++w) {
-        const uint32_t t = sh.tot[c & 1][w];
-        before += w < warp ? t : 0u;
-        all += t;
-      }
-      uint32_t pos = staged + before + incl - cnt;
-#pragma unroll
-      for (int q = 0; q < kTkPer; ++q)
-        if ((mask >> q) & 1u) {
-          const uint32_t id = kIds ? uint32_t(idv[q]) : uint32_t(id_base + i + q);
-          srec[e0 + pos] = (uint64_t(raw[q]) << 31) | uint64_t(0x7fffffffu - id);
-          ++pos;
-        }
-      staged += all;
-    }
-    if (aborted) {
-      // wait (bounded) for the copies still in flight, then leave; the status is set
-      if (ring && tid == 0)
-        for (int64_t d = c; d < nch && d < c + kTkStages; ++d) {
-          const uint32_t n_ = first + uint32_t(d);
-          mbar_drain(&sh.full[n_ % kTkStages], (n_ / kTkStages) & 1u);
-        }
-      return;
-    }
-    // an even count keeps every CTA's records 16-byte aligned for the last CTA's
-    // copies; the pad record is 0, which no entry produces (ids < 2^31 - 1)
-    if (staged & 1u) {
-      if (tid == 0) srec[e0 + staged] = 0ull;
-      ++staged;
-    }
-    if (tid == 0) gcnt[r * kTkMaxCtas + (cta - first_cta)] = staged;
+      const float* srow = scores + r * row_stride;
+      const int32_t* irow = kIds ? ids + r * row_stride : nullptr;
+      uint32_t* h0row = ghist + r * kTkBins;
+      uint32_t* h1row = ghist1 + r * kTkBins;
+      uint64_t* srec = gstage + r * L.sstride;
 
-    // ---- ticket: the last CTA of the row finishes it.  The barrier orders every
-    // thread's records and counts before thread 0's acq_rel ticket (cumulative at
-    // gpu scope); the last CTA's acquire and barrier order its reads after all.
-    __syncthreads();
-    if (tid == 0) sh.last = ticket_add(gdone + r) == touching - 1 ? 1u : 0u;
-    __syncthreads();
-    if (!sh.last) continue;
-
-    // other CTAs' counts, records and digit-1 counts are read from L2 (__ldcg, cp.async.cg)
-    uint32_t h1v[kTkBins / kTkThreads];
-    if (!whole_bin) {
-#pragma unroll
-      for (int j = 0; j < kTkBins / kTkThreads; ++j) h1v[j] = __ldcg(h1row + j * kTkThreads + tid);
-    }
-    const uint32_t my_cnt = uint32_t(tid) < touching ? __ldcg(gcnt + r * kTkMaxCtas + tid) : 0u;
-    if (uint32_t(tid) < touching) {
-      int64_t cw0, cw1;
-      cta_words(total_words, first_cta + tid, nctas, cw0, cw1);
-      sh.e0s[tid] = uint32_t((cw0 > rb ? cw0 - rb : 0) * 32);
-    }
-    uint32_t total_staged = 0;
-    const uint32_t my_pre = block_excl_scan(my_cnt, total_staged, sh);
-    sh.pre[tid] = my_pre;
-    if (tid == 0) sh.pre[touching] = total_staged;
-    // (slots >= touching are never searched: pre[touching] bounds every walk)
-    __syncthreads();
-
-    // ---- up to kTkRecCap records: all of them into shared memory at once,
-    // every warp copying whole slots in 16-byte pieces (counts are even)
-    const bool in_smem = total_staged <= uint32_t(kTkRecCap);
-    uint64_t* recs = reinterpret_cast<uint64_t*>(dyn);
-    if (in_smem) {
-      // thread tid copies slot tid with one bulk copy; the barrier expects the
-      // row's bytes before any copy is issued (fence: the area was last written
-      // through the generic proxy)
-      if (tid == 0) {
-        fence_proxy_async_smem();
-        mbar_arrive_expect_tx(&sh.recbar, total_staged * 8u);
+      // ---- chunks of kTkCh entries: thread tid takes the kTkPer consecutive
+      // entries c0 + kTkPer * tid + q.  Aligned rows stream through a ring of
+      // kTkStages bulk copies into shared memory (one elected thread issues them);
+      // others are read with plain loads.
+      const bool ring = (row_stride & 3) == 0 && (reinterpret_cast<uintptr_t>(srow) & 15u) == 0 &&
+                        (!kIds || (reinterpret_cast<uintptr_t>(irow) & 15u) == 0);
+      const int64_t nch = e1 > e0 ? (e1 - e0 + kTkCh - 1) / kTkCh : 0;
+      const uint32_t first = issued;
+      auto issue = [&](int64_t c) {  // elected thread: chunk c of the row onto its stage
+        const uint32_t st = (first + uint32_t(c)) % kTkStages;
+        const int64_t c0 = e0 + c * kTkCh;
+        const int64_t cnt = ((e1 - c0 < kTkCh ? e1 - c0 : kTkCh) + 3) & ~int64_t(3);  // stays in the row
+        const uint32_t bytes = uint32_t(cnt) * 4u;
+        mbar_arrive_expect_tx(&sh.full[st], kIds ? 2u * bytes : bytes);
+        bulk_load(smem_u32(dyn + size_t(st) * kTkCh * 4), srow + c0, bytes, &sh.full[st]);
+        if (kIds)
+          bulk_load(smem_u32(dyn + size_t(kTkStages + st) * kTkCh * 4), irow + c0, bytes, &sh.full[st]);
+      };
+      if (ring && tid == 0) {
+        fence_proxy_async_smem();  // the records of a previous row were written through the generic proxy
+        for (int64_t c = 0; c < nch && c < kTkStages; ++c) issue(c);
       }
+      if (ring) issued += uint32_t(nch);
+
+      // ---- row histogram -> threshold bin of digit 0
+      uint32_t hv[kTkBins / kTkThreads];
+  #pragma unroll
+      for (int j = 0; j < kTkBins / kTkThreads; ++j) hv[j] = h0row[j * kTkThreads + tid];
+  #pragma unroll
+      for (int j = 0; j < kTkBins / kTkThreads; ++j) sh.hist[j * kTkThreads + tid] = hv[j];
       __syncthreads();
-      if (uint32_t(tid) < touching) {
-        const uint32_t b = sh.pre[tid], e = sh.pre[tid + 1];
-        if (e > b) bulk_load(smem_u32(recs + b), srec + sh.e0s[tid], (e - b) * 8u, &sh.recbar);
-      }
-    }
+      const Select s0 = block_find_bin(sh.hist, kTkBins, uint32_t(k), sh);
+      const bool take_all = s0.total <= uint32_t(k);
+      const uint32_t need0 = uint32_t(k) - s0.above;
+      const bool whole_bin = take_all || sh.hist[s0.bin] == need0;  // no entry left to rank
 
-    // digit 1 of K* (while the copies fly)
-    uint32_t bin1 = 0, need1 = 0;
-    bool sub_all = true;  // every threshold-bin entry with digit 1 == bin1 is selected
-    if (!whole_bin) {
-#pragma unroll
-      for (int j = 0; j < kTkBins / kTkThreads; ++j) sh.hist[j * kTkThreads + tid] = h1v[j];
-      __syncthreads();
-      const Select s1 = block_find_bin(sh.hist, kTkBins, need0, sh);
-      bin1 = s1.bin;
-      need1 = need0 - s1.above;
-      sub_all = need1 == sh.hist[s1.bin];
-    }
-    const uint64_t prefix1 = (uint64_t(s0.bin) << kTkShift[0]) | (uint64_t(bin1) << kTkShift[1]);
-    if (tid == 0) {
-      sh.nrank = 0u;
-      sh.kstar = prefix1;
-    }
-    auto shares_two_digits = [&](uint64_t key) { return (key >> kTkShift[1]) == (prefix1 >> kTkShift[1]); };
-    auto selected = [&](uint64_t rec, uint64_t kstar) {
-      const uint64_t key = record_key(rec);
-      return rec != 0ull && (whole_bin || uint32_t(key >> kTkShift[0]) > s0.bin || key >= kstar);
-    };
-    int32_t* orow = out_ids + r * k;
-    float* osrow = out_scores != nullptr ? out_scores + r * k : nullptr;
-    uint64_t kstar = prefix1;  // with sub_all: every key with those digits qualifies
-    uint32_t chosen = 0;
-
-    if (in_smem) {
-      const bool landed = mbar_wait(&sh.recbar, recphase & 1u, &sh.abort, err);
-      ++recphase;
-      if (__syncthreads_or(!landed)) {
-        if (tid == 0) mbar_drain(&sh.recbar, (recphase - 1) & 1u);
-        return;  // the status is set
-      }
-      // thread tid owns the contiguous records [f0, f0 + held); an odd run length
-      // keeps the 8-byte shared reads of a warp on distinct banks.  The passes are
-      // short loops: this code runs once per row on a cold instruction cache.
-      const uint32_t per = ((total_staged + kTkThreads - 1) / kTkThreads) | 1u;
-      const uint32_t f0 = tid * per < total_staged ? tid * per : total_staged;
-      const uint32_t held = total_staged - f0 < per ? total_staged - f0 : per;
-      // one pass: records surely selected (above K*'s two digits) and candidates
-      // (sharing them); candidates join the rank list
-      uint32_t sure = 0, cand = 0;
-      const uint32_t p01 = uint32_t(prefix1 >> kTkShift[1]);
-#pragma unroll 3
-      for (uint32_t j = 0; j < held; ++j) {
-        const uint64_t rec = recs[f0 + j];
-        const uint32_t d01 = rank_u(uint32_t(rec >> 31)) >> 10;  // K*'s two digits: u >> 10
-        const bool is_cand = rec != 0ull && !whole_bin && d01 == p01;
-        sure |= uint32_t(rec != 0ull && (whole_bin || d01 > p01)) << j;
-        cand |= uint32_t(is_cand) << j;
-        if (is_cand && !sub_all) {
-          const uint32_t slot = atomicAdd(&sh.nrank, 1u);
-          if (slot < uint32_t(kTkRankCap)) sh.rank[slot] = record_key(rec);
-        }
-      }
-      if (!sub_all) {
-        // ---- K* among the candidates
-        __syncthreads();
-        const uint32_t nr = sh.nrank;
-        if (nr <= uint32_t(kTkThreads)) {
-          // keys are unique: exactly one candidate has need1 - 1 candidates above it
-          if (uint32_t(tid) < nr) {
-            const uint64_t mine = sh.rank[tid];
-            uint32_t above = 0;
-            for (uint32_t j = 0; j < nr; ++j) above += sh.rank[j] > mine ? 1u : 0u;
-            if (above == need1 - 1) sh.kstar = mine;
+      // ---- stage entries at or above the threshold bin, compacted in entry order
+      uint32_t staged = 0;  // block-uniform running count
+      int64_t c = 0;
+      bool aborted = false;
+      for (; c < nch; ++c) {
+        const int64_t i = e0 + c * kTkCh + int64_t(kTkPer) * tid;
+        uint32_t raw[kTkPer];
+        int32_t idv[kTkPer];
+        bool ok = true;
+        if (ring) {
+          const uint32_t n_ = first + uint32_t(c);
+          ok = mbar_wait(&sh.full[n_ % kTkStages], (n_ / kTkStages) & 1u, &sh.abort, err);
+          const uint8_t* stage = dyn + size_t(n_ % kTkStages) * kTkCh * 4 + size_t(kTkPer) * 4 * tid;
+  #pragma unroll
+          for (int v = 0; v < kTkPer / 4; ++v) {
+            const uint4 x = reinterpret_cast<const uint4*>(stage)[v];
+            raw[4 * v] = x.x, raw[4 * v + 1] = x.y, raw[4 * v + 2] = x.z, raw[4 * v + 3] = x.w;
+            if (kIds) {
+              const int4 y = reinterpret_cast<const int4*>(stage + size_t(kTkStages) * kTkCh * 4)[v];
+              idv[4 * v] = y.x, idv[4 * v + 1] = y.y, idv[4 * v + 2] = y.z, idv[4 * v + 3] = y.w;
+            }
           }
-          __syncthreads();
-          kstar = sh.kstar;
-        } else if (nr <= uint32_t(kTkRankCap)) {
-          kstar = resolve_kstar([&](int64_t j) { return sh.rank[j]; }, nr, prefix1, need1, 2, sh);
         } else {
-          auto row_key = [&](int64_t j) -> uint64_t {
-            const uint32_t u = entry_key(srow, irow, j);
-            const int32_t id = kIds ? irow[j] : int32_t(id_base + j);
-            return u ? composite(u, 0x7fffffffu - uint32_t(id)) : 0ull;
-          };
-          kstar = resolve_kstar(row_key, n, prefix1, need1, 2, sh);
-        }
-      }
-      // ---- ordered output: one block scan of the per-thread counts; the ids (and
-      // scores) are gathered in shared memory, then leave in 16-byte stores
-      uint32_t mask = sure;
-      for (uint32_t c = cand; c; c &= c - 1) {
-        const uint32_t j = __ffs(c) - 1;
-        if (record_key(recs[f0 + j]) >= kstar) mask |= 1u << j;
-      }
-      uint32_t total_sel = 0;
-      uint32_t pos = block_excl_scan(__popc(mask), total_sel, sh);
-      const bool gather = k <= (osrow != nullptr ? kTkRankCap : 2 * kTkRankCap) && (k & 3) == 0 &&
-                          (reinterpret_cast<uintptr_t>(orow) & 15u) == 0 &&
-                          (reinterpret_cast<uintptr_t>(osrow) & 15u) == 0;
-      int32_t* gid = reinterpret_cast<int32_t*>(sh.rank);
-      float* gsc = reinterpret_cast<float*>(sh.rank) + k;
-      while (mask) {
-        const uint32_t j = __ffs(mask) - 1;
-        mask &= mask - 1;
-        if (pos < uint32_t(k)) {
-          const uint64_t rec = recs[f0 + j];
-          const int32_t id = int32_t(0x7fffffffu - (uint32_t(rec) & 0x7fffffffu));
-          const float sc = __uint_as_float(uint32_t(rec >> 31));
-          if (gather) {
-            gid[pos] = id;
-            if (osrow != nullptr) gsc[pos] = sc;
-          } else {
-            orow[pos] = id;
-            if (osrow != nullptr) osrow[pos] = sc;
+  #pragma unroll
+          for (int q = 0; q < kTkPer; ++q) {
+            const bool in = i + q < e1;
+            raw[q] = in ? __float_as_uint(srow[i + q]) : 0u;
+            if (kIds) idv[q] = in ? irow[i + q] : -1;
           }
         }
-        ++pos;
+        uint32_t mask = 0;
+  #pragma unroll
+        for (int q = 0; q < kTkPer; ++q) {
+          const uint32_t u = rank_u(raw[q]);
+          const bool present = ok && i + q < e1 && (!kIds || idv[q] >= 0);
+          const bool keep = present && (take_all || (u >> 21) >= s0.bin);
+          if (kIds && present && idv[q] == 0x7fffffff) flag(err, DSR_ERR_ID);  // reserved for the pad record
+          if (keep && !whole_bin && (u >> 21) == s0.bin) atomicAdd(h1row + ((u >> 10) & (kTkBins - 1)), 1u);
+          mask |= uint32_t(keep) << q;
+        }
+        const uint32_t cnt = __popc(mask);
+        uint32_t incl = cnt;
+  #pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
+          if (lane >= o) incl += y;
+        }
+        if (lane == 31) sh.tot[c & 1][warp] = incl;
+        if (__syncthreads_or(!ok)) {  // a copy never landed: every thread leaves together
+          aborted = true;
+          break;
+        }
+        if (ring && tid == 0 && c + kTkStages < nch) issue(c + kTkStages);  // this stage is consumed
+        uint32_t before = 0, all = 0;
+  #pragma unroll
+        for (int w = 0; w < kTkWarps; ++w) {
+          const uint32_t t = sh.tot[c & 1][w];
+          before += w < warp ? t : 0u;
+          all += t;
+        }
+        uint32_t pos = staged + before + incl - cnt;
+  #pragma unroll
+        for (int q = 0; q < kTkPer; ++q)
+          if ((mask >> q) & 1u) {
+            const uint32_t id = kIds ? uint32_t(idv[q]) : uint32_t(id_base + i + q);
+            srec[e0 + pos] = (uint64_t(raw[q]) << 31) | uint64_t(0x7fffffffu - id);
+            ++pos;
+          }
+        staged += all;
       }
-      if (gather) {
-        const uint32_t got = total_sel < uint32_t(k) ? total_sel : uint32_t(k);
-        for (uint32_t p = got + tid; p < uint32_t(k); p += kTkThreads) {
-          gid[p] = -1;
-          if (osrow != nullptr) gsc[p] = -CUDART_INF_F;
+      if (aborted) {
+        // wait (bounded) for the copies still in flight, then leave; the status is set
+        if (ring && tid == 0)
+          for (int64_t d = c; d < nch && d < c + kTkStages; ++d) {
+            const uint32_t n_ = first + uint32_t(d);
+            mbar_drain(&sh.full[n_ % kTkStages], (n_ / kTkStages) & 1u);
+          }
+        return;
+      }
+      // an even count keeps every CTA's records 16-byte aligned for the last CTA's
+      // copies; the pad record is 0, which no entry produces (ids < 2^31 - 1)
+      if (staged & 1u) {
+        if (tid == 0) srec[e0 + staged] = 0ull;
+        ++staged;
+      }
+      if (tid == 0) gcnt[r * kTkMaxCtas + (cta - first_cta)] = staged;
+
+      // ---- ticket: the last CTA of the row finishes it.  The barrier orders every
+      // thread's records and counts before thread 0's acq_rel ticket (cumulative at
+      // gpu scope); the last CTA's acquire and barrier order its reads after all.
+      __syncthreads();
+      if (tid == 0) sh.last = ticket_add(gdone + r) == touching - 1 ? 1u : 0u;
+      __syncthreads();
+      if (sh.last) {
+        won |= 1u << uint32_t(r - rg);
+        if (tid == 0) {
+          sh.rbin[r - rg] = s0.bin;
+          sh.rneed[r - rg] = need0;
+          sh.rwhole[r - rg] = whole_bin ? 1u : 0u;
+        }
+      }
+    }
+    __syncthreads();
+    // ---- then the rows this CTA finishes
+    for (uint32_t pend = won; pend; pend &= pend - 1) {
+      const int64_t r = rg + (__ffs(pend) - 1);
+      const int64_t rb = r * L.words;
+      const int64_t n = row_length(lengths, r, row_stride);
+      const uint32_t first_cta = word_owner(rb, total_words, nctas);
+      const uint32_t touching = word_owner(rb + L.words - 1, total_words, nctas) - first_cta + 1;
+      const float* srow = scores + r * row_stride;
+      const int32_t* irow = kIds ? ids + r * row_stride : nullptr;
+      uint32_t* h0row = ghist + r * kTkBins;
+      uint32_t* h1row = ghist1 + r * kTkBins;
+      uint64_t* srec = gstage + r * L.sstride;
+      const uint32_t bin0 = sh.rbin[r - rg], need0 = sh.rneed[r - rg];
+      const bool whole_bin = sh.rwhole[r - rg] != 0u;
+
+      // other CTAs' counts, records and digit-1 counts are read from L2 (__ldcg, cp.async.cg)
+      uint32_t h1v[kTkBins / kTkThreads];
+      if (!whole_bin) {
+  #pragma unroll
+        for (int j = 0; j < kTkBins / kTkThreads; ++j) h1v[j] = __ldcg(h1row + j * kTkThreads + tid);
+      }
+      const uint32_t my_cnt = uint32_t(tid) < touching ? __ldcg(gcnt + r * kTkMaxCtas + tid) : 0u;
+      if (uint32_t(tid) < touching) {
+        int64_t cw0, cw1;
+        cta_words(total_words, first_cta + tid, nctas, cw0, cw1);
+        sh.e0s[tid] = uint32_t((cw0 > rb ? cw0 - rb : 0) * 32);
+      }
+      uint32_t total_staged = 0;
+      const uint32_t my_pre = block_excl_scan(my_cnt, total_staged, sh);
+      sh.pre[tid] = my_pre;
+      if (tid == 0) sh.pre[touching] = total_staged;
+      // (slots >= touching are never searched: pre[touching] bounds every walk)
+      __syncthreads();
+
+      // ---- up to kTkRecCap records: all of them into shared memory at once,
+      // every warp copying whole slots in 16-byte pieces (counts are even)
+      const bool in_smem = total_staged <= uint32_t(kTkRecCap);
+      uint64_t* recs = reinterpret_cast<uint64_t*>(dyn);
+      if (in_smem) {
+        // thread tid copies slot tid with one bulk copy; the barrier expects the
+        // row's bytes before any copy is issued (fence: the area was last written
+        // through the generic proxy)
+        if (tid == 0) {
+          fence_proxy_async_smem();
+          mbar_arrive_expect_tx(&sh.recbar, total_staged * 8u);
         }
         __syncthreads();
-        for (int p = 4 * tid; p < k; p += 4 * kTkThreads) {
-          *reinterpret_cast<int4*>(orow + p) = *reinterpret_cast<const int4*>(gid + p);
-          if (osrow != nullptr) *reinterpret_cast<float4*>(osrow + p) = *reinterpret_cast<const float4*>(gsc + p);
-        }
-        total_sel = uint32_t(k);  // the padding is written
-      }
-      chosen = total_sel < uint32_t(k) ? total_sel : uint32_t(k);
-    } else {
-      // ---- more records than shared memory holds (massively tied scores): walk
-      // them from L2 in chunks; a shared map gives every position of a chunk its
-      // slot, so consecutive threads load consecutive records
-      constexpr uint32_t kChunk = uint32_t(kTkThreads) * kTkRegs;
-      uint64_t rec[kTkRegs];
-      uint32_t loaded_c0 = 0xffffffffu;  // block-uniform
-      auto load_records = [&](uint32_t c0) {
-        if (loaded_c0 == c0) return;
-        loaded_c0 = c0;
-        __syncthreads();  // readers of the previous chunk's map are done
         if (uint32_t(tid) < touching) {
           const uint32_t b = sh.pre[tid], e = sh.pre[tid + 1];
-          const uint32_t lo = b > c0 ? b : c0, hi = e < c0 + kChunk ? e : c0 + kChunk;
-          for (uint32_t f = lo; f < hi; ++f) sh.map[f - c0] = uint8_t(tid);
+          if (e > b) bulk_load(smem_u32(recs + b), srec + sh.e0s[tid], (e - b) * 8u, &sh.recbar);
         }
+      }
+
+      // digit 1 of K* (while the copies fly)
+      uint32_t bin1 = 0, need1 = 0;
+      bool sub_all = true;  // every threshold-bin entry with digit 1 == bin1 is selected
+      if (!whole_bin) {
+  #pragma unroll
+        for (int j = 0; j < kTkBins / kTkThreads; ++j) sh.hist[j * kTkThreads + tid] = h1v[j];
         __syncthreads();
-#pragma unroll
-        for (int j = 0; j < kTkRegs; ++j) {
-          const uint32_t f = c0 + j * kTkThreads + tid;
-          if (f < total_staged) {
-            const uint32_t slot = sh.map[f - c0];
-            rec[j] = __ldcg(srec + sh.e0s[slot] + (f - sh.pre[slot]));
-          } else {
-            rec[j] = 0ull;
-          }
-        }
+        const Select s1 = block_find_bin(sh.hist, kTkBins, need0, sh);
+        bin1 = s1.bin;
+        need1 = need0 - s1.above;
+        sub_all = need1 == sh.hist[s1.bin];
+      }
+      const uint64_t prefix1 = (uint64_t(bin0) << kTkShift[0]) | (uint64_t(bin1) << kTkShift[1]);
+      if (tid == 0) {
+        sh.nrank = 0u;
+        sh.kstar = prefix1;
+      }
+      auto shares_two_digits = [&](uint64_t key) { return (key >> kTkShift[1]) == (prefix1 >> kTkShift[1]); };
+      auto selected = [&](uint64_t rec, uint64_t kstar) {
+        const uint64_t key = record_key(rec);
+        return rec != 0ull && (whole_bin || uint32_t(key >> kTkShift[0]) > bin0 || key >= kstar);
       };
-      if (!sub_all) {
-        __syncthreads();  // sh.nrank
-        for (uint32_t c0 = 0; c0 < total_staged; c0 += kChunk) {
-          load_records(c0);
-#pragma unroll
+      int32_t* orow = out_ids + r * k;
+      float* osrow = out_scores != nullptr ? out_scores + r * k : nullptr;
+      uint64_t kstar = prefix1;  // with sub_all: every key with those digits qualifies
+      uint32_t chosen = 0;
+
+      if (in_smem) {
+        const bool landed = mbar_wait(&sh.recbar, recphase & 1u, &sh.abort, err);
+        ++recphase;
+        if (__syncthreads_or(!landed)) {
+          if (tid == 0) mbar_drain(&sh.recbar, (recphase - 1) & 1u);
+          return;  // the status is set
+        }
+        // thread tid owns the contiguous records [f0, f0 + held); an odd run length
+        // keeps the 8-byte shared reads of a warp on distinct banks.  The passes are
+        // short loops: this code runs once per row on a cold instruction cache.
+        const uint32_t per = ((total_staged + kTkThreads - 1) / kTkThreads) | 1u;
+        const uint32_t f0 = tid * per < total_staged ? tid * per : total_staged;
+        const uint32_t held = total_staged - f0 < per ? total_staged - f0 : per;
+        // one pass: records surely selected (above K*'s two digits) and candidates
+        // (sharing them); candidates join the rank list
+        uint32_t sure = 0, cand = 0;
+        const uint32_t p01 = uint32_t(prefix1 >> kTkShift[1]);
+  #pragma unroll 3
+        for (uint32_t j = 0; j < held; ++j) {
+          const uint64_t rec = recs[f0 + j];
+          const uint32_t d01 = rank_u(uint32_t(rec >> 31)) >> 10;  // K*'s two digits: u >> 10
+          const bool is_cand = rec != 0ull && !whole_bin && d01 == p01;
+          sure |= uint32_t(rec != 0ull && (whole_bin || d01 > p01)) << j;
+          cand |= uint32_t(is_cand) << j;
+          if (is_cand && !sub_all) {
+            const uint32_t slot = atomicAdd(&sh.nrank, 1u);
+            if (slot < uint32_t(kTkRankCap)) sh.rank[slot] = record_key(rec);
+          }
+        }
+        if (!sub_all) {
+          // ---- K* among the candidates
+          __syncthreads();
+          const uint32_t nr = sh.nrank;
+          if (nr <= uint32_t(kTkThreads)) {
+            // keys are unique: exactly one candidate has need1 - 1 candidates above it
+            if (uint32_t(tid) < nr) {
+              const uint64_t mine = sh.rank[tid];
+              uint32_t above = 0;
+              for (uint32_t j = 0; j < nr; ++j) above += sh.rank[j] > mine ? 1u : 0u;
+              if (above == need1 - 1) sh.kstar = mine;
+            }
+            __syncthreads();
+            kstar = sh.kstar;
+          } else if (nr <= uint32_t(kTkRankCap)) {
+            kstar = resolve_kstar([&](int64_t j) { return sh.rank[j]; }, nr, prefix1, need1, 2, sh);
+          } else {
+            auto row_key = [&](int64_t j) -> uint64_t {
+              const uint32_t u = entry_key(srow, irow, j);
+              const int32_t id = kIds ? irow[j] : int32_t(id_base + j);
+              return u ? composite(u, 0x7fffffffu - uint32_t(id)) : 0ull;
+            };
+            kstar = resolve_kstar(row_key, n, prefix1, need1, 2, sh);
+          }
+        }
+        // ---- ordered output: one block scan of the per-thread counts; the ids (and
+        // scores) are gathered in shared memory, then leave in 16-byte stores
+        uint32_t mask = sure;
+        for (uint32_t c = cand; c; c &= c - 1) {
+          const uint32_t j = __ffs(c) - 1;
+          if (record_key(recs[f0 + j]) >= kstar) mask |= 1u << j;
+        }
+        uint32_t total_sel = 0;
+        uint32_t pos = block_excl_scan(__popc(mask), total_sel, sh);
+        const bool gather = k <= (osrow != nullptr ? kTkRankCap : 2 * kTkRankCap) && (k & 3) == 0 &&
+                            (reinterpret_cast<uintptr_t>(orow) & 15u) == 0 &&
+                            (reinterpret_cast<uintptr_t>(osrow) & 15u) == 0;
+        int32_t* gid = reinterpret_cast<int32_t*>(sh.rank);
+        float* gsc = reinterpret_cast<float*>(sh.rank) + k;
+        while (mask) {
+          const uint32_t j = __ffs(mask) - 1;
+          mask &= mask - 1;
+          if (pos < uint32_t(k)) {
+            const uint64_t rec = recs[f0 + j];
+            const int32_t id = int32_t(0x7fffffffu - (uint32_t(rec) & 0x7fffffffu));
+            const float sc = __uint_as_float(uint32_t(rec >> 31));
+            if (gather) {
+              gid[pos] = id;
+              if (osrow != nullptr) gsc[pos] = sc;
+            } else {
+              orow[pos] = id;
+              if (osrow != nullptr) osrow[pos] = sc;
+            }
+          }
+          ++pos;
+        }
+        if (gather) {
+          const uint32_t got = total_sel < uint32_t(k) ? total_sel : uint32_t(k);
+          for (uint32_t p = got + tid; p < uint32_t(k); p += kTkThreads) {
+            gid[p] = -1;
+            if (osrow != nullptr) gsc[p] = -CUDART_INF_F;
+          }
+          __syncthreads();
+          for (int p = 4 * tid; p < k; p += 4 * kTkThreads) {
+            *reinterpret_cast<int4*>(orow + p) = *reinterpret_cast<const int4*>(gid + p);
+            if (osrow != nullptr) *reinterpret_cast<float4*>(osrow + p) = *reinterpret_cast<const float4*>(gsc + p);
+          }
+          total_sel = uint32_t(k);  // the padding is written
+        }
+        chosen = total_sel < uint32_t(k) ? total_sel : uint32_t(k);
+      } else {
+        // ---- more records than shared memory holds (massively tied scores): walk
+        // them from L2 in chunks; a shared map gives every position of a chunk its
+        // slot, so consecutive threads load consecutive records
+        constexpr uint32_t kChunk = uint32_t(kTkThreads) * kTkRegs;
+        uint64_t rec[kTkRegs];
+        uint32_t loaded_c0 = 0xffffffffu;  // block-uniform
+        auto load_records = [&](uint32_t c0) {
+          if (loaded_c0 == c0) return;
+          loaded_c0 = c0;
+          __syncthreads();  // readers of the previous chunk's map are done
+          if (uint32_t(tid) < touching) {
+            const uint32_t b = sh.pre[tid], e = sh.pre[tid + 1];
+            const uint32_t lo = b > c0 ? b : c0, hi = e < c0 + kChunk ? e : c0 + kChunk;
+            for (uint32_t f = lo; f < hi; ++f) sh.map[f - c0] = uint8_t(tid);
+          }
+          __syncthreads();
+  #pragma unroll
           for (int j = 0; j < kTkRegs; ++j) {
-            const uint64_t key = record_key(rec[j]);
-            if (rec[j] != 0ull && shares_two_digits(key)) {
-              const uint32_t slot = atomicAdd(&sh.nrank, 1u);
-              if (slot < uint32_t(kTkRankCap)) sh.rank[slot] = key;
+            const uint32_t f = c0 + j * kTkThreads + tid;
+            if (f < total_staged) {
+              const uint32_t slot = sh.map[f - c0];
+              rec[j] = __ldcg(srec + sh.e0s[slot] + (f - sh.pre[slot]));
+            } else {
+              rec[j] = 0ull;
             }
           }
-        }
-        __syncthreads();
-        const uint32_t nr = sh.nrank;
-        if (nr <= uint32_t(kTkRankCap)) {
-          kstar = resolve_kstar([&](int64_t j) { return sh.rank[j]; }, nr, prefix1, need1, 2, sh);
-        } else {
-          auto row_key = [&](int64_t j) -> uint64_t {
-            const uint32_t u = entry_key(srow, irow, j);
-            const int32_t id = kIds ? irow[j] : int32_t(id_base + j);
-            return u ? composite(u, 0x7fffffffu - uint32_t(id)) : 0ull;
-          };
-          kstar = resolve_kstar(row_key, n, prefix1, need1, 2, sh);
-        }
-      }
-      // ---- keep the selected records in entry order and write them out
-      uint32_t written = 0;  // block-uniform
-      for (uint32_t c0 = 0; c0 < total_staged && written < uint32_t(k); c0 += kChunk) {
-        load_records(c0);  // the rank pass already holds a single chunk
-        unsigned bal[kTkRegs];
-#pragma unroll
-        for (int j = 0; j < kTkRegs; ++j) {
-          bal[j] = __ballot_sync(0xffffffffu, selected(rec[j], kstar));
-          if (lane == 0) sh.tot16[j][warp] = __popc(bal[j]);
-        }
-        __syncthreads();
-        uint32_t base = written;
-#pragma unroll
-        for (int j = 0; j < kTkRegs; ++j) {
-          uint32_t before = 0, all = 0;
-#pragma unroll
-          for (int w = 0; w < kTkWarps; ++w) {
-            const uint32_t t = sh.tot16[j][w];
-            before += w < warp ? t : 0u;
-            all += t;
-          }
-          if ((bal[j] >> lane) & 1u) {
-            const uint32_t pos = base + before + __popc(bal[j] & ((1u << lane) - 1u));
-            if (pos < uint32_t(k)) {
-              orow[pos] = int32_t(0x7fffffffu - (uint32_t(rec[j]) & 0x7fffffffu));
-              if (osrow != nullptr) osrow[pos] = __uint_as_float(uint32_t(rec[j] >> 31));
+        };
+        if (!sub_all) {
+          __syncthreads();  // sh.nrank
+          for (uint32_t c0 = 0; c0 < total_staged; c0 += kChunk) {
+            load_records(c0);
+  #pragma unroll
+            for (int j = 0; j < kTkRegs; ++j) {
+              const uint64_t key = record_key(rec[j]);
+              if (rec[j] != 0ull && shares_two_digits(key)) {
+                const uint32_t slot = atomicAdd(&sh.nrank, 1u);
+                if (slot < uint32_t(kTkRankCap)) sh.rank[slot] = key;
+              }
             }
           }
-          base += all;
+          __syncthreads();
+          const uint32_t nr = sh.nrank;
+          if (nr <= uint32_t(kTkRankCap)) {
+            kstar = resolve_kstar([&](int64_t j) { return sh.rank[j]; }, nr, prefix1, need1, 2, sh);
+          } else {
+            auto row_key = [&](int64_t j) -> uint64_t {
+              const uint32_t u = entry_key(srow, irow, j);
+              const int32_t id = kIds ? irow[j] : int32_t(id_base + j);
+              return u ? composite(u, 0x7fffffffu - uint32_t(id)) : 0ull;
+            };
+            kstar = resolve_kstar(row_key, n, prefix1, need1, 2, sh);
+          }
         }
-        written = base;
-        __syncthreads();  // sh.tot16 is reused by the next chunk
+        // ---- keep the selected records in entry order and write them out
+        uint32_t written = 0;  // block-uniform
+        for (uint32_t c0 = 0; c0 < total_staged && written < uint32_t(k); c0 += kChunk) {
+          load_records(c0);  // the rank pass already holds a single chunk
+          unsigned bal[kTkRegs];
+  #pragma unroll
+          for (int j = 0; j < kTkRegs; ++j) {
+            bal[j] = __ballot_sync(0xffffffffu, selected(rec[j], kstar));
+            if (lane == 0) sh.tot16[j][warp] = __popc(bal[j]);
+          }
+          __syncthreads();
+          uint32_t base = written;
+  #pragma unroll
+          for (int j = 0; j < kTkRegs; ++j) {
+            uint32_t before = 0, all = 0;
+  #pragma unroll
+            for (int w = 0; w < kTkWarps; ++w) {
+              const uint32_t t = sh.tot16[j][w];
+              before += w < warp ? t : 0u;
+              all += t;
+            }
+            if ((bal[j] >> lane) & 1u) {
+              const uint32_t pos = base + before + __popc(bal[j] & ((1u << lane) - 1u));
+              if (pos < uint32_t(k)) {
+                orow[pos] = int32_t(0x7fffffffu - (uint32_t(rec[j]) & 0x7fffffffu));
+                if (osrow != nullptr) osrow[pos] = __uint_as_float(uint32_t(rec[j] >> 31));
+              }
+            }
+            base += all;
+          }
+          written = base;
+          __syncthreads();  // sh.tot16 is reused by the next chunk
+        }
+        chosen = written < uint32_t(k) ? written : uint32_t(k);
       }
-      chosen = written < uint32_t(k) ? written : uint32_t(k);
+      for (int p = int(chosen) + tid; p < k; p += kTkThreads) {
+        orow[p] = -1;
+        if (osrow != nullptr) osrow[p] = -CUDART_INF_F;
+      }
+      // every CTA of the row is done with its state: clear it for the next call
+  #pragma unroll
+      for (int j = 0; j < kTkBins / kTkThreads; ++j) {
+        h0row[j * kTkThreads + tid] = 0u;
+        h1row[j * kTkThreads + tid] = 0u;
+      }
+      if (tid == 0) gdone[r] = 0u;
+      __syncthreads();  // the record area and the ring are reused by the next row
     }
-    for (int p = int(chosen) + tid; p < k; p += kTkThreads) {
-      orow[p] = -1;
-      if (osrow != nullptr) osrow[p] = -CUDART_INF_F;
-    }
-    // every CTA of the row is done with its state: clear it for the next call
-#pragma unroll
-    for (int j = 0; j < kTkBins / kTkThreads; ++j) {
-      h0row[j * kTkThreads + tid] = 0u;
-      h1row[j * kTkThreads + tid] = 0u;
-    }
-    if (tid == 0) gdone[r] = 0u;
-    __syncthreads();  // the record area and the ring are reused by the next row
   }
 }
 
@@ -976,11 +1012,9 @@ __global__ void __launch_bounds__(kMgThreads) merge_select_kernel(const int32_t*
                                                                   int world, int rows, int k,
                                                                   int32_t* __restrict__ out_ids) {
   __shared__ uint32_t hist[kTkBins];
-  __shared__ uint32_t wsum[kMgWarps];
-  __shared__ uint64_t wmin[kMgWarps], wmax[kMgWarps];
-  __shared__ uint64_t cand[kMgRankCap];
-  __shared__ uint64_t kstar_s;
-  __shared__ uint32_t result[2], ncand;
+  __shared__ uint32_t wsum[kMgWarps], wmin[kMgWarps], wmax[kMgWarps];
+  __shared__ uint32_t cand[kMgRankCap];
+  __shared__ uint32_t result[2], ncand, ustar_s, needt_s;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int r = blockIdx.x;
   const int n = world * k;
@@ -1016,96 +1050,111 @@ __global__ void __launch_bounds__(kMgThreads) merge_select_kernel(const int32_t*
       idv[j] = __ldg(src + int64_t(rows) * k);
     }
   }
-  uint64_t key[E];
-  uint32_t mine = 0;
-  uint64_t kmin = ~0ull, kmax = 0ull;
+  // score keys (0: absent; present keys are >= 0x007fffff), their count and range
+  uint32_t u[E];
+  uint32_t mine = 0, umin = 0xffffffffu, umax = 0u;
 #pragma unroll
   for (int j = 0; j < E; ++j) {
     const bool present = e0 + j < n && idv[j] >= 0;
-    key[j] = present ? composite(rank_u(raw[j]), 0x7fffffffu - uint32_t(idv[j])) : 0ull;
-    if (present) {
-      ++mine;
-      kmin = key[j] < kmin ? key[j] : kmin;
-      kmax = key[j] > kmax ? key[j] : kmax;
-    }
+    u[j] = present ? rank_u(raw[j]) : 0u;
+    mine += present ? 1u : 0u;
+    umin = present && u[j] < umin ? u[j] : umin;
+    umax = u[j] > umax ? u[j] : umax;
   }
-  // present entries in the row and the range of their keys
 #pragma unroll
   for (int o = 16; o; o >>= 1) {
     mine += __shfl_xor_sync(0xffffffffu, mine, o);
-    const uint64_t a = __shfl_xor_sync(0xffffffffu, kmin, o), b = __shfl_xor_sync(0xffffffffu, kmax, o);
-    kmin = a < kmin ? a : kmin;
-    kmax = b > kmax ? b : kmax;
+    umin = min(umin, __shfl_xor_sync(0xffffffffu, umin, o));
+    umax = max(umax, __shfl_xor_sync(0xffffffffu, umax, o));
   }
   if (lane == 0) {
     wsum[warp] = mine;
-    wmin[warp] = kmin;
-    wmax[warp] = kmax;
+    wmin[warp] = umin;
+    wmax[warp] = umax;
   }
   __syncthreads();
   uint32_t present = wsum[lane];
-  kmin = wmin[lane];
-  kmax = wmax[lane];
+  umin = wmin[lane];
+  umax = wmax[lane];
 #pragma unroll
   for (int o = 16; o; o >>= 1) {
     present += __shfl_xor_sync(0xffffffffu, present, o);
-    const uint64_t a = __shfl_xor_sync(0xffffffffu, kmin, o), b = __shfl_xor_sync(0xffffffffu, kmax, o);
-    kmin = a < kmin ? a : kmin;
-    kmax = b > kmax ? b : kmax;
+    umin = min(umin, __shfl_xor_sync(0xffffffffu, umin, o));
+    umax = max(umax, __shfl_xor_sync(0xffffffffu, umax, o));
   }
   __syncthreads();
 
-  // radix select over the remaining key range [lo, lo + span], 2048 equal bins a
-  // level (the merged lists hold each shard's best scores only, so fixed float
-  // digits would pile them into a few bins); selected = {key >= thr}
-  uint64_t thr = 1ull;  // take_all: every present key (key > 0) passes
+  // threshold score key u* and how many entries equal to it are taken (need_t):
+  // selected = {u > u*} + the first need_t entries with u == u* in entry order,
+  // which is the reference's lower-id-first rule for equal scores.  Each radix
+  // level bins the remaining range [lo, lo + span] into 2048 equal bins.
+  uint32_t ustar = 0u, need_t = 0u;  // take_all: every present entry (u > 0)
   if (present > uint32_t(k)) {
     uint32_t need = uint32_t(k);
-    uint64_t lo = kmin, span = kmax - kmin;
-    for (int level = 0; level < 8; ++level) {
-      const int bits = span ? 64 - __clzll(static_cast<long long>(span)) : 0;
+    uint32_t lo = umin, span = umax - umin;
+    for (int level = 0; level < 4; ++level) {
+      const int bits = span ? 32 - __clz(span) : 0;
       const int sh = bits > 11 ? bits - 11 : 0;
       for (int i = tid; i < kTkBins; i += kMgThreads) hist[i] = 0u;
       __syncthreads();
 #pragma unroll
       for (int j = 0; j < E; ++j)
-        if (key[j] >= lo && key[j] - lo <= span) atomicAdd(&hist[uint32_t((key[j] - lo) >> sh)], 1u);
+        if (u[j] >= lo && u[j] - lo <= span) atomicAdd(&hist[(u[j] - lo) >> sh], 1u);
       __syncthreads();
       uint32_t above;
       const uint32_t b = merge_find_bin(hist, kTkBins, need, above, wsum, result);
       need -= above;
-      thr = lo + (uint64_t(b) << sh);
+      const uint32_t thr = lo + (b << sh);
       const uint32_t inbin = hist[b];
       if (tid == 0) ncand = 0u;
       __syncthreads();  // hist is cleared by the next level
-      if (inbin == need || sh == 0) break;  // the whole sub-range is selected
-      const uint64_t width = (uint64_t(1) << sh) - 1;
-      span = span - (uint64_t(b) << sh) < width ? span - (uint64_t(b) << sh) : width;
+      if (inbin == need) {  // the whole sub-range is taken
+        ustar = thr - 1u;
+        break;
+      }
+      if (sh == 0) {  // one score value: its first `need` entries are taken
+        ustar = thr;
+        need_t = need;
+        break;
+      }
+      const uint32_t width = (1u << sh) - 1u;
+      span = span - (b << sh) < width ? span - (b << sh) : width;
       lo = thr;
       if (inbin <= uint32_t(kMgRankCap)) {
-        // few keys left in the bin: K* is the one with need - 1 of them above it
+        // few keys in the bin: u* is the one with fewer than `need` keys above it
+        // and at least `need` at or above it
 #pragma unroll
         for (int j = 0; j < E; ++j)
-          if (key[j] >= lo && key[j] - lo <= span) cand[atomicAdd(&ncand, 1u)] = key[j];
+          if (u[j] >= lo && u[j] - lo <= span) cand[atomicAdd(&ncand, 1u)] = u[j];
         __syncthreads();
         if (uint32_t(tid) < inbin) {
-          const uint64_t mine = cand[tid];
-          uint32_t more = 0;
-          for (uint32_t j = 0; j < inbin; ++j) more += cand[j] > mine ? 1u : 0u;
-          if (more == need - 1) kstar_s = mine;
+          const uint32_t me = cand[tid];
+          uint32_t gt = 0, ge = 0;
+          for (uint32_t j = 0; j < inbin; ++j) {
+            gt += cand[j] > me ? 1u : 0u;
+            ge += cand[j] >= me ? 1u : 0u;
+          }
+          if (gt < need && need <= ge) {
+            ustar_s = me;
+            needt_s = need - gt;
+          }
         }
         __syncthreads();
-        thr = kstar_s;
+        ustar = ustar_s;
+        need_t = needt_s;
         break;
       }
     }
   }
 
-  // ordered compaction: one block scan of the per-thread counts
-  uint32_t mask = 0;
+  // ordered compaction: one block scan of packed (taken-above << 16 | ties) counts
+  uint32_t sure = 0, tie = 0;
 #pragma unroll
-  for (int j = 0; j < E; ++j) mask |= uint32_t(key[j] != 0ull && key[j] >= thr) << j;
-  const uint32_t c = __popc(mask);
+  for (int j = 0; j < E; ++j) {
+    sure |= uint32_t(u[j] != 0u && u[j] > ustar) << j;
+    tie |= uint32_t(u[j] != 0u && u[j] == ustar) << j;
+  }
+  const uint32_t c = (uint32_t(__popc(sure)) << 16) | uint32_t(__popc(tie));
   uint32_t incl = c;
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
@@ -1120,15 +1169,21 @@ __global__ void __launch_bounds__(kMgThreads) merge_select_kernel(const int32_t*
     const uint32_t x = __shfl_up_sync(0xffffffffu, wincl, o);
     if (lane >= o) wincl += x;
   }
-  const uint32_t total = __shfl_sync(0xffffffffu, wincl, 31);
-  uint32_t pos = __shfl_sync(0xffffffffu, wincl - wv, warp) + incl - c;
+  const uint32_t tot = __shfl_sync(0xffffffffu, wincl, 31);
+  const uint32_t excl = __shfl_sync(0xffffffffu, wincl - wv, warp) + incl - c;
+  uint32_t ties_before = excl & 0xffffu;
+  uint32_t pos = (excl >> 16) + (ties_before < need_t ? ties_before : need_t);
+  const uint32_t total = (tot >> 16) + ((tot & 0xffffu) < need_t ? (tot & 0xffffu) : need_t);
   int32_t* orow = out_ids + int64_t(r) * k;
 #pragma unroll
-  for (int j = 0; j < E; ++j)
-    if ((mask >> j) & 1u) {
-      if (pos < uint32_t(k)) orow[pos] = int32_t(0x7fffffffu - (uint32_t(key[j]) & 0x7fffffffu));
+  for (int j = 0; j < E; ++j) {
+    bool take = (sure >> j) & 1u;
+    if ((tie >> j) & 1u) take = ties_before++ < need_t;
+    if (take) {
+      if (pos < uint32_t(k)) orow[pos] = idv[j];
       ++pos;
     }
+  }
   for (int p = int(total < uint32_t(k) ? total : uint32_t(k)) + tid; p < k; p += kMgThreads) orow[p] = -1;
 }
 
