@@ -57,6 +57,12 @@ SIGNATURES = {
                                     _P, _P, c_int64, _P]),
     "dsr_lse_combine": (c_int, [_P, _P, _P, c_int64, _P, _P, _P, _P, _P, c_int64, c_int64, c_int64,
                                 _P]),
+    "dsr_p2p_buffer_bytes": (c_size_t, [c_int64, c_int64]),
+    "dsr_p2p_alloc": (c_int, [c_size_t, _P, _P]),
+    "dsr_p2p_open": (c_int, [_P, _P]),
+    "dsr_p2p_close": (c_int, [_P]),
+    "dsr_p2p_free": (c_int, [_P]),
+    "dsr_p2p_allgather": (c_int, [_P, c_int64, _P, c_int64, c_int64, c_int64, c_int64, _P, _P]),
     "dsr_decode_workspace_bytes": (c_size_t, [c_int64, c_int64, c_int64, c_int64]),
     "dsr_decode_step": (c_int, [_P, _P, c_int64, _P, _P, _P, c_int64, c_int64, _P, c_int64, _P,
                                 c_int64, c_int64, _P, _P, _P, c_float, _P, _P, _P, _P, c_size_t, _P,

@@ -125,6 +125,90 @@ def all_gather(tensor: torch.Tensor, group=None) -> torch.Tensor:
     return out
 
 
+class _DeviceView:
+    """A raw device allocation as a torch tensor (CUDA array interface)."""
+
+    def __init__(self, ptr: int, shape, typestr: str):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr, "data": (ptr, False),
+                                         "version": 3, "strides": None}
+
+
+class PeerExchange:
+    """All-gather of one fixed-size payload per rank over NVLink peer mappings.
+
+    Every rank allocates an exchange buffer (dsr_p2p_alloc), the 64-byte CUDA IPC
+    handles travel through the process group once (all_gather_object), and each
+    rank maps its peers' buffers (dsr_p2p_open).  `all_gather(payload)` launches
+    dsr_p2p_allgather on the stream: the payload of rank r lands in slot r of every
+    rank's buffer, and the returned tensor (`gathered`, rank-major, the same
+    memory every call) is complete when that kernel is.  No collective library
+    runs per step; the kernels are capturable in a CUDA graph.  All ranks must
+    issue the same exchanges in the same order, as the collective would require.
+    """
+
+    def __init__(self, payload_shape, dtype: torch.dtype, device, group=None, chunks: int | None = None):
+        import ctypes
+        self.group = group
+        self.world, self.rank = dist.get_world_size(group), dist.get_rank(group)
+        if not 1 <= self.world <= 8:
+            raise ValueError("the peer exchange spans 1 to 8 ranks of one node")
+        self.lib = _native.library()
+        self.dtype, self.payload_shape = dtype, tuple(payload_shape)
+        numel = 1
+        for d in self.payload_shape:
+            numel *= d
+        self.payload_bytes = numel * torch.empty((), dtype=dtype).element_size()
+        if self.payload_bytes % 16:
+            raise ValueError("exchange payloads are whole 16-byte units")
+        self.chunks = chunks or max(1, min(16, self.payload_bytes // 65536))
+        size = self.lib.dsr_p2p_buffer_bytes(self.world, self.payload_bytes)
+        buf = ctypes.c_void_p()
+        handle = (ctypes.c_uint8 * 64)()
+        _native.call("dsr_p2p_alloc", size, ctypes.addressof(buf), ctypes.addressof(handle))
+        self._local = buf.value
+        handles = [None] * self.world
+        dist.all_gather_object(handles, bytes(handle), group=group)
+        self._opened = []
+        ptrs = []
+        for w, h in enumerate(handles):
+            if w == self.rank:
+                ptrs.append(self._local)
+                continue
+            peer = ctypes.c_void_p()
+            raw = (ctypes.c_uint8 * 64).from_buffer_copy(h)
+            _native.call("dsr_p2p_open", ctypes.addressof(raw), ctypes.addressof(peer))
+            self._opened.append(peer.value)
+            ptrs.append(peer.value)
+        self._ptrs = (ctypes.c_void_p * self.world)(*ptrs)
+        typestr = {torch.int32: "<i4", torch.float32: "<f4"}[dtype]
+        self.gathered = torch.as_tensor(
+            _DeviceView(self._local + 256, (self.world,) + self.payload_shape, typestr), device=device)
+        self.err = torch.zeros(1, dtype=torch.int32, device=device)
+        dist.barrier(group)  # every peer mapping exists before the first exchange
+
+    def all_gather(self, payload: torch.Tensor, stream=None) -> torch.Tensor:
+        if payload.dtype != self.dtype or tuple(payload.shape) != self.payload_shape or not payload.is_contiguous():
+            raise ValueError("payload does not match the exchange's shape and dtype")
+        import ctypes
+        _native.call("dsr_p2p_allgather", payload.data_ptr(), self.payload_bytes,
+                     ctypes.cast(self._ptrs, ctypes.c_void_p), self.rank, self.world, self.payload_bytes,
+                     self.chunks, self.err.data_ptr(), _native.stream_handle(stream))
+        return self.gathered
+
+    def close(self) -> None:
+        """After every rank's last exchange has completed (a barrier), unmap and free."""
+        if self._local is None:
+            return
+        torch.cuda.synchronize()
+        dist.barrier(self.group)
+        for peer in self._opened:
+            _native.call("dsr_p2p_close", peer)
+        self._opened = []
+        self.gathered = None
+        _native.call("dsr_p2p_free", self._local)
+        self._local = None
+
+
 # ------------------------------------------------------------- per-rank step
 
 
@@ -190,13 +274,35 @@ class ShardedDecoder:
                      p(self.err), self.batch, self.heads, _native.stream_handle(stream))
         return self.out
 
+    def use_peer_exchange(self, group=None) -> None:
+        """Exchange lists and partials over NVLink peer mappings instead of the
+        collective library (every rank of `group` on this node)."""
+        dev = self.err.device
+        self.exchanges = (PeerExchange(tuple(self.send_lists.shape), torch.int32, dev, group),
+                          PeerExchange(tuple(self.send_partial.shape), torch.float32, dev, group))
+
+    def close(self) -> None:
+        for x in getattr(self, "exchanges", ()) or ():
+            x.close()
+        self.exchanges = None
+
+    def _gather(self, which: int, payload, group, stream):
+        exchanges = getattr(self, "exchanges", None)
+        if exchanges:
+            return exchanges[which].all_gather(payload, stream)
+        return all_gather(payload, group)
+
+    def exchange_status(self) -> int:
+        """Worst device status of the peer exchanges (0 without them)."""
+        return max((int(x.err.item()) for x in getattr(self, "exchanges", ()) or ()), default=0)
+
     def step(self, inputs, group=None, stream=None):
-        """One full decode step with the two all-gathers; returns out f32[B, H, 512]."""
+        """One full decode step with the two exchanges; returns out f32[B, H, 512]."""
         lists = self.select_local(inputs["idx_q"], inputs["idx_w"], inputs["index_pool"],
                                   inputs["block_table"], stream)
-        self.merge(all_gather(lists, group), stream)
+        self.merge(self._gather(0, lists, group, stream), stream)
         partial = self.attend_local(inputs["q"], inputs["kv_pool"], inputs["block_table"], inputs["swa"], stream)
-        return self.combine(all_gather(partial, group), stream)
+        return self.combine(self._gather(1, partial, group, stream), stream)
 
 
 # ------------------------------------------------------------------ inputs
@@ -317,8 +423,8 @@ def single_gpu_base(steps: int, warmup: int, device) -> dict:
 
 
 # kernels of this library launched per sharded step: indexer, local top-k,
-# list gather + histogram + top-k of the merge, MLA partial (tiles + in-shard
-# combine), cross-shard combine
+# list exchange, merge, MLA partial (tiles + in-shard combine), partial
+# exchange, cross-shard combine
 LAUNCHES_PER_STEP = 8
 
 
@@ -342,14 +448,21 @@ def bench_main(args, metric: str) -> None:
         plan = ShardPlan(world, rank, tuple([cfg.context] * cfg.batch))
         inputs = make_shard_inputs(cfg, plan, dev)
         dec = ShardedDecoder(plan, cfg.heads, cfg.idx_heads, cfg.topk, cfg.scale, inputs["sink"], dev)
+        # the two exchanges: NVLink peer stores (default) or the collective library
+        exchange = os.environ.get("DSR_EXCHANGE", "peer")
+        if exchange == "peer" and world > 1:
+            dec.use_peer_exchange()
+        else:
+            exchange = "nccl"
         stream = torch.cuda.Stream(device=dev)
         with torch.cuda.stream(stream):
             for _ in range(args.warmup):
                 dec.step(inputs, stream=stream)
         torch.cuda.synchronize()
-        assert int(dec.err.item()) == 0, f"rank {rank}: device status {int(dec.err.item())}"
-        # one step (kernels and both NCCL all-gathers) as a CUDA graph; every rank
-        # captures, so the collectives line up; eager steps if capture is refused
+        assert int(dec.err.item()) == 0 and dec.exchange_status() == 0, \
+            f"rank {rank}: device status {int(dec.err.item())}/{dec.exchange_status()}"
+        # one step (kernels and both exchanges) as a CUDA graph; every rank
+        # captures, so the exchanges line up; eager steps if capture is refused
         graph = _capture(lambda: dec.step(inputs, stream=stream), stream)
         run = (lambda i: graph.replay()) if graph is not None else (lambda i: dec.step(inputs, stream=stream))
         step_ms = _timed_steps(run, args.steps, stream, dev)
@@ -380,8 +493,9 @@ def bench_main(args, metric: str) -> None:
         e2e_run = (lambda i: e2e_graph.replay()) if e2e_graph is not None else e2e_step
         e2e_ms = _timed_steps(e2e_run, args.steps, stream, dev)
         torch.cuda.synchronize()
-        assert int(dec.err.item()) == 0
-        graph = e2e_graph = None  # graphs holding NCCL work go before the process group
+        assert int(dec.err.item()) == 0 and dec.exchange_status() == 0
+        graph = e2e_graph = None  # graphs holding collective work go before the process group
+        dec.close()
         if rank == 0:
             from .workloads import algorithmic_bytes
             total_bytes = algorithmic_bytes(list(plan.lengths), cfg.heads, cfg.topk, cfg.idx_heads)
@@ -392,7 +506,9 @@ def bench_main(args, metric: str) -> None:
                 "data": "synthetic (seeded N(0,1), BF16 pools per rank)",
                 "config": {"workload": cfg.name + f", sharded over {world} GPUs", "batch": cfg.batch,
                            "context": cfg.context, "topk": cfg.topk, "heads": cfg.heads,
-                           "l2": "inputs larger than L2 on every rank", "parallelism": f"sequence shards x{world}"},
+                           "l2": "inputs larger than L2 on every rank", "parallelism": f"sequence shards x{world}",
+                           "exchange": ("NVLink peer stores (dsr_p2p_allgather)" if exchange == "peer"
+                                        else "NCCL all_gather")},
                 "step_hbm": {"bytes": total_bytes,
                              "achieved_gbs": round(total_bytes / (step_ms * 1e-3) / 1e9, 1)},
                 "e2e": {"value": round(e2e_ms * 1e3, 3), "unit": "us",

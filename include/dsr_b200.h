@@ -302,6 +302,32 @@ int dsr_decode_step(const float* idx_q, const float* idx_w, int64_t idx_heads,
                     float* scores_out, void* workspace, size_t workspace_bytes,
                     int32_t* err, int64_t batch, void* stream);
 
+/* ---------------------------------------------------------------------------
+ * NVLink peer exchange for the sequence-sharded step (one process per GPU).
+ * Replaces the collective library's all_gather at the two exchange points of a
+ * decode step (torch.distributed.all_gather_into_tensor in the reference-style
+ * host plumbing): rank r's payload lands in slot r of every rank's exchange
+ * buffer through CUDA IPC peer mappings, written with plain stores; arrival
+ * counters (system-scope release/acquire) signal completion, and the waiting
+ * side gives up after a bounded time with DSR_ERR_TIMEOUT in *err.
+ * Buffer layout: 256 control bytes, then world slots of slot_bytes
+ * (slot r at byte 256 + r * slot_bytes).  Every rank allocates one buffer per
+ * exchange (dsr_p2p_alloc, zeroed), shares the 64-byte IPC handle with its
+ * peers, and maps theirs (dsr_p2p_open).  buffers[w] is rank w's buffer as
+ * mapped in this process (buffers[rank] the local one); the host array is read
+ * at launch.  All ranks must issue the same exchanges in the same order.
+ * ------------------------------------------------------------------------- */
+#define DSR_P2P_MAX_WORLD 8
+#define DSR_P2P_HANDLE_BYTES 64
+size_t dsr_p2p_buffer_bytes(int64_t world, int64_t slot_bytes);
+int dsr_p2p_alloc(size_t bytes, void** buffer, uint8_t* ipc_handle);
+int dsr_p2p_open(const uint8_t* ipc_handle, void** peer_buffer);
+int dsr_p2p_close(void* peer_buffer);
+int dsr_p2p_free(void* buffer);
+int dsr_p2p_allgather(const void* payload, int64_t payload_bytes, void* const* buffers,
+                      int64_t rank, int64_t world, int64_t slot_bytes, int64_t chunks,
+                      int32_t* err, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

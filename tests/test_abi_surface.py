@@ -56,6 +56,10 @@ def test_torch_extension_keeps_reference_op_names():
     lambda n: n.dsr_indexer_decode(16, 16, 16, 1, 1, 1, 1, 1, 64, 1, 1, 48, None),
     # null pointers
     lambda n: n.dsr_append_kv_index(None, 1, 1, 1, 1, 1, 1, 1, 1, 1, 1, 1, None, 1, 1, None),
+    # peer exchange: no buffer table, more than 8 ranks, payload not in 16-byte units
+    lambda n: n.dsr_p2p_allgather(16, 64, None, 0, 2, 64, 1, 16, None),
+    lambda n: n.dsr_p2p_allgather(16, 64, 16, 0, 9, 64, 1, 16, None),
+    lambda n: n.dsr_p2p_allgather(16, 24, 16, 0, 2, 32, 1, 16, None),
 ])
 def test_host_side_validation_refuses_without_touching_a_device(call):
     lib = _native.library()
