@@ -4,8 +4,8 @@
 // candidate lists (before the exact merge) and every rank's attention partials
 // (before the log-sum-exp combine).  Both are all-gathers: rank r's payload lands
 // in slot r of every rank's receive buffer.  This kernel does it with plain
-// stores through CUDA IPC peer mappings over NVLink (no collective library, no
-// multicast): CTA (peer p, chunk c) copies chunk c of the local payload into
+// stores through CUDA IPC peer mappings over NVLink (no collective library; each
+// store goes to one peer): CTA (peer p, chunk c) copies chunk c of the local payload into
 // slot `rank` of p's receive buffer, then adds one to p's arrival counter for
 // `rank` with a system-scope release; CTA 0 then waits (bounded) until every
 // source's counter reaches epoch * chunks, and advances the local epoch.
