@@ -108,6 +108,7 @@ struct TopkShared {
   uint64_t recbar;               // last CTA: the row's staged records landed
   uint64_t kstar;
   uint32_t rbin[kTkRowGroup], rneed[kTkRowGroup], rwhole[kTkRowGroup];  // rows this CTA finishes
+  uint32_t rfirst[kTkRowGroup], rtouch[kTkRowGroup], rlen[kTkRowGroup];
   uint32_t nrank, last;
   int abort;
 };
@@ -125,7 +126,7 @@ __device__ __forceinline__ uint32_t entry_key(const float* srow, const int32_t* 
 // Whole block: over h[0, nbins) (nbins in {1024, 2048}), the bin b with
 // count(bins > b) < need <= count(bins >= b).  Same result in every thread;
 // total < need (or need == 0) -> {0, total, total}.
-__device__ __noinline__ Select block_find_bin(const uint32_t* h, int nbins, uint32_t need, TopkShared& sh) {
+__device__ Select block_find_bin(const uint32_t* h, int nbins, uint32_t need, TopkShared& sh) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int bpt = nbins / kTkThreads;  // 4 or 2 bins per thread; thread 0 = top bins
   const int top = nbins - tid * bpt;
@@ -174,7 +175,7 @@ __device__ __noinline__ Select block_find_bin(const uint32_t* h, int nbins, uint
 }
 
 // Exclusive block scan of one value per thread; `total` = the block's sum.
-__device__ __noinline__ uint32_t block_excl_scan(uint32_t v, uint32_t& total, TopkShared& sh) {
+__device__ __forceinline__ uint32_t block_excl_scan(uint32_t v, uint32_t& total, TopkShared& sh) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   uint32_t incl = v;
 #pragma unroll
@@ -195,16 +196,26 @@ __device__ __noinline__ uint32_t block_excl_scan(uint32_t v, uint32_t& total, To
 }
 
 // Word range [w0, w1) of CTA c over rows * words_per_row words.
+// floor(a / b) for 0 <= a, b < 2^52 (both exact in double): the double quotient is
+// off by at most one and corrected with integer products (64-bit integer
+// division is a long software routine on the GPU).
+__device__ __forceinline__ int64_t div_floor52(int64_t a, int64_t b) {
+  int64_t q = int64_t(double(a) / double(b));
+  if (q * b > a) --q;
+  else if ((q + 1) * b <= a) ++q;
+  return q;
+}
+// Word range [w0, w1) of CTA c over total_words words (total_words < 2^43, n <= 256).
 __device__ __forceinline__ void cta_words(int64_t total_words, uint32_t c, uint32_t n, int64_t& w0,
                                           int64_t& w1) {
-  w0 = total_words * c / n;
-  w1 = total_words * (c + 1) / n;
+  w0 = div_floor52(total_words * c, n);
+  w1 = div_floor52(total_words * (c + 1), n);
 }
 // CTA owning word w (inverse of cta_words).
 __device__ __forceinline__ uint32_t word_owner(int64_t w, int64_t total_words, uint32_t n) {
-  int64_t c = w * int64_t(n) / total_words;
-  while (c + 1 < int64_t(n) && total_words * (c + 1) / n <= w) ++c;
-  while (c > 0 && total_words * c / n > w) --c;
+  int64_t c = div_floor52(w * int64_t(n), total_words);
+  while (c + 1 < int64_t(n) && div_floor52(total_words * (c + 1), n) <= w) ++c;
+  while (c > 0 && div_floor52(total_words * c, n) > w) --c;
   return uint32_t(c);
 }
 
@@ -549,6 +560,9 @@ __global__ void __launch_bounds__(kTkThreads) topk_select_kernel(
           sh.rbin[r - rg] = s0.bin;
           sh.rneed[r - rg] = need0;
           sh.rwhole[r - rg] = whole_bin ? 1u : 0u;
+          sh.rfirst[r - rg] = first_cta;
+          sh.rtouch[r - rg] = touching;
+          sh.rlen[r - rg] = uint32_t(n);
         }
       }
     }
@@ -557,9 +571,9 @@ __global__ void __launch_bounds__(kTkThreads) topk_select_kernel(
     for (uint32_t pend = won; pend; pend &= pend - 1) {
       const int64_t r = rg + (__ffs(pend) - 1);
       const int64_t rb = r * L.words;
-      const int64_t n = row_length(lengths, r, row_stride);
-      const uint32_t first_cta = word_owner(rb, total_words, nctas);
-      const uint32_t touching = word_owner(rb + L.words - 1, total_words, nctas) - first_cta + 1;
+      const int64_t n = sh.rlen[r - rg];  // row geometry from the staging pass
+      const uint32_t first_cta = sh.rfirst[r - rg];
+      const uint32_t touching = sh.rtouch[r - rg];
       const float* srow = scores + r * row_stride;
       const int32_t* irow = kIds ? ids + r * row_stride : nullptr;
       uint32_t* h0row = ghist + r * kTkBins;
