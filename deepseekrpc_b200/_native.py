@@ -57,6 +57,10 @@ SIGNATURES = {
                                     _P, _P, c_int64, _P]),
     "dsr_lse_combine": (c_int, [_P, _P, _P, c_int64, _P, _P, _P, _P, _P, c_int64, c_int64, c_int64,
                                 _P]),
+    "dsr_pool_write": (c_int, [_P, _P, c_int64, c_int64, _P, _P, _P, c_int64, _P, c_int64, c_int64, _P, _P]),
+    "dsr_pool_rollback": (c_int, [_P, _P, c_int64, c_int64, _P, c_int64, _P, _P, _P, c_int64, _P, _P]),
+    "dsr_pool_gather": (c_int, [_P, _P, c_int64, c_int64, c_int64, _P, c_int64, _P, _P, _P]),
+    "dsr_pool_restore": (c_int, [_P, _P, c_int64, c_int64, c_int64, _P, _P, c_int64, _P, _P]),
     "dsr_p2p_buffer_bytes": (c_size_t, [c_int64, c_int64]),
     "dsr_p2p_alloc": (c_int, [c_size_t, _P, _P]),
     "dsr_p2p_open": (c_int, [_P, _P]),

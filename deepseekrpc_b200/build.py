@@ -26,7 +26,7 @@ LIB = PKG / "libdsr_b200.so"
 EXT_NAME = "deepseekrpc_cuda"
 
 CUDA_SOURCES = ["legacy_ops.cu", "topk.cu", "topk_noalloc.cu", "indexer_decode.cu", "indexer_prefill.cu",
-                "candidates.cu", "mla_decode.cu", "append.cu", "decode_step.cu", "p2p.cu"]
+                "candidates.cu", "mla_decode.cu", "append.cu", "decode_step.cu", "p2p.cu", "pool.cu"]
 HOST_SOURCES = ["host_common.cpp"]
 HEADERS = ["common.cuh", "host_common.h"]
 

@@ -303,6 +303,42 @@ int dsr_decode_step(const float* idx_q, const float* idx_w, int64_t idx_heads,
                     int32_t* err, int64_t batch, void* stream);
 
 /* ---------------------------------------------------------------------------
+ * Row-pool transactions and snapshot row streaming (DeviceRowPool,
+ * cache_pool.py:156-360; StageSnapshot._gpu, snapshot_state.py:205-216;
+ * snapshot_restore.py:158-165).  data bf16[slots, width] (width <= 576),
+ * generations i64[slots], undo bf16[undo_rows, width].  All four are single
+ * launches with no host synchronisation; device status in *err:
+ * DSR_ERR_SCATTER (bounds / repeated slot / generation mismatch), DSR_ERR_NONFINITE,
+ * DSR_ERR_ID (snapshot row not live).
+ *  - dsr_pool_write: a batch of 1..64 rows.  The whole batch is checked first;
+ *    every in-bounds target row is copied to undo[undo_start + i]; a valid batch
+ *    is then written and its generations set to expected + 1, a refused one
+ *    writes nothing else (restoring its undo rows leaves the pool unchanged).
+ *  - dsr_pool_rollback: `count` rejected mutations in journal order (slot,
+ *    previous generation, undo row); each slot ends with the backup of its
+ *    earliest rejected mutation (the reference restores newest first).
+ *  - dsr_pool_gather: a snapshot tile of 1..1024 logical rows (slot =
+ *    (logical + offset) % slots) into out bf16[rows, width]; generations
+ *    (nullable) must be live; non-finite payload is refused.
+ *  - dsr_pool_restore: a snapshot tile into fresh rows (generation 0, no
+ *    repeated slot), generations set to 1; a refused tile writes nothing.
+ * ------------------------------------------------------------------------- */
+int dsr_pool_write(uint16_t* data, int64_t* generations, int64_t slots, int64_t width,
+                   const int32_t* slot_ids, const int64_t* expected, const uint16_t* values,
+                   int64_t rows, uint16_t* undo, int64_t undo_rows, int64_t undo_start,
+                   int32_t* err, void* stream);
+int dsr_pool_rollback(uint16_t* data, int64_t* generations, int64_t slots, int64_t width,
+                      const uint16_t* undo, int64_t undo_rows, const int32_t* slot_ids,
+                      const int64_t* previous, const int32_t* undo_index, int64_t count,
+                      int32_t* err, void* stream);
+int dsr_pool_gather(const uint16_t* data, const int64_t* generations, int64_t slots, int64_t width,
+                    int64_t offset, const int64_t* logical, int64_t rows, uint16_t* out,
+                    int32_t* err, void* stream);
+int dsr_pool_restore(uint16_t* data, int64_t* generations, int64_t slots, int64_t width,
+                     int64_t offset, const int64_t* logical, const uint16_t* values, int64_t rows,
+                     int32_t* err, void* stream);
+
+/* ---------------------------------------------------------------------------
  * NVLink peer exchange for the sequence-sharded step (one process per GPU).
  * Replaces the collective library's all_gather at the two exchange points of a
  * decode step (torch.distributed.all_gather_into_tensor in the reference-style
