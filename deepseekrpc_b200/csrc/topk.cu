@@ -50,16 +50,19 @@ constexpr int kHsThreads = 256;   // histogram CTA
 constexpr int kHsWarps = kHsThreads / 32;
 constexpr int kTkVec = 8;          // 4-entry runs per thread per histogram batch
 constexpr int kTkChunk = kHsThreads * 4 * kTkVec;  // entries per histogram batch
-constexpr int kTkPer = 4;          // consecutive entries per thread per staging chunk
-constexpr int kTkCh = kTkThreads * kTkPer;         // entries per staging chunk
+// staging chunks: kTkThreads * kPer consecutive entries; kPer = 16 when a CTA
+// streams long ranges of implicit-id rows (fixed per-chunk costs amortised),
+// else 4 (short ranges, or an id array riding along in the ring)
+constexpr int64_t kTkWideRange = 16384;  // entries per CTA from which chunks widen
 constexpr int kTkStages = 4;       // staging chunks in flight (bulk copies)
 // staged records the last CTA holds in shared memory: a threshold bin spans up to a
 // quarter octave of scores, which for normal-like scores of 2^20-entry rows is
 // about 11K records above the bin's lower edge
 constexpr int kTkRecCap = 31 * kTkThreads;
 constexpr int kTkRun = kTkRecCap / kTkThreads;  // records per thread there (at most; odd)
-constexpr size_t kTkDynSmem = size_t(kTkRecCap) * 8;  // the copy ring, then the records
-static_assert(kTkDynSmem >= size_t(kTkStages) * kTkCh * 8, "the copy ring fits the records' space");
+constexpr size_t kTkRingBytes = size_t(kTkStages) * kTkThreads * 16 * 4;  // scores only, 16 per thread
+constexpr size_t kTkDynSmem = size_t(kTkRecCap) * 8 > kTkRingBytes ? size_t(kTkRecCap) * 8 : kTkRingBytes;
+static_assert(kTkDynSmem >= size_t(kTkStages) * kTkThreads * 4 * 8, "the ring with ids fits too");
 static_assert(kTkRun % 2 == 1 && kTkRun <= 32, "odd run, one mask word");
 static_assert(kTkMaxCtas <= kTkThreads, "one thread per slot");
 constexpr int kTkRegs = 8;         // staged records per thread per output chunk (strided)
@@ -367,7 +370,7 @@ __device__ __forceinline__ uint64_t record_key(uint64_t rec) {
 // ---------------------------------------------------------------------------
 // Selection: staging by every CTA, resolution and output by the row's last CTA.
 // ---------------------------------------------------------------------------
-template <bool kIds>
+template <bool kIds, int kPer>
 __global__ void __launch_bounds__(kTkThreads) topk_select_kernel(
     const float* __restrict__ scores, const int32_t* __restrict__ ids,
     const int32_t* __restrict__ lengths, int32_t* __restrict__ out_ids,
@@ -381,6 +384,9 @@ __global__ void __launch_bounds__(kTkThreads) topk_select_kernel(
   uint32_t* gdone = reinterpret_cast<uint32_t*>(ws_base + L.done);
   uint32_t* gcnt = reinterpret_cast<uint32_t*>(ws_base + L.cnt);
   uint64_t* gstage = reinterpret_cast<uint64_t*>(ws_base + L.stage);
+  static_assert(kPer == 4 || (kPer == 16 && !kIds), "chunk width");
+  constexpr int kTkPer = kPer;
+  constexpr int kTkCh = kTkThreads * kTkPer;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const uint32_t cta = blockIdx.x, nctas = gridDim.x;
   const int64_t total_words = rows * L.words;
@@ -460,6 +466,9 @@ __global__ void __launch_bounds__(kTkThreads) topk_select_kernel(
       const bool take_all = s0.total <= uint32_t(k);
       const uint32_t need0 = uint32_t(k) - s0.above;
       const bool whole_bin = take_all || sh.hist[s0.bin] == need0;  // no entry left to rank
+      // lowest score of the threshold bin; the edges of bins 0-3 decode to NaN bit
+      // patterns and those bins hold nothing above -inf, so every score passes there
+      const float thr_f = s0.bin < 4u ? -CUDART_INF_F : key_score(s0.bin << 21);
 
       // ---- stage entries at or above the threshold bin, compacted in entry order
       uint32_t staged = 0;  // block-uniform running count
@@ -491,15 +500,25 @@ __global__ void __launch_bounds__(kTkThreads) topk_select_kernel(
             if (kIds) idv[q] = in ? irow[i + q] : -1;
           }
         }
+        // keep: at or above the threshold bin's lower edge, compared as floats (the
+        // key map is monotone; NaN ranks above +inf); kept entries are rare, so
+        // their keys, digit-1 counts and records are built only in a branch
         uint32_t mask = 0;
+        const int64_t room = ok ? e1 - i : 0;  // valid entries of this thread's run
   #pragma unroll
         for (int q = 0; q < kTkPer; ++q) {
-          const uint32_t u = rank_u(raw[q]);
-          const bool present = ok && i + q < e1 && (!kIds || idv[q] >= 0);
-          const bool keep = present && (take_all || (u >> 21) >= s0.bin);
-          if (kIds && present && idv[q] == 0x7fffffff) flag(err, DSR_ERR_ID);  // reserved for the pad record
-          if (keep && !whole_bin && (u >> 21) == s0.bin) atomicAdd(h1row + ((u >> 10) & (kTkBins - 1)), 1u);
+          const float sv = __uint_as_float(raw[q]);
+          const bool keep = q < room && (!kIds || idv[q] >= 0) && (take_all || sv >= thr_f || sv != sv);
           mask |= uint32_t(keep) << q;
+        }
+        if (mask != 0u) {
+  #pragma unroll
+          for (int q = 0; q < kTkPer; ++q)
+            if ((mask >> q) & 1u) {
+              const uint32_t u = rank_u(raw[q]);
+              if (kIds && idv[q] == 0x7fffffff) flag(err, DSR_ERR_ID);  // reserved for the pad record
+              if (!whole_bin && (u >> 21) == s0.bin) atomicAdd(h1row + ((u >> 10) & (kTkBins - 1)), 1u);
+            }
         }
         const uint32_t cnt = __popc(mask);
         uint32_t incl = cnt;
@@ -521,14 +540,16 @@ __global__ void __launch_bounds__(kTkThreads) topk_select_kernel(
           before += w < warp ? t : 0u;
           all += t;
         }
-        uint32_t pos = staged + before + incl - cnt;
+        if (mask != 0u) {
+          uint32_t pos = staged + before + incl - cnt;
   #pragma unroll
-        for (int q = 0; q < kTkPer; ++q)
-          if ((mask >> q) & 1u) {
-            const uint32_t id = kIds ? uint32_t(idv[q]) : uint32_t(id_base + i + q);
-            srec[e0 + pos] = (uint64_t(raw[q]) << 31) | uint64_t(0x7fffffffu - id);
-            ++pos;
-          }
+          for (int q = 0; q < kTkPer; ++q)
+            if ((mask >> q) & 1u) {
+              const uint32_t id = kIds ? uint32_t(idv[q]) : uint32_t(id_base + i + q);
+              srec[e0 + pos] = (uint64_t(raw[q]) << 31) | uint64_t(0x7fffffffu - id);
+              ++pos;
+            }
+        }
         staged += all;
       }
       if (aborted) {
@@ -925,21 +946,27 @@ int launch_topk(const float* scores, const int32_t* ids, const int32_t* lengths,
   }
   static bool select_configured = false;
   if (!select_configured) {
-    cudaError_t e = cudaFuncSetAttribute(topk_select_kernel<true>,
+    cudaError_t e = cudaFuncSetAttribute(topk_select_kernel<true, 4>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, int(kTkDynSmem));
     if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(topk_select_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+      e = cudaFuncSetAttribute(topk_select_kernel<false, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               int(kTkDynSmem));
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(topk_select_kernel<false, 16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                int(kTkDynSmem));
     if (e != cudaSuccess) return fail(DSR_ECUDA, "topk smem attribute: %s", cudaGetErrorString(e));
     select_configured = true;
   }
   cfg.dynamicSmemBytes = kTkDynSmem;
+  const bool wide = rows * ((row_stride + 31) / 32) * 32 / ctas >= kTkWideRange;
   const cudaError_t e =
       ids != nullptr
-          ? cudaLaunchKernelEx(&cfg, topk_select_kernel<true>, scores, ids, lengths, out_ids,
+          ? cudaLaunchKernelEx(&cfg, topk_select_kernel<true, 4>, scores, ids, lengths, out_ids,
                                out_scores, err, rows, row_stride, int(k), id_base, ws)
-          : cudaLaunchKernelEx(&cfg, topk_select_kernel<false>, scores, ids, lengths, out_ids,
-                               out_scores, err, rows, row_stride, int(k), id_base, ws);
+      : wide ? cudaLaunchKernelEx(&cfg, topk_select_kernel<false, 16>, scores, ids, lengths, out_ids,
+                                  out_scores, err, rows, row_stride, int(k), id_base, ws)
+             : cudaLaunchKernelEx(&cfg, topk_select_kernel<false, 4>, scores, ids, lengths, out_ids,
+                                  out_scores, err, rows, row_stride, int(k), id_base, ws);
   if (e != cudaSuccess) return fail(DSR_ECUDA, "topk launch: %s", cudaGetErrorString(e));
   return DSR_OK;
 }

@@ -174,3 +174,21 @@ def test_topk_rows_not_16_byte_aligned(cuda):
         valid = ids[row, :m] >= 0
         expected = oracle.tiled_topk(scores[row, :m][valid], 2048, positions=ids[row, :m][valid])
         assert np.array_equal(out.cpu().numpy()[row], expected)
+
+
+def test_topk_threshold_in_the_lowest_and_highest_bins(cuda):
+    # thresholds at -inf (the lowest populated bin) and among NaN / +inf (the highest)
+    n, k = 30000, 2048
+    rows = np.zeros((4, n), np.float32)
+    rows[0] = -np.inf
+    rows[0, :1000] = np.arange(1000, dtype=np.float32)       # k-th largest is -inf
+    rows[1] = np.inf
+    rows[1, ::3] = np.nan                                     # 10,000 NaN above 20,000 +inf
+    rows[2] = -np.inf
+    rows[2, 5::7] = np.nan                                    # NaN, then -inf ties
+    rows[3] = np.float32(-3.0e38)
+    rows[3, 100:2100] = -np.inf                               # the most negative finite score
+    lengths = [n] * 4
+    out, code = c_topk(dev(rows), dev(np.array(lengths, np.int32)), k)
+    assert code == 0
+    assert np.array_equal(out.cpu().numpy(), expected_rows(rows, lengths, k))
