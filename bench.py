@@ -221,6 +221,66 @@ def cpu_reference_step_us(cfg, host, lengths, budget_s, threads):
     return statistics.median(times) * 1e6, len(times)
 
 
+def cpu_config_baselines(budget_s, threads):
+    """The oracle port of the reference CPU path on configs 1, 3 and 5 (bounded
+    samples; per-step estimates scale the sampled sequences by their keys)."""
+    import torch
+    import oracle
+    from deepseekrpc_b200.workloads import CONFIGS, make_decode_inputs
+
+    def one_row_us(cfg, host, row, budget):
+        times = []
+        t_end = time.perf_counter() + budget
+        while True:
+            t0 = time.perf_counter()
+            oracle.decode_step(host["idx_q"][row:row + 1], host["idx_w"][row:row + 1], host["index_pool"],
+                               host["q"][row:row + 1], host["kv_pool"], host["block_table"][row:row + 1],
+                               host["visible"][row:row + 1], cfg.topk, host["swa"][row:row + 1],
+                               host["swa_len"][row:row + 1], host["sink"], cfg.scale)
+            times.append(time.perf_counter() - t0)
+            if time.perf_counter() > t_end:
+                break
+        return statistics.median(times) * 1e6, len(times)
+
+    def to_host(inp, rows):
+        out = {}
+        for key, v in inp.items():
+            t = v if key in ("index_pool", "kv_pool", "sink") else v[:rows]
+            out[key] = (t.float() if t.dtype == torch.bfloat16 else t).cpu().numpy()
+        return out
+
+    result = {}
+    cfg = CONFIGS["cfg1"]
+    inp, lengths = make_decode_inputs(cfg, device="cuda:0", gen_device="cuda")
+    us, n = one_row_us(cfg, to_host(inp, 1), 0, budget_s / 4)
+    result["cfg1"] = {"value": round(us, 1), "unit": "us per step", "cores": threads, "kind": "port",
+                      "sample": f"{n} full steps, median"}
+    del inp
+    cfg = CONFIGS["cfg3"]
+    inp, lengths = make_decode_inputs(cfg, device="cuda:0", gen_device="cuda")
+    host = to_host(inp, 2)
+    del inp
+    torch.cuda.empty_cache()
+    per_key = []
+    for row in range(2):
+        us, n = one_row_us(cfg, host, row, budget_s / 8)
+        per_key.append(us / lengths[row])
+    est = sum(per_key) / 2 * sum(lengths)
+    result["cfg3"] = {"value": round(est, 1), "unit": "us per step (estimate)", "cores": threads, "kind": "port",
+                      "sample": f"sequences 0-1 (L = {lengths[0]}, {lengths[1]}) timed, scaled by the batch's "
+                                f"{sum(lengths)} keys"}
+    del host
+    cfg = CONFIGS["cfg5"]
+    inp, lengths = make_decode_inputs(cfg, device="cuda:0", gen_device="cuda", lengths=[cfg.context])
+    host = to_host(inp, 1)
+    del inp
+    torch.cuda.empty_cache()
+    us, n = one_row_us(cfg, host, 0, budget_s / 4)
+    result["cfg5"] = {"value": round(us * cfg.batch, 1), "unit": "us per step (estimate)", "cores": threads,
+                      "kind": "port", "sample": f"{n} decodes of one 1,048,576-key sequence, median x 4 sequences"}
+    return result
+
+
 def host_copy(inp, replica=0):
     import torch
     result = {}
@@ -434,6 +494,27 @@ def run_single(args):
     clocks = sampler.summary()
     assert int(runner.err.item()) == 0
 
+    # per-step distribution: one single-step graph per replica, an event pair
+    # around each replay (rotation kept, so every step starts from a cold L2)
+    singles = [capture(torch, lambda i, r=r: runner.step(r, stream=stream), 1, stream) for r in range(R)]
+    samples = []
+    with torch.cuda.stream(stream):
+        for i in range(max(200, 25 * R)):
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            singles[i % R].replay()
+            e1.record(stream)
+            samples.append((e0, e1))
+    torch.cuda.synchronize()
+    per_step = sorted(a.elapsed_time(b) * 1e3 for a, b in samples[R:])
+    step_dist = {"median": round(statistics.median(per_step), 3),
+                 "p10": round(per_step[len(per_step) // 10], 3),
+                 "p90": round(per_step[(9 * len(per_step)) // 10], 3),
+                 "samples": len(per_step), "unit": "us",
+                 "note": "single-step graph replays, an event pair each (includes one graph launch per step)"}
+    del singles
+
     # dominant kernel (indexer) timed alone, same replica rotation
     ix_graph = capture(torch, lambda i: runner.indexer(i % R, stream=stream), R, stream)
     time_replays(torch, ix_graph, 3, stream)
@@ -511,6 +592,7 @@ def run_single(args):
         cpu = {"value": round(us, 1), "unit": "us", "cores": threads, "kind": "port",
                "sample": f"{samples} full config-2 decode steps (oracle/ops.py decode_step, numpy float32), "
                          "median"}
+        cpu["other_configs"] = cpu_config_baselines(args.cpu_budget, threads)
 
     # config 5 through the sharded code on this one GPU: the N=1 point of the
     # 1/2/4/8 scaling series that `--gpus N` reports for config 5
@@ -543,6 +625,7 @@ def run_single(args):
                 "d2h_bytes_per_step": d2h, "mode": e2e_mode},
         "gpu_launches": KERNELS_PER_STEP * K,
         "breakdown": dict(breakdown, indexer_us=round(ix_ms * 1e3, 3)),
+        "step_distribution": step_dist,
         "clocks": clocks,
         "scaling_base": scaling_base,
         "prefill": prefill,
