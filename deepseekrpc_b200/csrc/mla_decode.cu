@@ -16,7 +16,7 @@
 //   O^T[d, h]    = sum_key V[key,d] P[h,key]         (M=128 dims x 4, N=heads)
 // The KV tile in shared memory serves both products: K-major A operand for S^T
 // and MN-major A operand (V^T) for O^T, so each selected row is read once.
-// Partials (m in log2 units, l, unnormalised o) go to the workspace and
+// Partials (m in log2 units, l, unnormalised o in bf16) go to the workspace and
 // lse_combine_kernel merges them with the sink.
 #include "common.cuh"
 #include "host_common.h"
@@ -61,7 +61,7 @@ __global__ void __launch_bounds__(kMlaThreads, 1)
                       int64_t table_stride, const int32_t* __restrict__ visible,
                       const int32_t* __restrict__ topk, int k, const uint16_t* __restrict__ swa,
                       const int32_t* __restrict__ swa_len, float scale_log2,
-                      float* __restrict__ part_o, float* __restrict__ part_m,
+                      uint16_t* __restrict__ part_o, float* __restrict__ part_m,
                       float* __restrict__ part_l, int32_t* err, int heads,
                       const uint16_t* __restrict__ q_img, int64_t id_base, int foreign_ok) {
   using L = MlaLayout<HG>;
@@ -279,7 +279,7 @@ __global__ void __launch_bounds__(kMlaThreads, 1)
     // ---- O^T: lane = value column, columns = heads
     if (ok && mbar_wait(bar_o, 0, abort, err)) {
       tc_fence_after();
-      float* o = part_o + pidx * kMlaDv;
+      uint16_t* o = part_o + pidx * kMlaDv;  // bf16: the range of fp32, half the bytes
 #pragma unroll 1
       for (int c = 0; c < kMlaDv / 128; ++c) {
         const uint32_t taddr = tmem_o + c * HG + (uint32_t(warp * 32) << 16);
@@ -289,7 +289,8 @@ __global__ void __launch_bounds__(kMlaThreads, 1)
         for (int hh = 0; hh < HG; hh += 16) tmem_ld16(taddr + hh, *reinterpret_cast<uint32_t(*)[16]>(r + hh));
         tmem_wait_ld();
 #pragma unroll
-        for (int hh = 0; hh < HG; ++hh) o[int64_t(hh) * kMlaDv + d] = __uint_as_float(r[hh]);
+        for (int hh = 0; hh < HG; ++hh)
+          o[int64_t(hh) * kMlaDv + d] = __bfloat16_as_ushort(__float2bfloat16_rn(__uint_as_float(r[hh])));
       }
     }
   } else if (lane == 0) {
@@ -404,12 +405,35 @@ __global__ void __launch_bounds__(128) lse_combine_packed_kernel(
 // LSE combine.  m in log2 units; with a sink (natural-log units, converted
 // here) the output is normalised, otherwise the merged partial is returned.
 // ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(128) lse_combine_kernel(
-    const float* __restrict__ part_o, const float* __restrict__ part_m,
+// four consecutive partial values as floats: fp32 partials (the public combine)
+// or bf16 bits (the tile partials of the MLA kernel)
+template <typename T>
+struct PartLoad;
+template <>
+struct PartLoad<float> {
+  using Raw = float4;
+  static __device__ __forceinline__ Raw load(const float* p) { return __ldg(reinterpret_cast<const float4*>(p)); }
+  static __device__ __forceinline__ float4 cvt(Raw r) { return r; }
+};
+template <>
+struct PartLoad<uint16_t> {
+  using Raw = uint2;
+  static __device__ __forceinline__ Raw load(const uint16_t* p) { return __ldg(reinterpret_cast<const uint2*>(p)); }
+  static __device__ __forceinline__ float4 cvt(Raw r) {
+    return make_float4(__uint_as_float(r.x << 16), __uint_as_float(r.x & 0xffff0000u),
+                       __uint_as_float(r.y << 16), __uint_as_float(r.y & 0xffff0000u));
+  }
+};
+
+// kInFlight: partials whose columns a thread requests before the weights exist.
+// Few CTAs (one sequence): 24, one memory round trip per CTA.  Thousands of CTAs
+// (a batch): 8, so that eight CTAs fit an SM and occupancy hides the latency.
+template <typename T, int kInFlight>
+__global__ void __launch_bounds__(128, kInFlight > 8 ? 1 : 8) lse_combine_kernel(
+    const T* __restrict__ part_o, const float* __restrict__ part_m,
     const float* __restrict__ part_l, int parts, const float* __restrict__ sink,
     float* __restrict__ out, float* __restrict__ out_m, float* __restrict__ out_l, int32_t* err,
     int heads, int dv) {
-  constexpr int kInFlight = 24;   // partials whose columns a thread holds at once
   extern __shared__ float wgt[];  // [parts] weights 2^{m_t - M}
   __shared__ float stat[2];       // M, L
   const int b = blockIdx.x, h = blockIdx.y;
@@ -418,11 +442,11 @@ __global__ void __launch_bounds__(128) lse_combine_kernel(
   // the columns of the first kInFlight partials are requested before the weights
   // exist, so the statistics and the values arrive in one memory round trip
   const int d0 = threadIdx.x * 4;
-  float4 v[kInFlight];
+  using P = PartLoad<T>;
+  typename P::Raw v[kInFlight];
 #pragma unroll
   for (int j = 0; j < kInFlight; ++j)
-    if (j < parts && d0 < dv)
-      v[j] = __ldg(reinterpret_cast<const float4*>(part_o + (pbase + int64_t(j) * heads) * dv + d0));
+    if (j < parts && d0 < dv) v[j] = P::load(part_o + (pbase + int64_t(j) * heads) * dv + d0);
   if (threadIdx.x < 32) {
     const int lane = threadIdx.x;
     float sk = 0.f, M = -CUDART_INF_F;
@@ -481,27 +505,28 @@ __global__ void __launch_bounds__(128) lse_combine_kernel(
       for (int j = 0; j < kInFlight; ++j)
         if (j < parts) {
           const float w = wgt[j];
-          acc.x = fmaf(v[j].x, w, acc.x);
-          acc.y = fmaf(v[j].y, w, acc.y);
-          acc.z = fmaf(v[j].z, w, acc.z);
-          acc.w = fmaf(v[j].w, w, acc.w);
+          const float4 x = P::cvt(v[j]);
+          acc.x = fmaf(x.x, w, acc.x);
+          acc.y = fmaf(x.y, w, acc.y);
+          acc.z = fmaf(x.z, w, acc.z);
+          acc.w = fmaf(x.w, w, acc.w);
         }
     }
     // columns past the first group, and partials past kInFlight, 8 loads at a time
     for (int t0 = d == d0 ? kInFlight : 0; t0 < parts; t0 += 8) {
-      float4 u[8];
+      typename P::Raw u[8];
 #pragma unroll
       for (int j = 0; j < 8; ++j)
-        if (t0 + j < parts)
-          u[j] = __ldg(reinterpret_cast<const float4*>(part_o + (pbase + int64_t(t0 + j) * heads) * dv + d));
+        if (t0 + j < parts) u[j] = P::load(part_o + (pbase + int64_t(t0 + j) * heads) * dv + d);
 #pragma unroll
       for (int j = 0; j < 8; ++j)
         if (t0 + j < parts) {
           const float w = wgt[t0 + j];
-          acc.x = fmaf(u[j].x, w, acc.x);
-          acc.y = fmaf(u[j].y, w, acc.y);
-          acc.z = fmaf(u[j].z, w, acc.z);
-          acc.w = fmaf(u[j].w, w, acc.w);
+          const float4 x = P::cvt(u[j]);
+          acc.x = fmaf(x.x, w, acc.x);
+          acc.y = fmaf(x.y, w, acc.y);
+          acc.z = fmaf(x.z, w, acc.z);
+          acc.w = fmaf(x.w, w, acc.w);
         }
     }
     const float4 o = make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
@@ -518,7 +543,7 @@ template <int HG>
 int launch_mla(const float* q, const uint16_t* kv_pool, int64_t pool_blocks,
                const int32_t* block_table, int64_t table_stride, const int32_t* visible,
                const int32_t* topk, int64_t k, const uint16_t* swa, const int32_t* swa_len,
-               float scale, float* part_o, float* part_m, float* part_l, int32_t* err,
+               float scale, uint16_t* part_o, float* part_m, float* part_l, int32_t* err,
                int64_t batch, int64_t heads, int tiles, cudaStream_t stream, bool pdl,
                const uint16_t* q_img, int64_t id_base, bool foreign_ok) {
   using L = MlaLayout<HG>;
@@ -563,10 +588,12 @@ size_t mla_workspace_bytes(int64_t batch, int64_t heads, int64_t k) {
   return parts * kMlaDv * 4 + 2 * parts * 4 + 256;
 }
 
-int launch_lse_combine(const float* part_o, const float* part_m, const float* part_l,
-                       int64_t parts, const float* sink, float* out, float* out_m, float* out_l,
-                       int32_t* err, int64_t batch, int64_t heads, int64_t dv,
-                       cudaStream_t stream, bool pdl) {
+namespace {
+template <typename T>
+int launch_combine(const T* part_o, const float* part_m, const float* part_l,
+                   int64_t parts, const float* sink, float* out, float* out_m, float* out_l,
+                   int32_t* err, int64_t batch, int64_t heads, int64_t dv,
+                   cudaStream_t stream, bool pdl) {
   DSR_REQUIRE(part_o && part_m && part_l && out && err, "lse_combine: null pointer");
   DSR_REQUIRE(sink != nullptr || (out_m != nullptr && out_l != nullptr),
               "lse_combine: an unnormalised combine needs out_m and out_l");
@@ -584,11 +611,23 @@ int launch_lse_combine(const float* part_o, const float* part_m, const float* pa
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, lse_combine_kernel, part_o, part_m, part_l,
-                                           int(parts), sink, out, out_m, out_l, err, int(heads),
-                                           int(dv));
+  const bool deep = batch * heads <= 2 * int64_t(sm_count());
+  const cudaError_t e =
+      deep ? cudaLaunchKernelEx(&cfg, lse_combine_kernel<T, 24>, part_o, part_m, part_l, int(parts), sink,
+                                out, out_m, out_l, err, int(heads), int(dv))
+           : cudaLaunchKernelEx(&cfg, lse_combine_kernel<T, 8>, part_o, part_m, part_l, int(parts), sink,
+                                out, out_m, out_l, err, int(heads), int(dv));
   if (e != cudaSuccess) return fail(DSR_ECUDA, "lse_combine launch: %s", cudaGetErrorString(e));
   return DSR_OK;
+}
+}  // namespace
+
+int launch_lse_combine(const float* part_o, const float* part_m, const float* part_l,
+                       int64_t parts, const float* sink, float* out, float* out_m, float* out_l,
+                       int32_t* err, int64_t batch, int64_t heads, int64_t dv,
+                       cudaStream_t stream, bool pdl) {
+  return launch_combine(part_o, part_m, part_l, parts, sink, out, out_m, out_l, err, batch, heads, dv,
+                        stream, pdl);
 }
 
 int launch_mla_decode(const float* q, const uint16_t* kv_pool, int64_t pool_blocks,
@@ -620,8 +659,8 @@ int launch_mla_decode(const float* q, const uint16_t* kv_pool, int64_t pool_bloc
               workspace_bytes, need);
   const int tiles = mla_tiles(k);
   const size_t parts = size_t(batch) * tiles * heads;
-  float* part_o = static_cast<float*>(workspace);
-  float* part_m = part_o + parts * kMlaDv;
+  uint16_t* part_o = static_cast<uint16_t*>(workspace);  // bf16 tile partials
+  float* part_m = reinterpret_cast<float*>(part_o + parts * kMlaDv);
   float* part_l = part_m + parts;
   // heads per CTA: the largest group (<= 64) whose grid still fits one wave of
   // CTAs; smaller groups re-gather the same rows (L2 hits) to use more SMs
@@ -646,8 +685,8 @@ int launch_mla_decode(const float* q, const uint16_t* kv_pool, int64_t pool_bloc
       break;
   }
   if (rc != DSR_OK) return rc;
-  return launch_lse_combine(part_o, part_m, part_l, tiles, sink, out, out_m, out_l, err, batch,
-                            heads, kMlaDv, stream, pdl);
+  return launch_combine(part_o, part_m, part_l, tiles, sink, out, out_m, out_l, err, batch, heads,
+                        kMlaDv, stream, pdl);
 }
 
 }  // namespace dsr
