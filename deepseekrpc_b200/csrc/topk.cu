@@ -19,15 +19,16 @@
 //     Every CTA streams its range through a ring of bulk copies into shared
 //     memory (kTkStages chunks in flight), finds the threshold bin of digit 0
 //     from the row histogram, stages its entries at or above that bin
-//     (compacted, in entry order, as (raw score bits << 31 | 0x7fffffff - id)
-//     records, the count padded to even with a 0 record) in the row's staging
+//     (compacted, in entry order, as their rank keys, the count padded to
+//     even with a 0 record, which no entry's key equals) in the row's staging
 //     area, counts the digit 1 of its threshold-bin entries into a second row
 //     histogram, and takes a ticket;
 //   * the CTA that takes the last ticket of a row copies all staged records
-//     into shared memory at once (16-byte cp.async), reads the digit-1
-//     histogram, ranks the few entries that share both digits with K* pairwise,
-//     and writes the selected ids (and scores) through one block scan of
-//     per-thread counts; then it clears the row's histograms and ticket.
+//     into shared memory at once (16-byte loads, every thread), reads the
+//     digit-1 histogram, ranks the few entries that share both digits with K*
+//     pairwise, selects {key >= K*} with one compare per record, and writes the
+//     selected ids (and scores) through one block scan of per-thread counts;
+//     then it clears the row's histograms and ticket.
 // More than kTkRankCap entries sharing K*'s two digits (massively tied scores)
 // are ranked over the whole row; more than kTkRecCap staged records are walked
 // from L2 in chunks.  The workspace must be zero before its first use; every
@@ -59,13 +60,14 @@ constexpr int kTkStages = 4;       // staging chunks in flight (bulk copies)
 // quarter octave of scores, which for normal-like scores of 2^20-entry rows is
 // about 11K records above the bin's lower edge
 constexpr int kTkRecCap = 31 * kTkThreads;
-constexpr int kTkRun = kTkRecCap / kTkThreads;  // records per thread there (at most; odd)
+constexpr int kTkRun = kTkRecCap / kTkThreads;  // records per thread there (at most)
 constexpr size_t kTkRingBytes = size_t(kTkStages) * kTkThreads * 16 * 4;  // scores only, 16 per thread
 constexpr size_t kTkDynSmem = size_t(kTkRecCap) * 8 > kTkRingBytes ? size_t(kTkRecCap) * 8 : kTkRingBytes;
 static_assert(kTkDynSmem >= size_t(kTkStages) * kTkThreads * 4 * 8, "the ring with ids fits too");
-static_assert(kTkRun % 2 == 1 && kTkRun <= 32, "odd run, one mask word");
+static_assert(kTkRun * kTkWarps <= kTkThreads, "one output group per thread");
 static_assert(kTkMaxCtas <= kTkThreads, "one thread per slot");
 constexpr int kTkRegs = 8;         // staged records per thread per output chunk (strided)
+constexpr int kTkSlotBatch = 10;   // slots per warp per batch of record loads (last CTA)
 constexpr int kTkRowGroup = 32;    // rows staged before their finishing (one bit each)
 constexpr int kTkRankCap = 2048;   // entries ranked in shared memory
 constexpr int kTkLevels = 6;
@@ -104,11 +106,14 @@ struct TopkShared {
   uint32_t pre[kTkThreads + 1];  // exclusive prefix of staged counts per slot
   uint32_t e0s[kTkMaxCtas];      // first entry of each slot's range in the row
   uint32_t tot[2][kTkWarps];      // per-warp staged counts, by chunk parity
+  uint32_t grp[kTkThreads];       // last CTA: selected counts, then offsets, of (record pass, warp) groups
+  uint4 sink16;                   // target of the stores of lanes with nothing to store
+  uint64_t recbar;                // last CTA: the long slots' bulk copies landed
+  uint32_t sink4[2];
   uint32_t tot16[kTkRegs][kTkWarps];
   uint8_t map[kTkThreads * kTkRegs];  // chunk position -> slot
   uint32_t scratch[2 * kTkWarps + 8];
   uint64_t full[kTkStages];      // copy ring: chunk landed
-  uint64_t recbar;               // last CTA: the row's staged records landed
   uint64_t kstar;
   uint32_t rbin[kTkRowGroup], rneed[kTkRowGroup], rwhole[kTkRowGroup];  // rows this CTA finishes
   uint32_t rfirst[kTkRowGroup], rtouch[kTkRowGroup], rlen[kTkRowGroup];
@@ -159,15 +164,13 @@ __device__ Select block_find_bin(const uint32_t* h, int nbins, uint32_t need, To
   if (need > 0 && total >= need && excl < need && incl >= need) {
     uint32_t cum = excl;
     int bin = top - 1;
+    bool found = false;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      if (i < bpt) {
-        if (cum + v[i] >= need) {
-          bin = top - 1 - i;
-          break;
-        }
-        cum += v[i];
-      }
+    for (int i = 0; i < 8; ++i) {  // straight-line: no early exit
+      const bool here = !found && i < bpt && cum + v[i] >= need;
+      bin = here ? top - 1 - i : bin;
+      cum += (!found && !here && i < bpt) ? v[i] : 0u;
+      found = found || here;
     }
     sh.scratch[kTkWarps] = uint32_t(bin);
     sh.scratch[kTkWarps + 1] = cum;
@@ -198,27 +201,53 @@ __device__ __forceinline__ uint32_t block_excl_scan(uint32_t v, uint32_t& total,
   return off + incl - v;
 }
 
-// Word range [w0, w1) of CTA c over rows * words_per_row words.
-// floor(a / b) for 0 <= a, b < 2^52 (both exact in double): the double quotient is
-// off by at most one and corrected with integer products (64-bit integer
-// division is a long software routine on the GPU).
-__device__ __forceinline__ int64_t div_floor52(int64_t a, int64_t b) {
-  int64_t q = int64_t(double(a) / double(b));
-  if (q * b > a) --q;
-  else if ((q + 1) * b <= a) ++q;
+// CTA c of n takes the words [floor(T c / n), floor(T (c + 1) / n)) of T words
+// (T < 2^43, n <= 256).  Divisions are long software routines on the GPU, so the
+// host passes m = floor((2^64 - 1) / n) + 1: then floor(a / n) = umulhi(a, m)
+// exactly for a < 2^52 (m = 2^64 / n + d with 0 < d <= 1 moves a / n by less
+// than 2^-12, while its fraction stays at most 1 - 1/n <= 1 - 2^-8).
+struct CtaSplit {
+  int64_t total;       // T
+  uint32_t n;
+  uint64_t inv_n;      // m (unused for n == 1)
+  double inv_total;    // 1 / T, for owner estimates
+  int64_t words;       // words per row
+  uint64_t inv_words;  // floor((2^64 - 1) / words) + 1 (unused for one word)
+};
+CtaSplit make_split(int64_t total, int64_t n, int64_t words) {
+  CtaSplit s;
+  s.total = total;
+  s.n = uint32_t(n);
+  s.inv_n = n > 1 ? ~uint64_t(0) / uint64_t(n) + 1u : 0u;
+  s.inv_total = total > 0 ? 1.0 / double(total) : 0.0;
+  s.words = words;
+  s.inv_words = words > 1 ? ~uint64_t(0) / uint64_t(words) + 1u : 0u;
+  return s;
+}
+// floor(w / words) for w < 2^43: umulhi is off by at most one (the error term
+// stays below 1), fixed with one product each way
+__device__ __forceinline__ int64_t row_of_word(const CtaSplit& s, int64_t w) {
+  if (s.words == 1) return w;
+  int64_t q = int64_t(__umul64hi(uint64_t(w), s.inv_words));
+  if (q * s.words > w) --q;
+  else if ((q + 1) * s.words <= w) ++q;
   return q;
 }
-// Word range [w0, w1) of CTA c over total_words words (total_words < 2^43, n <= 256).
-__device__ __forceinline__ void cta_words(int64_t total_words, uint32_t c, uint32_t n, int64_t& w0,
-                                          int64_t& w1) {
-  w0 = div_floor52(total_words * c, n);
-  w1 = div_floor52(total_words * (c + 1), n);
+__device__ __forceinline__ int64_t split_w0(const CtaSplit& s, int64_t c) {
+  const uint64_t a = uint64_t(s.total) * uint64_t(c);
+  return s.n == 1u ? int64_t(a) : int64_t(__umul64hi(a, s.inv_n));
 }
-// CTA owning word w (inverse of cta_words).
-__device__ __forceinline__ uint32_t word_owner(int64_t w, int64_t total_words, uint32_t n) {
-  int64_t c = div_floor52(w * int64_t(n), total_words);
-  while (c + 1 < int64_t(n) && div_floor52(total_words * (c + 1), n) <= w) ++c;
-  while (c > 0 && div_floor52(total_words * c, n) > w) --c;
+__device__ __forceinline__ void cta_words(const CtaSplit& s, uint32_t c, int64_t& w0, int64_t& w1) {
+  w0 = split_w0(s, c);
+  w1 = split_w0(s, int64_t(c) + 1);
+}
+// CTA owning word w (inverse of cta_words): an estimate, then exact steps.
+__device__ __forceinline__ uint32_t word_owner(const CtaSplit& s, int64_t w) {
+  int64_t c = int64_t(double(w) * double(s.n) * s.inv_total);
+  if (c > int64_t(s.n) - 1) c = int64_t(s.n) - 1;
+  if (c < 0) c = 0;
+  while (c + 1 < int64_t(s.n) && split_w0(s, c + 1) <= w) ++c;
+  while (c > 0 && split_w0(s, c) > w) --c;
   return uint32_t(c);
 }
 
@@ -241,20 +270,20 @@ template <bool kIds>
 __global__ void __launch_bounds__(kHsThreads) topk_hist_kernel(
     const float* __restrict__ scores, const int32_t* __restrict__ ids,
     const int32_t* __restrict__ lengths, int64_t rows, int64_t row_stride,
-    uint8_t* __restrict__ ws_base) {
+    uint8_t* __restrict__ ws_base, const CtaSplit split) {
   extern __shared__ uint32_t whist[];  // [kHsWarps][kTkBins]
   const TopkWs L(rows, row_stride);
   uint32_t* ghist = reinterpret_cast<uint32_t*>(ws_base + L.hist);
   const int tid = threadIdx.x, warp = tid >> 5;
   int64_t w0, w1;
-  cta_words(rows * L.words, blockIdx.x, gridDim.x, w0, w1);
+  cta_words(split, blockIdx.x, w0, w1);
   const int copies = (w1 - w0) * 32 >= kTkHistSplit ? kHsWarps : 1;
   uint32_t* hist = whist + (warp % copies) * kTkBins;
   for (int i = tid; i < copies * kTkBins; i += kHsThreads) whist[i] = 0u;
   pdl_launch_dependents();
   pdl_wait();
   __syncthreads();
-  for (int64_t r = w0 / L.words; r < rows && r * L.words < w1; ++r) {
+  for (int64_t r = row_of_word(split, w0); r < rows && r * L.words < w1; ++r) {
     const int64_t n = row_length(lengths, r, row_stride);
     const int64_t rb = r * L.words;
     const int64_t e0 = (w0 > rb ? w0 - rb : 0) * 32;
@@ -314,8 +343,9 @@ __device__ uint64_t resolve_kstar(KeyAt key_at, int64_t count, uint64_t prefix, 
     __syncthreads();
     for (int i = tid; i < nb; i += kTkThreads) sh.hist[i] = 0u;
     __syncthreads();
-    for (int64_t i = tid; i < count; i += kTkThreads) {
-      const uint64_t key = key_at(i);
+    for (int64_t i0 = 0; i0 < count; i0 += kTkThreads) {
+      const int64_t i = i0 + tid;
+      const uint64_t key = i < count ? key_at(i) : 0ull;
       if (key && (key >> hs) == (prefix >> hs))
         atomicAdd(&sh.hist[uint32_t(key >> kTkShift[level]) & uint32_t(nb - 1)], 1u);
     }
@@ -331,8 +361,9 @@ __device__ uint64_t resolve_kstar(KeyAt key_at, int64_t count, uint64_t prefix, 
   // K* = smallest key matching the resolved digits
   const int hs = kTkShift[level - 1];
   uint64_t best = ~uint64_t(0);
-  for (int64_t i = tid; i < count; i += kTkThreads) {
-    const uint64_t key = key_at(i);
+  for (int64_t i0 = 0; i0 < count; i0 += kTkThreads) {
+    const int64_t i = i0 + tid;
+    const uint64_t key = i < count ? key_at(i) : 0ull;
     if (key && (key >> hs) == (prefix >> hs) && key < best) best = key;
   }
 #pragma unroll
@@ -362,10 +393,14 @@ __device__ __forceinline__ uint32_t ticket_add(uint32_t* p) {
   return old;
 }
 
-// Staged record -> rank key.
-__device__ __forceinline__ uint64_t record_key(uint64_t rec) {
-  return composite(rank_u(uint32_t(rec >> 31)), uint32_t(rec) & 0x7fffffffu);
+// A staged record is its entry's rank key; 0 is the pad record.
+__device__ __forceinline__ uint64_t record_key(uint64_t rec) { return rec; }
+__device__ __forceinline__ int32_t record_id(uint64_t rec) {
+  return int32_t(0x7fffffffu - (uint32_t(rec) & 0x7fffffffu));
 }
+// The score of a staged record (canonical: -0.0 comes back as +0.0, every NaN as
+// one NaN pattern, both ranking as the original did).
+__device__ __forceinline__ float record_score(uint64_t rec) { return key_score(uint32_t(rec >> 31)); }
 
 // ---------------------------------------------------------------------------
 // Selection: staging by every CTA, resolution and output by the row's last CTA.
@@ -375,7 +410,7 @@ __global__ void __launch_bounds__(kTkThreads) topk_select_kernel(
     const float* __restrict__ scores, const int32_t* __restrict__ ids,
     const int32_t* __restrict__ lengths, int32_t* __restrict__ out_ids,
     float* __restrict__ out_scores, int32_t* err, int64_t rows, int64_t row_stride, int k,
-    int64_t id_base, uint8_t* __restrict__ ws_base) {
+    int64_t id_base, uint8_t* __restrict__ ws_base, const CtaSplit split) {
   __shared__ __align__(16) TopkShared sh;
   extern __shared__ __align__(128) uint8_t dyn[];  // copy ring, later the row's staged records
   const TopkWs L(rows, row_stride);
@@ -388,8 +423,7 @@ __global__ void __launch_bounds__(kTkThreads) topk_select_kernel(
   constexpr int kTkPer = kPer;
   constexpr int kTkCh = kTkThreads * kTkPer;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const uint32_t cta = blockIdx.x, nctas = gridDim.x;
-  const int64_t total_words = rows * L.words;
+  const uint32_t cta = blockIdx.x;
   if (tid == 0) {
     for (int s = 0; s < kTkStages; ++s) mbar_init(&sh.full[s], 1);
     mbar_init(&sh.recbar, 1);
@@ -401,12 +435,13 @@ __global__ void __launch_bounds__(kTkThreads) topk_select_kernel(
   pdl_launch_dependents();  // the consumer may start its prologue; it waits for our completion
   pdl_wait();               // scores and histograms come from the preceding kernel
   int64_t w0, w1;
-  cta_words(total_words, cta, nctas, w0, w1);
+  cta_words(split, cta, w0, w1);
   uint32_t issued = 0;    // chunks this CTA has put on the copy ring (stage = n % kTkStages)
-  uint32_t recphase = 0;  // rows whose records this CTA gathered (phase of sh.recbar)
+  uint32_t recphase = 0;  // rows whose long slots this CTA bulk-copied (phase of sh.recbar)
 
-  const int64_t r_first = w0 / L.words;
-  const int64_t r_end = (w1 + L.words - 1) / L.words < rows ? (w1 + L.words - 1) / L.words : rows;
+  const int64_t r_first = row_of_word(split, w0);
+  const int64_t r_last = row_of_word(split, w1 + L.words - 1);  // ceil(w1 / words)
+  const int64_t r_end = r_last < rows ? r_last : rows;
   for (int64_t rg = r_first; rg < r_end; rg += kTkRowGroup) {
     const int64_t rg_end = rg + kTkRowGroup < r_end ? rg + kTkRowGroup : r_end;
     uint32_t won = 0;  // rows of the group whose last ticket this CTA took
@@ -419,8 +454,8 @@ __global__ void __launch_bounds__(kTkThreads) topk_select_kernel(
       const int64_t a1 = (w1 < rb + L.words ? w1 : rb + L.words) - rb;  // end word of the row
       const int64_t e0 = a0 * 32;
       const int64_t e1 = a1 * 32 < n ? a1 * 32 : n;  // this CTA's entries [e0, e1)
-      const uint32_t first_cta = word_owner(rb, total_words, nctas);
-      const uint32_t touching = word_owner(rb + L.words - 1, total_words, nctas) - first_cta + 1;
+      const uint32_t first_cta = word_owner(split, rb);
+      const uint32_t touching = word_owner(split, rb + L.words - 1) - first_cta + 1;
       if (cta == first_cta && tid == 0) {
         const int32_t len = lengths[r];
         if (len < 0 || len > row_stride) flag(err, DSR_ERR_ID);
@@ -516,6 +551,7 @@ __global__ void __launch_bounds__(kTkThreads) topk_select_kernel(
           for (int q = 0; q < kTkPer; ++q)
             if ((mask >> q) & 1u) {
               const uint32_t u = rank_u(raw[q]);
+              raw[q] = u;  // kept entries carry their key from here on
               if (kIds && idv[q] == 0x7fffffff) flag(err, DSR_ERR_ID);  // reserved for the pad record
               if (!whole_bin && (u >> 21) == s0.bin) atomicAdd(h1row + ((u >> 10) & (kTkBins - 1)), 1u);
             }
@@ -546,7 +582,7 @@ __global__ void __launch_bounds__(kTkThreads) topk_select_kernel(
           for (int q = 0; q < kTkPer; ++q)
             if ((mask >> q) & 1u) {
               const uint32_t id = kIds ? uint32_t(idv[q]) : uint32_t(id_base + i + q);
-              srec[e0 + pos] = (uint64_t(raw[q]) << 31) | uint64_t(0x7fffffffu - id);
+              srec[e0 + pos] = composite(raw[q], 0x7fffffffu - id);
               ++pos;
             }
         }
@@ -612,7 +648,7 @@ __global__ void __launch_bounds__(kTkThreads) topk_select_kernel(
       const uint32_t my_cnt = uint32_t(tid) < touching ? __ldcg(gcnt + r * kTkMaxCtas + tid) : 0u;
       if (uint32_t(tid) < touching) {
         int64_t cw0, cw1;
-        cta_words(total_words, first_cta + tid, nctas, cw0, cw1);
+        cta_words(split, first_cta + tid, cw0, cw1);
         sh.e0s[tid] = uint32_t((cw0 > rb ? cw0 - rb : 0) * 32);
       }
       uint32_t total_staged = 0;
@@ -620,25 +656,56 @@ __global__ void __launch_bounds__(kTkThreads) topk_select_kernel(
       sh.pre[tid] = my_pre;
       if (tid == 0) sh.pre[touching] = total_staged;
       // (slots >= touching are never searched: pre[touching] bounds every walk)
-      __syncthreads();
+      const bool my_long = my_cnt > 64u;  // slot tid holds more than 32 pieces
+      const bool long_slots = __syncthreads_or(my_long);
 
-      // ---- up to kTkRecCap records: all of them into shared memory at once,
-      // every warp copying whole slots in 16-byte pieces (counts are even)
+      // ---- up to kTkRecCap records: all of them into shared memory, in slot
+      // order, as 16-byte pieces (counts are even).  A slot of up to 32 pieces
+      // is copied by one warp's lanes: warp w takes slots w, w + 16, ...,
+      // kTkSlotBatch slots per batch of loads (one L2 round trip; the batch lands
+      // while digit 1 is resolved).  A longer slot (few CTAs per row, as in
+      // prefill rows) is one bulk copy issued by its own thread.  No loop here has
+      // a per-lane trip count: on this GPU a loop whose lanes leave at different
+      // iterations costs a warp reconvergence of a few hundred cycles.
       const bool in_smem = total_staged <= uint32_t(kTkRecCap);
       uint64_t* recs = reinterpret_cast<uint64_t*>(dyn);
+      uint4 piece[kTkSlotBatch];
+      auto slot_range = [&](int slot, uint32_t& q0, uint32_t& q1) {
+        const bool valid = slot < int(touching);
+        q0 = valid ? sh.pre[slot] >> 1 : 0u;
+        q1 = valid ? sh.pre[slot + 1] >> 1 : 0u;
+      };
+      // lanes without a piece store theirs to a sink word: a divergent branch
+      // around a store costs more than the store
+      auto load_slots = [&](int s0) {
+  #pragma unroll
+        for (int b = 0; b < kTkSlotBatch; ++b) {
+          uint32_t q0, q1;
+          slot_range(s0 + b * kTkWarps, q0, q1);
+          if (q0 + lane < q1 && q1 - q0 <= 32u)
+            piece[b] = __ldcg(reinterpret_cast<const uint4*>(srec + sh.e0s[s0 + b * kTkWarps]) + lane);
+        }
+      };
+      auto store_slots = [&](int s0) {
+  #pragma unroll
+        for (int b = 0; b < kTkSlotBatch; ++b) {
+          uint32_t q0, q1;
+          slot_range(s0 + b * kTkWarps, q0, q1);
+          uint4* dst = q0 + lane < q1 && q1 - q0 <= 32u ? reinterpret_cast<uint4*>(recs) + q0 + lane : &sh.sink16;
+          *dst = piece[b];
+        }
+      };
       if (in_smem) {
-        // thread tid copies slot tid with one bulk copy; the barrier expects the
-        // row's bytes before any copy is issued (fence: the area was last written
-        // through the generic proxy)
-        if (tid == 0) {
-          fence_proxy_async_smem();
-          mbar_arrive_expect_tx(&sh.recbar, total_staged * 8u);
+        if (long_slots) {
+          // every copying thread announces its bytes before any copy is issued, so
+          // the barrier's pending bytes never drop below zero; thread 0 arrives
+          fence_proxy_async_smem();  // the area was last written through the generic proxy
+          if (my_long) mbar_expect_tx(&sh.recbar, my_cnt * 8u);
+          __syncthreads();
+          if (my_long) bulk_load(smem_u32(recs + sh.pre[tid]), srec + sh.e0s[tid], my_cnt * 8u, &sh.recbar);
+          if (tid == 0) mbar_arrive(&sh.recbar);
         }
-        __syncthreads();
-        if (uint32_t(tid) < touching) {
-          const uint32_t b = sh.pre[tid], e = sh.pre[tid + 1];
-          if (e > b) bulk_load(smem_u32(recs + b), srec + sh.e0s[tid], (e - b) * 8u, &sh.recbar);
-        }
+        load_slots(warp);
       }
 
       // digit 1 of K* (while the copies fly)
@@ -669,36 +736,40 @@ __global__ void __launch_bounds__(kTkThreads) topk_select_kernel(
       uint32_t chosen = 0;
 
       if (in_smem) {
-        const bool landed = mbar_wait(&sh.recbar, recphase & 1u, &sh.abort, err);
-        ++recphase;
-        if (__syncthreads_or(!landed)) {
-          if (tid == 0) mbar_drain(&sh.recbar, (recphase - 1) & 1u);
-          return;  // the status is set
+        store_slots(warp);
+        for (int s0 = warp + kTkWarps * kTkSlotBatch; s0 < int(touching); s0 += kTkWarps * kTkSlotBatch) {
+          load_slots(s0);
+          store_slots(s0);
         }
-        // thread tid owns the contiguous records [f0, f0 + held); an odd run length
-        // keeps the 8-byte shared reads of a warp on distinct banks.  The passes are
-        // short loops: this code runs once per row on a cold instruction cache.
-        const uint32_t per = ((total_staged + kTkThreads - 1) / kTkThreads) | 1u;
-        const uint32_t f0 = tid * per < total_staged ? tid * per : total_staged;
-        const uint32_t held = total_staged - f0 < per ? total_staged - f0 : per;
-        // one pass: records surely selected (above K*'s two digits) and candidates
-        // (sharing them); candidates join the rank list
-        uint32_t sure = 0, cand = 0;
-        const uint32_t p01 = uint32_t(prefix1 >> kTkShift[1]);
-  #pragma unroll 3
-        for (uint32_t j = 0; j < held; ++j) {
-          const uint64_t rec = recs[f0 + j];
-          const uint32_t d01 = rank_u(uint32_t(rec >> 31)) >> 10;  // K*'s two digits: u >> 10
-          const bool is_cand = rec != 0ull && !whole_bin && d01 == p01;
-          sure |= uint32_t(rec != 0ull && (whole_bin || d01 > p01)) << j;
-          cand |= uint32_t(is_cand) << j;
-          if (is_cand && !sub_all) {
-            const uint32_t slot = atomicAdd(&sh.nrank, 1u);
-            if (slot < uint32_t(kTkRankCap)) sh.rank[slot] = record_key(rec);
+        if (long_slots) {
+          const bool landed = mbar_wait(&sh.recbar, recphase & 1u, &sh.abort, err);
+          ++recphase;
+          if (__syncthreads_or(!landed)) {
+            if (tid == 0) mbar_drain(&sh.recbar, (recphase - 1) & 1u);
+            return;  // the status is set
           }
+        } else {
+          __syncthreads();
         }
+        // record f = j * kTkThreads + tid is thread tid's j-th (j < nj, block-
+        // uniform): every pass reads consecutive records per warp, and no loop has
+        // a per-lane trip count (on this GPU a loop whose lanes leave at
+        // different iterations costs a warp reconvergence of a few hundred cycles)
+        const uint32_t nj = (total_staged + kTkThreads - 1) / kTkThreads;  // <= kTkRun
+        auto rec_at = [&](uint32_t j) -> uint64_t {
+          const uint32_t f = j * kTkThreads + uint32_t(tid);
+          return f < total_staged ? recs[f] : 0ull;
+        };
         if (!sub_all) {
-          // ---- K* among the candidates
+          // ---- K* among the candidates: the records sharing its two digits
+          const uint64_t p01 = prefix1 >> 41;  // kTkShift[1]
+          for (uint32_t j = 0; j < nj; ++j) {
+            const uint64_t rec = rec_at(j);
+            if (rec != 0ull && (rec >> 41) == p01) {
+              const uint32_t slot = atomicAdd(&sh.nrank, 1u);
+              if (slot < uint32_t(kTkRankCap)) sh.rank[slot] = rec;
+            }
+          }
           __syncthreads();
           const uint32_t nr = sh.nrank;
           if (nr <= uint32_t(kTkThreads)) {
@@ -722,47 +793,69 @@ __global__ void __launch_bounds__(kTkThreads) topk_select_kernel(
             kstar = resolve_kstar(row_key, n, prefix1, need1, 2, sh);
           }
         }
-        // ---- ordered output: one block scan of the per-thread counts; the ids (and
-        // scores) are gathered in shared memory, then leave in 16-byte stores
-        uint32_t mask = sure;
-        for (uint32_t c = cand; c; c &= c - 1) {
-          const uint32_t j = __ffs(c) - 1;
-          if (record_key(recs[f0 + j]) >= kstar) mask |= 1u << j;
+        // ---- ordered output: {key >= K*} (K* >= 1 excludes the pad records).
+        // Pass 1 counts each (j, warp) group's selected records; one block scan
+        // over the nj * kTkWarps groups (group order = record order) gives their
+        // output offsets; pass 2 places each record at its group's offset plus its
+        // rank among the group's selected lanes.  The ids (and scores) are
+        // gathered in shared memory, then leave in 16-byte stores.
+        if (kstar == 0ull) kstar = 1ull;
+        const uint32_t lt = (1u << lane) - 1u;
+        for (uint32_t j = 0; j < nj; ++j) {
+          const unsigned b = __ballot_sync(0xffffffffu, rec_at(j) >= kstar);
+          if (lane == 0) sh.grp[j * kTkWarps + warp] = uint32_t(__popc(b));
         }
+        __syncthreads();
         uint32_t total_sel = 0;
-        uint32_t pos = block_excl_scan(__popc(mask), total_sel, sh);
+        const uint32_t goff =
+            block_excl_scan(uint32_t(tid) < nj * kTkWarps ? sh.grp[tid] : 0u, total_sel, sh);
+        if (uint32_t(tid) < nj * kTkWarps) sh.grp[tid] = goff;  // each thread rewrites only its own entry
+        __syncthreads();
         const bool gather = k <= (osrow != nullptr ? kTkRankCap : 2 * kTkRankCap) && (k & 3) == 0 &&
                             (reinterpret_cast<uintptr_t>(orow) & 15u) == 0 &&
                             (reinterpret_cast<uintptr_t>(osrow) & 15u) == 0;
         int32_t* gid = reinterpret_cast<int32_t*>(sh.rank);
         float* gsc = reinterpret_cast<float*>(sh.rank) + k;
-        while (mask) {
-          const uint32_t j = __ffs(mask) - 1;
-          mask &= mask - 1;
-          if (pos < uint32_t(k)) {
-            const uint64_t rec = recs[f0 + j];
-            const int32_t id = int32_t(0x7fffffffu - (uint32_t(rec) & 0x7fffffffu));
-            const float sc = __uint_as_float(uint32_t(rec >> 31));
-            if (gather) {
-              gid[pos] = id;
-              if (osrow != nullptr) gsc[pos] = sc;
-            } else {
-              orow[pos] = id;
-              if (osrow != nullptr) osrow[pos] = sc;
+        if (gather) {
+          // branch-free: unselected lanes store to the sink words
+          for (uint32_t j = 0; j < nj; ++j) {
+            const uint64_t rec = rec_at(j);
+            const bool sel = rec >= kstar;
+            const unsigned b = __ballot_sync(0xffffffffu, sel);
+            const uint32_t pos = sh.grp[j * kTkWarps + warp] + uint32_t(__popc(b & lt));
+            const bool put = sel && pos < uint32_t(k);
+            *(put ? gid + pos : reinterpret_cast<int32_t*>(&sh.sink4[0])) = record_id(rec);
+            if (osrow != nullptr) *(put ? gsc + pos : reinterpret_cast<float*>(&sh.sink4[1])) = record_score(rec);
+          }
+        } else {
+          for (uint32_t j = 0; j < nj; ++j) {
+            const uint64_t rec = rec_at(j);
+            const bool sel = rec >= kstar;
+            const unsigned b = __ballot_sync(0xffffffffu, sel);
+            const uint32_t pos = sh.grp[j * kTkWarps + warp] + uint32_t(__popc(b & lt));
+            if (sel && pos < uint32_t(k)) {
+              orow[pos] = record_id(rec);
+              if (osrow != nullptr) osrow[pos] = record_score(rec);
             }
           }
-          ++pos;
         }
         if (gather) {
           const uint32_t got = total_sel < uint32_t(k) ? total_sel : uint32_t(k);
-          for (uint32_t p = got + tid; p < uint32_t(k); p += kTkThreads) {
-            gid[p] = -1;
-            if (osrow != nullptr) gsc[p] = -CUDART_INF_F;
+          for (uint32_t p0 = 0; p0 < uint32_t(k); p0 += kTkThreads) {
+            const uint32_t p = p0 + uint32_t(tid);
+            if (p >= got && p < uint32_t(k)) {
+              gid[p] = -1;
+              if (osrow != nullptr) gsc[p] = -CUDART_INF_F;
+            }
           }
           __syncthreads();
-          for (int p = 4 * tid; p < k; p += 4 * kTkThreads) {
-            *reinterpret_cast<int4*>(orow + p) = *reinterpret_cast<const int4*>(gid + p);
-            if (osrow != nullptr) *reinterpret_cast<float4*>(osrow + p) = *reinterpret_cast<const float4*>(gsc + p);
+          for (int p0 = 0; p0 < k; p0 += 4 * kTkThreads) {
+            const int p = p0 + 4 * tid;
+            if (p < k) {
+              *reinterpret_cast<int4*>(orow + p) = *reinterpret_cast<const int4*>(gid + p);
+              if (osrow != nullptr)
+                *reinterpret_cast<float4*>(osrow + p) = *reinterpret_cast<const float4*>(gsc + p);
+            }
           }
           total_sel = uint32_t(k);  // the padding is written
         }
@@ -845,8 +938,8 @@ __global__ void __launch_bounds__(kTkThreads) topk_select_kernel(
             if ((bal[j] >> lane) & 1u) {
               const uint32_t pos = base + before + __popc(bal[j] & ((1u << lane) - 1u));
               if (pos < uint32_t(k)) {
-                orow[pos] = int32_t(0x7fffffffu - (uint32_t(rec[j]) & 0x7fffffffu));
-                if (osrow != nullptr) osrow[pos] = __uint_as_float(uint32_t(rec[j] >> 31));
+                orow[pos] = record_id(rec[j]);
+                if (osrow != nullptr) osrow[pos] = record_score(rec[j]);
               }
             }
             base += all;
@@ -856,9 +949,12 @@ __global__ void __launch_bounds__(kTkThreads) topk_select_kernel(
         }
         chosen = written < uint32_t(k) ? written : uint32_t(k);
       }
-      for (int p = int(chosen) + tid; p < k; p += kTkThreads) {
-        orow[p] = -1;
-        if (osrow != nullptr) osrow[p] = -CUDART_INF_F;
+      for (int p0 = int(chosen) & ~(kTkThreads - 1); p0 < k; p0 += kTkThreads) {
+        const int p = p0 + tid;
+        if (p >= int(chosen) && p < k) {
+          orow[p] = -1;
+          if (osrow != nullptr) osrow[p] = -CUDART_INF_F;
+        }
       }
       // every CTA of the row is done with its state: clear it for the next call
   #pragma unroll
@@ -919,6 +1015,7 @@ int launch_topk(const float* scores, const int32_t* ids, const int32_t* lengths,
   cfg.stream = stream;
   cfg.attrs = attr;
   uint8_t* ws = static_cast<uint8_t*>(workspace);
+  const CtaSplit split = make_split(rows * ((row_stride + 31) / 32), ctas, (row_stride + 31) / 32);
   if (!hist_ready) {
     static bool configured = false;
     if (!configured) {
@@ -935,8 +1032,9 @@ int launch_topk(const float* scores, const int32_t* ids, const int32_t* lengths,
     cfg.blockDim = dim3(kHsThreads, 1, 1);
     const cudaError_t e =
         ids != nullptr
-            ? cudaLaunchKernelEx(&cfg, topk_hist_kernel<true>, scores, ids, lengths, rows, row_stride, ws)
-            : cudaLaunchKernelEx(&cfg, topk_hist_kernel<false>, scores, ids, lengths, rows, row_stride, ws);
+            ? cudaLaunchKernelEx(&cfg, topk_hist_kernel<true>, scores, ids, lengths, rows, row_stride, ws, split)
+            : cudaLaunchKernelEx(&cfg, topk_hist_kernel<false>, scores, ids, lengths, rows, row_stride, ws,
+                                 split);
     cfg.dynamicSmemBytes = 0;
     cfg.blockDim = dim3(kTkThreads, 1, 1);
     if (e != cudaSuccess) return fail(DSR_ECUDA, "topk histogram launch: %s", cudaGetErrorString(e));
@@ -962,11 +1060,11 @@ int launch_topk(const float* scores, const int32_t* ids, const int32_t* lengths,
   const cudaError_t e =
       ids != nullptr
           ? cudaLaunchKernelEx(&cfg, topk_select_kernel<true, 4>, scores, ids, lengths, out_ids,
-                               out_scores, err, rows, row_stride, int(k), id_base, ws)
+                               out_scores, err, rows, row_stride, int(k), id_base, ws, split)
       : wide ? cudaLaunchKernelEx(&cfg, topk_select_kernel<false, 16>, scores, ids, lengths, out_ids,
-                                  out_scores, err, rows, row_stride, int(k), id_base, ws)
+                                  out_scores, err, rows, row_stride, int(k), id_base, ws, split)
              : cudaLaunchKernelEx(&cfg, topk_select_kernel<false, 4>, scores, ids, lengths, out_ids,
-                                  out_scores, err, rows, row_stride, int(k), id_base, ws);
+                                  out_scores, err, rows, row_stride, int(k), id_base, ws, split);
   if (e != cudaSuccess) return fail(DSR_ECUDA, "topk launch: %s", cudaGetErrorString(e));
   return DSR_OK;
 }
