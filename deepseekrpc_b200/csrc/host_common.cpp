@@ -76,26 +76,6 @@ int encode_tmap_bf16_2d(CUtensorMap* map, const void* base, uint64_t inner, uint
   return DSR_OK;
 }
 
-// A 64-key pool block (64 rows x 256 bytes) as ONE box: dims (64 columns, 8 rows,
-// 2 column halves, row groups of 8) with byte strides (256, 128, 2048), box
-// (64, 8, 2, 8).  The box lands as [8 groups][2 halves][8 rows][128 B], i.e. each
-// 8-row half is one 1024-byte 128-byte-swizzle atom; its global reads are the
-// block's 16 contiguous KB.
-int encode_tmap_bf16_rowblocks(CUtensorMap* map, const void* base, uint64_t rows) {
-  EncodeTiledFn fn = encode_fn();
-  if (!fn) return fail(DSR_ECUDA, "cuTensorMapEncodeTiled is unavailable");
-  const cuuint64_t dims[4] = {64, 8, 2, rows / 8};
-  const cuuint64_t strides[3] = {256, 128, 2048};
-  const cuuint32_t box[4] = {64, 8, 2, 8};
-  const cuuint32_t elem[4] = {1, 1, 1, 1};
-  const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims,
-                        strides, box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) return fail(DSR_ECUDA, "cuTensorMapEncodeTiled (row blocks) failed (%d)", int(r));
-  return DSR_OK;
-}
-
 }  // namespace dsr
 
 extern "C" const char* dsr_last_error(void) { return dsr::g_message.c_str(); }

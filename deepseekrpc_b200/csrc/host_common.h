@@ -24,8 +24,6 @@ int sm_count();
 // Encodes a 2-D bf16 tensor map (row-major [outer, inner]) with 128-byte swizzle.
 int encode_tmap_bf16_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer,
                         uint32_t box_inner, uint32_t box_outer);
-// 64-row blocks of a [rows][128] bf16 tensor, one 16 KB box each (4D view).
-int encode_tmap_bf16_rowblocks(CUtensorMap* map, const void* base, uint64_t rows);
 
 inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
 
