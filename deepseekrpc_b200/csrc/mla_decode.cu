@@ -43,14 +43,172 @@ struct MlaLayout {
   static constexpr int kRedOff = kQOff + kQBytes;
   static constexpr int kTpk = kMlaTile / HG;               // threads per head
   static constexpr int kRedBytes = 2 * kTpk * HG * 4;
-  static constexpr int kValidOff = kRedOff + kRedBytes;
-  static constexpr int kBarOff = kValidOff + kMlaTile * 4;
-  static constexpr int kMiscOff = kBarOff + (4 + kMlaBlocks) * 8;
+  static constexpr int kValidOff = kRedOff + kRedBytes;       // [2][kMlaTile] (two items in flight)
+  static constexpr int kBarOff = kValidOff + 2 * kMlaTile * 4;
+  static constexpr int kMiscOff = kBarOff + (5 + kMlaBlocks) * 8;
   static constexpr int kBytes = kMiscOff + 16;
   static constexpr int kAlloc = kBytes + 1024;
   static constexpr uint32_t kTmemCols = 5 * HG <= 128 ? 128 : (5 * HG <= 256 ? 256 : 512);
   static_assert(kPOff + 2 * HG * 128 <= kRedOff, "P^T must fit in the query region");
 };
+
+// Row sentinel past the tensor (the gather zero-fills it): tile 0 reads the SWA rows.
+__device__ __forceinline__ int32_t mla_oob_row(int tile, int batch, int64_t pool_blocks) {
+  return tile == 0 ? int32_t(batch) * DSR_SWA_ROWS : int32_t(pool_blocks * 64);
+}
+
+// Row of key slot t of `tile` for sequence b (top-k ids come from the preceding
+// kernel): tile 0 is the SWA window, tiles 1.. the selected positions through the
+// block table.  `oob` when the slot holds no key.
+__device__ __forceinline__ int32_t mla_key_row(int tile, int b, int t, int32_t oob, int64_t pool_blocks,
+                                               const int32_t* __restrict__ block_table, int64_t table_stride,
+                                               const int32_t* __restrict__ visible,
+                                               const int32_t* __restrict__ topk, int k,
+                                               const int32_t* __restrict__ swa_len, int64_t id_base,
+                                               int foreign_ok, int32_t* err) {
+  int32_t row = oob;
+  if (tile == 0) {
+    int len = swa_len[b];
+    if (len < 0 || len > DSR_SWA_ROWS) {
+      if (t == 0) flag(err, DSR_ERR_ID);
+      len = 0;
+    }
+    if (t < len) row = b * DSR_SWA_ROWS + t;
+  } else {
+    const int idx = (tile - 1) * kMlaTile + t;
+    if (idx < k) {
+      const int id = topk[int64_t(b) * k + idx];
+      if (id != -1) {
+        // position id lives in this pool at local row id - id_base; with
+        // foreign_ok, ids owned by another shard are skipped, not errors
+        const int64_t local = int64_t(id) - id_base;
+        if (id < 0) {
+          flag(err, DSR_ERR_ID);
+        } else if (local < 0 || local >= visible[b]) {
+          if (!foreign_ok) flag(err, DSR_ERR_ID);
+        } else {
+          const int64_t blk = block_table[int64_t(b) * table_stride + (local >> 6)];
+          if (blk < 0 || blk >= pool_blocks) flag(err, DSR_ERR_ID);
+          else row = int32_t(blk * 64 + (local & 63));
+        }
+      }
+    }
+  }
+  return row;
+}
+
+// Warp w gathers the rows of key slots 32w..32w+31 (lane l holds slot 32w + l's
+// row) as 4-row TMA gathers of 64-column slabs into the 9 swizzled column blocks
+// at kv_smem, column-block major: every warp issues block 0 of its 8 row groups
+// first, so the score MMA can start on block 0 while later blocks are in flight.
+__device__ __forceinline__ void mla_gather_rows(uint32_t kv_smem, const CUtensorMap* map, uint64_t* bar_kv,
+                                                int warp, int lane, int32_t row) {
+#pragma unroll
+  for (int i = 0; i < 3; ++i) {
+    const int j = lane + 32 * i;
+    const int jj = j < 8 * kMlaBlocks ? j : 0;
+    const int c = jj >> 3, g = jj & 7;
+    const int32_t r0 = __shfl_sync(0xffffffffu, row, 4 * g);
+    const int32_t r1 = __shfl_sync(0xffffffffu, row, 4 * g + 1);
+    const int32_t r2 = __shfl_sync(0xffffffffu, row, 4 * g + 2);
+    const int32_t r3 = __shfl_sync(0xffffffffu, row, 4 * g + 3);
+    if (j < 8 * kMlaBlocks)
+      tma_gather4(kv_smem + c * 16384 + (warp * 32 + 4 * g) * 128, map, bar_kv + c, c * 64, r0, r1, r2, r3);
+  }
+}
+
+// The 128 key threads of a tile, after the score MMA (`ok`: it completed): scores
+// of key t for the HG heads -> transposed fp32 buffer (query region) -> per-head
+// max / exp / sum (kTpk threads per head, HG keys each) -> P^T (bf16, K-major)
+// for the O MMA, then one arrival each on bar_p, then the tile's statistics
+// (log2-unit max, sum) at part_m / part_l + pidx.  Every thread reaches every
+// named barrier, whatever `ok`.
+template <int HG>
+__device__ __forceinline__ void mla_softmax(uint8_t* smem, uint32_t tmem_s, int warp, int t, bool ok,
+                                            const int* valid, float scale_log2, uint64_t* bar_p, float* red,
+                                            float* __restrict__ part_m, float* __restrict__ part_l,
+                                            int64_t pidx, int32_t* err) {
+  using L = MlaLayout<HG>;
+  float* sT = reinterpret_cast<float*>(smem + L::kQOff);  // [HG][kSPitch]
+  if (ok) {
+    tc_fence_after();
+    const bool v = valid[t] != 0;
+    const uint32_t taddr = tmem_s + (uint32_t(warp * 32) << 16);
+    uint32_t r[HG];
+#pragma unroll
+    for (int c = 0; c < HG; c += 16) tmem_ld16(taddr + c, *reinterpret_cast<uint32_t(*)[16]>(r + c));
+    tmem_wait_ld();
+#pragma unroll
+    for (int c = 0; c < HG; ++c) {
+      const float s = __uint_as_float(r[c]) * scale_log2;
+      if (v && !isfinite(s)) flag(err, DSR_ERR_NONFINITE);
+      sT[c * L::kSPitch + t] = v ? s : -CUDART_INF_F;
+    }
+  }
+  asm volatile("bar.sync 1, 128;" ::: "memory");
+  const int h = t % HG, part = t / HG;
+  const int kb = part * HG;  // first key of this thread
+  float mx = -CUDART_INF_F;
+  if (ok) {
+    float m4[4] = {-CUDART_INF_F, -CUDART_INF_F, -CUDART_INF_F, -CUDART_INF_F};  // independent chains
+#pragma unroll
+    for (int i = 0; i < HG; ++i) m4[i & 3] = fmaxf(m4[i & 3], sT[h * L::kSPitch + kb + i]);
+    mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
+    red[part * HG + h] = mx;
+  }
+  asm volatile("bar.sync 1, 128;" ::: "memory");
+  if (ok) {
+    for (int p = 0; p < L::kTpk; ++p) mx = fmaxf(mx, red[p * HG + h]);
+    const float base = mx == -CUDART_INF_F ? 0.f : mx;
+    uint8_t* pT = smem + L::kPOff;
+    float l4[4] = {0.f, 0.f, 0.f, 0.f};  // independent chains
+#pragma unroll
+    for (int i0 = 0; i0 < HG; i0 += 8) {
+      uint32_t packed[4];
+#pragma unroll
+      for (int j = 0; j < 8; j += 2) {
+        const float s0 = sT[h * L::kSPitch + kb + i0 + j];
+        const float s1 = sT[h * L::kSPitch + kb + i0 + j + 1];
+        const __nv_bfloat16 p0 = __float2bfloat16_rn(exp2f(s0 - base));
+        const __nv_bfloat16 p1 = __float2bfloat16_rn(exp2f(s1 - base));
+        l4[j >> 1] += __bfloat162float(p0) + __bfloat162float(p1);
+        packed[j >> 1] = __bfloat16_as_ushort(p0) | (uint32_t(__bfloat16_as_ushort(p1)) << 16);
+      }
+      const int key = kb + i0;  // P^T[h][key..key+7], K-major: 64 keys per column block
+      *reinterpret_cast<uint4*>(pT + (key >> 6) * (HG * 128) + sw128_offset(h, key & 63)) =
+          make_uint4(packed[0], packed[1], packed[2], packed[3]);
+    }
+    red[L::kTpk * HG + part * HG + h] = (l4[0] + l4[1]) + (l4[2] + l4[3]);
+  }
+  fence_proxy_async_smem();
+  mbar_arrive(bar_p);
+  asm volatile("bar.sync 1, 128;" ::: "memory");
+  // ---- partial statistics of this tile
+  if (t < HG) {
+    float l = 0.f;
+    for (int p = 0; p < L::kTpk; ++p) l += red[L::kTpk * HG + p * HG + t];
+    part_m[pidx + t] = mx;  // identical in every thread of head t (log2 units)
+    part_l[pidx + t] = l;
+  }
+}
+
+// O^T (lane = value column, columns = heads) from TMEM to the bf16 tile partial
+// at o (the range of fp32, half the bytes).
+template <int HG>
+__device__ __forceinline__ void mla_store_o(uint32_t tmem_o, int warp, int t, uint16_t* __restrict__ o) {
+#pragma unroll 1
+  for (int c = 0; c < kMlaDv / 128; ++c) {
+    const uint32_t taddr = tmem_o + c * HG + (uint32_t(warp * 32) << 16);
+    const int d = c * 128 + t;
+    uint32_t r[HG];
+#pragma unroll
+    for (int hh = 0; hh < HG; hh += 16) tmem_ld16(taddr + hh, *reinterpret_cast<uint32_t(*)[16]>(r + hh));
+    tmem_wait_ld();
+#pragma unroll
+    for (int hh = 0; hh < HG; ++hh)
+      o[int64_t(hh) * kMlaDv + d] = __bfloat16_as_ushort(__float2bfloat16_rn(__uint_as_float(r[hh])));
+  }
+}
 
 template <int HG>
 __global__ void __launch_bounds__(kMlaThreads, 1)
@@ -164,134 +322,24 @@ __global__ void __launch_bounds__(kMlaThreads, 1)
     }
     // ---- resolve the row of key t (top-k ids come from the preceding kernel);
     // rows past the tensor (the OOB sentinel) are zero-filled by the gather
-    const int32_t oob = tile == 0 ? int32_t(gridDim.y) * DSR_SWA_ROWS : int32_t(pool_blocks * 64);
-    int32_t row = oob;
-    if (tile == 0) {
-      int len = swa_len[b];
-      if (len < 0 || len > DSR_SWA_ROWS) {
-        if (t == 0) flag(err, DSR_ERR_ID);
-        len = 0;
-      }
-      if (t < len) row = b * DSR_SWA_ROWS + t;
-    } else {
-      const int idx = (tile - 1) * kMlaTile + t;
-      if (idx < k) {
-        const int id = topk[int64_t(b) * k + idx];
-        if (id != -1) {
-          // position id lives in this pool at local row id - id_base; with
-          // foreign_ok, ids owned by another shard are skipped, not errors
-          const int64_t local = int64_t(id) - id_base;
-          if (id < 0) {
-            flag(err, DSR_ERR_ID);
-          } else if (local < 0 || local >= visible[b]) {
-            if (!foreign_ok) flag(err, DSR_ERR_ID);
-          } else {
-            const int64_t blk = block_table[int64_t(b) * table_stride + (local >> 6)];
-            if (blk < 0 || blk >= pool_blocks) flag(err, DSR_ERR_ID);
-            else row = int32_t(blk * 64 + (local & 63));
-          }
-        }
-      }
-    }
+    const int32_t oob = mla_oob_row(tile, int(gridDim.y), pool_blocks);
+    const int32_t row = mla_key_row(tile, b, t, oob, pool_blocks, block_table, table_stride, visible, topk, k,
+                                    swa_len, id_base, foreign_ok, err);
     valid[t] = row != oob;
     // ---- gather: 4-row TMA gathers of 64-column slabs into the 9 swizzled
     // column blocks; warp w issues the 8 x 9 gathers of its rows 32w..32w+31
     if (t == 0)
       for (int c = 0; c < kMlaBlocks; ++c) mbar_arrive_expect_tx(bar_kv + c, kMlaTile * 128);
-    const CUtensorMap* map = tile == 0 ? &swa_map : &kv_map;
-    // column-block major: every warp issues block 0 of its 8 row groups first, so the
-    // score MMA can start on block 0 while the later blocks are still in flight
-#pragma unroll
-    for (int i = 0; i < 3; ++i) {
-      const int j = lane + 32 * i;
-      const int jj = j < 8 * kMlaBlocks ? j : 0;
-      const int c = jj >> 3, g = jj & 7;
-      const int32_t r0 = __shfl_sync(0xffffffffu, row, 4 * g);
-      const int32_t r1 = __shfl_sync(0xffffffffu, row, 4 * g + 1);
-      const int32_t r2 = __shfl_sync(0xffffffffu, row, 4 * g + 2);
-      const int32_t r3 = __shfl_sync(0xffffffffu, row, 4 * g + 3);
-      if (j < 8 * kMlaBlocks)
-        tma_gather4(sbase + L::kKvOff + c * 16384 + (warp * 32 + 4 * g) * 128, map, bar_kv + c, c * 64,
-                    r0, r1, r2, r3);
-    }
+    mla_gather_rows(sbase + L::kKvOff, tile == 0 ? &swa_map : &kv_map, bar_kv, warp, lane, row);
 
-    // ---- scores of key t for the HG heads -> transposed fp32 buffer (query region)
+    // ---- scores, softmax over the tile's keys, P^T for the O MMA, tile statistics
     bool ok = mbar_wait(bar_s, 0, abort, err);
-    float* sT = reinterpret_cast<float*>(smem + L::kQOff);  // [HG][kSPitch]
-    if (ok) {
-      tc_fence_after();
-      const bool v = valid[t] != 0;
-      const uint32_t taddr = tmem_s + (uint32_t(warp * 32) << 16);
-      uint32_t r[HG];
-#pragma unroll
-      for (int c = 0; c < HG; c += 16) tmem_ld16(taddr + c, *reinterpret_cast<uint32_t(*)[16]>(r + c));
-      tmem_wait_ld();
-#pragma unroll
-      for (int c = 0; c < HG; ++c) {
-        const float s = __uint_as_float(r[c]) * scale_log2;
-        if (v && !isfinite(s)) flag(err, DSR_ERR_NONFINITE);
-        sT[c * L::kSPitch + t] = v ? s : -CUDART_INF_F;
-      }
-    }
-    asm volatile("bar.sync 1, 128;" ::: "memory");
-    // ---- per-head max / exp / sum: kTpk threads per head, HG keys each
-    const int h = t % HG, part = t / HG;
-    const int kb = part * HG;  // first key of this thread
-    float mx = -CUDART_INF_F;
-    if (ok) {
-      for (int i = 0; i < HG; ++i) mx = fmaxf(mx, sT[h * L::kSPitch + kb + i]);
-      red[part * HG + h] = mx;
-    }
-    asm volatile("bar.sync 1, 128;" ::: "memory");
-    if (ok) {
-      for (int p = 0; p < L::kTpk; ++p) mx = fmaxf(mx, red[p * HG + h]);
-      const float base = mx == -CUDART_INF_F ? 0.f : mx;
-      uint8_t* pT = smem + L::kPOff;
-      float lsum = 0.f;
-      for (int i0 = 0; i0 < HG; i0 += 8) {
-        uint32_t packed[4];
-#pragma unroll
-        for (int j = 0; j < 8; j += 2) {
-          const float s0 = sT[h * L::kSPitch + kb + i0 + j];
-          const float s1 = sT[h * L::kSPitch + kb + i0 + j + 1];
-          const __nv_bfloat16 p0 = __float2bfloat16_rn(exp2f(s0 - base));
-          const __nv_bfloat16 p1 = __float2bfloat16_rn(exp2f(s1 - base));
-          lsum += __bfloat162float(p0) + __bfloat162float(p1);
-          packed[j >> 1] = __bfloat16_as_ushort(p0) | (uint32_t(__bfloat16_as_ushort(p1)) << 16);
-        }
-        const int key = kb + i0;  // P^T[h][key..key+7], K-major: 64 keys per column block
-        *reinterpret_cast<uint4*>(pT + (key >> 6) * (HG * 128) + sw128_offset(h, key & 63)) =
-            make_uint4(packed[0], packed[1], packed[2], packed[3]);
-      }
-      red[L::kTpk * HG + part * HG + h] = lsum;
-    }
-    fence_proxy_async_smem();
-    mbar_arrive(bar_p);
-    asm volatile("bar.sync 1, 128;" ::: "memory");
-    // ---- partial statistics of this tile
     const int64_t pidx = (int64_t(b) * tiles + tile) * heads + h0;
-    if (t < HG) {
-      float l = 0.f;
-      for (int p = 0; p < L::kTpk; ++p) l += red[L::kTpk * HG + p * HG + t];
-      part_m[pidx + t] = mx;  // identical in every thread of head t (log2 units)
-      part_l[pidx + t] = l;
-    }
+    mla_softmax<HG>(smem, tmem_s, warp, t, ok, valid, scale_log2, bar_p, red, part_m, part_l, pidx, err);
     // ---- O^T: lane = value column, columns = heads
     if (ok && mbar_wait(bar_o, 0, abort, err)) {
       tc_fence_after();
-      uint16_t* o = part_o + pidx * kMlaDv;  // bf16: the range of fp32, half the bytes
-#pragma unroll 1
-      for (int c = 0; c < kMlaDv / 128; ++c) {
-        const uint32_t taddr = tmem_o + c * HG + (uint32_t(warp * 32) << 16);
-        const int d = c * 128 + t;
-        uint32_t r[HG];
-#pragma unroll
-        for (int hh = 0; hh < HG; hh += 16) tmem_ld16(taddr + hh, *reinterpret_cast<uint32_t(*)[16]>(r + hh));
-        tmem_wait_ld();
-#pragma unroll
-        for (int hh = 0; hh < HG; ++hh)
-          o[int64_t(hh) * kMlaDv + d] = __bfloat16_as_ushort(__float2bfloat16_rn(__uint_as_float(r[hh])));
-      }
+      mla_store_o<HG>(tmem_o, warp, t, part_o + pidx * kMlaDv);
     }
   } else if (lane == 0) {
     // ------------------------------------------------------------ MMA issuer
@@ -341,6 +389,197 @@ __global__ void __launch_bounds__(kMlaThreads, 1)
     for (int c = 0; c < kMlaBlocks; ++c) mbar_drain(bar_kv + c, 0);
     if (q_img != nullptr) mbar_drain(bar_q, 0);
   }
+  if (warp == 4) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, L::kTmemCols);
+  }
+}
+
+// Persistent form for grids of more than one wave (a batch): one CTA per SM
+// walks the items (tile, sequence, head group), tile fastest, with stride
+// gridDim.x.  Per item the phases are those of mla_decode_kernel; what changes is
+// the overlap: the next item's rows are resolved while this item's score MMA
+// runs, and its query image and row gathers are issued as soon as this item's
+// O MMA has released the row and query buffers, so they land while this item's
+// O^T leaves TMEM.  Every barrier completes once per item (phase parity = item
+// count & 1); bar_ofree (128 arrivals) tells the MMA issuer that the previous
+// item's O^T has been read before it overwrites those TMEM columns.  The query
+// comes from the BF16 image only.  (The issuing stays with the key warps: the
+// TMA unit takes the 288 row gathers one at a time, faster from four warps than
+// from a dedicated loader warp, and one row buffer serialises gather and compute
+// of consecutive items anyway.)
+template <int HG>
+__global__ void __launch_bounds__(kMlaThreads, 1)
+    mla_persistent_kernel(const __grid_constant__ CUtensorMap kv_map,
+                          const __grid_constant__ CUtensorMap swa_map, int64_t pool_blocks,
+                          const int32_t* __restrict__ block_table, int64_t table_stride,
+                          const int32_t* __restrict__ visible, const int32_t* __restrict__ topk, int k,
+                          const int32_t* __restrict__ swa_len, float scale_log2,
+                          uint16_t* __restrict__ part_o, float* __restrict__ part_m,
+                          float* __restrict__ part_l, int32_t* err, int heads, int batch, int tiles,
+                          const uint16_t* __restrict__ q_img, int64_t id_base, int foreign_ok) {
+  using L = MlaLayout<HG>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  const uint32_t sbase = smem_u32(smem);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBarOff);
+  uint64_t* bar_s = bars + 0;
+  uint64_t* bar_p = bars + 1;
+  uint64_t* bar_o = bars + 2;
+  uint64_t* bar_q = bars + 3;
+  uint64_t* bar_kv = bars + 4;
+  uint64_t* bar_ofree = bars + 4 + kMlaBlocks;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kMiscOff);
+  volatile int* abort = reinterpret_cast<volatile int*>(smem + L::kMiscOff + 4);
+  int* valid = reinterpret_cast<int*>(smem + L::kValidOff);  // [2][kMlaTile]
+  float* red = reinterpret_cast<float*>(smem + L::kRedOff);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int items = tiles * batch * (heads / HG);
+  auto item_of = [&](int it, int& tile, int& b, int& hg) {
+    tile = it % tiles;
+    const int r = it / tiles;
+    b = r % batch;
+    hg = r / batch;
+  };
+
+  if (threadIdx.x == 0) {
+    tma_prefetch_desc(&swa_map);
+    tma_prefetch_desc(&kv_map);
+    for (int c = 0; c < kMlaBlocks; ++c) mbar_init(bar_kv + c, 1);
+    mbar_init(bar_s, 1);
+    mbar_init(bar_p, 128);
+    mbar_init(bar_o, 1);
+    mbar_init(bar_q, 1);
+    mbar_init(bar_ofree, 128);
+    *abort = 0;
+    fence_barrier_init();
+  }
+  if (warp == 4) {
+    tmem_alloc(tmem_slot, L::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const uint32_t tmem_s = tmem_base;
+  const uint32_t tmem_o = tmem_base + HG;
+
+  pdl_launch_dependents();  // the combine kernel may start its prologue early
+  pdl_wait();               // top-k ids and the query image come from the preceding kernels
+
+  if (warp < 4) {
+    const int t = threadIdx.x;  // key slot of this thread == TMEM lane
+    int issued = 0;             // items whose query and rows were requested (thread 0's count)
+    // query image (thread 0) and row gathers (every warp) of item `it`
+    auto issue = [&](int it, int32_t row) {
+      int tile, b, hg;
+      item_of(it, tile, b, hg);
+      if (t == 0) {
+        constexpr uint32_t kBytes = kMlaBlocks * HG * 128;
+        const int gi = heads < 64 ? heads : 64;
+        const int h0 = hg * HG;
+        const uint8_t* img = reinterpret_cast<const uint8_t*>(q_img) +
+                             ((int64_t(b) * (heads / gi) + h0 / gi) * kMlaBlocks * gi + h0 % gi) * 128;
+        mbar_arrive_expect_tx(bar_q, kBytes);
+        if (gi == HG) {
+          bulk_load(sbase + L::kQOff, img, kBytes, bar_q);
+        } else {
+#pragma unroll 1
+          for (int c = 0; c < kMlaBlocks; ++c)
+            bulk_load(sbase + L::kQOff + c * (HG * 128), img + int64_t(c) * gi * 128, HG * 128, bar_q);
+        }
+        for (int c = 0; c < kMlaBlocks; ++c) mbar_arrive_expect_tx(bar_kv + c, kMlaTile * 128);
+        ++issued;
+      }
+      mla_gather_rows(sbase + L::kKvOff, tile == 0 ? &swa_map : &kv_map, bar_kv, warp, lane, row);
+    };
+    auto resolve = [&](int it, int slot) -> int32_t {
+      int tile, b, hg;
+      item_of(it, tile, b, hg);
+      const int32_t oob = mla_oob_row(tile, batch, pool_blocks);
+      const int32_t row = mla_key_row(tile, b, t, oob, pool_blocks, block_table, table_stride, visible, topk,
+                                      k, swa_len, id_base, foreign_ok, err);
+      valid[slot * kMlaTile + t] = row != oob;
+      return row;
+    };
+    if (int(blockIdx.x) < items) issue(blockIdx.x, resolve(blockIdx.x, 0));
+    int n = 0;
+    for (int it = blockIdx.x; it < items; it += gridDim.x, ++n) {
+      const uint32_t par = uint32_t(n) & 1u;
+      const int next = it + int(gridDim.x);
+      // the next item's rows, while this item's score MMA runs (its valid[] slot was
+      // last read by the item before this one; each thread reads only its own entry)
+      const int32_t row_next = next < items ? resolve(next, (n + 1) & 1) : 0;
+      int tile, b, hg;
+      item_of(it, tile, b, hg);
+      const int64_t pidx = (int64_t(b) * tiles + tile) * heads + hg * HG;
+      const bool ok = mbar_wait(bar_s, par, abort, err);
+      mla_softmax<HG>(smem, tmem_s, warp, t, ok, valid + (n & 1) * kMlaTile, scale_log2, bar_p, red, part_m,
+                      part_l, pidx, err);
+      const bool o_ok = ok && mbar_wait(bar_o, par, abort, err);
+      // the O MMA has read the rows and P^T: the next item's query and rows may land
+      // (the abort flag is read once per warp: the gathers shuffle across all lanes)
+      const bool go = next < items && __shfl_sync(0xffffffffu, *abort == 0 ? 1 : 0, 0) != 0;
+      if (go) issue(next, row_next);
+      if (o_ok) {
+        tc_fence_after();
+        mla_store_o<HG>(tmem_o, warp, t, part_o + pidx * kMlaDv);
+      }
+      tc_fence_before();
+      mbar_arrive(bar_ofree);
+    }
+    if (*abort && t == 0 && issued > 0) {
+      // let the last requested query and rows land before exit
+      const uint32_t last = uint32_t(issued - 1) & 1u;
+      for (int c = 0; c < kMlaBlocks; ++c) mbar_drain(bar_kv + c, last);
+      mbar_drain(bar_q, last);
+    }
+  } else if (warp == 4 && lane == 0) {
+    // ------------------------------------------------------------ MMA issuer
+    constexpr uint32_t idesc_s = umma_idesc_bf16(128, HG, false, false);
+    constexpr uint32_t idesc_o = umma_idesc_bf16(128, HG, true, false);
+    int n = 0, committed_o = 0;
+    for (int it = blockIdx.x; it < items; it += gridDim.x, ++n) {
+      const uint32_t par = uint32_t(n) & 1u;
+      bool ready = mbar_wait(bar_q, par, abort, err);
+#pragma unroll 1
+      for (int c = 0; c < kMlaBlocks && ready; ++c) {
+        ready = mbar_wait(bar_kv + c, par, abort, err);
+        if (!ready) break;
+        tc_fence_after();
+#pragma unroll
+        for (int sub = 0; sub < 4; ++sub) {
+          const uint64_t ad = umma_desc_sw128(sbase + L::kKvOff + c * 16384 + sub * 32, 16, 1024);
+          const uint64_t bd = umma_desc_sw128(sbase + L::kQOff + c * (HG * 128) + sub * 32, 16, 1024);
+          umma_bf16(tmem_s, ad, bd, idesc_s, (c | sub) != 0 ? 1u : 0u);
+        }
+      }
+      if (!ready) break;
+      umma_commit(bar_s);
+      if (!mbar_wait(bar_p, par, abort, err)) break;
+      // the previous item's O^T has left TMEM
+      if (n > 0 && !mbar_wait(bar_ofree, par ^ 1u, abort, err)) break;
+      tc_fence_after();
+#pragma unroll 1
+      for (int ks = 0; ks < kMlaTile / 16; ++ks) {
+#pragma unroll
+        for (int c = 0; c < kMlaDv / 128; ++c) {
+          const uint64_t ad = umma_desc_sw128(sbase + L::kKvOff + (2 * c) * 16384 + ks * 2048, 16384, 1024);
+          const uint64_t bd =
+              umma_desc_sw128(sbase + L::kPOff + (ks >> 2) * (HG * 128) + (ks & 3) * 32, 16, 1024);
+          umma_bf16(tmem_o + c * HG, ad, bd, idesc_o, ks > 0 ? 1u : 0u);
+        }
+      }
+      umma_commit(bar_o);
+      ++committed_o;
+    }
+    // the last O MMAs retire before TMEM is released
+    if (committed_o > 0) mbar_drain(bar_o, uint32_t(committed_o - 1) & 1u);
+  }
+  tc_fence_before();
+  __syncthreads();
   if (warp == 4) {
     tc_fence_after();
     tmem_dealloc(tmem_base, L::kTmemCols);
@@ -549,8 +788,10 @@ int launch_mla(const float* q, const uint16_t* kv_pool, int64_t pool_blocks,
   using L = MlaLayout<HG>;
   static bool configured = false;
   if (!configured) {
-    const cudaError_t e = cudaFuncSetAttribute(
-        mla_decode_kernel<HG>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kAlloc);
+    cudaError_t e = cudaFuncSetAttribute(mla_decode_kernel<HG>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         L::kAlloc);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(mla_persistent_kernel<HG>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kAlloc);
     if (e != cudaSuccess) return fail(DSR_ECUDA, "mla smem attribute: %s", cudaGetErrorString(e));
     configured = true;
   }
@@ -570,6 +811,18 @@ int launch_mla(const float* q, const uint16_t* kv_pool, int64_t pool_blocks,
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
+  // more items than one wave (a batch): one persistent CTA per SM overlaps each
+  // item's output with the next item's loads (the BF16 query image is required)
+  const int64_t items = int64_t(tiles) * batch * (heads / HG);
+  if (q_img != nullptr && items > sm_count()) {
+    cfg.gridDim = dim3(unsigned(sm_count()), 1, 1);
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, mla_persistent_kernel<HG>, kv_map, swa_map, pool_blocks,
+                                             block_table, table_stride, visible, topk, int(k), swa_len,
+                                             scale * kLog2e, part_o, part_m, part_l, err, int(heads),
+                                             int(batch), tiles, q_img, id_base, int(foreign_ok));
+    if (e != cudaSuccess) return fail(DSR_ECUDA, "mla launch: %s", cudaGetErrorString(e));
+    return DSR_OK;
+  }
   const cudaError_t e = cudaLaunchKernelEx(&cfg, mla_decode_kernel<HG>, kv_map, swa_map, q, kv_pool,
                                            pool_blocks,
                                            block_table, table_stride, visible, topk, int(k), swa,

@@ -129,3 +129,10 @@ def test_decode_step_config2_full_size(cuda):
 def test_decode_step_ragged_batch(cuda):
     cfg = small_config("cfg3", batch=5, seed=36)
     run_step_and_check(cfg, lengths=[1, 130, 2048, 9000, 70000])
+
+
+def test_decode_step_multiwave_batch(cuda):
+    # 12 sequences x 17 tiles exceed one wave of CTAs: the persistent MLA kernel
+    # walks several (tile, sequence) items per CTA with the next item's loads in flight
+    cfg = small_config("cfg3", batch=12, seed=37)
+    run_step_and_check(cfg, lengths=[300, 2047, 2048, 2049, 4000, 5100, 6000, 6500, 7000, 8191, 8192, 9000])
