@@ -47,8 +47,7 @@ constexpr int kTkThreads = 512;   // selection CTA
 constexpr int kTkWarps = kTkThreads / 32;
 constexpr int kTkBins = 2048;      // digits 0 and 1: 11 bits each
 constexpr int kTkMaxCtas = 256;    // CTAs of one launch (one staged-count slot each; fits uint8)
-constexpr int kHsThreads = 256;   // histogram CTA
-constexpr int kHsWarps = kHsThreads / 32;
+constexpr int kHsThreads = 1024;  // histogram CTA
 constexpr int kTkVec = 8;          // 4-entry runs per thread per histogram batch
 constexpr int kTkChunk = kHsThreads * 4 * kTkVec;  // entries per histogram batch
 // staging chunks: kTkThreads * kPer consecutive entries; kPer = 16 when a CTA
@@ -259,26 +258,28 @@ __device__ __forceinline__ int64_t row_length(const int32_t* lengths, int64_t r,
 // ---------------------------------------------------------------------------
 // Standalone histogram pass (the decode step gets it from the indexer).
 // ---------------------------------------------------------------------------
-// Scores cluster in few digit-0 bins, so on long ranges every warp counts into a
-// histogram of its own (kHsWarps * kTkBins words of dynamic shared memory):
-// same-bin updates from different warps would serialise on one shared word.
-// Short ranges share one histogram (less to clear and flush).
-constexpr size_t kTkHistSmem = size_t(kHsWarps) * kTkBins * 4;
-constexpr int64_t kTkHistSplit = 16384;  // entries per CTA from which the warps split
+// Scores cluster in few digit-0 bins, and the lanes of a warp that add to one
+// shared word serialise.  On long ranges every bin therefore has kHsCopies
+// counters side by side (bin-major: word bin * kHsCopies + lane / 2), so the lanes
+// holding one bin hit kHsCopies different banks; a pair of lanes shares a word.
+// Short ranges use one counter per bin (less to clear and flush).
+constexpr int kHsCopies = 16;
+constexpr size_t kTkHistSmem = size_t(kTkBins) * kHsCopies * 4;
+constexpr int64_t kTkHistSplit = 16384;  // entries per CTA from which the counters split
 
 template <bool kIds>
 __global__ void __launch_bounds__(kHsThreads) topk_hist_kernel(
     const float* __restrict__ scores, const int32_t* __restrict__ ids,
     const int32_t* __restrict__ lengths, int64_t rows, int64_t row_stride,
     uint8_t* __restrict__ ws_base, const CtaSplit split) {
-  extern __shared__ uint32_t whist[];  // [kHsWarps][kTkBins]
+  extern __shared__ uint32_t whist[];  // [kTkBins][copies]
   const TopkWs L(rows, row_stride);
   uint32_t* ghist = reinterpret_cast<uint32_t*>(ws_base + L.hist);
-  const int tid = threadIdx.x, warp = tid >> 5;
+  const int tid = threadIdx.x;
   int64_t w0, w1;
   cta_words(split, blockIdx.x, w0, w1);
-  const int copies = (w1 - w0) * 32 >= kTkHistSplit ? kHsWarps : 1;
-  uint32_t* hist = whist + (warp % copies) * kTkBins;
+  const int copies = (w1 - w0) * 32 >= kTkHistSplit ? kHsCopies : 1;
+  const uint32_t my_copy = copies > 1 ? uint32_t((tid & 31) >> 1) : 0u;
   for (int i = tid; i < copies * kTkBins; i += kHsThreads) whist[i] = 0u;
   pdl_launch_dependents();
   pdl_wait();
@@ -316,14 +317,15 @@ __global__ void __launch_bounds__(kHsThreads) topk_hist_kernel(
       }
 #pragma unroll
       for (int j = 0; j < 4 * kTkVec; ++j)
-        if (u[j]) atomicAdd(&hist[u[j] >> 21], 1u);
+        if (u[j]) atomicAdd(&whist[(u[j] >> 21) * uint32_t(copies) + my_copy], 1u);
     }
     __syncthreads();
     for (int i = tid; i < kTkBins; i += kHsThreads) {
       uint32_t v = 0;
-      for (int w = 0; w < copies; ++w) {
-        v += whist[w * kTkBins + i];
-        whist[w * kTkBins + i] = 0u;
+      for (int c = 0; c < copies; ++c) {
+        const int w = i * copies + ((c + i) & (copies - 1));  // rotated: neighbouring bins on other banks
+        v += whist[w];
+        whist[w] = 0u;
       }
       if (v) atomicAdd(ghist + r * kTkBins + i, v);
     }
