@@ -26,9 +26,14 @@ def main(argv=None) -> int:
     parser.add_argument("--steps", type=int, default=4)
     parser.add_argument("--prefill", type=int, nargs=2, metavar=("QUERIES", "CONTEXT"),
                         help="instead: the prefill indexer GEMM, QUERIES causal queries ending at CONTEXT keys")
+    parser.add_argument("--topk-rows", type=int, nargs=2, metavar=("ROWS", "CONTEXT"),
+                        help="instead: the exact top-2048 (histogram pass + selection) of ROWS causal rows of "
+                             "scores ending at CONTEXT keys, as in one of config 4's launches")
     args = parser.parse_args(argv)
     if args.prefill:
         return prefill(*args.prefill, args.steps)
+    if args.topk_rows:
+        return topk_rows(*args.topk_rows, args.steps)
     cfg = CONFIGS[args.config]
     torch.cuda.set_device(0)
     inp, lengths = make_decode_inputs(cfg, device="cuda:0", gen_device="cuda")
@@ -73,6 +78,31 @@ def prefill(queries: int, context: int, steps: int) -> int:
     status = int(err.item())
     print(f"{steps} prefill indexer launches, {queries} queries x {context} keys: device status {status}")
     return 0 if status == 0 else 1
+
+
+
+def topk_rows(rows: int, context: int, steps: int) -> int:
+    """`steps` launches of the standalone top-k over `rows` causal rows of seeded
+    N(0, 64^2) scores (row r sees context - rows + 1 + r keys), histogram pass
+    included, as the prefill path runs it over materialised scores."""
+    torch.cuda.set_device(0)
+    k = 2048
+    gen = torch.Generator(device="cuda:0").manual_seed(3)
+    scores = torch.randn((rows, context), generator=gen, device="cuda:0") * 64
+    visible = torch.arange(context - rows + 1, context + 1, dtype=torch.int32, device="cuda:0")
+    lib = _native.library()
+    ws_bytes = lib.dsr_topk_workspace_bytes(rows, context)
+    ws = torch.zeros(ws_bytes, dtype=torch.uint8, device="cuda:0")
+    out = torch.empty((rows, k), dtype=torch.int32, device="cuda:0")
+    err = torch.zeros(1, dtype=torch.int32, device="cuda:0")
+    stream = _native.stream_handle(torch.cuda.current_stream())
+    for _ in range(steps):
+        _native.call("dsr_topk_select", scores.data_ptr(), None, visible.data_ptr(), out.data_ptr(), None,
+                     err.data_ptr(), rows, context, k, 0, ws.data_ptr(), ws_bytes, stream)
+    torch.cuda.synchronize()
+    code = int(err.item())
+    print(f"top-k {rows} x {context}: {steps} launches, device status {code}")
+    return 0 if code == 0 else 1
 
 
 if __name__ == "__main__":
