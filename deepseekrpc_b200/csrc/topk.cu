@@ -539,7 +539,8 @@ __global__ void __launch_bounds__(kTkThreads) topk_select_kernel(
         }
         // keep: at or above the threshold bin's lower edge, compared as floats (the
         // key map is monotone; NaN ranks above +inf); kept entries are rare, so
-        // their keys, digit-1 counts and records are built only in a branch
+        // their keys, digit-1 counts and records are built in one branch, after
+        // the block scan that places them
         uint32_t mask = 0;
         const int64_t room = ok ? e1 - i : 0;  // valid entries of this thread's run
   #pragma unroll
@@ -547,16 +548,6 @@ __global__ void __launch_bounds__(kTkThreads) topk_select_kernel(
           const float sv = __uint_as_float(raw[q]);
           const bool keep = q < room && (!kIds || idv[q] >= 0) && (take_all || sv >= thr_f || sv != sv);
           mask |= uint32_t(keep) << q;
-        }
-        if (mask != 0u) {
-  #pragma unroll
-          for (int q = 0; q < kTkPer; ++q)
-            if ((mask >> q) & 1u) {
-              const uint32_t u = rank_u(raw[q]);
-              raw[q] = u;  // kept entries carry their key from here on
-              if (kIds && idv[q] == 0x7fffffff) flag(err, DSR_ERR_ID);  // reserved for the pad record
-              if (!whole_bin && (u >> 21) == s0.bin) atomicAdd(h1row + ((u >> 10) & (kTkBins - 1)), 1u);
-            }
         }
         const uint32_t cnt = __popc(mask);
         uint32_t incl = cnt;
@@ -583,8 +574,11 @@ __global__ void __launch_bounds__(kTkThreads) topk_select_kernel(
   #pragma unroll
           for (int q = 0; q < kTkPer; ++q)
             if ((mask >> q) & 1u) {
+              const uint32_t u = rank_u(raw[q]);
+              if (kIds && idv[q] == 0x7fffffff) flag(err, DSR_ERR_ID);  // reserved for the pad record
+              if (!whole_bin && (u >> 21) == s0.bin) atomicAdd(h1row + ((u >> 10) & (kTkBins - 1)), 1u);
               const uint32_t id = kIds ? uint32_t(idv[q]) : uint32_t(id_base + i + q);
-              srec[e0 + pos] = composite(raw[q], 0x7fffffffu - id);
+              srec[e0 + pos] = composite(u, 0x7fffffffu - id);
               ++pos;
             }
         }
