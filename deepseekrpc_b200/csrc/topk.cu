@@ -24,11 +24,12 @@
 //     area, counts the digit 1 of its threshold-bin entries into a second row
 //     histogram, and takes a ticket;
 //   * the CTA that takes the last ticket of a row copies all staged records
-//     into shared memory at once (16-byte loads, every thread), reads the
-//     digit-1 histogram, ranks the few entries that share both digits with K*
-//     pairwise, selects {key >= K*} with one compare per record, and writes the
-//     selected ids (and scores) through one block scan of per-thread counts;
-//     then it clears the row's histograms and ticket.
+//     into shared memory at once (warp-wide 16-byte loads for short slots, one
+//     bulk copy per long slot), reads the digit-1 histogram, ranks the few
+//     entries that share both digits with K* pairwise, selects {key >= K*} with
+//     one compare per record, and places the selected ids (and scores) in
+//     entry order by two ballot passes around one block scan of per-(pass,
+//     warp) counts; then it clears the row's histograms and ticket.
 // More than kTkRankCap entries sharing K*'s two digits (massively tied scores)
 // are ranked over the whole row; more than kTkRecCap staged records are walked
 // from L2 in chunks.  The workspace must be zero before its first use; every
