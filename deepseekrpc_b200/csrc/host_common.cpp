@@ -1,7 +1,9 @@
 // Host-side helpers: per-thread error messages, device queries, tensor maps.
 #include "host_common.h"
 
+#include <map>
 #include <mutex>
+#include <utility>
 
 namespace dsr {
 
@@ -58,6 +60,21 @@ int sm_count() {
     counts[device] = n;
   }
   return counts[device];
+}
+
+int set_max_smem_raw(const void* fn, int bytes, const char* what) {
+  int device = 0;
+  if (cudaGetDevice(&device) != cudaSuccess) return fail(DSR_ECUDA, "%s: no current CUDA device", what);
+  static std::mutex mu;
+  static std::map<std::pair<int, const void*>, int> limit;  // largest limit set so far
+  std::lock_guard<std::mutex> lock(mu);
+  int& have = limit[{device, fn}];
+  if (have >= bytes) return DSR_OK;
+  const cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e != cudaSuccess)
+    return fail(DSR_ECUDA, "%s: shared-memory attribute: %s", what, cudaGetErrorString(e));
+  have = bytes;
+  return DSR_OK;
 }
 
 int encode_tmap_bf16_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer,

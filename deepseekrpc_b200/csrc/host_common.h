@@ -21,6 +21,14 @@ void clear_error();
 int launch_status(const char* what);
 // Multiprocessor count of the current device (cached per device).
 int sm_count();
+// Raises the dynamic shared-memory limit of kernel `fn` on the CURRENT device to
+// at least `bytes` (the attribute belongs to the device's copy of the kernel).
+// Remembered per (device, kernel), thread-safe; returns DSR_OK or DSR_ECUDA.
+int set_max_smem_raw(const void* fn, int bytes, const char* what);
+template <typename F>
+inline int set_max_smem(F* fn, size_t bytes, const char* what) {
+  return set_max_smem_raw(reinterpret_cast<const void*>(fn), int(bytes), what);
+}
 // Encodes a 2-D bf16 tensor map (row-major [outer, inner]) with 128-byte swizzle.
 int encode_tmap_bf16_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer,
                         uint32_t box_inner, uint32_t box_outer);

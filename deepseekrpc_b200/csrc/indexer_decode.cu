@@ -448,12 +448,9 @@ int launch_ix(const CUtensorMap& map, const float* q, const float* weights,
               const float* mla_q, uint16_t* mla_img, int mla_heads, uint32_t* hist,
               cudaStream_t stream, bool pdl) {
   using L = IxLayout<H>;
-  static bool configured = false;
-  if (!configured) {
-    const cudaError_t e = cudaFuncSetAttribute(
-        indexer_decode_kernel<H>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kAlloc);
-    if (e != cudaSuccess) return fail(DSR_ECUDA, "indexer smem attribute: %s", cudaGetErrorString(e));
-    configured = true;
+  {
+    const int rc = set_max_smem(indexer_decode_kernel<H>, L::kAlloc, "indexer decode");
+    if (rc != DSR_OK) return rc;
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(unsigned(sm_count()), 1, 1);

@@ -366,12 +366,9 @@ int launch_pf(const CUtensorMap& map, const float* q, const float* weights,
               int64_t pool_blocks, float* scores, int64_t score_stride, int32_t* err, int queries,
               cudaStream_t stream) {
   using L = PfLayout<H>;
-  static bool configured = false;
-  if (!configured) {
-    const cudaError_t e = cudaFuncSetAttribute(
-        indexer_prefill_kernel<H>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kAlloc);
-    if (e != cudaSuccess) return fail(DSR_ECUDA, "prefill indexer smem attribute: %s", cudaGetErrorString(e));
-    configured = true;
+  {
+    const int rc = set_max_smem(indexer_prefill_kernel<H>, L::kAlloc, "prefill indexer");
+    if (rc != DSR_OK) return rc;
   }
   indexer_prefill_kernel<H><<<sm_count(), kPfThreads, L::kAlloc, stream>>>(
       map, q, weights, block_table, table_stride, visible, pool_blocks, scores, score_stride, err,

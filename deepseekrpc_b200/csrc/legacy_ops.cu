@@ -341,10 +341,9 @@ extern "C" int dsr_index_scores(const float* q, const uint16_t* keys, const floa
   const int64_t blocks_x = (columns + kIdxKeys - 1) / kIdxKeys;
   DSR_REQUIRE(blocks_x <= 2147483647LL, "too many index columns");
   const size_t smem = (kIdxDim * 64 + kIdxKeys * kIdxDim + 64 + 64) * sizeof(float);
-  static bool configured = false;
-  if (!configured) {
-    cudaFuncSetAttribute(legacy_index_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
-    configured = true;
+  {
+    const int rc = set_max_smem(legacy_index_kernel, smem, "index_scores");
+    if (rc != DSR_OK) return rc;
   }
   legacy_index_kernel<<<dim3(unsigned(blocks_x), unsigned(rows)), 256, smem, as_stream(stream)>>>(
       q, keys, weights, ids, visible, out, err, int(heads), columns, capacity);
@@ -372,12 +371,9 @@ extern "C" int dsr_sparse_attention(const float* q, const uint16_t* window, cons
                   (reinterpret_cast<uintptr_t>(source) & 3u) == 0,
               "window/source rows must be 4-byte aligned");
   const size_t smem = size_t(kAttChunk) * (width / 2 + 1) * 4 + 8 * width * 4 + kAttChunk * 4;
-  static bool configured = false;
-  if (!configured) {
-    cudaFuncSetAttribute(legacy_sparse_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         int(size_t(kAttChunk) * (kAttMaxWidth / 2 + 1) * 4 + 8 * kAttMaxWidth * 4 +
-                             kAttChunk * 4));
-    configured = true;
+  {
+    const int rc = set_max_smem(legacy_sparse_kernel, smem, "sparse_attention");
+    if (rc != DSR_OK) return rc;
   }
   legacy_sparse_kernel<<<dim3(unsigned(rows), unsigned((heads + 7) / 8)), 256, smem,
                          as_stream(stream)>>>(q, window, source, ids, sink, out, err, int(heads),

@@ -786,14 +786,10 @@ int launch_mla(const float* q, const uint16_t* kv_pool, int64_t pool_blocks,
                int64_t batch, int64_t heads, int tiles, cudaStream_t stream, bool pdl,
                const uint16_t* q_img, int64_t id_base, bool foreign_ok) {
   using L = MlaLayout<HG>;
-  static bool configured = false;
-  if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(mla_decode_kernel<HG>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         L::kAlloc);
-    if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(mla_persistent_kernel<HG>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kAlloc);
-    if (e != cudaSuccess) return fail(DSR_ECUDA, "mla smem attribute: %s", cudaGetErrorString(e));
-    configured = true;
+  {
+    int rc = set_max_smem(mla_decode_kernel<HG>, L::kAlloc, "mla decode");
+    if (rc == DSR_OK) rc = set_max_smem(mla_persistent_kernel<HG>, L::kAlloc, "mla decode");
+    if (rc != DSR_OK) return rc;
   }
   // row-gather tensor maps: one-row boxes of 64 columns over the pool and the SWA rows
   CUtensorMap kv_map, swa_map;

@@ -8,7 +8,10 @@
 // store goes to one peer): CTA (peer p, chunk c) copies chunk c of the local payload into
 // slot `rank` of p's receive buffer, then adds one to p's arrival counter for
 // `rank` with a system-scope release; CTA 0 then waits (bounded) until every
-// source's counter reaches epoch * chunks, and advances the local epoch.
+// source's counter reaches epoch * chunks, and advances the local epoch.  A wait
+// that runs out sets DSR_ERR_TIMEOUT and still advances the epoch; the slots of
+// that exchange then hold a mix of steps, so after a timeout every rank
+// re-creates its exchange buffers before exchanging again.
 //
 // Exchange buffer (identical layout on every rank; allocated and mapped by
 // dsr_p2p_alloc / dsr_p2p_open):
@@ -76,10 +79,12 @@ __global__ void __launch_bounds__(kP2pThreads) p2p_allgather_kernel(
       if (__all_sync(0xffffffffu, done)) break;
       if ((spin & 63u) == 63u && global_ns() - start > kWaitNs) {
         if (threadIdx.x == 0) flag(err, DSR_ERR_TIMEOUT);
-        return;  // a peer never arrived: the status is set, the epoch is not advanced
+        break;  // a peer never arrived: the status is set
       }
     }
-    if (threadIdx.x == 0) ctl[kEpochIdx] = epoch;  // read by this rank's next exchange only
+    // read by this rank's next exchange only; advanced after a timeout too, so
+    // that a late arrival of the abandoned exchange cannot complete the next one
+    if (threadIdx.x == 0) ctl[kEpochIdx] = epoch;
   }
 }
 

@@ -1014,16 +1014,9 @@ int launch_topk(const float* scores, const int32_t* ids, const int32_t* lengths,
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   const CtaSplit split = make_split(rows * ((row_stride + 31) / 32), ctas, (row_stride + 31) / 32);
   if (!hist_ready) {
-    static bool configured = false;
-    if (!configured) {
-      cudaError_t e = cudaFuncSetAttribute(topk_hist_kernel<true>,
-                                           cudaFuncAttributeMaxDynamicSharedMemorySize, int(kTkHistSmem));
-      if (e == cudaSuccess)
-        e = cudaFuncSetAttribute(topk_hist_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 int(kTkHistSmem));
-      if (e != cudaSuccess) return fail(DSR_ECUDA, "topk histogram smem attribute: %s", cudaGetErrorString(e));
-      configured = true;
-    }
+    int rc = set_max_smem(topk_hist_kernel<true>, kTkHistSmem, "topk histogram");
+    if (rc == DSR_OK) rc = set_max_smem(topk_hist_kernel<false>, kTkHistSmem, "topk histogram");
+    if (rc != DSR_OK) return rc;
     cfg.numAttrs = pdl ? 1 : 0;
     cfg.dynamicSmemBytes = kTkHistSmem;
     cfg.blockDim = dim3(kHsThreads, 1, 1);
@@ -1039,18 +1032,11 @@ int launch_topk(const float* scores, const int32_t* ids, const int32_t* lengths,
   } else {
     cfg.numAttrs = pdl ? 1 : 0;
   }
-  static bool select_configured = false;
-  if (!select_configured) {
-    cudaError_t e = cudaFuncSetAttribute(topk_select_kernel<true, 4>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, int(kTkDynSmem));
-    if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(topk_select_kernel<false, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               int(kTkDynSmem));
-    if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(topk_select_kernel<false, 16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               int(kTkDynSmem));
-    if (e != cudaSuccess) return fail(DSR_ECUDA, "topk smem attribute: %s", cudaGetErrorString(e));
-    select_configured = true;
+  {
+    int rc = set_max_smem(topk_select_kernel<true, 4>, kTkDynSmem, "topk select");
+    if (rc == DSR_OK) rc = set_max_smem(topk_select_kernel<false, 4>, kTkDynSmem, "topk select");
+    if (rc == DSR_OK) rc = set_max_smem(topk_select_kernel<false, 16>, kTkDynSmem, "topk select");
+    if (rc != DSR_OK) return rc;
   }
   cfg.dynamicSmemBytes = kTkDynSmem;
   const bool wide = rows * ((row_stride + 31) / 32) * 32 / ctas >= kTkWideRange;

@@ -2,9 +2,13 @@
  * dsr_b200.h -- C ABI of the B200 (sm_100a) attention hot path of DeepSeekRPC.
  *
  * Every entry point takes plain device pointers, element counts and a
- * cudaStream_t passed as `void*` (NULL = legacy default stream).  No entry point
- * allocates device memory, synchronizes the stream or reads device data on the
- * host.  Work is enqueued on `stream` only.
+ * cudaStream_t passed as `void*` (NULL = legacy default stream).  The compute
+ * entry points allocate no device memory (callers pass outputs and scratch),
+ * never synchronize the stream and never read device data on the host; work is
+ * enqueued on `stream` only.  The exceptions are the peer-exchange set-up calls
+ * at the end of this header: dsr_p2p_alloc / dsr_p2p_free allocate and free the
+ * exchange buffer (cudaMalloc / cudaFree) and dsr_p2p_open / dsr_p2p_close map
+ * and unmap a peer's buffer (CUDA IPC), once per process, outside the step.
  *
  * Two error channels, as in the reference extension:
  *   - host return value: DSR_OK, or a negative code for argument / shape / bound
@@ -117,9 +121,11 @@ int dsr_topk_select(const float* scores, const int32_t* ids, const int32_t* leng
  * Scratch is a fixed DSR_TOPK_NOALLOC_BYTES array inside this library (one per
  * device); calls with dsr_topk_workspace_bytes(rows, row_stride) above it are
  * refused with DSR_EINVAL before any CUDA call (e.g. 8 rows x 131072 entries
- * fit, 16 rows x 131072 do not).  Nothing is allocated: the first call on a
- * device resolves the array's address (cudaGetSymbolAddress), so make that
- * first call outside any stream capture; each call clears the zero-initialised
+ * fit, 16 rows x 131072 do not).  Nothing is allocated: a call outside stream
+ * capture looks the array's address up (cudaGetSymbolAddress) on the current
+ * device; a captured call reuses the address of the last uncaptured call on
+ * that device, so make the first call on each device outside any stream
+ * capture (after a device reset, make one more); each call clears the zero-initialised
  * part of the scratch with cudaMemsetAsync on `stream` before its kernels.
  * All calls on one device share the scratch: calls that overlap on the GPU
  * (different streams, or threads without ordering) race and must be
@@ -352,6 +358,8 @@ int dsr_pool_restore(uint16_t* data, int64_t* generations, int64_t slots, int64_
  * peers, and maps theirs (dsr_p2p_open).  buffers[w] is rank w's buffer as
  * mapped in this process (buffers[rank] the local one); the host array is read
  * at launch.  All ranks must issue the same exchanges in the same order.
+ * After DSR_ERR_TIMEOUT the receive slots may hold a mix of steps: every rank
+ * frees and re-creates its exchange buffers before the next exchange.
  * ------------------------------------------------------------------------- */
 #define DSR_P2P_MAX_WORLD 8
 #define DSR_P2P_HANDLE_BYTES 64

@@ -36,6 +36,10 @@ def test_noalloc_refuses_sizes_beyond_its_scratch_without_a_device():
     assert lib.dsr_topk_select_noalloc(1, None, 1, 1, None, 1, 16, 131072, 2048, 0, None) == _native.DSR_EINVAL
     assert "scratch" in _native.last_error()
     assert lib.dsr_topk_select_noalloc(1, None, 1, 1, None, 1, 1, 1 << 30, 2048, 0, None) == _native.DSR_EINVAL
+    # ids past int32 (id_base + entries) are refused before any CUDA call too
+    assert lib.dsr_topk_select_noalloc(1, None, 1, 1, None, 1, 1, 4096, 2048, (1 << 31) - 4096, None) == \
+        _native.DSR_EINVAL
+    assert "id_base" in _native.last_error()
 
 
 @pytest.mark.gpu
