@@ -5,7 +5,7 @@ Layers:
   deepseekrpc_cuda (torch extension)    the reference module's op names on that ABI
   cuda_ops, index_selection             host-side mirrors of the reference modules
   sharded                               sequence sharding across GPUs (NCCL)
-  workloads, profile_step               seeded BASELINE-config inputs, profiler driver
+  workloads                             seeded BASELINE-config inputs
 """
 from __future__ import annotations
 

@@ -6,9 +6,12 @@
 // each a checked scatter_slots followed by a generation bump
 // (cache_pool.py:299-310, native/operations.cu:144-161); forward_mqa then writes
 // the SWA ring (vllm_attention.py:261).  Checks kept: physical bounds, no
-// repeated target in one batch, generation equal to the expected value, finite
-// BF16 payload.  Difference (documented in the C ABI): a failing row writes
-// nothing at all, instead of the reference's element-wise partial write.
+// repeated target in one batch (for the SWA ring: no repeated ring row, as the
+// reference's 128-slot windows pool refuses), generation equal to the expected
+// value, finite BF16 payload.  Difference (documented in the C ABI): a failing
+// row writes nothing at all, instead of the reference's element-wise partial
+// write, and the rows that pass are written and bumped even when another row of
+// the batch fails (the reference bumps a batch only when all of it passed).
 #include "common.cuh"
 #include "host_common.h"
 
@@ -39,9 +42,14 @@ __global__ void __launch_bounds__(128) append_kernel(
   if (threadIdx.x == 0) reject = row < 0 ? DSR_ERR_SCATTER : 0;
   __syncthreads();
   if (row >= 0) {
-    for (int j = threadIdx.x; j < i; j += blockDim.x)
-      if (physical_row(block_table, table_stride, table_rows, pool_blocks, seq[j], positions[j]) == row)
+    // an earlier row of the batch with the same physical row, or (with the SWA
+    // ring) the same sequence and ring row p % 128, refuses this one
+    for (int j = threadIdx.x; j < i; j += blockDim.x) {
+      const int32_t sj = seq[j], pj = positions[j];
+      if (physical_row(block_table, table_stride, table_rows, pool_blocks, sj, pj) == row ||
+          (swa != nullptr && sj == s && ((pj ^ p) & (DSR_SWA_ROWS - 1)) == 0))
         atomicCAS(&reject, 0, DSR_ERR_SCATTER);
+    }
     if (threadIdx.x == 0 && generations[row] != expected[i]) atomicCAS(&reject, 0, DSR_ERR_SCATTER);
   }
   __syncthreads();

@@ -308,36 +308,16 @@ class ShardedDecoder:
 # ------------------------------------------------------------------ inputs
 
 
-def make_shard_inputs(cfg, plan: ShardPlan, device, seed_offset: int = 0):
+def make_shard_inputs(cfg, plan: ShardPlan, device, layout_seed: int | None = None):
     """Seeded synthetic inputs of one rank: its own paged pools for the owned
-    positions of every sequence (blocks laid out by a seeded permutation), the
-    queries (identical on every rank: drawn from the config seed) and, on the
-    tail owner, the SWA rows."""
-    dev = torch.device(device)
-    gq = torch.Generator(device=dev)
-    gq.manual_seed(cfg.seed)
-    B = len(plan.lengths)
-    idx_q = torch.randn((B, cfg.idx_heads, INDEX_DIM), generator=gq, device=dev).to(torch.bfloat16).float()
-    idx_w = torch.randn((B, cfg.idx_heads), generator=gq, device=dev) * cfg.weight_scale
-    q = torch.randn((B, cfg.heads, KV_DIM), generator=gq, device=dev).to(torch.bfloat16).float()
-    sink = torch.randn((cfg.heads,), generator=gq, device=dev)
-    g = torch.Generator(device=dev)
-    g.manual_seed(cfg.seed * 1000003 + 7919 * (plan.rank + 1) + seed_offset)
-    local = plan.local_visible()
-    blocks = [(n + BLOCK - 1) // BLOCK for n in local]
-    total = max(1, sum(blocks))
-    index_pool = torch.randn((total * BLOCK, INDEX_DIM), generator=g, device=dev).to(torch.bfloat16)
-    kv_pool = torch.randn((total * BLOCK, KV_DIM), generator=g, device=dev).to(torch.bfloat16)
-    swa = torch.randn((B, SWA_ROWS, KV_DIM), generator=g, device=dev).to(torch.bfloat16)
-    perm = torch.randperm(total, generator=g, device=dev).to(torch.int32).cpu()
-    table = torch.full((B, plan.local_blocks()), -1, dtype=torch.int32)
-    start = 0
-    for b, nb in enumerate(blocks):
-        table[b, :nb] = perm[start:start + nb]
-        start += nb
-    return dict(idx_q=idx_q.contiguous(), idx_w=idx_w.float().contiguous(), q=q.contiguous(),
-                sink=sink.float().contiguous(), index_pool=index_pool.contiguous(), kv_pool=kv_pool.contiguous(),
-                swa=swa.contiguous(), block_table=table.to(dev).contiguous())
+    positions [id_base, id_base + span) of every sequence, drawn chunk by chunk
+    from generators seeded by (config seed, sequence, chunk) -- so every world
+    size holds the same logical rows -- and laid out by a per-rank permutation;
+    the queries, weights, SWA rows and sink (identical on every rank; swa_len is
+    nonzero on the tail owner only)."""
+    from .workloads import long_context_inputs
+    seed = 7919 * (plan.rank + 1) if layout_seed is None else layout_seed
+    return long_context_inputs(cfg, plan.lengths, device, start=plan.id_base, span=plan.span, layout_seed=seed)
 
 
 # ------------------------------------------------------------------- bench
@@ -379,63 +359,79 @@ def _timed_steps(fn, steps, stream, dev, group=None) -> float:
     return float(ms.item())
 
 
-def single_gpu_base(steps: int, warmup: int, device) -> dict:
-    """Config 5 on ONE GPU through the same sharded code (one shard, no
-    collectives): the 1-GPU point of the 1/2/4/8 strong-scaling series."""
-    cfg = CONFIGS["cfg5"]
-    dev = torch.device(device)
-    plan = ShardPlan(1, 0, tuple([cfg.context] * cfg.batch))
-    inputs = make_shard_inputs(cfg, plan, dev)
-    dec = ShardedDecoder(plan, cfg.heads, cfg.idx_heads, cfg.topk, cfg.scale, inputs["sink"], dev)
-    stream = torch.cuda.Stream(device=dev)
-
-    def step(_):
-        packed = dec.select_local(inputs["idx_q"], inputs["idx_w"], inputs["index_pool"], inputs["block_table"],
-                                  stream)
-        dec.merge(packed, stream)
-        partial = dec.attend_local(inputs["q"], inputs["kv_pool"], inputs["block_table"], inputs["swa"], stream)
-        dec.combine(partial, stream)
-
-    with torch.cuda.stream(stream):
-        for i in range(warmup):
-            step(i)
-    torch.cuda.synchronize()
-    assert int(dec.err.item()) == 0, f"device status {int(dec.err.item())}"
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph, stream=stream):
-        step(0)
-    torch.cuda.synchronize()
-    start = torch.cuda.Event(enable_timing=True)
-    end = torch.cuda.Event(enable_timing=True)
-    with torch.cuda.stream(stream):
-        graph.replay()
-        start.record(stream)
-        for i in range(steps):
-            graph.replay()
-        end.record(stream)
-    end.synchronize()
-    ms = start.elapsed_time(end) / steps
-    del inputs, dec
-    torch.cuda.empty_cache()
-    return {"workload": cfg.name + ", one shard on 1 GPU", "value": round(ms * 1e3, 3), "unit": "us",
-            "steps": steps, "note": "1-GPU point of the config-5 scaling series (bench.py --gpus N>1 "
-                                    "runs config 5 sharded over N ranks)"}
-
-
 # kernels of this library launched per sharded step: indexer, local top-k,
 # list exchange, merge, MLA partial (tiles + in-shard combine), partial
 # exchange, cross-shard combine
 LAUNCHES_PER_STEP = 8
 
 
-def bench_main(args, metric: str) -> None:
+def replicas_for_cold_l2(per_rank_bytes: int, device) -> int:
+    """Pool replicas a rank rotates through so that every step reads its pools
+    from DRAM: enough that R x the step's bytes exceed twice the L2 cache."""
+    l2 = torch.cuda.get_device_properties(device).L2_cache_size
+    return max(1, -(-int(2.2 * l2) // max(1, per_rank_bytes)))
+
+
+def single_gpu_reference(cfg, lengths, seq: int, device):
+    """Sequence `seq` decoded alone on this GPU through dsr_decode_step (whole
+    pools, same seeded rows): the (ids i32[k], out f32[heads, 512]) the sharded
+    step must reproduce."""
+    from .workloads import long_context_inputs
+    inp = long_context_inputs(cfg, lengths, device, sequences=[seq], layout_seed=12345)
+    lib = _native.library()
+    n = int(lengths[seq])
+    ws_bytes = lib.dsr_decode_workspace_bytes(1, n, cfg.heads, cfg.topk)
+    ws = torch.zeros(ws_bytes, dtype=torch.uint8, device=device)
+    out = torch.empty((1, cfg.heads, V_DIM), device=device)
+    ids = torch.empty((1, cfg.topk), dtype=torch.int32, device=device)
+    err = torch.zeros(1, dtype=torch.int32, device=device)
+    p = _native.ptr
+    _native.call("dsr_decode_step", p(inp["idx_q"]), p(inp["idx_w"]), cfg.idx_heads, p(inp["index_pool"]),
+                 p(inp["q"]), p(inp["kv_pool"]), cfg.heads, inp["kv_pool"].shape[0] // BLOCK,
+                 p(inp["block_table"]), inp["block_table"].shape[1], p(inp["visible"]), n, cfg.topk,
+                 p(inp["swa"]), p(inp["swa_len"]), p(inp["sink"]), float(cfg.scale), p(out), p(ids), None, p(ws),
+                 ws_bytes, p(err), 1, _native.stream_handle(torch.cuda.current_stream(device)))
+    torch.cuda.synchronize(device)
+    if int(err.item()) != 0:
+        raise RuntimeError(f"single-GPU reference step: device status {int(err.item())}")
+    return ids[0], out[0]
+
+
+def parity_against_single_gpu(cfg, lengths, ids, out, device, seq: int = 0, group=None) -> dict:
+    """Every rank compares its merged top-k (bit for bit) and its combined output
+    (BF16 tolerance: max abs <= 2e-2, mean abs <= 2e-3) for sequence `seq` with
+    rank 0's single-GPU decode of that sequence; all ranks agree on the verdict."""
+    rank = dist.get_rank(group)
+    ref_ids = torch.empty((cfg.topk,), dtype=torch.int32, device=device)
+    ref_out = torch.empty((cfg.heads, V_DIM), device=device)
+    if rank == 0:
+        r_ids, r_out = single_gpu_reference(cfg, lengths, seq, device)
+        ref_ids.copy_(r_ids)
+        ref_out.copy_(r_out)
+        torch.cuda.empty_cache()
+    dist.broadcast(ref_ids, 0, group=group)
+    dist.broadcast(ref_out, 0, group=group)
+    diff = (out[seq] - ref_out).abs()
+    ids_ok = bool(torch.equal(ids[seq], ref_ids))
+    max_abs, mean_abs = float(diff.max().item()), float(diff.mean().item())
+    ok = torch.tensor([1 if ids_ok and max_abs <= 2e-2 and mean_abs <= 2e-3 else 0], device=device)
+    dist.all_reduce(ok, op=dist.ReduceOp.MIN, group=group)
+    return {"parity_ok": bool(ok.item()), "sequence": seq, "topk_identical": ids_ok,
+            "out_max_abs": max_abs, "out_mean_abs": mean_abs,
+            "against": "dsr_decode_step of the same sequence on one GPU (same seeded rows)"}
+
+
+def bench_main(args, metric: str, config: dict, data: str) -> None:
     """bench.py --gpus N under torch.distributed.run: config 5 sharded over N ranks.
 
     `value` = µs per decode step of the whole job (4 sequences x 1,048,576
     positions, fixed as N grows: strong scaling), max over ranks of CUDA-event
-    time around K steps, barrier + synchronize on both sides.  `e2e` repeats the
-    steps with each rank's query inputs copied from pinned host memory and the
-    attention output copied back inside the timed region."""
+    time around K steps, barrier + synchronize on both sides.  Each rank rotates
+    through R copies of its pools when its share of a step is too small to
+    evict L2 by itself.  `e2e` repeats the steps with each rank's query inputs
+    copied from pinned host memory and the attention output copied back inside
+    the timed region.  After timing, every rank checks its result against a
+    single-GPU decode of sequence 0 (`parity_ok`)."""
     from datetime import timedelta
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", str(args.gpus)))
@@ -443,10 +439,18 @@ def bench_main(args, metric: str) -> None:
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
     dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    graph = e2e_graph = None
+    dec = None
     try:
+        from .workloads import algorithmic_bytes
         cfg = CONFIGS["cfg5"]
-        plan = ShardPlan(world, rank, tuple([cfg.context] * cfg.batch))
+        lengths = tuple([cfg.context] * cfg.batch)
+        plan = ShardPlan(world, rank, lengths)
         inputs = make_shard_inputs(cfg, plan, dev)
+        total_bytes = algorithmic_bytes(list(lengths), cfg.heads, cfg.topk, cfg.idx_heads)
+        R = replicas_for_cold_l2(total_bytes // world, dev)
+        replicas = [inputs] + [dict(inputs, index_pool=inputs["index_pool"].clone(),
+                                    kv_pool=inputs["kv_pool"].clone()) for _ in range(R - 1)]
         dec = ShardedDecoder(plan, cfg.heads, cfg.idx_heads, cfg.topk, cfg.scale, inputs["sink"], dev)
         # the two exchanges: NVLink peer stores (default) or the collective library
         exchange = os.environ.get("DSR_EXCHANGE", "peer")
@@ -456,17 +460,35 @@ def bench_main(args, metric: str) -> None:
             exchange = "nccl"
         stream = torch.cuda.Stream(device=dev)
         with torch.cuda.stream(stream):
-            for _ in range(args.warmup):
-                dec.step(inputs, stream=stream)
+            for i in range(args.warmup):
+                dec.step(replicas[i % R], stream=stream)
         torch.cuda.synchronize()
         assert int(dec.err.item()) == 0 and dec.exchange_status() == 0, \
             f"rank {rank}: device status {int(dec.err.item())}/{dec.exchange_status()}"
-        # one step (kernels and both exchanges) as a CUDA graph; every rank
-        # captures, so the exchanges line up; eager steps if capture is refused
-        graph = _capture(lambda: dec.step(inputs, stream=stream), stream)
-        run = (lambda i: graph.replay()) if graph is not None else (lambda i: dec.step(inputs, stream=stream))
-        step_ms = _timed_steps(run, args.steps, stream, dev)
-        run_graphed = graph is not None
+        # R steps (one per replica: kernels and both exchanges) as one CUDA graph,
+        # plus a graph of the K mod R remaining steps; every rank captures, so the
+        # exchanges line up; eager steps if capture is refused
+        K = args.steps
+        reps, rest = divmod(K, R)
+
+        def steps_fn(n):
+            return lambda: [dec.step(replicas[i % R], stream=stream) for i in range(n)]
+
+        graph = _capture(steps_fn(R), stream) if reps else None
+        tail = _capture(steps_fn(rest), stream) if rest else None
+        graphed = (graph is not None or not reps) and (tail is not None or not rest)
+        if graphed:
+            def run(i):
+                if i < reps:
+                    graph.replay()
+                else:
+                    tail.replay()
+            calls = reps + (1 if rest else 0)
+        else:
+            def run(i):
+                dec.step(replicas[i % R], stream=stream)
+            calls = K
+        step_ms = _timed_steps(run, calls, stream, dev) * calls / K
 
         # end to end: query inputs host -> device, output device -> host, every step
         names = ("idx_q", "idx_w", "q")
@@ -474,48 +496,57 @@ def bench_main(args, metric: str) -> None:
         h_in = torch.empty(sum(sizes), pin_memory=True)
         h_in.copy_(torch.cat([inputs[n].reshape(-1).cpu() for n in names]))
         d_in = torch.empty(sum(sizes), device=dev)
-        staged = dict(inputs)
-        off = 0
-        for n, size in zip(names, sizes):
-            staged[n] = d_in[off:off + size].view(inputs[n].shape)
-            off += size
+        staged = []
+        for rep in replicas:
+            st = dict(rep)
+            off = 0
+            for n, size in zip(names, sizes):
+                st[n] = d_in[off:off + size].view(inputs[n].shape)
+                off += size
+            staged.append(st)
         h_out = torch.empty(tuple(dec.out.shape), pin_memory=True)
 
-        def e2e_step(_):
+        def e2e_step(i):
             d_in.copy_(h_in, non_blocking=True)
-            out = dec.step(staged, stream=stream)
+            out = dec.step(staged[i % R], stream=stream)
             h_out.copy_(out, non_blocking=True)
 
         with torch.cuda.stream(stream):
             for i in range(3):
                 e2e_step(i)
-        e2e_graph = _capture(lambda: e2e_step(0), stream)
-        e2e_run = (lambda i: e2e_graph.replay()) if e2e_graph is not None else e2e_step
-        e2e_ms = _timed_steps(e2e_run, args.steps, stream, dev)
+        e2e_graph = _capture(lambda: [e2e_step(i) for i in range(R)], stream)
+        if e2e_graph is not None:
+            e2e_calls = max(1, K // R)
+            e2e_ms = _timed_steps(lambda i: e2e_graph.replay(), e2e_calls, stream, dev) / R
+        else:
+            e2e_ms = _timed_steps(e2e_step, K, stream, dev)
         torch.cuda.synchronize()
         assert int(dec.err.item()) == 0 and dec.exchange_status() == 0
-        graph = e2e_graph = None  # graphs holding collective work go before the process group
-        dec.close()
+        assert torch.equal(h_out, dec.out.cpu()), "e2e output differs from the device-resident run"
+
+        parity = parity_against_single_gpu(cfg, lengths, dec.ids, dec.out, dev)
+        graph = tail = e2e_graph = None  # graphs holding exchange work go before the process group
         if rank == 0:
-            from .workloads import algorithmic_bytes
-            total_bytes = algorithmic_bytes(list(plan.lengths), cfg.heads, cfg.topk, cfg.idx_heads)
             print(json.dumps({
                 "metric": metric, "value": round(step_ms * 1e3, 3), "unit": "us", "n_gpus": world,
-                "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(step_ms, 6),
+                "steps": K, "warmup": args.warmup, "ms_per_step": round(step_ms, 6),
                 "higher_is_better": False, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
-                "data": "synthetic (seeded N(0,1), BF16 pools per rank)",
-                "config": {"workload": cfg.name + f", sharded over {world} GPUs", "batch": cfg.batch,
-                           "context": cfg.context, "topk": cfg.topk, "heads": cfg.heads,
-                           "l2": "inputs larger than L2 on every rank", "parallelism": f"sequence shards x{world}",
-                           "exchange": ("NVLink peer stores (dsr_p2p_allgather)" if exchange == "peer"
-                                        else "NCCL all_gather")},
-                "step_hbm": {"bytes": total_bytes,
-                             "achieved_gbs": round(total_bytes / (step_ms * 1e-3) / 1e9, 1)},
+                "data": data, "config": config,
+                "step_hbm": {"bytes": total_bytes, "achieved_gbs": round(total_bytes / (step_ms * 1e-3) / 1e9, 1),
+                             "per_rank_bytes": total_bytes // world},
                 "e2e": {"value": round(e2e_ms * 1e3, 3), "unit": "us",
                         "h2d_bytes_per_step": world * h_in.numel() * 4,
                         "d2h_bytes_per_step": world * h_out.numel() * 4},
-                "gpu_launches": LAUNCHES_PER_STEP * args.steps,
-                "mode": "cuda graph per step" if run_graphed else "eager launches",
+                "gpu_launches": LAUNCHES_PER_STEP * K,
+                "parity_ok": parity["parity_ok"], "parity": parity,
+                "exchange": ("NVLink peer stores (dsr_p2p_allgather)" if exchange == "peer" else "NCCL all_gather"),
+                "replicas": R,
+                "l2": f"{R} pool replica(s) per rank rotated, {R * total_bytes // world / 1e6:.0f} MB per rotation "
+                      f"(> 2 x L2)" if R > 1 else "inputs larger than L2 on every rank",
+                "mode": "cuda graph per step" if graphed else "eager launches",
             }))
     finally:
+        graph = tail = e2e_graph = None
+        if dec is not None:
+            dec.close()
         dist.destroy_process_group()

@@ -274,7 +274,11 @@ int dsr_lse_combine_packed(const float* packed, int64_t world, const float* sink
  * earlier row of the batch, generations[row]==expected[i] and both value rows
  * are finite; then generations[row] = expected[i]+1.  Otherwise err = 3
  * (bounds / duplicate / stale) or 2 (non-finite) and nothing of that row is
- * written.  swa (bf16[table_rows,128,576], row p%128) may be NULL. */
+ * written.  swa (bf16[table_rows,128,576], row p%128) may be NULL; with it, a
+ * row whose ring row (seq, p%128) repeats an earlier row's is refused too (3).
+ * Rows that pass are written and bumped even if others fail: on a nonzero
+ * status the caller rolls back or discards the whole batch, as the reference's
+ * caller does after a failed scatter (cache_pool.py:304-313). */
 int dsr_append_kv_index(uint16_t* kv_pool, uint16_t* index_pool, int64_t* generations,
                         int64_t pool_blocks, const int32_t* block_table, int64_t table_rows,
                         int64_t table_stride, const int32_t* seq, const int32_t* positions,

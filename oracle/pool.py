@@ -13,6 +13,8 @@ from __future__ import annotations
 
 import numpy as np
 
+from .ops import scatter_slots
+
 
 class PoolOracle:
     def __init__(self, slots: int, width: int, undo_rows: int):
@@ -60,3 +62,35 @@ class PoolOracle:
         """snapshot_state.py:205-216: rows of logical ids, in order; None if non-finite."""
         rows = self.data[(np.asarray(logical, np.int64) + offset) % len(self.data)]
         return None if self._nonfinite(rows) else rows.copy()
+
+
+class ReferenceRowPool:
+    """The reference's own DeviceRowPool.write / finish data path, partial writes
+    included (cache_pool.py:289-313,336-352): the target rows are backed up, the
+    batch is scattered by scatter_kernel's rule (native/operations.cu:144-161,
+    restated by oracle.scatter_slots: refused rows skipped, non-finite elements
+    skipped, the rest written), and the generations are bumped only when the
+    scatter status is 0; a failed write needs finish(accepted=0), which restores
+    the rejected mutations newest first.  PoolOracle above restates this
+    library's whole-batch refusal; the two must agree on every end state after
+    finish."""
+
+    def __init__(self, slots: int, width: int, undo_rows: int):
+        self.data = np.zeros((slots, width), np.uint16)
+        self.generations = np.zeros(slots, np.int64)
+        self.undo = np.zeros((undo_rows, width), np.uint16)
+
+    def write(self, slots, expected, values, undo_start):
+        slots = np.asarray(slots, np.int32)
+        for i, s in enumerate(slots.tolist()):
+            self.undo[undo_start + i] = self.data[s]  # index_select into the undo rows (cache_pool.py:300)
+        code = scatter_slots(self.data, self.generations, slots, np.asarray(expected, np.int64),
+                             np.asarray(values, np.uint16))
+        if code == 0:
+            self.generations[slots] = np.asarray(expected, np.int64) + 1  # cache_pool.py:309
+        return code
+
+    def finish(self, rejected_journal_order):
+        for index, slot, previous in reversed(list(rejected_journal_order)):
+            self.data[slot] = self.undo[index]
+            self.generations[slot] = previous

@@ -159,3 +159,37 @@ def assert_bf16_close(actual, expected, max_abs=2e-2, mean_abs=2e-3):
     assert np.all(np.isfinite(actual))
     assert diff.max() <= max_abs, f"max abs error {diff.max():.3e} > {max_abs}"
     assert diff.mean() <= mean_abs, f"mean abs error {diff.mean():.3e} > {mean_abs}"
+
+
+def score_stats(got, ref, bound, rtol=1e-3):
+    """Agreement of GPU index scores with the oracle's.
+
+    The pass criterion is |got - ref| <= rtol * bound + 1e-6 with bound =
+    sum_h |w_h| |q_h . k| (the magnitude that bounds the rounding of a sum of
+    signed-weight terms, which can cancel to near zero).  Reported beside it:
+    the plain relative error |got - ref| / |ref| (max over keys with |ref| above
+    1e-3 of its bound, where cancellation is mild) and the share of all keys
+    within rtol plain relative error (|ref| = 0 counts only when got is 0 too).
+    """
+    got = np.asarray(got, np.float64)
+    ref = np.asarray(ref, np.float64)
+    bound = np.asarray(bound, np.float64)
+    err = np.abs(got - ref)
+    mild = np.abs(ref) > 1e-3 * bound
+    rel = err / np.maximum(np.abs(ref), 1e-300)
+    return {
+        "keys": int(len(ref)),
+        "within_bound": bool(np.all(err <= rtol * bound + 1e-6)),
+        "max_err_over_bound": float(np.max(err / (bound + 1e-30))) if len(ref) else 0.0,
+        "max_rel_mild": float(np.max(rel[mild])) if mild.any() else 0.0,
+        "share_rel_within": float(np.mean(err <= rtol * np.abs(ref))) if len(ref) else 1.0,
+    }
+
+
+def assert_scores(got, ref, bound, rtol=1e-3, min_share=0.999, what="scores"):
+    stats = score_stats(got, ref, bound, rtol)
+    assert np.all(np.isfinite(got)), f"{what}: non-finite score"
+    assert stats["within_bound"], f"{what}: {stats}"
+    assert stats["share_rel_within"] >= min_share, f"{what}: {stats}"
+    print(f"{what}: {stats}")
+    return stats

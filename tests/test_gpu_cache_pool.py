@@ -31,6 +31,9 @@ class Mirror:
         self.pool = DeviceRowPool(slots, width, context=context, offset=offset, admitted_bytes=1 << 30,
                                   max_mutations=undo)
         self.ref = oracle.PoolOracle(slots, width, undo)
+        # the reference's own write path (partial writes, bump only on success):
+        # after every finish its state must equal the device's too
+        self.ref_partial = oracle.ReferenceRowPool(slots, width, undo)
         self.width = width
 
     def write(self, rng, logical, tokens, poison=False):
@@ -44,16 +47,22 @@ class Mirror:
         finally:
             if len(self.pool.map.journal) > start:  # the host reserved the batch: mirror it
                 new = self.pool.map.journal[start:]
-                self.ref.write([m.slot for m in new], [m.previous_generation for m in new], bits, start)
+                for ref in (self.ref, self.ref_partial):
+                    ref.write([m.slot for m in new], [m.previous_generation for m in new], bits, start)
 
     def finish(self, op, accepted):
         rejected = self.pool.map.rejected(op, accepted)[::-1]
         self.pool.finish(op, accepted)
-        self.ref.finish([(i, m.slot, m.previous_generation) for i, m in rejected])
+        for ref in (self.ref, self.ref_partial):
+            ref.finish([(i, m.slot, m.previous_generation) for i, m in rejected])
 
     def check(self):
+        """After a finish: the device equals both restatements (whole-batch refusal and
+        the reference's partial writes) bit for bit."""
         data, gens = device_state(self.pool)
         assert np.array_equal(data, self.ref.data) and np.array_equal(gens, self.ref.generations)
+        assert np.array_equal(data, self.ref_partial.data), "end state differs from the reference's write -> finish"
+        assert np.array_equal(gens, self.ref_partial.generations)
 
 
 def test_random_transactions_match_the_reference_semantics(cuda):

@@ -1,9 +1,10 @@
 """Paged decode path on the B200 (indexer -> top-k -> sparse MLA) against the oracle.
 
-Tolerances: index scores within 1e-3 relative (measured
-against sum_h |w_h| |q_h.k|, the magnitude that bounds the rounding of a
-signed-weight sum); top-k bit-exact given identical fp32 scores; attention
-max abs error <= 2e-2 and mean abs error <= 2e-3.
+Tolerances: index scores within 1e-3 relative, checked two
+ways: every key within 1e-3 of sum_h |w_h| |q_h.k| (the magnitude that bounds the
+rounding of a signed-weight sum, which can cancel to near zero), and at least
+99.9% of the keys within 1e-3 plain relative error; top-k bit-exact given
+identical fp32 scores; attention max abs error <= 2e-2 and mean abs error <= 2e-3.
 """
 from __future__ import annotations
 
@@ -12,22 +13,21 @@ import pytest
 import torch
 
 import oracle
-from _helpers import (assert_bf16_close, c_decode_step, c_indexer, c_mla, host, oracle_attention,
-                      oracle_scores, score_bound)
+from _helpers import (assert_bf16_close, assert_scores, c_decode_step, c_indexer, c_mla, host,
+                      oracle_attention, oracle_scores, score_bound)
 from deepseekrpc_b200.workloads import CONFIGS, make_decode_inputs, small_config
 
 pytestmark = pytest.mark.gpu
 SCORE_RTOL = 1e-3
 
 
-def check_scores(h, scores, b):
+def check_scores(h, scores, b, min_share=0.999):
+    """Within 1e-3 of the bound for every key, and within 1e-3 plain relative error
+    for at least `min_share` of the keys (both reported by score_stats)."""
     n = int(h["visible"][b])
     ref = oracle_scores(h, b)
-    bound = score_bound(h, b)
-    got = scores[b, :n]
-    assert np.all(np.isfinite(got))
-    err = np.abs(got.astype(np.float64) - ref)
-    assert np.all(err <= SCORE_RTOL * bound + 1e-6), f"max rel {np.max(err / (bound + 1e-30)):.2e}"
+    assert_scores(scores[b, :n], ref, score_bound(h, b), SCORE_RTOL, min_share=min_share,
+                  what=f"sequence {b} ({n} keys)")
     return ref
 
 
@@ -50,7 +50,12 @@ def test_indexer_fp32_query_uses_hi_lo_split(cuda):
     inp["idx_q"] = inp["idx_q"] + torch.randn_like(inp["idx_q"]) * 1e-3  # not BF16-representable
     scores, code = c_indexer(inp)
     assert code == 0
-    check_scores(host(inp), scores.cpu().numpy(), 0)
+    # q = bf16(q) + bf16(q - bf16(q)) carries ~16 of FP32's 24 mantissa bits, so the
+    # score error is ~2^-17 of the bound: within 1e-3 of the bound everywhere, but
+    # keys whose signed head terms cancel below ~1% of the bound exceed 1e-3 plain
+    # relative error (about 2% of N(0,1) keys).  BF16-valued queries (the
+    # reference's FP8 query, every BASELINE config) take the exact path above.
+    check_scores(host(inp), scores.cpu().numpy(), 0, min_share=0.95)
 
 
 def test_indexer_flags_bad_visibility_and_blocks(cuda):
