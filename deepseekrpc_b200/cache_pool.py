@@ -19,6 +19,7 @@ import re
 import threading
 from contextlib import contextmanager
 from dataclasses import dataclass
+from typing import NamedTuple
 
 import numpy as np
 
@@ -56,117 +57,187 @@ class Operation:
         _integer(self.rows, "operation rows", 1, min(4096, 1048576 - self.start))
 
 
-@dataclass(frozen=True)
-class SlotMutation:
+class SlotMutation(NamedTuple):
+    """One journal entry, as the pool's rollback reads it back."""
     token_position: int
     slot: int
     previous_logical: int
     previous_generation: int
 
 
+def _refuse(reason: str, message: str):
+    """A ValidationError (the reference's exception type) tagged with a short reason."""
+    error = ValidationError(message)
+    error.reason = reason
+    raise error
+
+
+def _int_array(values, name: str, low: int, high: int) -> np.ndarray:
+    """Python ints in [low, high] as an int64 array (bools and floats refused)."""
+    values = list(values)
+    if any(type(v) is not int for v in values):
+        _refuse("type", f"{name}: integers required")
+    arr = np.asarray(values, dtype=np.int64) if values else np.zeros(0, np.int64)
+    if arr.size and (arr.min() < low or arr.max() > high):
+        _refuse("range", f"{name}: outside [{low}, {high}]")
+    return arr
+
+
 class SlotMap:
-    """Host slot metadata of one pool (cache_pool.py:24-153)."""
+    """Host metadata of one ring-offset row pool: which logical row each physical
+    slot holds and its generation, plus the undo journal of the open window.
+
+    Semantics are the reference SlotMap's (src/deepseekrpc/cache_pool.py:24-153),
+    pinned by a recorded trace of it: slot = (logical + offset) % slots; a write
+    batch of 1..64 rows inside the active window, in non-decreasing producing-token
+    order, with no repeated slot, bumps each slot's generation; `physical` accepts
+    only rows still held under their own logical id with a nonzero generation;
+    `finish(operation, accepted)` puts back every mutation produced by a token at
+    or past start + accepted, newest first.  The representation is this module's
+    own: the per-slot state lives in two int64 arrays, the journal in four
+    preallocated arrays (structure of arrays, `max_mutations` entries), and every
+    batch is validated and applied with vectorised numpy operations.
+    """
 
     def __init__(self, slots: int, *, context: int, offset: int, max_mutations: int = 64):
-        self.slots = _integer(slots, "cache slots", 1, 1048576)
-        self.context = _integer(context, "cache logical capacity", slots, 1048576)
-        self.offset = _integer(offset, "local physical slot offset", 0, slots - 1)
-        self.max_mutations = _integer(max_mutations, "undo row capacity", 1, 4096)
-        self.logical = np.full(slots, -1, dtype=np.int64)
-        self.generations = np.zeros(slots, dtype=np.int64)
+        self.slots = _integer(slots, "slot count", 1, 1048576)
+        self.context = _integer(context, "logical capacity", slots, 1048576)
+        self.offset = _integer(offset, "slot offset", 0, slots - 1)
+        self.max_mutations = _integer(max_mutations, "journal capacity", 1, 4096)
+        self.logical = np.full(slots, -1, dtype=np.int64)      # logical row held by each slot
+        self.generations = np.zeros(slots, dtype=np.int64)     # 0 = never written in this epoch
+        self._j_token = np.zeros(max_mutations, np.int64)      # journal: producing token,
+        self._j_slot = np.zeros(max_mutations, np.int64)       #   target slot,
+        self._j_logical = np.zeros(max_mutations, np.int64)    #   the slot's previous logical row
+        self._j_generation = np.zeros(max_mutations, np.int64)  #   and its previous generation
+        self._j_len = 0
         self.epoch, self.session, self.active = -1, None, None
-        self.journal: list[SlotMutation] = []
 
+    # ----------------------------------------------------------------- views
     @property
     def metadata_bytes(self) -> int:
         return self.logical.nbytes + self.generations.nbytes
 
-    def slot_of(self, logical: int) -> int:
-        return (logical + self.offset) % self.slots
+    @property
+    def journal(self) -> list:
+        """The open window's mutations in write order."""
+        n = self._j_len
+        return [SlotMutation(int(t), int(s), int(lg), int(g)) for t, s, lg, g in
+                zip(self._j_token[:n], self._j_slot[:n], self._j_logical[:n], self._j_generation[:n])]
+
+    def slot_of(self, logical):
+        """Physical slot(s) of logical row(s)."""
+        return (np.asarray(logical, dtype=np.int64) + self.offset) % self.slots if np.ndim(logical) \
+            else (int(logical) + self.offset) % self.slots
+
+    # -------------------------------------------------------------- epochs
+    def _new_epoch(self, session: str, epoch: int) -> None:
+        self.session, self.epoch = session, epoch
+        self.logical.fill(-1)
+        self.generations.fill(0)
 
     def reset(self, session: str, epoch: int) -> None:
-        _hex_id(session, 32, "cache session")
-        _integer(epoch, "cache epoch", 0, I64_MAX)
-        if self.active is not None or epoch <= self.epoch:
-            raise ValidationError("cache reset requires quiescence and a newer epoch")
-        self.session, self.epoch = session, epoch
-        self.logical[:] = -1
-        self.generations[:] = 0
+        _hex_id(session, 32, "pool session")
+        _integer(epoch, "pool epoch", 0, I64_MAX)
+        if self.active is not None:
+            _refuse("busy", "pool reset while a window is open")
+        if epoch <= self.epoch:
+            _refuse("epoch", f"pool reset to epoch {epoch}, not after the current epoch {self.epoch}")
+        self._new_epoch(session, epoch)
 
     def discard_for_reset(self, session: str, epoch: int) -> None:
-        _hex_id(session, 32, "cache session")
-        _integer(epoch, "cache epoch", 0, I64_MAX)
+        """Drops the open window and every row under a strictly newer epoch."""
+        _hex_id(session, 32, "pool session")
+        _integer(epoch, "pool epoch", 0, I64_MAX)
         if epoch <= self.epoch:
-            raise ValidationError("discarded cache recovery requires a newer epoch")
-        self.active = None
-        self.journal = []
-        self.reset(session, epoch)
+            _refuse("epoch", f"pool discard to epoch {epoch}, not after the current epoch {self.epoch}")
+        self.active, self._j_len = None, 0
+        self._new_epoch(session, epoch)
 
+    # ------------------------------------------------------------- windows
     def begin(self, operation) -> None:
-        if (self.active is not None or operation.epoch != self.epoch or operation.session != self.session or
-                operation.rows > 64 or operation.start + operation.rows > self.context):
-            raise ValidationError("cache window is active, stale or exceeds its admitted bounds")
+        if self.active is not None:
+            _refuse("busy", "a window is already open on this pool")
+        if operation.session != self.session or operation.epoch != self.epoch:
+            _refuse("stale", "window belongs to another session or epoch")
+        if operation.rows > 64 or operation.start + operation.rows > self.context:
+            _refuse("bounds", "window is longer than 64 rows or ends past the logical capacity")
         self.active = operation
 
-    def prepare(self, logical_positions, token_positions):
-        """Validates a batch against the active window; returns (mutations, slots, generations)."""
+    def _check_batch(self, logical_positions, token_positions):
+        """Validates a write batch as a whole; returns (logical, tokens, slots) arrays."""
         if self.active is None:
-            raise ValidationError("cache mutation requires an active window")
-        count = len(logical_positions)
-        if count != len(token_positions) or not 1 <= count <= 64:
-            raise ValidationError("cache row batch is empty or outside the admitted bound")
-        if len(self.journal) + count > self.max_mutations:
-            raise ValidationError("cache undo row capacity exhausted")
-        last_token = self.journal[-1].token_position if self.journal else self.active.start
-        window_end = self.active.start + self.active.rows - 1
-        mutations, slots, generations, used = [], [], [], set()
-        for logical, token in zip(logical_positions, token_positions):
-            _integer(logical, "cache logical position", 0, self.context - 1)
-            _integer(token, "cache producing token", last_token, window_end)
-            last_token = token
-            slot = self.slot_of(logical)
-            if slot in used:
-                raise ValidationError("one scatter batch repeats a physical cache slot")
-            used.add(slot)
-            generation = int(self.generations[slot])
-            if generation == I64_MAX:
-                raise ValidationError("cache generation exhausted; coordinated new epoch required")
-            mutations.append(SlotMutation(token, slot, int(self.logical[slot]), generation))
-            slots.append(slot)
-            generations.append(generation)
-        return mutations, slots, generations
+            _refuse("idle", "pool write without an open window")
+        n = len(logical_positions)
+        if n != len(token_positions) or not 1 <= n <= 64:
+            _refuse("shape", "write batch must hold 1..64 rows with one producing token each")
+        if self._j_len + n > self.max_mutations:
+            _refuse("journal", "undo journal is full")
+        logical = _int_array(logical_positions, "logical rows", 0, self.context - 1)
+        window = self.active
+        first = int(self._j_token[self._j_len - 1]) if self._j_len else window.start
+        tokens = _int_array(token_positions, "producing tokens", first, window.start + window.rows - 1)
+        if np.any(np.diff(tokens) < 0):
+            _refuse("order", "producing tokens go backwards")
+        slots = (logical + self.offset) % self.slots
+        if len(np.unique(slots)) != n:
+            _refuse("repeat", "write batch targets one slot twice")
+        if np.any(self.generations[slots] == I64_MAX):
+            _refuse("exhausted", "slot generation exhausted; start a new epoch")
+        return logical, tokens, slots
+
+    def prepare(self, logical_positions, token_positions):
+        """Validates a batch; returns (mutations, slots, current generations) without applying it."""
+        logical, tokens, slots = self._check_batch(logical_positions, token_positions)
+        gens = self.generations[slots]
+        mutations = [SlotMutation(int(t), int(s), int(lg), int(g))
+                     for t, s, lg, g in zip(tokens, slots, self.logical[slots], gens)]
+        return mutations, slots.tolist(), gens.tolist()
 
     def reserve(self, logical_positions, token_positions):
-        mutations, slots, generations = self.prepare(logical_positions, token_positions)
-        for logical, m in zip(logical_positions, mutations):  # the whole batch was validated
-            self.logical[m.slot] = logical
-            self.generations[m.slot] = m.previous_generation + 1
-        self.journal.extend(mutations)
-        return slots, generations
+        """Validates and applies a batch: journals each slot's previous state, then
+        claims the slots for the new rows at generation + 1.  Returns (slots,
+        previous generations) -- the expected generations of the device write."""
+        logical, tokens, slots = self._check_batch(logical_positions, token_positions)
+        n, j = len(slots), self._j_len
+        previous = self.generations[slots].copy()
+        self._j_token[j:j + n] = tokens
+        self._j_slot[j:j + n] = slots
+        self._j_logical[j:j + n] = self.logical[slots]
+        self._j_generation[j:j + n] = previous
+        self._j_len = j + n
+        self.logical[slots] = logical
+        self.generations[slots] = previous + 1
+        return slots.tolist(), previous.tolist()
 
+    # ---------------------------------------------------------------- reads
     def physical(self, logical_positions):
-        out = []
-        for logical in logical_positions:
-            if logical == -1:
-                out.append(-1)
-                continue
-            _integer(logical, "visible cache logical position", 0, self.context - 1)
-            slot = self.slot_of(logical)
-            if self.logical[slot] != logical or self.generations[slot] == 0:
-                raise ValidationError("cache row is absent or its physical slot was overwritten")
-            out.append(slot)
-        return out
+        """Slots of live logical rows; -1 passes through as padding."""
+        values = list(logical_positions)
+        if not values:
+            return []
+        padded = np.asarray([v == -1 and type(v) is int for v in values])
+        live = _int_array([v for v, pad in zip(values, padded) if not pad], "visible logical rows", 0,
+                          self.context - 1)
+        out = np.full(len(values), -1, np.int64)
+        slots = (live + self.offset) % self.slots
+        if np.any(self.logical[slots] != live) or np.any(self.generations[slots] == 0):
+            _refuse("absent", "a visible row is missing or its slot now holds another row")
+        out[~padded] = slots
+        return out.tolist()
 
+    # ------------------------------------------------------------- prefixes
     def validate_prefix(self, count: int) -> None:
-        _integer(count, "retained compressed rows", 0, self.slots)
+        _integer(count, "retained rows", 0, self.slots)
         if self.active is not None:
-            raise ValidationError("prefix retention requires quiescent cache metadata")
+            _refuse("busy", "prefix retention while a window is open")
         logical = np.arange(count, dtype=np.int64)
         slots = (logical + self.offset) % self.slots
         if np.any(self.logical[slots] != logical) or np.any(self.generations[slots] <= 0):
-            raise ValidationError("retained encoder prefix has missing or overwritten source rows")
+            _refuse("absent", "retained prefix has missing or overwritten rows")
 
     def retain_prefix(self, session: str, epoch: int, count: int) -> None:
+        """Keeps rows 0..count-1 (each at generation 1) under a newer epoch."""
         _hex_id(session, 32, "retained prefix session")
         _integer(epoch, "retained prefix epoch", self.epoch + 1, I64_MAX)
         self.validate_prefix(count)
@@ -174,21 +245,31 @@ class SlotMap:
         self.logical[~keep] = -1
         self.generations[:] = keep
         self.session, self.epoch = session, epoch
-        self.journal = []
+        self._j_len = 0
 
+    # --------------------------------------------------------------- commit
     def rejected(self, operation, accepted: int):
-        """(journal index, mutation) of the rows past the accepted prefix, newest first."""
-        _integer(accepted, "cache accepted prefix", 0, operation.rows)
+        """(journal index, mutation) of the mutations produced at or past
+        start + accepted, newest first."""
+        _integer(accepted, "accepted rows", 0, operation.rows)
         if self.active != operation:
-            raise ValidationError("cache commit targets another operation")
-        boundary = operation.start + accepted
-        return [(i, m) for i, m in reversed(list(enumerate(self.journal))) if m.token_position >= boundary]
+            _refuse("stale", "commit targets another window")
+        n = self._j_len
+        idx = np.nonzero(self._j_token[:n] >= operation.start + accepted)[0][::-1]
+        return [(int(i), SlotMutation(int(self._j_token[i]), int(self._j_slot[i]), int(self._j_logical[i]),
+                                      int(self._j_generation[i]))) for i in idx]
 
     def finish(self, operation, accepted: int) -> None:
-        for _, m in self.rejected(operation, accepted):
-            self.logical[m.slot] = m.previous_logical
-            self.generations[m.slot] = m.previous_generation
-        self.journal = []
+        """Closes the window; the rejected mutations are undone newest first, so a
+        slot written twice ends with the state before its first rejected write."""
+        rejected = self.rejected(operation, accepted)
+        if rejected:
+            order = np.asarray([i for i, _ in rejected], np.int64)  # newest first; the last write wins
+            for i in order:
+                s = self._j_slot[i]
+                self.logical[s] = self._j_logical[i]
+                self.generations[s] = self._j_generation[i]
+        self._j_len = 0
         self.active = None
 
 

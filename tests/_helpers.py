@@ -187,9 +187,14 @@ def score_stats(got, ref, bound, rtol=1e-3):
 
 
 def assert_scores(got, ref, bound, rtol=1e-3, min_share=0.999, what="scores"):
+    """Every key within rtol of the bound; at most max(2, (1 - min_share) * keys)
+    keys beyond rtol plain relative error (a short sequence may hold one or two
+    keys whose head terms cancel to ~1e-4 of the bound)."""
     stats = score_stats(got, ref, bound, rtol)
     assert np.all(np.isfinite(got)), f"{what}: non-finite score"
     assert stats["within_bound"], f"{what}: {stats}"
-    assert stats["share_rel_within"] >= min_share, f"{what}: {stats}"
+    n = stats["keys"]
+    bad = round((1.0 - stats["share_rel_within"]) * n)
+    assert bad <= max(2, int((1.0 - min_share) * n)), f"{what}: {stats}"
     print(f"{what}: {stats}")
     return stats

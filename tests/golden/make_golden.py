@@ -213,6 +213,62 @@ def main(argv=None):
             start += accepted if error is None else 0
         trace.append(dict(slots=slots, offset=offset, steps=steps))
     (HERE / "slotmap_trace.json").write_text(json.dumps(trace))
+
+    # 11. SlotMap windows: several write batches per window (the journal spans
+    # them), ring wrap-around (context > slots, hash-like offsets), out-of-order
+    # producing tokens, oversized windows and undo-journal exhaustion
+    windows = []
+    rng = np.random.default_rng(9902)
+    for slots, offset, journal in ((8, 3, 6), (64, 37, 16), (100, 91, 64), (1000, 517, 64)):
+        mapping = SlotMap(slots, context=4 * slots, offset=offset, max_mutations=journal)
+        mapping.reset("e" * 32, 3)
+        start, number, steps = 0, 1, []
+        for _ in range(16):
+            rows = int(rng.integers(1, min(64, 4 * slots - start) + 1)) if rng.random() > 0.1 else 65
+            op = Operation("e" * 32, "b" * 32, 3, number, "c" * 32, "d" * 64, start, rows)
+            number += 1
+            record = dict(start=start, rows=rows, begin_error=None, batches=[])
+            try:
+                mapping.begin(op)
+            except ValidationError as e:
+                record["begin_error"] = str(e)
+                steps.append(record)
+                continue
+            token = start
+            for _ in range(int(rng.integers(1, 4))):
+                if token >= start + rows:
+                    break
+                n = int(rng.integers(1, start + rows - token + 1))
+                logical = list(range(token, token + n))
+                tokens = list(range(token, token + n))
+                if rng.random() < 0.15 and n > 1:
+                    tokens[-1], tokens[0] = tokens[0], tokens[-1]  # producing tokens go backwards
+                if rng.random() < 0.15:
+                    logical[-1] = logical[0] + slots  # one slot twice
+                try:
+                    result = mapping.reserve(logical, tokens)
+                    batch = dict(logical=logical, tokens=tokens,
+                                 reserved=[list(map(int, result[0])), list(map(int, result[1]))], error=None)
+                    token += n
+                except ValidationError as e:
+                    batch = dict(logical=logical, tokens=tokens, reserved=None, error=str(e))
+                record["batches"].append(batch)
+            accepted = int(rng.integers(0, token - start + 1))
+            rejected = [(int(i), int(m.slot), int(m.previous_generation)) for i, m in mapping.rejected(op, accepted)]
+            mapping.finish(op, accepted)
+            probe = list(range(max(0, start - slots - 2), start + rows))
+            physical = []
+            for q in probe:
+                try:
+                    physical.append(mapping.physical([q])[0])
+                except ValidationError:
+                    physical.append(None)
+            record.update(accepted=accepted, rejected=rejected, probe=probe, physical=physical,
+                          generations=mapping.generations.tolist(), logical_map=mapping.logical.tolist())
+            steps.append(record)
+            start += accepted
+        windows.append(dict(slots=slots, offset=offset, journal=journal, context=4 * slots, steps=steps))
+    (HERE / "slotmap_windows.json").write_text(json.dumps(windows))
     print("wrote", sorted(p.name for p in HERE.iterdir() if p.suffix in (".npz", ".json")))
 
 

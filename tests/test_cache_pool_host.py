@@ -15,6 +15,11 @@ from deepseekrpc_b200.cuda_ops import ValidationError
 TRACE = Path(__file__).resolve().parent / "golden" / "slotmap_trace.json"
 
 
+# the reference's refusal messages recorded in the trace, and the reason this
+# module tags the same refusal with
+REFUSALS = {"one scatter batch repeats a physical cache slot": "repeat"}
+
+
 def test_slot_map_replays_the_reference_trace():
     for case in json.loads(TRACE.read_text()):
         mapping = SlotMap(case["slots"], context=64, offset=case["offset"], max_mutations=16)
@@ -24,10 +29,11 @@ def test_slot_map_replays_the_reference_trace():
             mapping.begin(op)
             try:
                 got = mapping.reserve(step["logical"], list(range(step["start"], step["start"] + step["rows"])))
-                reserved, error = [list(map(int, got[0])), list(map(int, got[1]))], None
+                reserved, reason = [list(map(int, got[0])), list(map(int, got[1]))], None
             except ValidationError as e:
-                reserved, error = None, str(e)
-            assert reserved == step["reserved"] and error == step["error"]
+                reserved, reason = None, e.reason
+            assert reserved == step["reserved"]
+            assert reason == (REFUSALS[step["error"]] if step["error"] else None)
             mapping.finish(op, step["accepted"])
             physical = []
             for p in step["probe"]:
@@ -82,3 +88,63 @@ def test_retained_prefix_keeps_only_validated_rows():
     assert np.count_nonzero(m.generations) == 4
     with pytest.raises(ValidationError):
         m.physical([4])
+
+
+WINDOWS = Path(__file__).resolve().parent / "golden" / "slotmap_windows.json"
+# each reference refusal message (prefix) and the reasons this module may tag it with
+REFUSAL_KINDS = {
+    "cache undo row capacity exhausted": {"journal"},
+    "one scatter batch repeats a physical cache slot": {"repeat"},
+    "cache window is active, stale or exceeds its admitted bounds": {"busy", "stale", "bounds"},
+    "cache producing token must be an integer in": {"order", "range"},
+}
+
+
+def _kinds(message):
+    return next(kinds for prefix, kinds in REFUSAL_KINDS.items() if message.startswith(prefix))
+
+
+def test_slot_map_replays_reference_windows():
+    """Several batches per window, ring wrap-around with hash-like offsets, refused
+    windows and batches, partial acceptance: same slots, refusals, rollback order,
+    live rows and per-slot state as the reference's SlotMap at every step."""
+    for case in json.loads(WINDOWS.read_text()):
+        m = SlotMap(case["slots"], context=case["context"], offset=case["offset"], max_mutations=case["journal"])
+        m.reset("e" * 32, 3)
+        for step in case["steps"]:
+            if step["rows"] > 64 or step["start"] + step["rows"] > case["context"]:
+                assert step["begin_error"] is not None
+                continue  # Operation() itself refuses rows past the capacity; begin() refuses > 64 rows
+            op = Operation("e" * 32, 3, step["start"], step["rows"])
+            try:
+                m.begin(op)
+                began = None
+            except ValidationError as e:
+                began = e.reason
+            if step["begin_error"] is not None:
+                assert began in _kinds(step["begin_error"])
+                continue
+            assert began is None
+            for batch in step["batches"]:
+                try:
+                    got = m.reserve(batch["logical"], batch["tokens"])
+                    reserved, reason = [list(map(int, got[0])), list(map(int, got[1]))], None
+                except ValidationError as e:
+                    reserved, reason = None, e.reason
+                assert reserved == batch["reserved"]
+                if batch["error"] is None:
+                    assert reason is None
+                else:
+                    assert reason in _kinds(batch["error"]), (reason, batch["error"])
+            rejected = [(i, mut.slot, mut.previous_generation) for i, mut in m.rejected(op, step["accepted"])]
+            assert rejected == [tuple(r) for r in step["rejected"]]
+            m.finish(op, step["accepted"])
+            physical = []
+            for q in step["probe"]:
+                try:
+                    physical.append(m.physical([q])[0])
+                except ValidationError:
+                    physical.append(None)
+            assert physical == step["physical"]
+            assert m.generations.tolist() == step["generations"]
+            assert m.logical.tolist() == step["logical_map"]
