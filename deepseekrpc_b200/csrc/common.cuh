@@ -8,6 +8,7 @@
 #include <stdint.h>
 
 #include "../../include/dsr_b200.h"
+#include "host_common.h"
 
 namespace dsr {
 
@@ -30,6 +31,50 @@ __device__ __forceinline__ uint32_t score_key(float s) {
 __device__ __forceinline__ float key_score(uint32_t u) {
   uint32_t b = (u & 0x80000000u) ? (u & 0x7fffffffu) : ~u;
   return __uint_as_float(b);
+}
+
+// ---------------------------------------------------------------------------
+// pool addressing: where logical position p of sequence b lives in a row pool
+// ---------------------------------------------------------------------------
+// Paged (ring == nullptr): 64-row blocks, block table i32[batch, stride]:
+//   row = table[b * stride + p / 64] * 64 + p % 64.
+// Ring (table == nullptr): the reference's DeviceRowPool / SlotMap layout
+// (src/deepseekrpc/cache_pool.py:24-113, bootstrap.py:185-192), one region per
+// sequence, ring[3b .. 3b+2] = {first row, slots, offset}:
+//   row = first + (p + offset) % slots,
+// valid when slots > 0, 0 <= offset < slots and first + slots <= rows.
+// Ring descriptor of sequence b; false (and zeros) when it is invalid.
+__device__ __forceinline__ bool ring_desc(const PoolAddr& a, int b, int64_t& first, int64_t& slots,
+                                          int64_t& offset) {
+  first = a.ring[3 * int64_t(b)];
+  slots = a.ring[3 * int64_t(b) + 1];
+  offset = a.ring[3 * int64_t(b) + 2];
+  if (slots <= 0 || offset < 0 || offset >= slots || first < 0 || first > a.rows - slots) {
+    first = slots = offset = 0;
+    return false;
+  }
+  return true;
+}
+
+// Positions a sequence may hold: the table's capacity, or the ring's slots.
+__device__ __forceinline__ int64_t addr_capacity(const PoolAddr& a, int b) {
+  if (a.ring == nullptr) return a.stride * 64;
+  int64_t first, slots, offset;
+  return ring_desc(a, b, first, slots, offset) ? slots : 0;
+}
+
+// Pool row of position p (0 <= p < capacity) of sequence b; -1 when unmapped.
+__device__ __forceinline__ int64_t addr_row(const PoolAddr& a, int b, int64_t p) {
+  if (p < 0) return -1;
+  if (a.ring == nullptr) {
+    if ((p >> 6) >= a.stride) return -1;
+    const int64_t blk = a.table[int64_t(b) * a.stride + (p >> 6)];
+    if (blk < 0 || blk * 64 >= a.rows) return -1;
+    return blk * 64 + (p & 63);
+  }
+  int64_t first, slots, offset;
+  if (!ring_desc(a, b, first, slots, offset)) return -1;
+  return first + (p + offset) % slots;
 }
 
 // ---------------------------------------------------------------------------

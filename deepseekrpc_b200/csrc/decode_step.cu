@@ -19,21 +19,21 @@ extern "C" size_t dsr_decode_workspace_bytes(int64_t batch, int64_t max_visible,
          dsr::mla_query_image_bytes(batch, heads) + dsr::mla_workspace_bytes(batch, heads, k) + 256;
 }
 
-extern "C" int dsr_decode_step(const float* idx_q, const float* idx_w, int64_t idx_heads,
-                               const uint16_t* index_pool, const float* q,
-                               const uint16_t* kv_pool, int64_t heads, int64_t pool_blocks,
-                               const int32_t* block_table, int64_t table_stride,
-                               const int32_t* visible, int64_t max_visible, int64_t k,
-                               const uint16_t* swa, const int32_t* swa_len, const float* sink,
-                               float scale, float* out, int32_t* topk_out, float* scores_out,
-                               void* workspace, size_t workspace_bytes, int32_t* err,
-                               int64_t batch, void* stream) {
-  using namespace dsr;
-  clear_error();
+namespace dsr {
+namespace {
+
+// The step over any pool addressing: index keys through `ix`, KV rows through
+// `kv`, the SWA window from the [batch, 128, 576] ring (swa_ring == nullptr) or
+// from an SWA row pool through swa_ring.
+int decode_step(const float* idx_q, const float* idx_w, int64_t idx_heads, const uint16_t* index_pool,
+                const PoolAddr& ix, const float* q, const uint16_t* kv_pool, const PoolAddr& kv, int64_t heads,
+                const int32_t* visible, int64_t max_visible, int64_t k, const uint16_t* swa,
+                const int64_t* swa_ring, int64_t swa_rows, const int32_t* swa_len, const float* sink, float scale,
+                float* out, int32_t* topk_out, float* scores_out, void* workspace, size_t workspace_bytes,
+                int32_t* err, int64_t batch, void* stream) {
   DSR_REQUIRE(workspace != nullptr, "decode_step: workspace is required");
-  DSR_REQUIRE(max_visible > 0 && max_visible <= table_stride * 64,
-              "decode_step: max_visible %lld outside [1, table capacity %lld]",
-              (long long)max_visible, (long long)(table_stride * 64));
+  DSR_REQUIRE(max_visible > 0 && max_visible <= (int64_t(1) << 31) - 64,
+              "decode_step: max_visible %lld outside [1, 2^31 - 64]", (long long)max_visible);
   const size_t need = dsr_decode_workspace_bytes(batch, max_visible, heads, k);
   DSR_REQUIRE(workspace_bytes >= need, "decode_step: workspace %zu < %zu bytes", workspace_bytes,
               need);
@@ -53,16 +53,60 @@ extern "C" int dsr_decode_step(const float* idx_q, const float* idx_w, int64_t i
   const cudaStream_t s = as_stream(stream);
   // the indexer also converts the MLA query into the BF16 image the MLA kernel loads
   // and builds the per-row score histograms the top-k kernel starts from
-  int rc = launch_indexer_decode(idx_q, idx_w, index_pool, pool_blocks, block_table, table_stride,
-                                 visible, scores, stride, err, batch, idx_heads, s, false, q, q_img,
-                                 heads, reinterpret_cast<uint32_t*>(topk_ws));
+  int rc = launch_indexer_decode(idx_q, idx_w, index_pool, ix, visible, scores, stride, err, batch, idx_heads, s,
+                                 false, q, q_img, heads, reinterpret_cast<uint32_t*>(topk_ws));
   if (rc != DSR_OK) return rc;
   rc = launch_topk(scores, nullptr, visible, topk_out, nullptr, err, batch, stride, k, 0, topk_ws,
                    topk_bytes, s, true, /*hist_ready=*/true);
   if (rc != DSR_OK) return rc;
-  return launch_mla_decode(q, kv_pool, pool_blocks, block_table, table_stride, visible, topk_out, k,
-                           swa, swa_len, sink, scale, out, mla_ws, mla_bytes, err, batch, heads, s,
-                           true, q_img);
+  return launch_mla_decode(q, kv_pool, kv, visible, topk_out, k, swa, swa_ring, swa_rows, swa_len, sink, scale,
+                           out, mla_ws, mla_bytes, err, batch, heads, s, true, q_img);
+}
+
+}  // namespace
+}  // namespace dsr
+
+extern "C" int dsr_decode_step(const float* idx_q, const float* idx_w, int64_t idx_heads,
+                               const uint16_t* index_pool, const float* q,
+                               const uint16_t* kv_pool, int64_t heads, int64_t pool_blocks,
+                               const int32_t* block_table, int64_t table_stride,
+                               const int32_t* visible, int64_t max_visible, int64_t k,
+                               const uint16_t* swa, const int32_t* swa_len, const float* sink,
+                               float scale, float* out, int32_t* topk_out, float* scores_out,
+                               void* workspace, size_t workspace_bytes, int32_t* err,
+                               int64_t batch, void* stream) {
+  using namespace dsr;
+  clear_error();
+  PoolAddr pa;
+  const int rc = paged_addr(&pa, block_table, table_stride, pool_blocks, "decode_step");
+  if (rc != DSR_OK) return rc;
+  DSR_REQUIRE(max_visible <= table_stride * 64, "decode_step: max_visible %lld beyond the table capacity %lld",
+              (long long)max_visible, (long long)(table_stride * 64));
+  return decode_step(idx_q, idx_w, idx_heads, index_pool, pa, q, kv_pool, pa, heads, visible, max_visible, k, swa,
+                     nullptr, 0, swa_len, sink, scale, out, topk_out, scores_out, workspace, workspace_bytes, err,
+                     batch, stream);
+}
+
+extern "C" int dsr_decode_step_ring(const float* idx_q, const float* idx_w, int64_t idx_heads,
+                                    const uint16_t* index_pool, int64_t index_rows, const int64_t* index_ring,
+                                    const float* q, const uint16_t* kv_pool, int64_t kv_rows,
+                                    const int64_t* kv_ring, int64_t heads, const int32_t* visible,
+                                    int64_t max_visible, int64_t k, const uint16_t* swa_pool, int64_t swa_rows,
+                                    const int64_t* swa_ring, const int32_t* swa_len, const float* sink,
+                                    float scale, float* out, int32_t* topk_out, float* scores_out,
+                                    void* workspace, size_t workspace_bytes, int32_t* err, int64_t batch,
+                                    void* stream) {
+  using namespace dsr;
+  clear_error();
+  PoolAddr ix, kv;
+  int rc = ring_addr(&ix, index_ring, index_rows, "decode_step_ring (index pool)");
+  if (rc != DSR_OK) return rc;
+  rc = ring_addr(&kv, kv_ring, kv_rows, "decode_step_ring (KV pool)");
+  if (rc != DSR_OK) return rc;
+  DSR_REQUIRE(swa_ring != nullptr, "decode_step_ring: null SWA ring descriptors");
+  return decode_step(idx_q, idx_w, idx_heads, index_pool, ix, q, kv_pool, kv, heads, visible, max_visible, k,
+                     swa_pool, swa_ring, swa_rows, swa_len, sink, scale, out, topk_out, scores_out, workspace,
+                     workspace_bytes, err, batch, stream);
 }
 
 // Indexer scores -> exact top-k with the scores of the chosen entries, the
@@ -98,9 +142,11 @@ extern "C" int dsr_indexer_topk_decode(const float* idx_q, const float* idx_w, i
   float* scores =
       scores_out != nullptr ? scores_out : reinterpret_cast<float*>(topk_ws + topk_bytes);
   const cudaStream_t s = as_stream(stream);
-  int rc = launch_indexer_decode(idx_q, idx_w, index_pool, pool_blocks, block_table, table_stride,
-                                 visible, scores, stride, err, batch, idx_heads, s, false, nullptr,
-                                 nullptr, 0, reinterpret_cast<uint32_t*>(topk_ws));
+  PoolAddr pa;
+  int rc = paged_addr(&pa, block_table, table_stride, pool_blocks, "indexer_topk");
+  if (rc != DSR_OK) return rc;
+  rc = launch_indexer_decode(idx_q, idx_w, index_pool, pa, visible, scores, stride, err, batch, idx_heads, s,
+                             false, nullptr, nullptr, 0, reinterpret_cast<uint32_t*>(topk_ws));
   if (rc != DSR_OK) return rc;
   return launch_topk(scores, nullptr, visible, out_ids, out_scores, err, batch, stride, k, id_base,
                      topk_ws, topk_bytes, s, true, /*hist_ready=*/true);

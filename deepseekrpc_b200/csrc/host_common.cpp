@@ -77,6 +77,24 @@ int set_max_smem_raw(const void* fn, int bytes, const char* what) {
   return DSR_OK;
 }
 
+int paged_addr(PoolAddr* a, const int32_t* table, int64_t stride, int64_t pool_blocks, const char* what) {
+  if (table == nullptr) return fail(DSR_EINVAL, "%s: null block table", what);
+  if (stride <= 0 || stride * 64 > (int64_t(1) << 31) - 1)
+    return fail(DSR_EINVAL, "%s: block-table stride %lld outside [1, 2^25)", what, (long long)stride);
+  if (pool_blocks <= 0 || pool_blocks * 64 > (int64_t(1) << 31) - 1)
+    return fail(DSR_EINVAL, "%s: pool blocks %lld outside [1, 2^25)", what, (long long)pool_blocks);
+  *a = PoolAddr{table, stride, nullptr, pool_blocks * 64};
+  return DSR_OK;
+}
+
+int ring_addr(PoolAddr* a, const int64_t* ring, int64_t rows, const char* what) {
+  if (ring == nullptr) return fail(DSR_EINVAL, "%s: null ring descriptors", what);
+  if (rows <= 0 || rows > (int64_t(1) << 31) - 1)
+    return fail(DSR_EINVAL, "%s: pool rows %lld outside [1, 2^31)", what, (long long)rows);
+  *a = PoolAddr{nullptr, 0, ring, rows};
+  return DSR_OK;
+}
+
 int encode_tmap_bf16_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer,
                         uint32_t box_inner, uint32_t box_outer) {
   EncodeTiledFn fn = encode_fn();

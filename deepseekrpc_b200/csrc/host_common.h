@@ -13,6 +13,18 @@
 
 namespace dsr {
 
+// Where a sequence's logical positions live in a row pool (see common.cuh):
+// paged through a block table of 64-row blocks, or ring-offset.
+struct PoolAddr {
+  const int32_t* table;  // paged: i32[batch, stride] physical 64-row block of logical block j
+  int64_t stride;
+  const int64_t* ring;   // ring: i64[batch][3] = {first row, slots, offset}
+  int64_t rows;          // rows of the pool tensor
+};
+// Checked constructors (DSR_EINVAL with a message on bad arguments).
+int paged_addr(PoolAddr* a, const int32_t* table, int64_t stride, int64_t pool_blocks, const char* what);
+int ring_addr(PoolAddr* a, const int64_t* ring, int64_t rows, const char* what);
+
 // Records a message for dsr_last_error() and returns `code`.
 int fail(int code, const char* fmt, ...);
 // Clears the calling thread's message.
@@ -52,8 +64,7 @@ size_t topk_workspace_bytes(int64_t rows, int64_t row_stride);
 // Leading bytes of that scratch (histograms, tickets, counts) that must be zero at launch.
 size_t topk_zeroed_prefix_bytes(int64_t rows, int64_t row_stride);
 int launch_indexer_decode(const float* q, const float* weights, const uint16_t* index_pool,
-                          int64_t pool_blocks, const int32_t* block_table, int64_t table_stride,
-                          const int32_t* visible, float* scores, int64_t score_stride,
+                          const PoolAddr& pa, const int32_t* visible, float* scores, int64_t score_stride,
                           int32_t* err, int64_t batch, int64_t heads, cudaStream_t stream,
                           bool pdl, const float* mla_q = nullptr, uint16_t* mla_img = nullptr,
                           int64_t mla_heads = 0, uint32_t* hist = nullptr);
@@ -65,10 +76,9 @@ int launch_indexer_prefill(const float* q, const float* weights, const uint16_t*
 inline size_t mla_query_image_bytes(int64_t batch, int64_t heads) {
   return size_t(batch) * size_t(heads) * DSR_KV_DIM * 2;
 }
-int launch_mla_decode(const float* q, const uint16_t* kv_pool, int64_t pool_blocks,
-                      const int32_t* block_table, int64_t table_stride, const int32_t* visible,
-                      const int32_t* topk, int64_t k, const uint16_t* swa,
-                      const int32_t* swa_len, const float* sink, float scale, float* out,
+int launch_mla_decode(const float* q, const uint16_t* kv_pool, const PoolAddr& kv, const int32_t* visible,
+                      const int32_t* topk, int64_t k, const uint16_t* swa, const int64_t* swa_ring,
+                      int64_t swa_rows, const int32_t* swa_len, const float* sink, float scale, float* out,
                       void* workspace, size_t workspace_bytes, int32_t* err, int64_t batch,
                       int64_t heads, cudaStream_t stream, bool pdl,
                       const uint16_t* q_img = nullptr, int64_t id_base = 0,

@@ -3,10 +3,15 @@
 // score[b,p] = sum_h w[b,h] * max(q[b,h,:] . K[row(b,p),:], 0)
 // (reference equation: native/operations.cu:104-121, reference_attention.py:34-47)
 //
-// Layout: index_pool bf16 [pool_blocks*64, 128]; a logical block j of sequence b
-// (positions 64j..64j+63) lives in physical block block_table[b, j].
+// Layout: index_pool bf16 [rows, 128], addressed per sequence either through a
+// block table (a logical block j of sequence b, positions 64j..64j+63, lives in
+// physical block block_table[b, j]) or as a ring (the reference's row pools:
+// position p at row first + (p + offset) % slots).  A ring sequence's visible
+// positions occupy at most two contiguous runs of rows -- [first + offset, ...)
+// up to the end of its slots, then [first, ...) -- and its tiles follow those
+// runs, so every load stays a tiled TMA box at any row.
 //
-// Kernel: persistent, one CTA per SM, tiles of 128 keys (two pool blocks).
+// Kernel: persistent, one CTA per SM, tiles of 128 keys (two 64-row halves).
 //   warp 0      TMA producer: two 64x64 boxes per pool block, 128-byte swizzle
 //   warp 1      TMEM allocator + single-thread tcgen05.mma issuer
 //   warps 2..9  epilogue, two warpgroups sharing every tile (each reduces half
@@ -47,11 +52,35 @@ struct IxLayout {
   static constexpr int kMiscOff = kBarOff + kNumBars * 8;  // tmem slot, abort flag, q_lo flags
   static constexpr int kPrefixOff = kMiscOff + 32;
   static constexpr int kVisOff = kPrefixOff + (kIxMaxBatch + 1) * 4;
-  static constexpr int kBytes = kVisOff + kIxMaxBatch * 4;
+  static constexpr int kRunOff = kVisOff + kIxMaxBatch * 4;  // ring rows: positions in the first run
+  static constexpr int kBytes = kRunOff + kIxMaxBatch * 4;
   static constexpr int kAlloc = kBytes + 1024;  // slack for 1024-byte alignment
   static constexpr uint32_t kTmemCols =
       (kIxAcc * N <= 32) ? 32 : (kIxAcc * N <= 64 ? 64 : (kIxAcc * N <= 128 ? 128 : (kIxAcc * N <= 256 ? 256 : 512)));
 };
+
+// Tile `tile` (128 keys) of sequence b: its first position, its first pool row
+// (ring only; paged tiles take their rows from the block table) and its keys.
+// n1 = the sequence's positions in the first ring run.
+__device__ __forceinline__ void tile_span(const PoolAddr& pa, int b, int tile, int vis, int n1, int& pos0,
+                                          int64_t& row0, int& valid) {
+  if (pa.ring == nullptr) {
+    pos0 = tile * kIxTile;
+    row0 = -1;
+  } else {
+    const int t1 = (n1 + kIxTile - 1) / kIxTile;
+    const int64_t first = pa.ring[3 * int64_t(b)];
+    if (tile < t1) {
+      pos0 = tile * kIxTile;
+      row0 = first + pa.ring[3 * int64_t(b) + 2] + pos0;
+    } else {
+      pos0 = n1 + (tile - t1) * kIxTile;
+      row0 = first + (tile - t1) * kIxTile;
+    }
+    vis = tile < t1 ? n1 : vis;  // a tile of the first run ends with it
+  }
+  valid = min(kIxTile, vis - pos0);
+}
 
 __device__ __forceinline__ int find_row(const int* prefix, int batch, int t) {
   int lo = 0, hi = batch;  // prefix[lo] <= t < prefix[hi]
@@ -119,9 +148,8 @@ __device__ __forceinline__ void mla_query_image(const float* __restrict__ q, uin
 template <int H>
 __global__ void __launch_bounds__(kIxThreads, 1)
     indexer_decode_kernel(const __grid_constant__ CUtensorMap kmap, const float* __restrict__ q,
-                          const float* __restrict__ weights, const int32_t* __restrict__ block_table,
-                          int64_t table_stride, const int32_t* __restrict__ visible,
-                          int64_t pool_blocks, float* __restrict__ scores, int64_t score_stride,
+                          const float* __restrict__ weights, const PoolAddr pa,
+                          const int32_t* __restrict__ visible, float* __restrict__ scores, int64_t score_stride,
                           int32_t* err, int batch, const float* __restrict__ mla_q,
                           uint16_t* __restrict__ mla_img, int mla_heads, uint32_t* __restrict__ hist) {
   using L = IxLayout<H>;
@@ -143,6 +171,7 @@ __global__ void __launch_bounds__(kIxThreads, 1)
   int* qlonz = reinterpret_cast<int*>(smem + L::kMiscOff + 8);  // [2] q_lo != 0 per slot
   int* prefix = reinterpret_cast<int*>(smem + L::kPrefixOff);
   int* vis_s = reinterpret_cast<int*>(smem + L::kVisOff);  // validated visible counts
+  int* run_s = reinterpret_cast<int*>(smem + L::kRunOff);  // ring: positions in the first run
   float* wsm = reinterpret_cast<float*>(smem + L::kWOff);
   float* xch = reinterpret_cast<float*>(smem + L::kXchOff);
   uint32_t* hsm = reinterpret_cast<uint32_t*>(smem + L::kHistOff);
@@ -178,12 +207,15 @@ __global__ void __launch_bounds__(kIxThreads, 1)
     int local = 0;
     for (int b = b0; b < b0 + per_lane && b < batch; ++b) {
       int v = visible[b];
-      if (v < 0 || int64_t(v) > table_stride * 64 || int64_t(v) > score_stride) {
+      if (v < 0 || int64_t(v) > addr_capacity(pa, b) || int64_t(v) > score_stride) {
         flag(err, DSR_ERR_ID);
         v = 0;
       }
+      // a ring sequence: the positions before the wrap, then the rest from the region's first row
+      const int n1 = pa.ring == nullptr ? v : int(min(int64_t(v), pa.ring[3 * int64_t(b) + 1] - pa.ring[3 * int64_t(b) + 2]));
       vis_s[b] = v;
-      local += (v + kIxTile - 1) / kIxTile;
+      run_s[b] = n1;
+      local += (n1 + kIxTile - 1) / kIxTile + (v - n1 + kIxTile - 1) / kIxTile;
     }
     int incl = local;
 #pragma unroll
@@ -194,7 +226,7 @@ __global__ void __launch_bounds__(kIxThreads, 1)
     int run = incl - local;
     for (int b = b0; b < b0 + per_lane && b < batch; ++b) {
       prefix[b] = run;
-      run += (vis_s[b] + kIxTile - 1) / kIxTile;
+      run += (run_s[b] + kIxTile - 1) / kIxTile + (vis_s[b] - run_s[b] + kIxTile - 1) / kIxTile;
     }
     if (lane == 31) prefix[batch] = incl;
     __syncwarp();
@@ -222,39 +254,42 @@ __global__ void __launch_bounds__(kIxThreads, 1)
   if (t_lo < t_hi) {
     if (warp == 0) {
       // ------------------------------------------------------------ producer
-      // Block-table entries of 16 tiles are fetched by the 32 lanes at once
-      // (one load latency per 16 tiles); lane 0 then issues the TMA boxes.
+      // The first pool rows of the 64-row halves of 16 tiles (block-table
+      // entries, or ring runs) are resolved by the 32 lanes at once (one load
+      // latency per 16 tiles); lane 0 then issues the TMA boxes.
       for (int g0 = t_lo, s0 = 0; g0 < t_hi; g0 += 16, s0 += 16) {
         const int t = g0 + (lane >> 1), blk = lane & 1;
-        int64_t pb = -1;  // -1: block beyond the visible keys, not loaded
+        int32_t hrow = -1;  // -1: a half beyond the tile's keys, not loaded
         if (t < t_hi) {
           const int b = find_row(prefix, batch, t);
-          const int tile = t - prefix[b];
-          if (tile * kIxTile + blk * 64 < vis_s[b]) {
-            pb = block_table[int64_t(b) * table_stride + tile * 2 + blk];
-            if (pb < 0 || pb >= pool_blocks) {
+          int pos0, valid;
+          int64_t row0;
+          tile_span(pa, b, t - prefix[b], vis_s[b], run_s[b], pos0, row0, valid);
+          if (blk * 64 < valid) {
+            int64_t r = row0 >= 0 ? row0 + blk * 64 : addr_row(pa, b, pos0 + blk * 64);
+            if (r < 0 || r >= pa.rows) {
               flag(err, DSR_ERR_ID);
-              pb = 0;
+              r = 0;
             }
+            hrow = int32_t(r);
           }
         }
         bool ok = true;
         for (int j = 0; j < 16 && g0 + j < t_hi; ++j) {
-          const int64_t pb0 = __shfl_sync(0xffffffffu, pb, 2 * j);
-          const int64_t pb1 = __shfl_sync(0xffffffffu, pb, 2 * j + 1);
+          const int32_t r0 = __shfl_sync(0xffffffffu, hrow, 2 * j);
+          const int32_t r1 = __shfl_sync(0xffffffffu, hrow, 2 * j + 1);
           if (lane == 0) {
             const int s = s0 + j;
             const int stage = s % kIxStages;
             ok = mbar_wait(&empty[stage], ((s / kIxStages) & 1) ^ 1, abort, err);
             if (ok) {
-              const int nblk = pb1 >= 0 ? 2 : 1;
+              const int nblk = r1 >= 0 ? 2 : 1;
               mbar_arrive_expect_tx(&full[stage], uint32_t(nblk) * 2u * 8192u);
               const uint32_t dst = sbase + L::kStagesOff + stage * kIxStageBytes;
 #pragma unroll
               for (int kh = 0; kh < 2; ++kh) {
-                tma_load_2d(dst + kh * 16384, &kmap, &full[stage], kh * 64, int32_t(pb0 * 64));
-                if (nblk == 2)
-                  tma_load_2d(dst + kh * 16384 + 8192, &kmap, &full[stage], kh * 64, int32_t(pb1 * 64));
+                tma_load_2d(dst + kh * 16384, &kmap, &full[stage], kh * 64, r0);
+                if (nblk == 2) tma_load_2d(dst + kh * 16384 + 8192, &kmap, &full[stage], kh * 64, r1);
               }
             }
           }
@@ -417,11 +452,14 @@ __global__ void __launch_bounds__(kIxThreads, 1)
           mbar_arrive(&tempty[acc]);
         }
         if (wg == 1) xch[(s & 1) * 128 + row_in_tile] = score;
-        const int tile = t - prefix[b];
-        const int p = tile * kIxTile + row_in_tile;
-        if (live && p < vis_s[b] && !isfinite(check)) flag(err, DSR_ERR_NONFINITE);
+        int pos0, valid;
+        int64_t row0;
+        tile_span(pa, b, t - prefix[b], vis_s[b], run_s[b], pos0, row0, valid);
+        const int p = pos0 + row_in_tile;
+        const bool mine = row_in_tile < valid;
+        if (live && mine && !isfinite(check)) flag(err, DSR_ERR_NONFINITE);
         asm volatile("bar.sync 3, 256;" ::: "memory");
-        if (live && wg == 0 && p < vis_s[b]) {
+        if (live && wg == 0 && mine) {
           score += xch[(s & 1) * 128 + row_in_tile];
           if (!isfinite(score)) flag(err, DSR_ERR_NONFINITE);
           scores[int64_t(b) * score_stride + p] = score;
@@ -442,9 +480,8 @@ __global__ void __launch_bounds__(kIxThreads, 1)
 }
 
 template <int H>
-int launch_ix(const CUtensorMap& map, const float* q, const float* weights,
-              const int32_t* block_table, int64_t table_stride, const int32_t* visible,
-              int64_t pool_blocks, float* scores, int64_t score_stride, int32_t* err, int batch,
+int launch_ix(const CUtensorMap& map, const float* q, const float* weights, const PoolAddr& pa,
+              const int32_t* visible, float* scores, int64_t score_stride, int32_t* err, int batch,
               const float* mla_q, uint16_t* mla_img, int mla_heads, uint32_t* hist,
               cudaStream_t stream, bool pdl) {
   using L = IxLayout<H>;
@@ -463,9 +500,8 @@ int launch_ix(const CUtensorMap& map, const float* q, const float* weights,
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
   const cudaError_t e =
-      cudaLaunchKernelEx(&cfg, indexer_decode_kernel<H>, map, q, weights, block_table, table_stride,
-                         visible, pool_blocks, scores, score_stride, err, batch, mla_q, mla_img,
-                         mla_heads, hist);
+      cudaLaunchKernelEx(&cfg, indexer_decode_kernel<H>, map, q, weights, pa, visible, scores, score_stride,
+                         err, batch, mla_q, mla_img, mla_heads, hist);
   if (e != cudaSuccess) return fail(DSR_ECUDA, "indexer launch: %s", cudaGetErrorString(e));
   return DSR_OK;
 }
@@ -473,8 +509,7 @@ int launch_ix(const CUtensorMap& map, const float* q, const float* weights,
 }  // namespace
 
 int launch_indexer_decode(const float* q, const float* weights, const uint16_t* index_pool,
-                          int64_t pool_blocks, const int32_t* block_table, int64_t table_stride,
-                          const int32_t* visible, float* scores, int64_t score_stride,
+                          const PoolAddr& pa, const int32_t* visible, float* scores, int64_t score_stride,
                           int32_t* err, int64_t batch, int64_t heads, cudaStream_t stream,
                           bool pdl, const float* mla_q, uint16_t* mla_img, int64_t mla_heads,
                           uint32_t* hist) {
@@ -482,32 +517,27 @@ int launch_indexer_decode(const float* q, const float* weights, const uint16_t* 
                                    (mla_heads == 16 || mla_heads == 32 || mla_heads == 64 ||
                                     mla_heads == 128)),
               "indexer_decode: invalid MLA query image job");
-  DSR_REQUIRE(q && weights && index_pool && block_table && visible && scores && err,
-              "indexer_decode: null pointer");
+  DSR_REQUIRE(q && weights && index_pool && visible && scores && err, "indexer_decode: null pointer");
   DSR_REQUIRE(heads == 16 || heads == 32 || heads == 64,
               "indexer_decode: heads %lld not in {16,32,64}", (long long)heads);
   DSR_REQUIRE(batch > 0 && batch <= kIxMaxBatch, "indexer_decode: batch %lld outside [1,%d]",
               (long long)batch, kIxMaxBatch);
-  DSR_REQUIRE(pool_blocks > 0 && pool_blocks * 64 <= (int64_t(1) << 31) - 1,
-              "indexer_decode: pool_blocks %lld outside [1, 2^25)", (long long)pool_blocks);
-  DSR_REQUIRE(table_stride > 0 && table_stride * 64 <= (int64_t(1) << 31) - 1,
-              "indexer_decode: invalid block-table stride");
   DSR_REQUIRE(score_stride > 0 && score_stride <= (int64_t(1) << 31) - 1,
               "indexer_decode: invalid score stride");
   DSR_REQUIRE(aligned16(index_pool) && aligned16(q), "indexer_decode: pool and q must be 16-byte aligned");
   CUtensorMap map;
-  const int rc = encode_tmap_bf16_2d(&map, index_pool, 128, uint64_t(pool_blocks) * 64, 64, 64);
+  const int rc = encode_tmap_bf16_2d(&map, index_pool, 128, uint64_t(pa.rows), 64, 64);
   if (rc != DSR_OK) return rc;
   switch (heads) {
     case 16:
-      return launch_ix<16>(map, q, weights, block_table, table_stride, visible, pool_blocks, scores,
-                           score_stride, err, int(batch), mla_q, mla_img, int(mla_heads), hist, stream, pdl);
+      return launch_ix<16>(map, q, weights, pa, visible, scores, score_stride, err, int(batch), mla_q, mla_img,
+                           int(mla_heads), hist, stream, pdl);
     case 32:
-      return launch_ix<32>(map, q, weights, block_table, table_stride, visible, pool_blocks, scores,
-                           score_stride, err, int(batch), mla_q, mla_img, int(mla_heads), hist, stream, pdl);
+      return launch_ix<32>(map, q, weights, pa, visible, scores, score_stride, err, int(batch), mla_q, mla_img,
+                           int(mla_heads), hist, stream, pdl);
     default:
-      return launch_ix<64>(map, q, weights, block_table, table_stride, visible, pool_blocks, scores,
-                           score_stride, err, int(batch), mla_q, mla_img, int(mla_heads), hist, stream, pdl);
+      return launch_ix<64>(map, q, weights, pa, visible, scores, score_stride, err, int(batch), mla_q, mla_img,
+                           int(mla_heads), hist, stream, pdl);
   }
 }
 
@@ -519,7 +549,21 @@ extern "C" int dsr_indexer_decode(const float* q, const float* weights, const ui
                                   int64_t score_stride, int32_t* err, int64_t batch, int64_t heads,
                                   void* stream) {
   dsr::clear_error();
-  return dsr::launch_indexer_decode(q, weights, index_pool, pool_blocks, block_table, table_stride,
-                                    visible, scores, score_stride, err, batch, heads,
+  dsr::PoolAddr pa;
+  const int rc = dsr::paged_addr(&pa, block_table, table_stride, pool_blocks, "indexer_decode");
+  if (rc != DSR_OK) return rc;
+  return dsr::launch_indexer_decode(q, weights, index_pool, pa, visible, scores, score_stride, err, batch, heads,
+                                    dsr::as_stream(stream), false, nullptr, nullptr, 0, nullptr);
+}
+
+extern "C" int dsr_indexer_decode_ring(const float* q, const float* weights, const uint16_t* index_pool,
+                                       int64_t pool_rows, const int64_t* ring, const int32_t* visible,
+                                       float* scores, int64_t score_stride, int32_t* err, int64_t batch,
+                                       int64_t heads, void* stream) {
+  dsr::clear_error();
+  dsr::PoolAddr pa;
+  const int rc = dsr::ring_addr(&pa, ring, pool_rows, "indexer_decode_ring");
+  if (rc != DSR_OK) return rc;
+  return dsr::launch_indexer_decode(q, weights, index_pool, pa, visible, scores, score_stride, err, batch, heads,
                                     dsr::as_stream(stream), false, nullptr, nullptr, 0, nullptr);
 }

@@ -53,15 +53,19 @@ struct MlaLayout {
 };
 
 // Row sentinel past the tensor (the gather zero-fills it): tile 0 reads the SWA rows.
-__device__ __forceinline__ int32_t mla_oob_row(int tile, int batch, int64_t pool_blocks) {
-  return tile == 0 ? int32_t(batch) * DSR_SWA_ROWS : int32_t(pool_blocks * 64);
+__device__ __forceinline__ int32_t mla_oob_row(int tile, int64_t swa_rows, const PoolAddr& kv) {
+  return tile == 0 ? int32_t(swa_rows) : int32_t(kv.rows);
 }
 
 // Row of key slot t of `tile` for sequence b (top-k ids come from the preceding
 // kernel): tile 0 is the SWA window, tiles 1.. the selected positions through the
-// block table.  `oob` when the slot holds no key.
-__device__ __forceinline__ int32_t mla_key_row(int tile, int b, int t, int32_t oob, int64_t pool_blocks,
-                                               const int32_t* __restrict__ block_table, int64_t table_stride,
+// pool addressing (block table or ring).  The SWA window is the sequence's last
+// swa_len positions: by default rows b*128 .. b*128 + swa_len - 1 of the SWA
+// tensor (ring row p % 128 holds position p); with swa_ring, the rows
+// first + (p + offset) % slots of an SWA row pool for those positions.  `oob`
+// when the slot holds no key.
+__device__ __forceinline__ int32_t mla_key_row(int tile, int b, int t, int32_t oob, const PoolAddr& kv,
+                                               const int64_t* __restrict__ swa_ring, int64_t swa_rows,
                                                const int32_t* __restrict__ visible,
                                                const int32_t* __restrict__ topk, int k,
                                                const int32_t* __restrict__ swa_len, int64_t id_base,
@@ -73,7 +77,20 @@ __device__ __forceinline__ int32_t mla_key_row(int tile, int b, int t, int32_t o
       if (t == 0) flag(err, DSR_ERR_ID);
       len = 0;
     }
-    if (t < len) row = b * DSR_SWA_ROWS + t;
+    if (t < len) {
+      if (swa_ring == nullptr) {
+        row = b * DSR_SWA_ROWS + t;
+      } else {
+        const PoolAddr sa{nullptr, 0, swa_ring, swa_rows};
+        int64_t first, slots, offset;
+        const int64_t end = id_base + visible[b];  // one past the sequence's last position
+        if (!ring_desc(sa, b, first, slots, offset) || slots < len) {
+          if (t == 0) flag(err, DSR_ERR_ID);
+        } else {
+          row = int32_t(first + (end - len + t + offset) % slots);
+        }
+      }
+    }
   } else {
     const int idx = (tile - 1) * kMlaTile + t;
     if (idx < k) {
@@ -87,9 +104,9 @@ __device__ __forceinline__ int32_t mla_key_row(int tile, int b, int t, int32_t o
         } else if (local < 0 || local >= visible[b]) {
           if (!foreign_ok) flag(err, DSR_ERR_ID);
         } else {
-          const int64_t blk = block_table[int64_t(b) * table_stride + (local >> 6)];
-          if (blk < 0 || blk >= pool_blocks) flag(err, DSR_ERR_ID);
-          else row = int32_t(blk * 64 + (local & 63));
+          const int64_t r = addr_row(kv, b, local);
+          if (r < 0 || r >= kv.rows) flag(err, DSR_ERR_ID);
+          else row = int32_t(r);
         }
       }
     }
@@ -214,10 +231,10 @@ template <int HG>
 __global__ void __launch_bounds__(kMlaThreads, 1)
     mla_decode_kernel(const __grid_constant__ CUtensorMap kv_map,
                       const __grid_constant__ CUtensorMap swa_map,
-                      const float* __restrict__ q, const uint16_t* __restrict__ kv_pool,
-                      int64_t pool_blocks, const int32_t* __restrict__ block_table,
-                      int64_t table_stride, const int32_t* __restrict__ visible,
-                      const int32_t* __restrict__ topk, int k, const uint16_t* __restrict__ swa,
+                      const float* __restrict__ q, const PoolAddr kv,
+                      const int64_t* __restrict__ swa_ring, int64_t swa_rows,
+                      const int32_t* __restrict__ visible,
+                      const int32_t* __restrict__ topk, int k,
                       const int32_t* __restrict__ swa_len, float scale_log2,
                       uint16_t* __restrict__ part_o, float* __restrict__ part_m,
                       float* __restrict__ part_l, int32_t* err, int heads,
@@ -322,9 +339,9 @@ __global__ void __launch_bounds__(kMlaThreads, 1)
     }
     // ---- resolve the row of key t (top-k ids come from the preceding kernel);
     // rows past the tensor (the OOB sentinel) are zero-filled by the gather
-    const int32_t oob = mla_oob_row(tile, int(gridDim.y), pool_blocks);
-    const int32_t row = mla_key_row(tile, b, t, oob, pool_blocks, block_table, table_stride, visible, topk, k,
-                                    swa_len, id_base, foreign_ok, err);
+    const int32_t oob = mla_oob_row(tile, swa_rows, kv);
+    const int32_t row = mla_key_row(tile, b, t, oob, kv, swa_ring, swa_rows, visible, topk, k, swa_len, id_base,
+                                    foreign_ok, err);
     valid[t] = row != oob;
     // ---- gather: 4-row TMA gathers of 64-column slabs into the 9 swizzled
     // column blocks; warp w issues the 8 x 9 gathers of its rows 32w..32w+31
@@ -411,8 +428,8 @@ __global__ void __launch_bounds__(kMlaThreads, 1)
 template <int HG>
 __global__ void __launch_bounds__(kMlaThreads, 1)
     mla_persistent_kernel(const __grid_constant__ CUtensorMap kv_map,
-                          const __grid_constant__ CUtensorMap swa_map, int64_t pool_blocks,
-                          const int32_t* __restrict__ block_table, int64_t table_stride,
+                          const __grid_constant__ CUtensorMap swa_map, const PoolAddr kv,
+                          const int64_t* __restrict__ swa_ring, int64_t swa_rows,
                           const int32_t* __restrict__ visible, const int32_t* __restrict__ topk, int k,
                           const int32_t* __restrict__ swa_len, float scale_log2,
                           uint16_t* __restrict__ part_o, float* __restrict__ part_m,
@@ -498,9 +515,9 @@ __global__ void __launch_bounds__(kMlaThreads, 1)
     auto resolve = [&](int it, int slot) -> int32_t {
       int tile, b, hg;
       item_of(it, tile, b, hg);
-      const int32_t oob = mla_oob_row(tile, batch, pool_blocks);
-      const int32_t row = mla_key_row(tile, b, t, oob, pool_blocks, block_table, table_stride, visible, topk,
-                                      k, swa_len, id_base, foreign_ok, err);
+      const int32_t oob = mla_oob_row(tile, swa_rows, kv);
+      const int32_t row = mla_key_row(tile, b, t, oob, kv, swa_ring, swa_rows, visible, topk, k, swa_len, id_base,
+                                      foreign_ok, err);
       valid[slot * kMlaTile + t] = row != oob;
       return row;
     };
@@ -779,9 +796,9 @@ __global__ void __launch_bounds__(128, kInFlight > 8 ? 1 : 8) lse_combine_kernel
 }
 
 template <int HG>
-int launch_mla(const float* q, const uint16_t* kv_pool, int64_t pool_blocks,
-               const int32_t* block_table, int64_t table_stride, const int32_t* visible,
-               const int32_t* topk, int64_t k, const uint16_t* swa, const int32_t* swa_len,
+int launch_mla(const float* q, const uint16_t* kv_pool, const PoolAddr& kv, const int32_t* visible,
+               const int32_t* topk, int64_t k, const uint16_t* swa, const int64_t* swa_ring, int64_t swa_rows,
+               const int32_t* swa_len,
                float scale, uint16_t* part_o, float* part_m, float* part_l, int32_t* err,
                int64_t batch, int64_t heads, int tiles, cudaStream_t stream, bool pdl,
                const uint16_t* q_img, int64_t id_base, bool foreign_ok) {
@@ -793,9 +810,9 @@ int launch_mla(const float* q, const uint16_t* kv_pool, int64_t pool_blocks,
   }
   // row-gather tensor maps: one-row boxes of 64 columns over the pool and the SWA rows
   CUtensorMap kv_map, swa_map;
-  int rc = encode_tmap_bf16_2d(&kv_map, kv_pool, kMlaD, uint64_t(pool_blocks) * 64, 64, 1);
+  int rc = encode_tmap_bf16_2d(&kv_map, kv_pool, kMlaD, uint64_t(kv.rows), 64, 1);
   if (rc != DSR_OK) return rc;
-  rc = encode_tmap_bf16_2d(&swa_map, swa, kMlaD, uint64_t(batch) * DSR_SWA_ROWS, 64, 1);
+  rc = encode_tmap_bf16_2d(&swa_map, swa, kMlaD, uint64_t(swa_rows), 64, 1);
   if (rc != DSR_OK) return rc;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(unsigned(tiles), unsigned(batch), unsigned(heads / HG));
@@ -812,17 +829,16 @@ int launch_mla(const float* q, const uint16_t* kv_pool, int64_t pool_blocks,
   const int64_t items = int64_t(tiles) * batch * (heads / HG);
   if (q_img != nullptr && items > sm_count()) {
     cfg.gridDim = dim3(unsigned(sm_count()), 1, 1);
-    const cudaError_t e = cudaLaunchKernelEx(&cfg, mla_persistent_kernel<HG>, kv_map, swa_map, pool_blocks,
-                                             block_table, table_stride, visible, topk, int(k), swa_len,
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, mla_persistent_kernel<HG>, kv_map, swa_map, kv, swa_ring,
+                                             swa_rows, visible, topk, int(k), swa_len,
                                              scale * kLog2e, part_o, part_m, part_l, err, int(heads),
                                              int(batch), tiles, q_img, id_base, int(foreign_ok));
     if (e != cudaSuccess) return fail(DSR_ECUDA, "mla launch: %s", cudaGetErrorString(e));
     return DSR_OK;
   }
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, mla_decode_kernel<HG>, kv_map, swa_map, q, kv_pool,
-                                           pool_blocks,
-                                           block_table, table_stride, visible, topk, int(k), swa,
-                                           swa_len, scale * kLog2e, part_o, part_m, part_l, err,
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, mla_decode_kernel<HG>, kv_map, swa_map, q, kv, swa_ring,
+                                           swa_rows, visible, topk, int(k), swa_len, scale * kLog2e, part_o,
+                                           part_m, part_l, err,
                                            int(heads), q_img, id_base, int(foreign_ok));
   if (e != cudaSuccess) return fail(DSR_ECUDA, "mla launch: %s", cudaGetErrorString(e));
   return DSR_OK;
@@ -879,16 +895,14 @@ int launch_lse_combine(const float* part_o, const float* part_m, const float* pa
                         stream, pdl);
 }
 
-int launch_mla_decode(const float* q, const uint16_t* kv_pool, int64_t pool_blocks,
-                      const int32_t* block_table, int64_t table_stride, const int32_t* visible,
-                      const int32_t* topk, int64_t k, const uint16_t* swa,
-                      const int32_t* swa_len, const float* sink, float scale, float* out,
+int launch_mla_decode(const float* q, const uint16_t* kv_pool, const PoolAddr& kv, const int32_t* visible,
+                      const int32_t* topk, int64_t k, const uint16_t* swa, const int64_t* swa_ring,
+                      int64_t swa_rows, const int32_t* swa_len, const float* sink, float scale, float* out,
                       void* workspace, size_t workspace_bytes, int32_t* err, int64_t batch,
                       int64_t heads, cudaStream_t stream, bool pdl, const uint16_t* q_img,
                       int64_t id_base, bool partial, float* out_m, float* out_l) {
   DSR_REQUIRE(q_img == nullptr || aligned16(q_img), "sparse_mla_decode: query image must be 16-byte aligned");
-  DSR_REQUIRE(q && kv_pool && block_table && visible && topk && swa && swa_len && out && err &&
-                  workspace,
+  DSR_REQUIRE(q && kv_pool && visible && topk && swa && swa_len && out && err && workspace,
               "sparse_mla_decode: null pointer");
   DSR_REQUIRE(partial ? (sink == nullptr && out_m != nullptr && out_l != nullptr) : sink != nullptr,
               "sparse_mla_decode: a sink (full) or out_m and out_l (partial) are required");
@@ -897,9 +911,8 @@ int launch_mla_decode(const float* q, const uint16_t* kv_pool, int64_t pool_bloc
               "sparse_mla_decode: heads %lld not in {16,32,64,128}", (long long)heads);
   DSR_REQUIRE(batch > 0 && batch <= 65535, "sparse_mla_decode: invalid batch");
   DSR_REQUIRE(k >= 0 && k <= 8192, "sparse_mla_decode: k %lld outside [0, 8192]", (long long)k);
-  DSR_REQUIRE(pool_blocks > 0 && pool_blocks * 64 < (int64_t(1) << 31) && table_stride > 0,
-              "sparse_mla_decode: invalid pool/table (pool rows must fit int32)");
-  DSR_REQUIRE(batch * DSR_SWA_ROWS < (int64_t(1) << 31), "sparse_mla_decode: too many SWA rows");
+  if (swa_ring == nullptr) swa_rows = batch * DSR_SWA_ROWS;  // the [batch, 128, 576] ring layout
+  DSR_REQUIRE(swa_rows > 0 && swa_rows < (int64_t(1) << 31), "sparse_mla_decode: invalid SWA rows");
   DSR_REQUIRE(isfinite(scale) && scale > 0.f, "invalid attention scale");
   DSR_REQUIRE(aligned16(q) && aligned16(kv_pool) && aligned16(swa),
               "sparse_mla_decode: q, kv_pool and swa must be 16-byte aligned");
@@ -918,19 +931,16 @@ int launch_mla_decode(const float* q, const uint16_t* kv_pool, int64_t pool_bloc
   int rc;
   switch (hg) {
     case 16:
-      rc = launch_mla<16>(q, kv_pool, pool_blocks, block_table, table_stride, visible, topk, k, swa,
-                          swa_len, scale, part_o, part_m, part_l, err, batch, heads, tiles, stream,
-                          pdl, q_img, id_base, partial);
+      rc = launch_mla<16>(q, kv_pool, kv, visible, topk, k, swa, swa_ring, swa_rows, swa_len, scale, part_o,
+                          part_m, part_l, err, batch, heads, tiles, stream, pdl, q_img, id_base, partial);
       break;
     case 32:
-      rc = launch_mla<32>(q, kv_pool, pool_blocks, block_table, table_stride, visible, topk, k, swa,
-                          swa_len, scale, part_o, part_m, part_l, err, batch, heads, tiles, stream,
-                          pdl, q_img, id_base, partial);
+      rc = launch_mla<32>(q, kv_pool, kv, visible, topk, k, swa, swa_ring, swa_rows, swa_len, scale, part_o,
+                          part_m, part_l, err, batch, heads, tiles, stream, pdl, q_img, id_base, partial);
       break;
     default:
-      rc = launch_mla<64>(q, kv_pool, pool_blocks, block_table, table_stride, visible, topk, k, swa,
-                          swa_len, scale, part_o, part_m, part_l, err, batch, heads, tiles, stream,
-                          pdl, q_img, id_base, partial);
+      rc = launch_mla<64>(q, kv_pool, kv, visible, topk, k, swa, swa_ring, swa_rows, swa_len, scale, part_o,
+                          part_m, part_l, err, batch, heads, tiles, stream, pdl, q_img, id_base, partial);
       break;
   }
   if (rc != DSR_OK) return rc;
@@ -952,9 +962,27 @@ extern "C" int dsr_sparse_mla_decode(const float* q, const uint16_t* kv_pool, in
                                      size_t workspace_bytes, int32_t* err, int64_t batch,
                                      int64_t heads, void* stream) {
   dsr::clear_error();
-  return dsr::launch_mla_decode(q, kv_pool, pool_blocks, block_table, table_stride, visible, topk,
-                                k, swa, swa_len, sink, scale, out, workspace, workspace_bytes, err,
-                                batch, heads, dsr::as_stream(stream), false);
+  dsr::PoolAddr kv;
+  const int rc = dsr::paged_addr(&kv, block_table, table_stride, pool_blocks, "sparse_mla_decode");
+  if (rc != DSR_OK) return rc;
+  return dsr::launch_mla_decode(q, kv_pool, kv, visible, topk, k, swa, nullptr, 0, swa_len, sink, scale, out,
+                                workspace, workspace_bytes, err, batch, heads, dsr::as_stream(stream), false);
+}
+
+extern "C" int dsr_sparse_mla_decode_ring(const float* q, const uint16_t* kv_pool, int64_t kv_rows,
+                                          const int64_t* kv_ring, const int32_t* visible, const int32_t* topk,
+                                          int64_t k, const uint16_t* swa_pool, int64_t swa_rows,
+                                          const int64_t* swa_ring, const int32_t* swa_len, const float* sink,
+                                          float scale, float* out, void* workspace, size_t workspace_bytes,
+                                          int32_t* err, int64_t batch, int64_t heads, void* stream) {
+  dsr::clear_error();
+  dsr::PoolAddr kv;
+  int rc = dsr::ring_addr(&kv, kv_ring, kv_rows, "sparse_mla_decode_ring");
+  if (rc != DSR_OK) return rc;
+  DSR_REQUIRE(swa_ring != nullptr, "sparse_mla_decode_ring: null SWA ring descriptors");
+  return dsr::launch_mla_decode(q, kv_pool, kv, visible, topk, k, swa_pool, swa_ring, swa_rows, swa_len, sink,
+                                scale, out, workspace, workspace_bytes, err, batch, heads, dsr::as_stream(stream),
+                                false);
 }
 
 extern "C" int dsr_sparse_mla_partial(const float* q, const uint16_t* kv_pool, int64_t pool_blocks,
@@ -965,10 +993,12 @@ extern "C" int dsr_sparse_mla_partial(const float* q, const uint16_t* kv_pool, i
                                       void* workspace, size_t workspace_bytes, int32_t* err,
                                       int64_t batch, int64_t heads, void* stream) {
   dsr::clear_error();
-  return dsr::launch_mla_decode(q, kv_pool, pool_blocks, block_table, table_stride, visible, topk,
-                                k, swa, swa_len, nullptr, scale, out_o, workspace, workspace_bytes,
-                                err, batch, heads, dsr::as_stream(stream), false, nullptr, id_base,
-                                true, out_m, out_l);
+  dsr::PoolAddr kv;
+  const int rc = dsr::paged_addr(&kv, block_table, table_stride, pool_blocks, "sparse_mla_partial");
+  if (rc != DSR_OK) return rc;
+  return dsr::launch_mla_decode(q, kv_pool, kv, visible, topk, k, swa, nullptr, 0, swa_len, nullptr, scale, out_o,
+                                workspace, workspace_bytes, err, batch, heads, dsr::as_stream(stream), false,
+                                nullptr, id_base, true, out_m, out_l);
 }
 
 extern "C" int dsr_lse_combine_packed(const float* packed, int64_t world, const float* sink,

@@ -331,6 +331,153 @@ std::vector<at::Tensor> ds_decode_step(at::Tensor idx_q, at::Tensor idx_w, at::T
   return {out, topk, error};
 }
 
+// ---- ring-offset pools (the reference's DeviceRowPool layout): rings i64[batch, 3]
+void check_ring(const at::Tensor& ring, int64_t batch, const at::Tensor& anchor, const char* what) {
+  check(ring, at::kLong, anchor);
+  TORCH_CHECK(ring.dim() == 2 && ring.size(0) == batch && ring.size(1) == 3, what,
+              ": ring descriptors [batch, 3] = (first row, slots, offset) expected");
+}
+
+std::vector<at::Tensor> ds_indexer_decode_ring(at::Tensor q, at::Tensor weights, at::Tensor index_pool,
+                                               at::Tensor ring, at::Tensor visible, int64_t score_stride) {
+  check(q, at::kFloat, q);
+  check(weights, at::kFloat, q);
+  check_cache(index_pool, q);
+  check(visible, at::kInt, q);
+  TORCH_CHECK(q.dim() == 3 && q.size(2) == 128 && weights.dim() == 2 && weights.size(0) == q.size(0) &&
+                  weights.size(1) == q.size(1) && index_pool.dim() == 2 && index_pool.size(1) == 128 &&
+                  visible.dim() == 1 && visible.size(0) == q.size(0),
+              "indexer_decode_ring: q [batch, heads, 128], weights [batch, heads], index_pool [rows, 128], "
+              "visible [batch] expected");
+  check_ring(ring, q.size(0), q, "indexer_decode_ring");
+  const c10::cuda::CUDAGuard guard(q.device());
+  auto scores = at::empty({q.size(0), score_stride}, q.options());
+  auto error = status_like(q);
+  ok(dsr_indexer_decode_ring(q.data_ptr<float>(), weights.data_ptr<float>(), bf16(index_pool),
+                             index_pool.size(0), ring.data_ptr<int64_t>(), visible.data_ptr<int32_t>(),
+                             scores.data_ptr<float>(), score_stride, error.data_ptr<int32_t>(), q.size(0),
+                             q.size(1), current_stream()));
+  return {scores, error};
+}
+
+std::vector<at::Tensor> ds_sparse_mla_decode_ring(at::Tensor q, at::Tensor kv_pool, at::Tensor kv_ring,
+                                                  at::Tensor visible, at::Tensor topk, at::Tensor swa_pool,
+                                                  at::Tensor swa_ring, at::Tensor swa_len, at::Tensor sink,
+                                                  double scale) {
+  check(q, at::kFloat, q);
+  check_cache(kv_pool, q);
+  check(visible, at::kInt, q);
+  check(topk, at::kInt, q);
+  check_cache(swa_pool, q);
+  check(swa_len, at::kInt, q);
+  check(sink, at::kFloat, q);
+  const int64_t batch = q.size(0), heads = q.size(1);
+  TORCH_CHECK(q.dim() == 3 && q.size(2) == DSR_KV_DIM && kv_pool.dim() == 2 && kv_pool.size(1) == DSR_KV_DIM &&
+                  swa_pool.dim() == 2 && swa_pool.size(1) == DSR_KV_DIM && topk.dim() == 2 &&
+                  topk.size(0) == batch && visible.size(0) == batch && swa_len.size(0) == batch &&
+                  sink.dim() == 1 && sink.size(0) == heads,
+              "sparse_mla_decode_ring: inconsistent shapes");
+  check_ring(kv_ring, batch, q, "sparse_mla_decode_ring (KV pool)");
+  check_ring(swa_ring, batch, q, "sparse_mla_decode_ring (SWA pool)");
+  const c10::cuda::CUDAGuard guard(q.device());
+  const int64_t k = topk.size(1);
+  auto out = at::empty({batch, heads, DSR_V_DIM}, q.options());
+  const size_t ws_bytes = dsr_mla_workspace_bytes(batch, heads, k);
+  auto ws = at::empty({int64_t(ws_bytes)}, q.options().dtype(at::kByte));
+  auto error = status_like(q);
+  ok(dsr_sparse_mla_decode_ring(q.data_ptr<float>(), bf16(kv_pool), kv_pool.size(0), kv_ring.data_ptr<int64_t>(),
+                                visible.data_ptr<int32_t>(), topk.data_ptr<int32_t>(), k, bf16(swa_pool),
+                                swa_pool.size(0), swa_ring.data_ptr<int64_t>(), swa_len.data_ptr<int32_t>(),
+                                sink.data_ptr<float>(), static_cast<float>(scale), out.data_ptr<float>(),
+                                ws.data_ptr(), ws_bytes, error.data_ptr<int32_t>(), batch, heads,
+                                current_stream()));
+  return {out, error};
+}
+
+std::vector<at::Tensor> ds_decode_step_ring(at::Tensor idx_q, at::Tensor idx_w, at::Tensor index_pool,
+                                            at::Tensor index_ring, at::Tensor q, at::Tensor kv_pool,
+                                            at::Tensor kv_ring, at::Tensor visible, int64_t max_visible, int64_t k,
+                                            at::Tensor swa_pool, at::Tensor swa_ring, at::Tensor swa_len,
+                                            at::Tensor sink, double scale, bool return_scores) {
+  check(idx_q, at::kFloat, q);
+  check(idx_w, at::kFloat, q);
+  check_cache(index_pool, q);
+  check(q, at::kFloat, q);
+  check_cache(kv_pool, q);
+  check(visible, at::kInt, q);
+  check_cache(swa_pool, q);
+  check(swa_len, at::kInt, q);
+  check(sink, at::kFloat, q);
+  const int64_t batch = q.size(0), heads = q.size(1);
+  TORCH_CHECK(idx_q.dim() == 3 && idx_q.size(0) == batch && idx_q.size(2) == 128 && idx_w.dim() == 2 &&
+                  idx_w.size(0) == batch && idx_w.size(1) == idx_q.size(1),
+              "decode_step_ring: idx_q [batch, idx_heads, 128], idx_w [batch, idx_heads] expected");
+  TORCH_CHECK(q.dim() == 3 && q.size(2) == DSR_KV_DIM && kv_pool.dim() == 2 && kv_pool.size(1) == DSR_KV_DIM &&
+                  index_pool.dim() == 2 && index_pool.size(1) == DSR_INDEX_DIM && swa_pool.dim() == 2 &&
+                  swa_pool.size(1) == DSR_KV_DIM,
+              "decode_step_ring: pool geometry mismatch");
+  TORCH_CHECK(visible.size(0) == batch && swa_len.size(0) == batch && sink.size(0) == heads,
+              "decode_step_ring: inconsistent batch shapes");
+  check_ring(index_ring, batch, q, "decode_step_ring (index pool)");
+  check_ring(kv_ring, batch, q, "decode_step_ring (KV pool)");
+  check_ring(swa_ring, batch, q, "decode_step_ring (SWA pool)");
+  const c10::cuda::CUDAGuard guard(q.device());
+  auto out = at::empty({batch, heads, DSR_V_DIM}, q.options());
+  auto topk = at::empty({batch, k}, q.options().dtype(at::kInt));
+  const int64_t stride = (max_visible + 63) / 64 * 64;
+  at::Tensor scores = return_scores ? at::empty({batch, stride}, q.options()) : at::Tensor();
+  const size_t ws_bytes = dsr_decode_workspace_bytes(batch, max_visible, heads, k);
+  auto ws = at::zeros({int64_t(ws_bytes)}, q.options().dtype(at::kByte));
+  auto error = status_like(q);
+  ok(dsr_decode_step_ring(idx_q.data_ptr<float>(), idx_w.data_ptr<float>(), idx_q.size(1), bf16(index_pool),
+                          index_pool.size(0), index_ring.data_ptr<int64_t>(), q.data_ptr<float>(), bf16(kv_pool),
+                          kv_pool.size(0), kv_ring.data_ptr<int64_t>(), heads, visible.data_ptr<int32_t>(),
+                          max_visible, k, bf16(swa_pool), swa_pool.size(0), swa_ring.data_ptr<int64_t>(),
+                          swa_len.data_ptr<int32_t>(), sink.data_ptr<float>(), static_cast<float>(scale),
+                          out.data_ptr<float>(), topk.data_ptr<int32_t>(),
+                          return_scores ? scores.data_ptr<float>() : nullptr, ws.data_ptr(), ws_bytes,
+                          error.data_ptr<int32_t>(), batch, current_stream()));
+  if (return_scores) return {out, topk, error, scores};
+  return {out, topk, error};
+}
+
+at::Tensor ds_append_kv_index_ring(at::Tensor kv_pool, at::Tensor kv_ring, at::Tensor kv_generations,
+                                   at::Tensor kv_expected, at::Tensor index_pool, at::Tensor index_ring,
+                                   at::Tensor index_generations, at::Tensor index_expected, at::Tensor seq,
+                                   at::Tensor positions, at::Tensor kv_values, at::Tensor index_values) {
+  check_cache(kv_pool, kv_pool);
+  check_cache(index_pool, kv_pool);
+  check(kv_generations, at::kLong, kv_pool);
+  check(index_generations, at::kLong, kv_pool);
+  check(kv_expected, at::kLong, kv_pool);
+  check(index_expected, at::kLong, kv_pool);
+  check(seq, at::kInt, kv_pool);
+  check(positions, at::kInt, kv_pool);
+  check_cache(kv_values, kv_pool);
+  check_cache(index_values, kv_pool);
+  const int64_t n = seq.size(0), sequences = kv_ring.size(0);
+  TORCH_CHECK(kv_pool.dim() == 2 && kv_pool.size(1) == DSR_KV_DIM && index_pool.dim() == 2 &&
+                  index_pool.size(1) == DSR_INDEX_DIM && kv_generations.dim() == 1 &&
+                  kv_generations.size(0) == kv_pool.size(0) && index_generations.dim() == 1 &&
+                  index_generations.size(0) == index_pool.size(0),
+              "append_kv_index_ring: pools [rows, 576/128] with generations [rows] expected");
+  TORCH_CHECK(positions.size(0) == n && kv_expected.size(0) == n && index_expected.size(0) == n &&
+                  kv_values.dim() == 2 && kv_values.size(0) == n && kv_values.size(1) == DSR_KV_DIM &&
+                  index_values.dim() == 2 && index_values.size(0) == n && index_values.size(1) == DSR_INDEX_DIM,
+              "append_kv_index_ring: inconsistent row shapes");
+  check_ring(kv_ring, sequences, kv_pool, "append_kv_index_ring (KV pool)");
+  check_ring(index_ring, sequences, kv_pool, "append_kv_index_ring (index pool)");
+  const c10::cuda::CUDAGuard guard(kv_pool.device());
+  auto error = status_like(kv_pool);
+  ok(dsr_append_kv_index_ring(bf16_mut(kv_pool), kv_pool.size(0), kv_ring.data_ptr<int64_t>(),
+                              kv_generations.data_ptr<int64_t>(), kv_expected.data_ptr<int64_t>(),
+                              bf16_mut(index_pool), index_pool.size(0), index_ring.data_ptr<int64_t>(),
+                              index_generations.data_ptr<int64_t>(), index_expected.data_ptr<int64_t>(), sequences,
+                              seq.data_ptr<int32_t>(), positions.data_ptr<int32_t>(), bf16(kv_values),
+                              bf16(index_values), error.data_ptr<int32_t>(), n, current_stream()));
+  return error;
+}
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("sparse_attention", &ds_sparse_attention);
   m.def("index_scores", &ds_index_scores);
@@ -350,4 +497,17 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("q"), py::arg("kv_pool"), py::arg("block_table"), py::arg("visible"),
         py::arg("max_visible"), py::arg("k"), py::arg("swa"), py::arg("swa_len"), py::arg("sink"),
         py::arg("scale"), py::arg("return_scores") = false);
+  m.def("indexer_decode_ring", &ds_indexer_decode_ring, py::arg("q"), py::arg("weights"), py::arg("index_pool"),
+        py::arg("ring"), py::arg("visible"), py::arg("score_stride"));
+  m.def("sparse_mla_decode_ring", &ds_sparse_mla_decode_ring, py::arg("q"), py::arg("kv_pool"),
+        py::arg("kv_ring"), py::arg("visible"), py::arg("topk"), py::arg("swa_pool"), py::arg("swa_ring"),
+        py::arg("swa_len"), py::arg("sink"), py::arg("scale"));
+  m.def("decode_step_ring", &ds_decode_step_ring, py::arg("idx_q"), py::arg("idx_w"), py::arg("index_pool"),
+        py::arg("index_ring"), py::arg("q"), py::arg("kv_pool"), py::arg("kv_ring"), py::arg("visible"),
+        py::arg("max_visible"), py::arg("k"), py::arg("swa_pool"), py::arg("swa_ring"), py::arg("swa_len"),
+        py::arg("sink"), py::arg("scale"), py::arg("return_scores") = false);
+  m.def("append_kv_index_ring", &ds_append_kv_index_ring, py::arg("kv_pool"), py::arg("kv_ring"),
+        py::arg("kv_generations"), py::arg("kv_expected"), py::arg("index_pool"), py::arg("index_ring"),
+        py::arg("index_generations"), py::arg("index_expected"), py::arg("seq"), py::arg("positions"),
+        py::arg("kv_values"), py::arg("index_values"));
 }

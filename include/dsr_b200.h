@@ -313,6 +313,74 @@ int dsr_decode_step(const float* idx_q, const float* idx_w, int64_t idx_heads,
                     int32_t* err, int64_t batch, void* stream);
 
 /* ---------------------------------------------------------------------------
+ * Ring-offset pools: the reference's own pool layout.  The reference keeps one
+ * DeviceRowPool per (kind, layer) -- sources (KV rows), index_keys, windows
+ * (the 128-row SWA ring) -- each a flat [slots, width] tensor in which logical
+ * row p lives at slot (p + offset) % slots, offset = a hash of (run, role,
+ * kind, layer) (src/deepseekrpc/cache_pool.py:24-113, bootstrap.py:185-192).
+ * These entry points address such pools directly.  Per sequence b a ring
+ * descriptor i64[3] = {first row, slots, offset} places its region at rows
+ * [first, first + slots) of the pool tensor (first = 0, one sequence per pool,
+ * is the reference's case); position p is at row first + (p + offset) % slots.
+ * A descriptor is valid when slots > 0, 0 <= offset < slots and
+ * first + slots <= the pool's rows; an invalid one, or visible[b] > slots,
+ * gives status 1.  Offsets need not be multiples of 64 and a sequence may wrap
+ * around the end of its slots.  Everything else is as in the paged forms.
+ * ------------------------------------------------------------------------- */
+
+/* dsr_indexer_decode over a ring-offset index-key pool bf16[pool_rows, 128];
+ * ring i64[batch][3].  Replaces TiledIndexer.select's per-tile index_scores
+ * over DeviceRowPool.physical() slots (index_selection.py:94-107). */
+int dsr_indexer_decode_ring(const float* q, const float* weights, const uint16_t* index_pool,
+                            int64_t pool_rows, const int64_t* ring, const int32_t* visible,
+                            float* scores, int64_t score_stride, int32_t* err, int64_t batch,
+                            int64_t heads, void* stream);
+
+/* dsr_sparse_mla_decode over a ring-offset KV pool bf16[kv_rows, 576] (kv_ring
+ * i64[batch][3]); the SWA window is the sequence's last swa_len[b] positions,
+ * read from an SWA row pool bf16[swa_rows, 576] through swa_ring i64[batch][3]
+ * (the reference's 128-slot windows pools: slots 128).  Replaces forward_mqa's
+ * staging + physical() translation + sparse_attention (vllm_attention.py:231-262). */
+int dsr_sparse_mla_decode_ring(const float* q, const uint16_t* kv_pool, int64_t kv_rows,
+                               const int64_t* kv_ring, const int32_t* visible, const int32_t* topk,
+                               int64_t k, const uint16_t* swa_pool, int64_t swa_rows,
+                               const int64_t* swa_ring, const int32_t* swa_len, const float* sink,
+                               float scale, float* out, void* workspace, size_t workspace_bytes,
+                               int32_t* err, int64_t batch, int64_t heads, void* stream);
+
+/* dsr_decode_step over ring-offset pools: index keys (index_ring), KV rows
+ * (kv_ring) and the SWA window (swa_ring), each pool with its own offsets.
+ * Workspace: dsr_decode_workspace_bytes(). */
+int dsr_decode_step_ring(const float* idx_q, const float* idx_w, int64_t idx_heads,
+                         const uint16_t* index_pool, int64_t index_rows, const int64_t* index_ring,
+                         const float* q, const uint16_t* kv_pool, int64_t kv_rows,
+                         const int64_t* kv_ring, int64_t heads, const int32_t* visible,
+                         int64_t max_visible, int64_t k, const uint16_t* swa_pool, int64_t swa_rows,
+                         const int64_t* swa_ring, const int32_t* swa_len, const float* sink,
+                         float scale, float* out, int32_t* topk_out, float* scores_out,
+                         void* workspace, size_t workspace_bytes, int32_t* err, int64_t batch,
+                         void* stream);
+
+/* dsr_append_kv_index over ring-offset pools, each with its own generations:
+ * the KV row of (seq[i], positions[i]) goes to kv_pool at its kv_ring row, the
+ * index row to index_pool at its index_ring row.  A row is written only if both
+ * rows are in bounds, neither repeats an earlier row's target in its pool,
+ * kv_generations[kv row] == kv_expected[i], index_generations[index row] ==
+ * index_expected[i] and both value rows are finite; then both generations are
+ * bumped to expected + 1.  Otherwise status 3 (bounds / repeat / stale) or 2
+ * (non-finite) and nothing of that row is written.  Replaces publish_source's
+ * two DeviceRowPool.write calls (attention_state.py:183-192); the SWA windows
+ * pool stays the caller's (DeviceRowPool.write over dsr_pool_write).
+ * sequences = the rows of each ring descriptor array. */
+int dsr_append_kv_index_ring(uint16_t* kv_pool, int64_t kv_rows, const int64_t* kv_ring,
+                             int64_t* kv_generations, const int64_t* kv_expected,
+                             uint16_t* index_pool, int64_t index_rows, const int64_t* index_ring,
+                             int64_t* index_generations, const int64_t* index_expected,
+                             int64_t sequences, const int32_t* seq, const int32_t* positions,
+                             const uint16_t* kv_values, const uint16_t* index_values, int32_t* err,
+                             int64_t n, void* stream);
+
+/* ---------------------------------------------------------------------------
  * Row-pool transactions and snapshot row streaming (DeviceRowPool,
  * cache_pool.py:156-360; StageSnapshot._gpu, snapshot_state.py:205-216;
  * snapshot_restore.py:158-165).  data bf16[slots, width] (width <= 576),

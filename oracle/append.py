@@ -102,3 +102,34 @@ def append_kv_index(kv_pool, index_pool, generations, rows, seq, positions, expe
             swa[seq[i], ring_of[i]] = kv_values[i]
         generations[row] = expected[i] + 1  # cache_pool.py:309
     return codes
+
+
+def append_kv_index_ring(kv_pool, kv_generations, kv_rows, kv_expected, index_pool, index_generations,
+                         index_rows, index_expected, kv_values, index_values):
+    """The append over two ring-offset pools with their own generations (the
+    reference's source and index-key DeviceRowPools, each written by
+    DeviceRowPool.write with its own expected generations, cache_pool.py:289-313).
+
+    kv_rows / index_rows: the target row of each new row in each pool (ring_rows;
+    -1 = out of bounds).  A row is refused (code 3) when either target is out of
+    bounds, repeats an earlier row's target in its pool, or either generation
+    differs from its expected value; a row with a non-finite element is refused
+    whole (code 2, the departure documented above).  Written rows bump both
+    generations to expected + 1.  Returns the set of codes raised."""
+    codes = set()
+    kv_rows = np.asarray(kv_rows).tolist()
+    index_rows = np.asarray(index_rows).tolist()
+    for i, (kr, ir) in enumerate(zip(kv_rows, index_rows)):
+        valid = kr >= 0 and ir >= 0 and kr not in kv_rows[:i] and ir not in index_rows[:i]
+        if (not valid or kv_generations[kr] != kv_expected[i] or
+                index_generations[ir] != index_expected[i]):
+            codes.add(ERR_SCATTER)
+            continue
+        if _nonfinite(kv_values[i]) or _nonfinite(index_values[i]):
+            codes.add(ERR_NONFINITE)
+            continue
+        kv_pool[kr] = kv_values[i]
+        index_pool[ir] = index_values[i]
+        kv_generations[kr] = kv_expected[i] + 1
+        index_generations[ir] = index_expected[i] + 1
+    return codes
