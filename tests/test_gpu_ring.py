@@ -184,14 +184,19 @@ def test_ring_append_two_pools_against_the_oracle(cuda):
 
     def append(seq, positions, kv_exp, ix_exp, kv_vals, ix_vals):
         err = status()
+        # every argument tensor stays referenced until the launch has completed
+        args = dict(kv_exp=torch.tensor(kv_exp, dtype=torch.int64, device="cuda"),
+                    ix_exp=torch.tensor(ix_exp, dtype=torch.int64, device="cuda"),
+                    seq=torch.tensor(seq, dtype=torch.int32, device="cuda"),
+                    pos=torch.tensor(positions, dtype=torch.int32, device="cuda"),
+                    kv_vals=torch.from_numpy(kv_vals.view(np.int16)).cuda(),
+                    ix_vals=torch.from_numpy(ix_vals.view(np.int16)).cuda())
         call("dsr_append_kv_index_ring", ptr(dev["kv"]), kv_rows, ptr(d_kv_ring), ptr(dev["kv_gen"]),
-             ptr(torch.tensor(kv_exp, dtype=torch.int64, device="cuda")), ptr(dev["ix"]), ix_rows, ptr(d_ix_ring),
-             ptr(dev["ix_gen"]), ptr(torch.tensor(ix_exp, dtype=torch.int64, device="cuda")), len(lengths),
-             ptr(torch.tensor(seq, dtype=torch.int32, device="cuda")),
-             ptr(torch.tensor(positions, dtype=torch.int32, device="cuda")),
-             ptr(torch.from_numpy(kv_vals.view(np.int16)).cuda()), ptr(torch.from_numpy(ix_vals.view(np.int16)).cuda()),
+             ptr(args["kv_exp"]), ptr(dev["ix"]), ix_rows, ptr(d_ix_ring), ptr(dev["ix_gen"]), ptr(args["ix_exp"]),
+             len(lengths), ptr(args["seq"]), ptr(args["pos"]), ptr(args["kv_vals"]), ptr(args["ix_vals"]),
              ptr(err), len(seq), stream_handle())
         code = finish(err)
+        del args
         codes = append_kv_index_ring(kv, kv_gen, ring_rows(kv_ring, kv_rows, seq, positions), kv_exp, ix, ix_gen,
                                      ring_rows(ix_ring, ix_rows, seq, positions), ix_exp, kv_vals, ix_vals)
         assert np.array_equal(dev["kv"].cpu().numpy().view(np.uint16), kv)
