@@ -93,6 +93,14 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
 
+// The dynamic shared memory rounded up to a 1024-byte boundary (swizzled TMA and
+// UMMA tiles), as an offset from the array itself: a pointer derived from the
+// __shared__ array by arithmetic keeps its address space, so the accesses through
+// it compile to shared-memory instructions rather than generic ones.
+__device__ __forceinline__ uint8_t* align_smem_1024(uint8_t* raw) {
+  return raw + ((1024u - (smem_u32(raw) & 1023u)) & 1023u);
+}
+
 // ---------------------------------------------------------------------------
 // mbarrier
 // ---------------------------------------------------------------------------

@@ -7,6 +7,7 @@
 // (vllm_attention.py:231-262).
 #include "common.cuh"
 #include "host_common.h"
+#include "select.cuh"
 
 namespace {
 inline int64_t round_up(int64_t x, int64_t m) { return (x + m - 1) / m * m; }
@@ -15,7 +16,7 @@ inline int64_t round_up(int64_t x, int64_t m) { return (x + m - 1) / m * m; }
 extern "C" size_t dsr_decode_workspace_bytes(int64_t batch, int64_t max_visible, int64_t heads,
                                              int64_t k) {
   const int64_t stride = round_up(max_visible > 0 ? max_visible : 1, 64);
-  return dsr::topk_workspace_bytes(batch, stride) + size_t(batch) * size_t(stride) * 4 +
+  return round_up(int64_t(dsr::select_workspace_bytes(batch, k)), 256) + size_t(batch) * size_t(stride) * 4 +
          dsr::mla_query_image_bytes(batch, heads) + dsr::mla_workspace_bytes(batch, heads, k) + 256;
 }
 
@@ -32,6 +33,7 @@ int decode_step(const float* idx_q, const float* idx_w, int64_t idx_heads, const
                 float* out, int32_t* topk_out, float* scores_out, void* workspace, size_t workspace_bytes,
                 int32_t* err, int64_t batch, void* stream) {
   DSR_REQUIRE(workspace != nullptr, "decode_step: workspace is required");
+  DSR_REQUIRE(scores_out == nullptr || aligned16(scores_out), "decode_step: scores_out must be 16-byte aligned");
   DSR_REQUIRE(max_visible > 0 && max_visible <= (int64_t(1) << 31) - 64,
               "decode_step: max_visible %lld outside [1, 2^31 - 64]", (long long)max_visible);
   const size_t need = dsr_decode_workspace_bytes(batch, max_visible, heads, k);
@@ -40,24 +42,24 @@ int decode_step(const float* idx_q, const float* idx_w, int64_t idx_heads, const
   DSR_REQUIRE((reinterpret_cast<uintptr_t>(workspace) & 255u) == 0,
               "decode_step: workspace must be 256-byte aligned");
   const int64_t stride = round_up(max_visible, 64);
-  // [top-k state (zero between calls) | scores | MLA query image | MLA partials]
-  uint8_t* topk_ws = static_cast<uint8_t*>(workspace);
-  const size_t topk_bytes = topk_workspace_bytes(batch, stride);
-  uint8_t* ws = topk_ws + topk_bytes;
-  workspace_bytes -= topk_bytes;
+  // [selection state (zero between calls) | scores | MLA query image | MLA partials]
+  uint8_t* sel_ws = static_cast<uint8_t*>(workspace);
+  const size_t sel_bytes = size_t(round_up(int64_t(select_workspace_bytes(batch, k)), 256));
+  uint8_t* ws = sel_ws + sel_bytes;
+  workspace_bytes -= sel_bytes;
   float* scores = scores_out != nullptr ? scores_out : reinterpret_cast<float*>(ws);
   uint16_t* q_img = reinterpret_cast<uint16_t*>(ws + size_t(batch) * stride * 4);
   uint8_t* mla_ws = ws + size_t(batch) * stride * 4 + mla_query_image_bytes(batch, heads);
   const size_t mla_bytes =
       workspace_bytes - size_t(batch) * stride * 4 - mla_query_image_bytes(batch, heads);
   const cudaStream_t s = as_stream(stream);
-  // the indexer also converts the MLA query into the BF16 image the MLA kernel loads
-  // and builds the per-row score histograms the top-k kernel starts from
-  int rc = launch_indexer_decode(idx_q, idx_w, index_pool, ix, visible, scores, stride, err, batch, idx_heads, s,
-                                 false, q, q_img, heads, reinterpret_cast<uint32_t*>(topk_ws));
+  SelectArgs sel;
+  int rc = select_args(&sel, sel_ws, batch, k, 0, topk_out, nullptr);
   if (rc != DSR_OK) return rc;
-  rc = launch_topk(scores, nullptr, visible, topk_out, nullptr, err, batch, stride, k, 0, topk_ws,
-                   topk_bytes, s, true, /*hist_ready=*/true);
+  // one cooperative launch: the indexer scores, converts the MLA query into the
+  // BF16 image the MLA kernel loads, and selects the exact top-k of the scores
+  rc = launch_indexer_decode(idx_q, idx_w, index_pool, ix, visible, scores, stride, err, batch, idx_heads, s,
+                             false, q, q_img, heads, nullptr, &sel);
   if (rc != DSR_OK) return rc;
   return launch_mla_decode(q, kv_pool, kv, visible, topk_out, k, swa, swa_ring, swa_rows, swa_len, sink, scale,
                            out, mla_ws, mla_bytes, err, batch, heads, s, true, q_img);
@@ -115,7 +117,8 @@ extern "C" int dsr_decode_step_ring(const float* idx_q, const float* idx_w, int6
 // decode, and the dense TiledIndexer.select of index_selection.py:79-124).
 extern "C" size_t dsr_indexer_topk_workspace_bytes(int64_t batch, int64_t max_visible) {
   const int64_t stride = round_up(max_visible > 0 ? max_visible : 1, 64);
-  return dsr::topk_workspace_bytes(batch, stride) + size_t(batch) * size_t(stride) * 4 + 256;
+  return round_up(int64_t(dsr::select_workspace_bytes(batch, 8192)), 256) + size_t(batch) * size_t(stride) * 4 +
+         256;
 }
 
 extern "C" int dsr_indexer_topk_decode(const float* idx_q, const float* idx_w, int64_t idx_heads,
@@ -128,6 +131,7 @@ extern "C" int dsr_indexer_topk_decode(const float* idx_q, const float* idx_w, i
   using namespace dsr;
   clear_error();
   DSR_REQUIRE(workspace != nullptr, "indexer_topk: workspace is required");
+  DSR_REQUIRE(scores_out == nullptr || aligned16(scores_out), "indexer_topk: scores_out must be 16-byte aligned");
   DSR_REQUIRE(max_visible > 0 && max_visible <= table_stride * 64,
               "indexer_topk: max_visible %lld outside [1, table capacity %lld]",
               (long long)max_visible, (long long)(table_stride * 64));
@@ -136,18 +140,19 @@ extern "C" int dsr_indexer_topk_decode(const float* idx_q, const float* idx_w, i
               need);
   DSR_REQUIRE((reinterpret_cast<uintptr_t>(workspace) & 255u) == 0,
               "indexer_topk: workspace must be 256-byte aligned");
+  DSR_REQUIRE(id_base >= 0 && id_base + max_visible < (int64_t(1) << 31) - 1,
+              "indexer_topk: id_base %lld + visible keys exceed int32 ids", (long long)id_base);
   const int64_t stride = round_up(max_visible, 64);
-  uint8_t* topk_ws = static_cast<uint8_t*>(workspace);
-  const size_t topk_bytes = topk_workspace_bytes(batch, stride);
-  float* scores =
-      scores_out != nullptr ? scores_out : reinterpret_cast<float*>(topk_ws + topk_bytes);
+  uint8_t* sel_ws = static_cast<uint8_t*>(workspace);
+  const size_t sel_bytes = size_t(round_up(int64_t(select_workspace_bytes(batch, 8192)), 256));
+  float* scores = scores_out != nullptr ? scores_out : reinterpret_cast<float*>(sel_ws + sel_bytes);
   const cudaStream_t s = as_stream(stream);
   PoolAddr pa;
   int rc = paged_addr(&pa, block_table, table_stride, pool_blocks, "indexer_topk");
   if (rc != DSR_OK) return rc;
-  rc = launch_indexer_decode(idx_q, idx_w, index_pool, pa, visible, scores, stride, err, batch, idx_heads, s,
-                             false, nullptr, nullptr, 0, reinterpret_cast<uint32_t*>(topk_ws));
+  SelectArgs sel;
+  rc = select_args(&sel, sel_ws, batch, k, id_base, out_ids, out_scores);
   if (rc != DSR_OK) return rc;
-  return launch_topk(scores, nullptr, visible, out_ids, out_scores, err, batch, stride, k, id_base,
-                     topk_ws, topk_bytes, s, true, /*hist_ready=*/true);
+  return launch_indexer_decode(idx_q, idx_w, index_pool, pa, visible, scores, stride, err, batch, idx_heads, s,
+                               false, nullptr, nullptr, 0, nullptr, &sel);
 }

@@ -63,11 +63,19 @@ int launch_topk(const float* scores, const int32_t* ids, const int32_t* lengths,
 size_t topk_workspace_bytes(int64_t rows, int64_t row_stride);
 // Leading bytes of that scratch (histograms, tickets, counts) that must be zero at launch.
 size_t topk_zeroed_prefix_bytes(int64_t rows, int64_t row_stride);
+struct SelectArgs;
+// The decode indexer; with `sel`, the exact top-k of its scores in the same
+// (cooperative) launch (select.cuh).
 int launch_indexer_decode(const float* q, const float* weights, const uint16_t* index_pool,
                           const PoolAddr& pa, const int32_t* visible, float* scores, int64_t score_stride,
                           int32_t* err, int64_t batch, int64_t heads, cudaStream_t stream,
                           bool pdl, const float* mla_q = nullptr, uint16_t* mla_img = nullptr,
-                          int64_t mla_heads = 0, uint32_t* hist = nullptr);
+                          int64_t mla_heads = 0, uint32_t* hist = nullptr, const SelectArgs* sel = nullptr);
+// Bytes of the fused selection's workspace (zero before first use, left zero by every completed launch).
+size_t select_workspace_bytes(int64_t batch, int64_t k);
+// Binds a SelectArgs to a workspace of select_workspace_bytes(batch, k).
+int select_args(SelectArgs* a, void* workspace, int64_t batch, int64_t k, int64_t id_base, int32_t* out_ids,
+                float* out_scores);
 int launch_indexer_prefill(const float* q, const float* weights, const uint16_t* index_pool,
                            int64_t pool_blocks, const int32_t* block_table, int64_t table_stride,
                            const int32_t* visible, float* scores, int64_t score_stride, int32_t* err,

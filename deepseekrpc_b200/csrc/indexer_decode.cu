@@ -26,6 +26,7 @@
 // query (q_lo == 0, the FP8-valued reference query) contracts the q_hi rows only.
 #include "common.cuh"
 #include "host_common.h"
+#include "select.cuh"
 
 namespace dsr {
 namespace {
@@ -92,6 +93,382 @@ __device__ __forceinline__ int find_row(const int* prefix, int batch, int t) {
   return lo;
 }
 
+// ---------------------------------------------------------------------------
+// Exact top-k after the scores (select.cuh): this CTA's rows are those whose
+// tiles intersect [t_lo, t_hi); its positions of row b are one contiguous range.
+// Every CTA of the grid calls this (it holds the grid barriers).  `work` is the
+// shared memory the indexer no longer needs (work_bytes >= list_cap * 8 + 16 KB),
+// `hist` 2048 words, `scratch` >= 128 words (scans, compaction groups, a barrier).
+// ---------------------------------------------------------------------------
+constexpr int kSelThreads = 320;  // the indexer CTA: every warp joins the selection
+constexpr int kSelPer = 4;        // entries per thread per compaction chunk
+
+__device__ __forceinline__ void select_range(const PoolAddr& pa, const int* prefix, const int* vis_s,
+                                             const int* run_s, int b, int t_lo, int t_hi, int& p_lo, int& p_hi,
+                                             bool& first) {
+  const int ta = max(t_lo, prefix[b]), tb = min(t_hi, prefix[b + 1]);
+  first = ta == prefix[b];
+  if (ta >= tb) {
+    p_lo = p_hi = 0;
+    return;
+  }
+  int pos0, valid;
+  int64_t row0;
+  tile_span(pa, b, ta - prefix[b], vis_s[b], run_s[b], pos0, row0, valid);
+  p_lo = pos0;
+  tile_span(pa, b, tb - 1 - prefix[b], vis_s[b], run_s[b], pos0, row0, valid);
+  p_hi = pos0 + valid;
+}
+
+// 2048 histogram words of global memory into shared memory, every load in flight at once
+__device__ __forceinline__ void load_hist(uint32_t* dst, const uint32_t* src) {
+  constexpr int kPerT = (kSelBins + kSelThreads - 1) / kSelThreads;
+  uint32_t hv[kPerT];
+#pragma unroll
+  for (int j = 0; j < kPerT; ++j) {
+    const int i = threadIdx.x + j * kSelThreads;
+    hv[j] = i < kSelBins ? __ldcg(src + i) : 0u;
+  }
+#pragma unroll
+  for (int j = 0; j < kPerT; ++j) {
+    const int i = threadIdx.x + j * kSelThreads;
+    if (i < kSelBins) dst[i] = hv[j];
+  }
+}
+
+// Bulk copy of `bytes` (16-byte multiple, 16-byte aligned ends) of global memory
+// into shared memory, completing on `bar`; thread 0 issues, everyone waits.
+// Returns false (status set) when the copy does not land in time.
+__device__ __forceinline__ bool bulk_fetch(void* dst, const void* src, uint32_t bytes, uint64_t* bar,
+                                           uint32_t& phase, int32_t* err) {
+  if (threadIdx.x == 0) {
+    asm volatile("fence.proxy.async.global;" ::: "memory");  // generic stores before -> async-proxy reads
+    mbar_arrive_expect_tx(bar, bytes);
+    for (uint32_t off = 0; off < bytes; off += 32768u)
+      bulk_load(smem_u32(static_cast<uint8_t*>(dst) + off), static_cast<const uint8_t*>(src) + off,
+                min(32768u, bytes - off), bar);
+  }
+  volatile int no_abort = 0;
+  const bool landed = mbar_wait(bar, phase & 1u, &no_abort, err);
+  ++phase;
+  if (!__syncthreads_and(landed)) {
+    if (threadIdx.x == 0) mbar_drain(bar, (phase - 1) & 1u);
+    return false;
+  }
+  return true;
+}
+
+__device__ void select_phase(const SelectArgs& a, const float* __restrict__ scores, int64_t score_stride,
+                             int batch, const int* prefix, const int* vis_s, const int* run_s, const PoolAddr& pa,
+                             int t_lo, int t_hi, uint8_t* work, size_t work_bytes, uint32_t* hist,
+                             uint32_t* scratch, int32_t* err, bool live) {
+  constexpr int T = kSelThreads;
+  const int tid = threadIdx.x;
+  const int k = a.k;
+  uint32_t* grp = scratch + 64;
+  uint32_t* ncand = scratch + 42;
+  uint64_t* lbar = reinterpret_cast<uint64_t*>(scratch + 44);  // the bulk copies' barrier
+  uint32_t lphase = 0;
+  const int rb0 = t_lo < t_hi ? find_row(prefix, batch, t_lo) : 0;
+  const int rb1 = t_lo < t_hi ? find_row(prefix, batch, t_hi - 1) : -1;
+  if (tid == 0) {
+    mbar_init(lbar, 1);
+    fence_barrier_init();
+  }
+  // the scores this CTA stored through the generic proxy are read back by bulk copies
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+  live = grid_barrier(a.ctl, 1, err) && live;  // every row's digit-0 histogram is complete
+
+  // rows without keys: all padding (one CTA writes them)
+  if (live && blockIdx.x == 0)
+    for (int b = 0; b < batch; ++b)
+      if (vis_s[b] == 0)
+#pragma unroll 1
+        for (int i = tid; i < k; i += T) {
+          a.out_ids[int64_t(b) * k + i] = -1;
+          if (a.out_scores != nullptr) a.out_scores[int64_t(b) * k + i] = -CUDART_INF_F;
+        }
+
+  // ---- per row: threshold bin, this CTA's candidates appended to the row's list
+  // (unordered: position order is restored for the few selected ones after
+  // barrier 2), and the digit-1 counts of its threshold-bin entries
+  uint64_t* buf = reinterpret_cast<uint64_t*>(work);
+  for (int b = rb0; b <= rb1 && live; ++b) {
+    int p_lo, p_hi;
+    bool first;
+    select_range(pa, prefix, vis_s, run_s, b, t_lo, t_hi, p_lo, p_hi, first);
+    if (p_lo >= p_hi) continue;
+    const int v = vis_s[b];
+    const float* srow = scores + int64_t(b) * score_stride;
+    int32_t* orow = a.out_ids + int64_t(b) * k;
+    float* oscore = a.out_scores != nullptr ? a.out_scores + int64_t(b) * k : nullptr;
+    if (v <= k) {  // every key is selected: output slot = position
+#pragma unroll 1
+      for (int p = p_lo + tid; p < p_hi; p += T) {
+        orow[p] = int32_t(a.id_base + p);
+        if (oscore != nullptr) oscore[p] = key_score(sel_rank_u(__float_as_uint(__ldcg(srow + p))));
+      }
+      if (first)
+#pragma unroll 1
+        for (int p = v + tid; p < k; p += T) {
+          orow[p] = -1;
+          if (oscore != nullptr) oscore[p] = -CUDART_INF_F;
+        }
+      continue;
+    }
+    load_hist(hist, a.hist + int64_t(b) * kSelBins);
+    if (tid == 0) *ncand = 0u;
+    __syncthreads();
+    uint32_t above;
+    const uint32_t b0 = sel_find_bin<T>(hist, kSelBins, uint32_t(k), above, scratch);
+    const uint32_t in_bin = hist[b0];
+    uint4* meta = a.meta + int64_t(b) * gridDim.x + blockIdx.x;
+    if (in_bin > uint32_t(a.list_cap - k)) {  // massive ties: the row's first CTA takes it after barrier 2
+      if (tid == 0) *meta = make_uint4(0u, 0xffffffffu, b0, above);
+      __syncthreads();
+      continue;
+    }
+    // candidates (digit 0 >= b0): the range's scores come into shared memory by bulk
+    // copies (aligned groups of four covering [p_lo, p_hi); the scores outside the
+    // range, at most three each side and inside the row's stride, are masked),
+    // chunk by chunk behind the candidate buffer, and are scanned there.
+    // digit 0 >= b0 <=> score >= the lowest score of bin b0 (the key map is monotone;
+    // NaN ranks above +inf); bins 0-3 decode to NaN patterns and hold nothing above
+    // -inf, so with b0 < 4 every score passes; keys are built for the few that do
+    const int a0 = p_lo & ~3;
+    const int a1 = (p_hi + 3) & ~3;
+    const float thr = b0 < 4u ? -CUDART_INF_F : key_score(b0 << 21);
+    uint32_t* h1row = a.hist1 + int64_t(b) * kSelBins;
+    float* chunk = reinterpret_cast<float*>(work + size_t(a.list_cap) * 8);
+    const int chunk_len = int((work_bytes - size_t(a.list_cap) * 8) / 4) & ~4095;
+    for (int c0 = a0; c0 < a1 && live; c0 += chunk_len) {
+      const int c1 = min(a1, c0 + chunk_len);
+      if (!bulk_fetch(chunk, srow + c0, uint32_t(c1 - c0) * 4u, lbar, lphase, err)) {
+        live = false;
+        break;
+      }
+#pragma unroll 1
+      for (int i = tid * 4; i < c1 - c0; i += T * 4) {
+        const float4 x4 = *reinterpret_cast<const float4*>(chunk + i);
+        const float xs[4] = {x4.x, x4.y, x4.z, x4.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int p = c0 + i + e;
+          if (!(xs[e] >= thr || xs[e] != xs[e]) || p < p_lo || p >= p_hi) continue;
+          const uint32_t u = sel_rank_u(__float_as_uint(xs[e]));
+          if ((u >> 21) < b0) continue;
+          buf[atomicAdd(ncand, 1u)] = sel_key(u, a.id_base + p);
+          if ((u >> 21) == b0) atomicAdd(h1row + ((u >> 10) & (kSelBins - 1)), 1u);  // digit 1: key bits 41..51
+        }
+      }
+      __syncthreads();  // the chunk is read before the next copy lands on it
+    }
+    const uint32_t n = *ncand;
+    if (tid == 0) scratch[40] = n ? atomicAdd(a.list_len + b, n) : 0u;
+    __syncthreads();
+    const uint32_t base = scratch[40];
+    uint64_t* lrow = a.list + int64_t(b) * a.list_cap + base;
+#pragma unroll 1
+    for (uint32_t i = tid; i < n; i += T) lrow[i] = buf[i];
+    if (tid == 0) *meta = make_uint4(base, n, b0, above);
+    __syncthreads();
+  }
+
+  live = grid_barrier(a.ctl, 2, err) && live;  // every row's candidate list is complete
+
+  // ---- per row: K* from the digit-1 histogram and the list, this CTA's offset, its ids
+  uint64_t* lst = reinterpret_cast<uint64_t*>(work);
+  uint64_t* mine = reinterpret_cast<uint64_t*>(hist);  // this CTA's selected keys (up to 1024)
+  for (int b = rb0; b <= rb1 && live; ++b) {
+    int p_lo, p_hi;
+    bool first;
+    select_range(pa, prefix, vis_s, run_s, b, t_lo, t_hi, p_lo, p_hi, first);
+    if (p_lo >= p_hi) continue;
+    const int v = vis_s[b];
+    if (v <= k) continue;
+    const float* srow = scores + int64_t(b) * score_stride;
+    int32_t* orow = a.out_ids + int64_t(b) * k;
+    float* oscore = a.out_scores != nullptr ? a.out_scores + int64_t(b) * k : nullptr;
+    const uint4 m = a.meta[int64_t(b) * gridDim.x + blockIdx.x];
+    const uint32_t b0 = m.z, need0 = uint32_t(k) - m.w;
+    auto put = [&](uint32_t slot, uint64_t key) {
+      if (slot >= uint32_t(k)) return;  // only after a CTA gave up (its list block is missing)
+      orow[slot] = sel_key_id(key);
+      if (oscore != nullptr) oscore[slot] = sel_key_score(key);
+    };
+    if (m.y == 0xffffffffu) {
+      // massive ties: the first CTA resolves K* over the whole row and writes it
+      if (first) {
+        const int64_t id0 = a.id_base;
+        auto row_key = [&](int64_t i) -> uint64_t {
+          return sel_key(sel_rank_u(__float_as_uint(__ldcg(srow + i))), id0 + i);
+        };
+        const uint64_t kstar = sel_kstar<T>(row_key, v, uint64_t(b0) << kSelShift[0], need0, 1, hist, scratch);
+        uint32_t written = 0;
+#pragma unroll 1
+        for (int c0 = 0; c0 < v && written < uint32_t(k); c0 += T * kSelPer) {
+          uint32_t keep = 0;
+          uint64_t keys[kSelPer];
+#pragma unroll
+          for (int j = 0; j < kSelPer; ++j) {
+            const int i = c0 + j * T + tid;
+            keys[j] = i < v ? row_key(i) : 0ull;
+            keep |= uint32_t(i < v && keys[j] >= kstar) << j;
+          }
+          written += sel_compact<T, kSelPer>(keep, written, grp, scratch, [&](uint32_t slot, int j) { put(slot, keys[j]); });
+        }
+      }
+      continue;
+    }
+    // the row's candidate list into shared memory by one bulk copy (16-byte units;
+    // the capacity is even, so the rounded-up copy stays inside the row's list),
+    // after the digit-1 histogram of its threshold bin is read and searched
+    if (tid == 0) scratch[40] = __ldcg(a.list_len + b);
+    load_hist(hist, a.hist1 + int64_t(b) * kSelBins);
+    __syncthreads();
+    const uint32_t L = scratch[40];
+    uint32_t above1;
+    const uint32_t b1 = sel_find_bin<T>(hist, kSelBins, need0, above1, scratch);
+    const uint32_t need1 = need0 - above1, in_sub = hist[b1];
+    if (!bulk_fetch(lst, a.list + int64_t(b) * a.list_cap, ((L + 1u) & ~1u) * 8u, lbar, lphase, err)) break;
+    // K*: with the whole sub-bin (b0, b1) selected, the rule is key >= its lower
+    // edge; otherwise the need1-th largest of the sub-bin's few keys
+    const uint64_t sub = (uint64_t(b0) << kSelShift[0]) | (uint64_t(b1) << kSelShift[1]);
+    uint64_t kstar = sub;
+    if (in_sub != need1) {
+      if (in_sub <= 1024u) {
+        uint64_t* subk = reinterpret_cast<uint64_t*>(hist);
+        if (tid == 0) *ncand = 0u;
+        __syncthreads();
+#pragma unroll 1
+        for (uint32_t i = tid; i < L; i += T) {
+          const uint64_t key = lst[i];
+          if ((key >> kSelShift[1]) == (sub >> kSelShift[1])) subk[atomicAdd(ncand, 1u)] = key;
+        }
+        __syncthreads();
+        const uint32_t c = *ncand;
+#pragma unroll 1
+        for (uint32_t i = tid; i < c; i += T) {
+          const uint64_t key = subk[i];
+          uint32_t above = 0;
+#pragma unroll 1
+          for (uint32_t j = 0; j < c; ++j) above += subk[j] > key ? 1u : 0u;
+          if (above == need1 - 1) {
+            scratch[46] = uint32_t(key);
+            scratch[47] = uint32_t(key >> 32);
+          }
+        }
+        __syncthreads();
+        kstar = (uint64_t(scratch[47]) << 32) | scratch[46];
+      } else {
+        kstar = sel_kstar<T>([&](int64_t i) { return lst[i]; }, L, sub, need1, 2, hist, scratch);
+      }
+    }
+    __syncthreads();
+    // one pass: selected candidates of lower positions (this CTA's output offset),
+    // and this CTA's own selected keys (its positions [p_lo, p_hi))
+    const int32_t id_lo = int32_t(a.id_base + p_lo), id_hi = int32_t(a.id_base + p_hi);
+    if (tid == 0) *ncand = 0u;
+    __syncthreads();
+    uint32_t lower = 0;
+#pragma unroll 1
+    for (uint32_t i = tid; i < L; i += T) {
+      const uint64_t key = lst[i];
+      if (key < kstar) continue;
+      const int32_t id = sel_key_id(key);
+      lower += id < id_lo ? 1u : 0u;
+      if (id >= id_lo && id < id_hi) {
+        const uint32_t slot = atomicAdd(ncand, 1u);
+        if (slot < 1024u) mine[slot] = key;
+      }
+    }
+    uint32_t offset;
+    sel_excl_scan<T>(lower, offset, scratch);  // offset = the block's sum (synchronises)
+    const uint32_t s_mine = *ncand;
+    if (s_mine <= 1024u) {
+      // position order among this CTA's selected keys: rank by id
+#pragma unroll 1
+      for (uint32_t i = tid; i < s_mine; i += T) {
+        const uint64_t key = mine[i];
+        const int32_t id = sel_key_id(key);
+        uint32_t rank = 0;
+#pragma unroll 1
+        for (uint32_t j = 0; j < s_mine; ++j) rank += sel_key_id(mine[j]) < id ? 1u : 0u;
+        put(offset + rank, key);
+      }
+    } else {
+      // more than 1024 of the row's selected keys in this CTA: rank over the list
+#pragma unroll 1
+      for (uint32_t i = tid; i < L; i += T) {
+        const uint64_t key = lst[i];
+        const int32_t id = sel_key_id(key);
+        if (key < kstar || id < id_lo || id >= id_hi) continue;
+        uint32_t rank = 0;
+#pragma unroll 1
+        for (uint32_t j = 0; j < L; ++j) {
+          const uint64_t other = lst[j];
+          const int32_t oid = sel_key_id(other);
+          rank += (other >= kstar && oid >= id_lo && oid < id) ? 1u : 0u;
+        }
+        put(offset + rank, key);
+      }
+    }
+    __syncthreads();
+  }
+
+  // ---- leave the workspace as found.  Every CTA that scored part of a row counts
+  // itself done with the row (after its last read of the row's histograms and list);
+  // the row's last CTA clears them; the last CTA to leave resets the barrier counters
+  const int total = prefix[batch];
+  auto t_start = [&](int c) { return int((int64_t(total) * c) / gridDim.x); };
+  auto owner = [&](int t) {  // the CTA whose tiles [t_start(c), t_start(c + 1)) hold tile t
+    int lo = 0, hi = int(gridDim.x) - 1;
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (t_start(mid) <= t) lo = mid;
+      else hi = mid - 1;
+    }
+    return lo;
+  };
+  uint32_t* row_done = a.list_len + batch;
+  for (int b = rb0; b <= rb1; ++b) {
+    const int ta = max(t_lo, prefix[b]), tb = min(t_hi, prefix[b + 1]);
+    if (ta >= tb) continue;
+    // CTAs with tiles of this row (a CTA with no tiles at all touches no row)
+    const int c0 = owner(prefix[b]), c1 = owner(prefix[b + 1] - 1);
+    uint32_t mine_n = 0;
+    for (int c = c0 + tid; c <= c1; c += T) mine_n += t_start(c) < t_start(c + 1) ? 1u : 0u;
+    uint32_t nctas;
+    sel_excl_scan<T>(mine_n, nctas, scratch);
+    if (tid == 0) {
+      __threadfence();
+      scratch[43] = atomicAdd(row_done + b, 1u) == nctas - 1 ? 1u : 0u;
+    }
+    __syncthreads();
+    if (scratch[43]) {
+      __threadfence();
+#pragma unroll 1
+      for (int i = tid; i < kSelBins; i += T) {
+        a.hist[int64_t(b) * kSelBins + i] = 0u;
+        a.hist1[int64_t(b) * kSelBins + i] = 0u;
+      }
+      if (tid == 0) {
+        a.list_len[b] = 0u;
+        row_done[b] = 0u;
+      }
+    }
+    __syncthreads();
+  }
+  if (tid == 0) {
+    __threadfence();
+    const uint32_t done = atomicAdd(a.ctl + 1, 1u);
+    if (done == gridDim.x - 1) {  // every other CTA has passed both barriers
+      a.ctl[0] = 0u;
+      a.ctl[1] = 0u;
+    }
+  }
+}
+
 // 32 lanes x 8 consecutive 32-bit TMEM columns
 __device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t* r) {
   asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
@@ -151,13 +528,13 @@ __global__ void __launch_bounds__(kIxThreads, 1)
                           const float* __restrict__ weights, const PoolAddr pa,
                           const int32_t* __restrict__ visible, float* __restrict__ scores, int64_t score_stride,
                           int32_t* err, int batch, const float* __restrict__ mla_q,
-                          uint16_t* __restrict__ mla_img, int mla_heads, uint32_t* __restrict__ hist) {
+                          uint16_t* __restrict__ mla_img, int mla_heads, uint32_t* __restrict__ hist,
+                          const SelectArgs sel) {
   using L = IxLayout<H>;
   constexpr int N = L::N;
   constexpr int HH = H / 2;  // heads per epilogue warpgroup
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                             ~uintptr_t(1023));
+  uint8_t* smem = align_smem_1024(smem_raw);
   const uint32_t sbase = smem_u32(smem);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBarOff);
   uint64_t* full = bars;
@@ -477,13 +854,20 @@ __global__ void __launch_bounds__(kIxThreads, 1)
     tc_fence_after();
     tmem_dealloc(tmem_base, L::kTmemCols);
   }
+  // exact top-k of the scores (cooperative launches only: the phase holds grid barriers)
+  if (sel.out_ids != nullptr) {
+    const bool live = *abort == 0;
+    __syncthreads();
+    select_phase(sel, scores, score_stride, batch, prefix, vis_s, run_s, pa, t_lo, t_hi, smem + L::kStagesOff,
+                 size_t(L::kWOff - L::kStagesOff), hsm, reinterpret_cast<uint32_t*>(xch), err, live);
+  }
 }
 
 template <int H>
 int launch_ix(const CUtensorMap& map, const float* q, const float* weights, const PoolAddr& pa,
               const int32_t* visible, float* scores, int64_t score_stride, int32_t* err, int batch,
               const float* mla_q, uint16_t* mla_img, int mla_heads, uint32_t* hist,
-              cudaStream_t stream, bool pdl) {
+              cudaStream_t stream, bool pdl, const SelectArgs& sel) {
   using L = IxLayout<H>;
   {
     const int rc = set_max_smem(indexer_decode_kernel<H>, L::kAlloc, "indexer decode");
@@ -495,13 +879,19 @@ int launch_ix(const CUtensorMap& map, const float* q, const float* weights, cons
   cfg.dynamicSmemBytes = L::kAlloc;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  if (sel.out_ids != nullptr) {
+    // the selection's grid barriers need every CTA resident at once
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+  } else {
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+  }
   cfg.attrs = attr;
-  cfg.numAttrs = pdl ? 1 : 0;
+  cfg.numAttrs = (pdl || sel.out_ids != nullptr) ? 1 : 0;
   const cudaError_t e =
       cudaLaunchKernelEx(&cfg, indexer_decode_kernel<H>, map, q, weights, pa, visible, scores, score_stride,
-                         err, batch, mla_q, mla_img, mla_heads, hist);
+                         err, batch, mla_q, mla_img, mla_heads, sel.out_ids != nullptr ? sel.hist : hist, sel);
   if (e != cudaSuccess) return fail(DSR_ECUDA, "indexer launch: %s", cudaGetErrorString(e));
   return DSR_OK;
 }
@@ -512,7 +902,9 @@ int launch_indexer_decode(const float* q, const float* weights, const uint16_t* 
                           const PoolAddr& pa, const int32_t* visible, float* scores, int64_t score_stride,
                           int32_t* err, int64_t batch, int64_t heads, cudaStream_t stream,
                           bool pdl, const float* mla_q, uint16_t* mla_img, int64_t mla_heads,
-                          uint32_t* hist) {
+                          uint32_t* hist, const SelectArgs* sel) {
+  const SelectArgs none{};
+  const SelectArgs& sa = sel != nullptr ? *sel : none;
   DSR_REQUIRE(mla_q == nullptr || (mla_img != nullptr && aligned16(mla_q) && aligned16(mla_img) &&
                                    (mla_heads == 16 || mla_heads == 32 || mla_heads == 64 ||
                                     mla_heads == 128)),
@@ -531,14 +923,37 @@ int launch_indexer_decode(const float* q, const float* weights, const uint16_t* 
   switch (heads) {
     case 16:
       return launch_ix<16>(map, q, weights, pa, visible, scores, score_stride, err, int(batch), mla_q, mla_img,
-                           int(mla_heads), hist, stream, pdl);
+                           int(mla_heads), hist, stream, pdl, sa);
     case 32:
       return launch_ix<32>(map, q, weights, pa, visible, scores, score_stride, err, int(batch), mla_q, mla_img,
-                           int(mla_heads), hist, stream, pdl);
+                           int(mla_heads), hist, stream, pdl, sa);
     default:
       return launch_ix<64>(map, q, weights, pa, visible, scores, score_stride, err, int(batch), mla_q, mla_img,
-                           int(mla_heads), hist, stream, pdl);
+                           int(mla_heads), hist, stream, pdl, sa);
   }
+}
+
+size_t select_workspace_bytes(int64_t batch, int64_t k) { return SelectLayout(batch, k, sm_count()).total; }
+
+int select_args(SelectArgs* a, void* workspace, int64_t batch, int64_t k, int64_t id_base, int32_t* out_ids,
+                float* out_scores) {
+  DSR_REQUIRE(workspace != nullptr && out_ids != nullptr, "select: null workspace or output");
+  DSR_REQUIRE((reinterpret_cast<uintptr_t>(workspace) & 255u) == 0, "select: workspace must be 256-byte aligned");
+  DSR_REQUIRE(k > 0 && k <= 8192, "select: k %lld outside [1, 8192]", (long long)k);
+  const SelectLayout L(batch, k, sm_count());
+  uint8_t* base = static_cast<uint8_t*>(workspace);
+  a->out_ids = out_ids;
+  a->out_scores = out_scores;
+  a->k = int(k);
+  a->id_base = id_base;
+  a->hist = reinterpret_cast<uint32_t*>(base + L.hist);
+  a->hist1 = reinterpret_cast<uint32_t*>(base + L.hist1);
+  a->ctl = reinterpret_cast<uint32_t*>(base + L.ctl);
+  a->list_len = reinterpret_cast<uint32_t*>(base + L.len);
+  a->list = reinterpret_cast<uint64_t*>(base + L.list);
+  a->list_cap = int(L.cap);
+  a->meta = reinterpret_cast<uint4*>(base + L.meta);
+  return DSR_OK;
 }
 
 }  // namespace dsr

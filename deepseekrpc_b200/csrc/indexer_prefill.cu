@@ -71,8 +71,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   constexpr int QB = L::QB;
   constexpr int QH = QB / 2;  // queries per epilogue warpgroup
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                             ~uintptr_t(1023));
+  uint8_t* smem = align_smem_1024(smem_raw);
   const uint32_t sbase = smem_u32(smem);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBarOff);
   uint64_t* full = bars;

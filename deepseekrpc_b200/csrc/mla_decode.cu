@@ -241,8 +241,7 @@ __global__ void __launch_bounds__(kMlaThreads, 1)
                       const uint16_t* __restrict__ q_img, int64_t id_base, int foreign_ok) {
   using L = MlaLayout<HG>;
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                             ~uintptr_t(1023));
+  uint8_t* smem = align_smem_1024(smem_raw);
   const uint32_t sbase = smem_u32(smem);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBarOff);
   uint64_t* bar_s = bars + 0;   // S^T complete (commit)
@@ -437,8 +436,7 @@ __global__ void __launch_bounds__(kMlaThreads, 1)
                           const uint16_t* __restrict__ q_img, int64_t id_base, int foreign_ok) {
   using L = MlaLayout<HG>;
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                             ~uintptr_t(1023));
+  uint8_t* smem = align_smem_1024(smem_raw);
   const uint32_t sbase = smem_u32(smem);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBarOff);
   uint64_t* bar_s = bars + 0;

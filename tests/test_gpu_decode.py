@@ -15,6 +15,7 @@ import torch
 import oracle
 from _helpers import (assert_bf16_close, assert_scores, c_decode_step, c_indexer, c_mla, host,
                       oracle_attention, oracle_scores, score_bound)
+from deepseekrpc_b200 import _native
 from deepseekrpc_b200.workloads import CONFIGS, make_decode_inputs, small_config
 
 pytestmark = pytest.mark.gpu
@@ -141,3 +142,59 @@ def test_decode_step_multiwave_batch(cuda):
     # walks several (tile, sequence) items per CTA with the next item's loads in flight
     cfg = small_config("cfg3", batch=12, seed=37)
     run_step_and_check(cfg, lengths=[300, 2047, 2048, 2049, 4000, 5100, 6000, 6500, 7000, 8191, 8192, 9000])
+
+
+def test_decode_step_ties_empty_rows_and_short_rows(cuda):
+    """The fused selection's paths in one batch: a row whose keys repeat 16 patterns
+    (heavy ties, threshold bin within the parallel path), a row of 200,000 keys with
+    one repeated pattern (every score equal: the threshold bin overflows and the
+    row's first CTA resolves it alone; the lowest ids win), a row shorter than k
+    (every key taken), an empty row (all padding) and an ordinary row."""
+    cfg = small_config("cfg3", batch=5, seed=38)
+    lengths = [9000, 200000, 1500, 0, 30000]
+    inp, _ = make_decode_inputs(cfg, lengths=[max(n, 1) for n in lengths])
+    inp["visible"] = torch.tensor(lengths, dtype=torch.int32, device="cuda")
+    inp["swa_len"] = torch.clamp(inp["visible"], max=128).to(torch.int32)
+    table = inp["block_table"]
+    pool = inp["index_pool"]
+    for b, patterns in ((0, 16), (1, 1)):
+        n = lengths[b]
+        pos = torch.arange(n, device="cuda")
+        rows = table[b].long()[pos // 64] * 64 + pos % 64
+        pool[rows] = pool[rows[pos % patterns]]
+    out, topk, scores, code = c_decode_step(inp, cfg.topk, cfg.scale)
+    assert code == 0
+    h = host(inp)
+    s, t, o = scores.cpu().numpy(), topk.cpu().numpy(), out.cpu().numpy()
+    for b, n in enumerate(lengths):
+        assert np.array_equal(t[b], oracle.tiled_topk(s[b, :n], cfg.topk)), f"row {b}: top-k differs"
+        assert_bf16_close(o[b], oracle_attention(h, b, t[b], cfg.scale))
+    assert np.array_equal(t[1], np.arange(cfg.topk)), "equal scores select the lowest ids"
+    assert np.array_equal(t[2][:1500], np.arange(1500)) and np.all(t[2][1500:] == -1)
+    assert np.all(t[3] == -1)
+
+
+def test_decode_step_repeated_calls_reuse_the_workspace(cuda):
+    """The fused selection leaves its workspace zeroed: the same workspace serves
+    three calls in a row (different batches and lengths) with the same results as
+    fresh workspaces."""
+    cfg = small_config("cfg3", batch=3, seed=39)
+    inp, lengths = make_decode_inputs(cfg, lengths=[40000, 2500, 70000])
+    b, h, k = 3, cfg.heads, cfg.topk
+    lib = _native.library()
+    ws_bytes = lib.dsr_decode_workspace_bytes(b, max(lengths), h, k)
+    ws = torch.zeros(ws_bytes, dtype=torch.uint8, device="cuda")
+    from _helpers import status, finish
+    from deepseekrpc_b200._native import call, ptr, stream_handle
+    ref_out, ref_topk, _, code = c_decode_step(inp, k, cfg.scale)
+    assert code == 0
+    for _ in range(3):
+        out = torch.empty((b, h, 512), device="cuda")
+        topk = torch.empty((b, k), dtype=torch.int32, device="cuda")
+        err = status()
+        call("dsr_decode_step", ptr(inp["idx_q"]), ptr(inp["idx_w"]), inp["idx_q"].shape[1], ptr(inp["index_pool"]),
+             ptr(inp["q"]), ptr(inp["kv_pool"]), h, inp["kv_pool"].shape[0] // 64, ptr(inp["block_table"]),
+             inp["block_table"].shape[1], ptr(inp["visible"]), max(lengths), k, ptr(inp["swa"]), ptr(inp["swa_len"]),
+             ptr(inp["sink"]), cfg.scale, ptr(out), ptr(topk), None, ptr(ws), ws_bytes, ptr(err), b, stream_handle())
+        assert finish(err) == 0
+        assert torch.equal(topk, ref_topk) and torch.equal(out, ref_out)
