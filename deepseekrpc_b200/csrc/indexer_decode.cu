@@ -248,18 +248,38 @@ __device__ void select_phase(const SelectArgs& a, const float* __restrict__ scor
         break;
       }
 #pragma unroll 1
-      for (int i = tid * 4; i < c1 - c0; i += T * 4) {
-        const float4 x4 = *reinterpret_cast<const float4*>(chunk + i);
+      for (int i0 = 0; i0 < c1 - c0; i0 += T * 4) {  // uniform trip count: the warp appends together
+        const int i = i0 + tid * 4;
+        float4 x4 = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (i < c1 - c0) x4 = *reinterpret_cast<const float4*>(chunk + i);
         const float xs[4] = {x4.x, x4.y, x4.z, x4.w};
+        uint64_t kk[4];
+        uint32_t take = 0;
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           const int p = c0 + i + e;
-          if (!(xs[e] >= thr || xs[e] != xs[e]) || p < p_lo || p >= p_hi) continue;
+          kk[e] = 0ull;
+          if (i >= c1 - c0 || !(xs[e] >= thr || xs[e] != xs[e]) || p < p_lo || p >= p_hi) continue;
           const uint32_t u = sel_rank_u(__float_as_uint(xs[e]));
           if ((u >> 21) < b0) continue;
-          buf[atomicAdd(ncand, 1u)] = sel_key(u, a.id_base + p);
+          kk[e] = sel_key(u, a.id_base + p);
+          take |= 1u << e;
           if ((u >> 21) == b0) atomicAdd(h1row + ((u >> 10) & (kSelBins - 1)), 1u);  // digit 1: key bits 41..51
         }
+        // one shared-memory atomic per warp: lane offsets by a warp scan
+        const uint32_t cnt = __popc(take);
+        uint32_t incl = cnt;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const uint32_t x = __shfl_up_sync(0xffffffffu, incl, o);
+          if ((tid & 31) >= o) incl += x;
+        }
+        uint32_t wbase = 0;
+        if ((tid & 31) == 31 && incl != 0u) wbase = atomicAdd(ncand, incl);
+        uint32_t at = __shfl_sync(0xffffffffu, wbase, 31) + incl - cnt;
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          if ((take >> e) & 1u) buf[at++] = kk[e];
       }
       __syncthreads();  // the chunk is read before the next copy lands on it
     }
@@ -278,7 +298,6 @@ __device__ void select_phase(const SelectArgs& a, const float* __restrict__ scor
 
   // ---- per row: K* from the digit-1 histogram and the list, this CTA's offset, its ids
   uint64_t* lst = reinterpret_cast<uint64_t*>(work);
-  uint64_t* mine = reinterpret_cast<uint64_t*>(hist);  // this CTA's selected keys (up to 1024)
   for (int b = rb0; b <= rb1 && live; ++b) {
     int p_lo, p_hi;
     bool first;
@@ -336,7 +355,7 @@ __device__ void select_phase(const SelectArgs& a, const float* __restrict__ scor
     const uint64_t sub = (uint64_t(b0) << kSelShift[0]) | (uint64_t(b1) << kSelShift[1]);
     uint64_t kstar = sub;
     if (in_sub != need1) {
-      if (in_sub <= 1024u) {
+      if (in_sub <= 256u) {  // pairwise rank among the few keys of the sub-bin
         uint64_t* subk = reinterpret_cast<uint64_t*>(hist);
         if (tid == 0) *ncand = 0u;
         __syncthreads();
@@ -365,55 +384,60 @@ __device__ void select_phase(const SelectArgs& a, const float* __restrict__ scor
       }
     }
     __syncthreads();
-    // one pass: selected candidates of lower positions (this CTA's output offset),
-    // and this CTA's own selected keys (its positions [p_lo, p_hi))
-    const int32_t id_lo = int32_t(a.id_base + p_lo), id_hi = int32_t(a.id_base + p_hi);
-    if (tid == 0) *ncand = 0u;
-    __syncthreads();
-    uint32_t lower = 0;
+    // this CTA's selected keys in position order: a bitmap of its positions
+    // [p_lo, p_hi), 65536 at a time; the first pass over the list also counts the
+    // selected candidates of lower positions (this CTA's output offset).  One
+    // prefix popcount gives every set bit its slot; the score is read back from
+    // the row (the key's score is the row's score at that position).
+    uint32_t* bits = hist;
+    const int32_t id_lo = int32_t(a.id_base + p_lo);
+    uint32_t slot = 0;
 #pragma unroll 1
-    for (uint32_t i = tid; i < L; i += T) {
-      const uint64_t key = lst[i];
-      if (key < kstar) continue;
-      const int32_t id = sel_key_id(key);
-      lower += id < id_lo ? 1u : 0u;
-      if (id >= id_lo && id < id_hi) {
-        const uint32_t slot = atomicAdd(ncand, 1u);
-        if (slot < 1024u) mine[slot] = key;
-      }
-    }
-    uint32_t offset;
-    sel_excl_scan<T>(lower, offset, scratch);  // offset = the block's sum (synchronises)
-    const uint32_t s_mine = *ncand;
-    if (s_mine <= 1024u) {
-      // position order among this CTA's selected keys: rank by id
+    for (int w0 = p_lo; w0 < p_hi; w0 += kSelBins * 32) {
+      const int w1 = min(p_hi, w0 + kSelBins * 32);
+      const int nw = (w1 - w0 + 31) >> 5;
 #pragma unroll 1
-      for (uint32_t i = tid; i < s_mine; i += T) {
-        const uint64_t key = mine[i];
-        const int32_t id = sel_key_id(key);
-        uint32_t rank = 0;
-#pragma unroll 1
-        for (uint32_t j = 0; j < s_mine; ++j) rank += sel_key_id(mine[j]) < id ? 1u : 0u;
-        put(offset + rank, key);
-      }
-    } else {
-      // more than 1024 of the row's selected keys in this CTA: rank over the list
+      for (int i = tid; i < nw; i += T) bits[i] = 0u;
+      __syncthreads();
+      const int32_t i0 = int32_t(a.id_base + w0), i1 = int32_t(a.id_base + w1);
+      uint32_t lower = 0;
 #pragma unroll 1
       for (uint32_t i = tid; i < L; i += T) {
         const uint64_t key = lst[i];
+        if (key < kstar) continue;
         const int32_t id = sel_key_id(key);
-        if (key < kstar || id < id_lo || id >= id_hi) continue;
-        uint32_t rank = 0;
-#pragma unroll 1
-        for (uint32_t j = 0; j < L; ++j) {
-          const uint64_t other = lst[j];
-          const int32_t oid = sel_key_id(other);
-          rank += (other >= kstar && oid >= id_lo && oid < id) ? 1u : 0u;
-        }
-        put(offset + rank, key);
+        lower += id < id_lo ? 1u : 0u;
+        if (id >= i0 && id < i1) atomicOr(bits + ((id - i0) >> 5), 1u << ((id - i0) & 31));
       }
+      if (w0 == p_lo) sel_excl_scan<T>(lower, slot, scratch);  // slot = the block's sum (synchronises)
+      else __syncthreads();
+      const int per = (nw + T - 1) / T;  // consecutive words per thread
+      uint32_t cnt = 0;
+#pragma unroll 1
+      for (int j = 0; j < per; ++j) {
+        const int wi = tid * per + j;
+        cnt += wi < nw ? __popc(bits[wi]) : 0u;
+      }
+      uint32_t found;
+      uint32_t s = slot + sel_excl_scan<T>(cnt, found, scratch);
+#pragma unroll 1
+      for (int j = 0; j < per; ++j) {
+        const int wi = tid * per + j;
+        if (wi >= nw) break;
+        uint32_t m = bits[wi];
+        while (m != 0u) {
+          const int p = w0 + wi * 32 + (__ffs(m) - 1);
+          m &= m - 1u;
+          if (s < uint32_t(k)) {  // only after a CTA gave up (its list block is missing)
+            orow[s] = int32_t(a.id_base + p);
+            if (oscore != nullptr) oscore[s] = key_score(sel_rank_u(__float_as_uint(__ldcg(srow + p))));
+          }
+          ++s;
+        }
+      }
+      slot += found;
+      __syncthreads();
     }
-    __syncthreads();
   }
 
   // ---- leave the workspace as found.  Every CTA that scored part of a row counts
