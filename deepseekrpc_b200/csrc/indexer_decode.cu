@@ -96,12 +96,15 @@ __device__ __forceinline__ int find_row(const int* prefix, int batch, int t) {
 // ---------------------------------------------------------------------------
 // Exact top-k after the scores (select.cuh): this CTA's rows are those whose
 // tiles intersect [t_lo, t_hi); its positions of row b are one contiguous range.
-// Every CTA of the grid calls this (it holds the grid barriers).  `work` is the
-// shared memory the indexer no longer needs (work_bytes >= list_cap * 8 + 16 KB),
-// `hist` 2048 words, `scratch` >= 128 words (scans, compaction groups, a barrier).
+// Every CTA of the grid calls this (it holds the grid barrier).  `work` is the
+// shared memory the indexer no longer needs (work_bytes >= list_cap * 8),
+// `hist` 2048 words, `scratch` >= 128 words (scans, compaction groups).
 // ---------------------------------------------------------------------------
 constexpr int kSelThreads = 320;  // the indexer CTA: every warp joins the selection
 constexpr int kSelPer = 4;        // entries per thread per compaction chunk
+constexpr int kSelScoreLd = 8;    // float4 score loads in flight per thread
+constexpr int kSelListLd = 16;    // candidate-list loads in flight per thread
+constexpr uint32_t kSelPairwise = 256;  // sub-bin keys ranked pairwise (more: one more radix level)
 
 __device__ __forceinline__ void select_range(const PoolAddr& pa, const int* prefix, const int* vis_s,
                                              const int* run_s, int b, int t_lo, int t_hi, int& p_lo, int& p_hi,
@@ -136,26 +139,123 @@ __device__ __forceinline__ void load_hist(uint32_t* dst, const uint32_t* src) {
   }
 }
 
-// Bulk copy of `bytes` (16-byte multiple, 16-byte aligned ends) of global memory
-// into shared memory, completing on `bar`; thread 0 issues, everyone waits.
-// Returns false (status set) when the copy does not land in time.
-__device__ __forceinline__ bool bulk_fetch(void* dst, const void* src, uint32_t bytes, uint64_t* bar,
-                                           uint32_t& phase, int32_t* err) {
-  if (threadIdx.x == 0) {
-    asm volatile("fence.proxy.async.global;" ::: "memory");  // generic stores before -> async-proxy reads
-    mbar_arrive_expect_tx(bar, bytes);
-    for (uint32_t off = 0; off < bytes; off += 32768u)
-      bulk_load(smem_u32(static_cast<uint8_t*>(dst) + off), static_cast<const uint8_t*>(src) + off,
-                min(32768u, bytes - off), bar);
+// f(key) for every key of the shared-memory list lst[0, L): every thread takes a
+// run of consecutive keys (an odd count: the 8-byte loads of a half warp fall on
+// distinct banks, and the lanes of a warp hold keys from far-apart places of the
+// list, so their bitmap atomics rarely meet), four loads in flight.
+template <typename F>
+__device__ __forceinline__ void list_runs(const uint64_t* lst, uint32_t L, F f) {
+  constexpr uint32_t T = kSelThreads;
+  const uint32_t per = ((L + T - 1) / T) | 1u;
+  const uint32_t l0 = min(L, threadIdx.x * per), l1 = min(L, l0 + per);
+#pragma unroll 1
+  for (uint32_t i = l0; i < l1; i += 4) {
+    uint64_t kq[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) kq[u] = i + u < l1 ? lst[i + u] : 0ull;
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+      if (i + u < l1) f(kq[u]);
   }
-  volatile int no_abort = 0;
-  const bool landed = mbar_wait(bar, phase & 1u, &no_abort, err);
-  ++phase;
-  if (!__syncthreads_and(landed)) {
-    if (threadIdx.x == 0) mbar_drain(bar, (phase - 1) & 1u);
-    return false;
+}
+
+// The finisher's ordered output of row b: the list's blocks (lst in shared
+// memory, block i of the row's CTA i at blk_base[i], blk_n[i] keys, in position
+// order) walked in CTA order in pieces of at most 32 keys; every thread takes a
+// run of consecutive pieces.  One pass counts the keys >= K* of its pieces, a
+// block scan gives its output offset, a second pass writes the ids.  With
+// k <= 2048 the ids gather in `stage` (2048 words) and leave in one coalesced
+// copy, the scores read back from the row.  `pc` holds nblk + 1 words.
+__device__ void write_blocks(const SelectArgs& a, int b, const float* srow, const uint64_t* lst,
+                             const uint32_t* blk_base, const uint32_t* blk_n, uint32_t* pc, uint32_t nblk,
+                             uint64_t kstar, uint32_t* stage, uint32_t* scratch) {
+  constexpr int T = kSelThreads;
+  const int tid = threadIdx.x;
+  const int k = a.k;
+  __builtin_assume(__isShared(lst));
+  __builtin_assume(__isShared(blk_base));
+  __builtin_assume(__isShared(blk_n));
+  __builtin_assume(__isShared(pc));
+  __builtin_assume(__isShared(stage));
+  __builtin_assume(__isShared(scratch));
+  int32_t* orow = a.out_ids + int64_t(b) * k;
+  float* oscore = a.out_scores != nullptr ? a.out_scores + int64_t(b) * k : nullptr;
+  const bool staged = k <= kSelBins;
+  // pieces per block, scanned in CTA order (nblk <= the grid <= T)
+  uint32_t npieces;
+  const uint32_t mine = uint32_t(tid) < nblk ? (blk_n[tid] + 31u) >> 5 : 0u;
+  const uint32_t first = sel_excl_scan<T>(mine, npieces, scratch);
+  if (uint32_t(tid) <= nblk) pc[tid] = uint32_t(tid) < nblk ? first : npieces;
+  __syncthreads();
+  const uint32_t ipt = (npieces + T - 1) / T;
+  const uint32_t j0 = min(npieces, tid * ipt), j1 = min(npieces, j0 + ipt);
+  // the block of piece j0: the last block starting at or before it
+  uint32_t blk = 0;
+  if (j0 < j1) {
+    uint32_t lo = 0, hi = nblk - 1;
+    while (lo < hi) {
+      const uint32_t mid = (lo + hi + 1) >> 1;
+      if (pc[mid] <= j0) lo = mid;
+      else hi = mid - 1;
+    }
+    blk = lo;
   }
-  return true;
+  // visits the keys of this thread's pieces in order: f(key)
+  auto walk = [&](auto f) {
+    uint32_t i = blk;
+#pragma unroll 1
+    for (uint32_t j = j0; j < j1; ++j) {
+      while (pc[i + 1] <= j) ++i;  // empty blocks have no pieces
+      const uint32_t e0 = blk_base[i] + ((j - pc[i]) << 5);
+      const uint32_t e1 = blk_base[i] + min(blk_n[i], ((j - pc[i]) << 5) + 32u);
+#pragma unroll 1
+      for (uint32_t e = e0; e < e1; e += 4) {
+        uint64_t kq[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) kq[u] = e + u < e1 ? lst[e + u] : 0ull;
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          if (e + u < e1) f(kq[u]);
+      }
+    }
+  };
+  uint32_t cnt = 0;
+  walk([&](uint64_t key) { cnt += key >= kstar ? 1u : 0u; });
+  uint32_t found;
+  uint32_t s = sel_excl_scan<T>(cnt, found, scratch);
+  walk([&](uint64_t key) {
+    if (key < kstar) return;
+    if (s < uint32_t(k)) {  // more only after a CTA gave up (its candidates are missing)
+      if (staged) {
+        stage[s] = uint32_t(sel_key_id(key));
+      } else {
+        orow[s] = sel_key_id(key);
+        if (oscore != nullptr) oscore[s] = sel_key_score(key);
+      }
+    }
+    ++s;
+  });
+  __syncthreads();
+  if (staged) {
+    const uint32_t n = min(found, uint32_t(k));
+#pragma unroll 1
+    for (uint32_t i = tid; i < n; i += T) orow[i] = int32_t(stage[i]);
+    if (oscore != nullptr)
+#pragma unroll 1
+      for (uint32_t i0 = 0; i0 < n; i0 += T * 8) {
+        float sc[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const uint32_t i = i0 + u * T + tid;
+          if (i < n) sc[u] = __ldcg(srow + (int64_t(int32_t(stage[i])) - a.id_base));
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const uint32_t i = i0 + u * T + tid;
+          if (i < n) oscore[i] = key_score(sel_rank_u(__float_as_uint(sc[u])));
+        }
+      }
+  }
 }
 
 __device__ void select_phase(const SelectArgs& a, const float* __restrict__ scores, int64_t score_stride,
@@ -165,21 +265,20 @@ __device__ void select_phase(const SelectArgs& a, const float* __restrict__ scor
   constexpr int T = kSelThreads;
   const int tid = threadIdx.x;
   const int k = a.k;
+  // every pointer into shared memory stays in the shared state space (shared
+  // loads, stores and atomics rather than generic ones)
+  __builtin_assume(__isShared(work));
+  __builtin_assume(__isShared(hist));
+  __builtin_assume(__isShared(scratch));
   uint32_t* grp = scratch + 64;
   uint32_t* ncand = scratch + 42;
-  uint64_t* lbar = reinterpret_cast<uint64_t*>(scratch + 44);  // the bulk copies' barrier
-  uint32_t lphase = 0;
   const int rb0 = t_lo < t_hi ? find_row(prefix, batch, t_lo) : 0;
   const int rb1 = t_lo < t_hi ? find_row(prefix, batch, t_hi - 1) : -1;
-  if (tid == 0) {
-    mbar_init(lbar, 1);
-    fence_barrier_init();
-  }
-  // the scores this CTA stored through the generic proxy are read back by bulk copies
-  asm volatile("fence.proxy.async.global;" ::: "memory");
-  live = grid_barrier(a.ctl, 1, err) && live;  // every row's digit-0 histogram is complete
+  const int total = prefix[batch];
 
-  // rows without keys: all padding (one CTA writes them)
+  // ---- before the barrier: rows without keys (one CTA pads them) and rows of
+  // at most k keys (every key selected: output slot = position), which need no
+  // histogram
   if (live && blockIdx.x == 0)
     for (int b = 0; b < batch; ++b)
       if (vis_s[b] == 0)
@@ -188,305 +287,304 @@ __device__ void select_phase(const SelectArgs& a, const float* __restrict__ scor
           a.out_ids[int64_t(b) * k + i] = -1;
           if (a.out_scores != nullptr) a.out_scores[int64_t(b) * k + i] = -CUDART_INF_F;
         }
-
-  // ---- per row: threshold bin, this CTA's candidates appended to the row's list
-  // (unordered: position order is restored for the few selected ones after
-  // barrier 2), and the digit-1 counts of its threshold-bin entries
-  uint64_t* buf = reinterpret_cast<uint64_t*>(work);
   for (int b = rb0; b <= rb1 && live; ++b) {
     int p_lo, p_hi;
     bool first;
     select_range(pa, prefix, vis_s, run_s, b, t_lo, t_hi, p_lo, p_hi, first);
-    if (p_lo >= p_hi) continue;
     const int v = vis_s[b];
+    if (p_lo >= p_hi || v > k) continue;
     const float* srow = scores + int64_t(b) * score_stride;
     int32_t* orow = a.out_ids + int64_t(b) * k;
     float* oscore = a.out_scores != nullptr ? a.out_scores + int64_t(b) * k : nullptr;
-    if (v <= k) {  // every key is selected: output slot = position
 #pragma unroll 1
-      for (int p = p_lo + tid; p < p_hi; p += T) {
-        orow[p] = int32_t(a.id_base + p);
-        if (oscore != nullptr) oscore[p] = key_score(sel_rank_u(__float_as_uint(__ldcg(srow + p))));
-      }
-      if (first)
-#pragma unroll 1
-        for (int p = v + tid; p < k; p += T) {
-          orow[p] = -1;
-          if (oscore != nullptr) oscore[p] = -CUDART_INF_F;
-        }
-      continue;
+    for (int p = p_lo + tid; p < p_hi; p += T) {
+      orow[p] = int32_t(a.id_base + p);
+      if (oscore != nullptr) oscore[p] = key_score(sel_rank_u(__float_as_uint(__ldcg(srow + p))));
     }
-    load_hist(hist, a.hist + int64_t(b) * kSelBins);
-    if (tid == 0) *ncand = 0u;
-    __syncthreads();
-    uint32_t above;
-    const uint32_t b0 = sel_find_bin<T>(hist, kSelBins, uint32_t(k), above, scratch);
-    const uint32_t in_bin = hist[b0];
-    uint4* meta = a.meta + int64_t(b) * gridDim.x + blockIdx.x;
-    if (in_bin > uint32_t(a.list_cap - k)) {  // massive ties: the row's first CTA takes it after barrier 2
-      if (tid == 0) *meta = make_uint4(0u, 0xffffffffu, b0, above);
-      __syncthreads();
-      continue;
-    }
-    // candidates (digit 0 >= b0): the range's scores come into shared memory by bulk
-    // copies (aligned groups of four covering [p_lo, p_hi); the scores outside the
-    // range, at most three each side and inside the row's stride, are masked),
-    // chunk by chunk behind the candidate buffer, and are scanned there.
-    // digit 0 >= b0 <=> score >= the lowest score of bin b0 (the key map is monotone;
-    // NaN ranks above +inf); bins 0-3 decode to NaN patterns and hold nothing above
-    // -inf, so with b0 < 4 every score passes; keys are built for the few that do
-    const int a0 = p_lo & ~3;
-    const int a1 = (p_hi + 3) & ~3;
-    const float thr = b0 < 4u ? -CUDART_INF_F : key_score(b0 << 21);
-    uint32_t* h1row = a.hist1 + int64_t(b) * kSelBins;
-    float* chunk = reinterpret_cast<float*>(work + size_t(a.list_cap) * 8);
-    const int chunk_len = int((work_bytes - size_t(a.list_cap) * 8) / 4) & ~4095;
-    for (int c0 = a0; c0 < a1 && live; c0 += chunk_len) {
-      const int c1 = min(a1, c0 + chunk_len);
-      if (!bulk_fetch(chunk, srow + c0, uint32_t(c1 - c0) * 4u, lbar, lphase, err)) {
-        live = false;
-        break;
-      }
+    if (first)
 #pragma unroll 1
-      for (int i0 = 0; i0 < c1 - c0; i0 += T * 4) {  // uniform trip count: the warp appends together
-        const int i = i0 + tid * 4;
-        float4 x4 = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (i < c1 - c0) x4 = *reinterpret_cast<const float4*>(chunk + i);
-        const float xs[4] = {x4.x, x4.y, x4.z, x4.w};
-        uint64_t kk[4];
-        uint32_t take = 0;
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int p = c0 + i + e;
-          kk[e] = 0ull;
-          if (i >= c1 - c0 || !(xs[e] >= thr || xs[e] != xs[e]) || p < p_lo || p >= p_hi) continue;
-          const uint32_t u = sel_rank_u(__float_as_uint(xs[e]));
-          if ((u >> 21) < b0) continue;
-          kk[e] = sel_key(u, a.id_base + p);
-          take |= 1u << e;
-          if ((u >> 21) == b0) atomicAdd(h1row + ((u >> 10) & (kSelBins - 1)), 1u);  // digit 1: key bits 41..51
-        }
-        // one shared-memory atomic per warp: lane offsets by a warp scan
-        const uint32_t cnt = __popc(take);
-        uint32_t incl = cnt;
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-          const uint32_t x = __shfl_up_sync(0xffffffffu, incl, o);
-          if ((tid & 31) >= o) incl += x;
-        }
-        uint32_t wbase = 0;
-        if ((tid & 31) == 31 && incl != 0u) wbase = atomicAdd(ncand, incl);
-        uint32_t at = __shfl_sync(0xffffffffu, wbase, 31) + incl - cnt;
-#pragma unroll
-        for (int e = 0; e < 4; ++e)
-          if ((take >> e) & 1u) buf[at++] = kk[e];
+      for (int p = v + tid; p < k; p += T) {
+        orow[p] = -1;
+        if (oscore != nullptr) oscore[p] = -CUDART_INF_F;
       }
-      __syncthreads();  // the chunk is read before the next copy lands on it
-    }
-    const uint32_t n = *ncand;
-    if (tid == 0) scratch[40] = n ? atomicAdd(a.list_len + b, n) : 0u;
-    __syncthreads();
-    const uint32_t base = scratch[40];
-    uint64_t* lrow = a.list + int64_t(b) * a.list_cap + base;
-#pragma unroll 1
-    for (uint32_t i = tid; i < n; i += T) lrow[i] = buf[i];
-    if (tid == 0) *meta = make_uint4(base, n, b0, above);
-    __syncthreads();
   }
 
-  live = grid_barrier(a.ctl, 2, err) && live;  // every row's candidate list is complete
+  live = grid_barrier(a.ctl, 1, err) && live;  // every row's digit-0 histogram is complete
 
-  // ---- per row: K* from the digit-1 histogram and the list, this CTA's offset, its ids
-  uint64_t* lst = reinterpret_cast<uint64_t*>(work);
-  for (int b = rb0; b <= rb1 && live; ++b) {
-    int p_lo, p_hi;
-    bool first;
-    select_range(pa, prefix, vis_s, run_s, b, t_lo, t_hi, p_lo, p_hi, first);
-    if (p_lo >= p_hi) continue;
-    const int v = vis_s[b];
-    if (v <= k) continue;
-    const float* srow = scores + int64_t(b) * score_stride;
-    int32_t* orow = a.out_ids + int64_t(b) * k;
-    float* oscore = a.out_scores != nullptr ? a.out_scores + int64_t(b) * k : nullptr;
-    const uint4 m = a.meta[int64_t(b) * gridDim.x + blockIdx.x];
-    const uint32_t b0 = m.z, need0 = uint32_t(k) - m.w;
-    auto put = [&](uint32_t slot, uint64_t key) {
-      if (slot >= uint32_t(k)) return;  // only after a CTA gave up (its list block is missing)
-      orow[slot] = sel_key_id(key);
-      if (oscore != nullptr) oscore[slot] = sel_key_score(key);
-    };
-    if (m.y == 0xffffffffu) {
-      // massive ties: the first CTA resolves K* over the whole row and writes it
-      if (first) {
-        const int64_t id0 = a.id_base;
-        auto row_key = [&](int64_t i) -> uint64_t {
-          return sel_key(sel_rank_u(__float_as_uint(__ldcg(srow + i))), id0 + i);
-        };
-        const uint64_t kstar = sel_kstar<T>(row_key, v, uint64_t(b0) << kSelShift[0], need0, 1, hist, scratch);
-        uint32_t written = 0;
-#pragma unroll 1
-        for (int c0 = 0; c0 < v && written < uint32_t(k); c0 += T * kSelPer) {
-          uint32_t keep = 0;
-          uint64_t keys[kSelPer];
-#pragma unroll
-          for (int j = 0; j < kSelPer; ++j) {
-            const int i = c0 + j * T + tid;
-            keys[j] = i < v ? row_key(i) : 0ull;
-            keep |= uint32_t(i < v && keys[j] >= kstar) << j;
-          }
-          written += sel_compact<T, kSelPer>(keep, written, grp, scratch, [&](uint32_t slot, int j) { put(slot, keys[j]); });
-        }
-      }
-      continue;
-    }
-    // the row's candidate list into shared memory by one bulk copy (16-byte units;
-    // the capacity is even, so the rounded-up copy stays inside the row's list),
-    // after the digit-1 histogram of its threshold bin is read and searched
-    if (tid == 0) scratch[40] = __ldcg(a.list_len + b);
-    load_hist(hist, a.hist1 + int64_t(b) * kSelBins);
-    __syncthreads();
-    const uint32_t L = scratch[40];
-    uint32_t above1;
-    const uint32_t b1 = sel_find_bin<T>(hist, kSelBins, need0, above1, scratch);
-    const uint32_t need1 = need0 - above1, in_sub = hist[b1];
-    if (!bulk_fetch(lst, a.list + int64_t(b) * a.list_cap, ((L + 1u) & ~1u) * 8u, lbar, lphase, err)) break;
-    // K*: with the whole sub-bin (b0, b1) selected, the rule is key >= its lower
-    // edge; otherwise the need1-th largest of the sub-bin's few keys
-    const uint64_t sub = (uint64_t(b0) << kSelShift[0]) | (uint64_t(b1) << kSelShift[1]);
-    uint64_t kstar = sub;
-    if (in_sub != need1) {
-      if (in_sub <= 256u) {  // pairwise rank among the few keys of the sub-bin
-        uint64_t* subk = reinterpret_cast<uint64_t*>(hist);
-        if (tid == 0) *ncand = 0u;
-        __syncthreads();
-#pragma unroll 1
-        for (uint32_t i = tid; i < L; i += T) {
-          const uint64_t key = lst[i];
-          if ((key >> kSelShift[1]) == (sub >> kSelShift[1])) subk[atomicAdd(ncand, 1u)] = key;
-        }
-        __syncthreads();
-        const uint32_t c = *ncand;
-#pragma unroll 1
-        for (uint32_t i = tid; i < c; i += T) {
-          const uint64_t key = subk[i];
-          uint32_t above = 0;
-#pragma unroll 1
-          for (uint32_t j = 0; j < c; ++j) above += subk[j] > key ? 1u : 0u;
-          if (above == need1 - 1) {
-            scratch[46] = uint32_t(key);
-            scratch[47] = uint32_t(key >> 32);
-          }
-        }
-        __syncthreads();
-        kstar = (uint64_t(scratch[47]) << 32) | scratch[46];
-      } else {
-        kstar = sel_kstar<T>([&](int64_t i) { return lst[i]; }, L, sub, need1, 2, hist, scratch);
-      }
-    }
-    __syncthreads();
-    // this CTA's selected keys in position order: a bitmap of its positions
-    // [p_lo, p_hi), 65536 at a time; the first pass over the list also counts the
-    // selected candidates of lower positions (this CTA's output offset).  One
-    // prefix popcount gives every set bit its slot; the score is read back from
-    // the row (the key's score is the row's score at that position).
-    uint32_t* bits = hist;
-    const int32_t id_lo = int32_t(a.id_base + p_lo);
-    uint32_t slot = 0;
-#pragma unroll 1
-    for (int w0 = p_lo; w0 < p_hi; w0 += kSelBins * 32) {
-      const int w1 = min(p_hi, w0 + kSelBins * 32);
-      const int nw = (w1 - w0 + 31) >> 5;
-#pragma unroll 1
-      for (int i = tid; i < nw; i += T) bits[i] = 0u;
-      __syncthreads();
-      const int32_t i0 = int32_t(a.id_base + w0), i1 = int32_t(a.id_base + w1);
-      uint32_t lower = 0;
-#pragma unroll 1
-      for (uint32_t i = tid; i < L; i += T) {
-        const uint64_t key = lst[i];
-        if (key < kstar) continue;
-        const int32_t id = sel_key_id(key);
-        lower += id < id_lo ? 1u : 0u;
-        if (id >= i0 && id < i1) atomicOr(bits + ((id - i0) >> 5), 1u << ((id - i0) & 31));
-      }
-      if (w0 == p_lo) sel_excl_scan<T>(lower, slot, scratch);  // slot = the block's sum (synchronises)
-      else __syncthreads();
-      const int per = (nw + T - 1) / T;  // consecutive words per thread
-      uint32_t cnt = 0;
-#pragma unroll 1
-      for (int j = 0; j < per; ++j) {
-        const int wi = tid * per + j;
-        cnt += wi < nw ? __popc(bits[wi]) : 0u;
-      }
-      uint32_t found;
-      uint32_t s = slot + sel_excl_scan<T>(cnt, found, scratch);
-#pragma unroll 1
-      for (int j = 0; j < per; ++j) {
-        const int wi = tid * per + j;
-        if (wi >= nw) break;
-        uint32_t m = bits[wi];
-        while (m != 0u) {
-          const int p = w0 + wi * 32 + (__ffs(m) - 1);
-          m &= m - 1u;
-          if (s < uint32_t(k)) {  // only after a CTA gave up (its list block is missing)
-            orow[s] = int32_t(a.id_base + p);
-            if (oscore != nullptr) oscore[s] = key_score(sel_rank_u(__float_as_uint(__ldcg(srow + p))));
-          }
-          ++s;
-        }
-      }
-      slot += found;
-      __syncthreads();
-    }
-  }
-
-  // ---- leave the workspace as found.  Every CTA that scored part of a row counts
-  // itself done with the row (after its last read of the row's histograms and list);
-  // the row's last CTA clears them; the last CTA to leave resets the barrier counters
-  const int total = prefix[batch];
-  auto t_start = [&](int c) { return int((int64_t(total) * c) / gridDim.x); };
-  auto owner = [&](int t) {  // the CTA whose tiles [t_start(c), t_start(c + 1)) hold tile t
-    int lo = 0, hi = int(gridDim.x) - 1;
-    while (lo < hi) {
-      const int mid = (lo + hi + 1) >> 1;
-      if (t_start(mid) <= t) lo = mid;
-      else hi = mid - 1;
-    }
-    return lo;
+  // CTAs holding tiles of row b.  CTA c holds tiles [floor(total*c/G), floor(total*(c+1)/G)),
+  // so tile t belongs to CTA floor(((t+1)*G - 1) / total); with fewer tiles than
+  // CTAs every CTA holds at most one tile, and the row has one CTA per tile
+  auto row_ctas = [&](int b) -> uint32_t {
+    const int tiles = prefix[b + 1] - prefix[b];
+    if (total < int(gridDim.x)) return uint32_t(tiles);
+    const uint64_t G = gridDim.x;
+    const uint64_t c0 = ((uint64_t(prefix[b]) + 1) * G - 1) / uint64_t(total);
+    const uint64_t c1 = (uint64_t(prefix[b + 1]) * G - 1) / uint64_t(total);
+    return uint32_t(c1 - c0 + 1);
   };
-  uint32_t* row_done = a.list_len + batch;
+  unsigned long long* state = a.row_state;
+
+  // ---- per row of more than k keys: threshold bin b0, this CTA's candidates
+  // (digit 0 >= b0) appended to the row's list in one block, the digit 1 of its
+  // threshold-bin entries counted into the row's digit-1 histogram; then the
+  // CTA counts itself done with the row, and the row's last CTA finishes it.
+  // Shared memory: the candidate buffer (list_cap keys), then the staging of
+  // the scores (each thread's loads all in flight, then read back by rolled loops)
+  uint64_t* buf = reinterpret_cast<uint64_t*>(work);
+  float4* stage = reinterpret_cast<float4*>(work + size_t(a.list_cap) * 8);
+  const int nld = int(min(size_t(kSelScoreLd), (work_bytes - size_t(a.list_cap) * 8) / (T * 16)));  // >= 1 (host check)
   for (int b = rb0; b <= rb1; ++b) {
-    const int ta = max(t_lo, prefix[b]), tb = min(t_hi, prefix[b + 1]);
-    if (ta >= tb) continue;
-    // CTAs with tiles of this row (a CTA with no tiles at all touches no row)
-    const int c0 = owner(prefix[b]), c1 = owner(prefix[b + 1] - 1);
-    uint32_t mine_n = 0;
-    for (int c = c0 + tid; c <= c1; c += T) mine_n += t_start(c) < t_start(c + 1) ? 1u : 0u;
-    uint32_t nctas;
-    sel_excl_scan<T>(mine_n, nctas, scratch);
+    int p_lo, p_hi;
+    bool first;
+    select_range(pa, prefix, vis_s, run_s, b, t_lo, t_hi, p_lo, p_hi, first);
+    const int v = vis_s[b];
+    if (p_lo >= p_hi || v <= k) continue;
+    const uint32_t nctas = row_ctas(b);
+    const float* srow = scores + int64_t(b) * score_stride;
+    uint32_t b0 = 0, above = 0;
+    bool overflow = false;
+    const bool appended = live;  // (an overflowing row appends an empty block)
+    if (live) {
+      // the range's scores (aligned float4 groups covering [p_lo, p_hi); the row's
+      // stride is a multiple of 64 floats) go in flight before the histogram loads
+      const int a0 = p_lo & ~3;
+      const int n4 = (((p_hi + 3) & ~3) - a0) >> 2;
+      const float4* s4 = reinterpret_cast<const float4*>(srow + a0);
+      float4 x[kSelScoreLd];
+      auto load = [&](int i0) {
+#pragma unroll
+        for (int j = 0; j < kSelScoreLd; ++j) {
+          const int q = i0 + j * T + tid;
+          if (j < nld && q < n4) x[j] = __ldcg(s4 + q);
+        }
+      };
+      auto store = [&](int i0) {  // a thread reads back only its own staged loads
+#pragma unroll
+        for (int j = 0; j < kSelScoreLd; ++j) {
+          const int q = i0 + j * T + tid;
+          if (j < nld && q < n4) stage[j * T + tid] = x[j];
+        }
+      };
+      load(0);
+      load_hist(hist, a.hist + int64_t(b) * kSelBins);
+      store(0);
+      if (tid == 0) *ncand = 0u;
+      __syncthreads();
+      b0 = sel_find_bin<T>(hist, kSelBins, uint32_t(k), above, scratch) & uint32_t(kSelBins - 1);
+      // massive ties: more threshold-bin entries than the list has room for; the
+      // row's last CTA resolves the row from its scores
+      overflow = hist[b0] > uint32_t(a.list_cap - k);
+      if (overflow && tid == 0) a.meta[int64_t(b) * gridDim.x + blockIdx.x] = make_uint2(0u, 0u);
+      if (!overflow) {
+        // digit 0 >= b0 <=> score >= the lowest score of bin b0 (the key map is
+        // monotone; NaN ranks above +inf); bins 0-3 decode to NaN patterns and
+        // hold nothing above -inf, so with b0 < 4 every score passes
+        const float thr = b0 < 4u ? -CUDART_INF_F : key_score(b0 << 21);
+        uint32_t* h1row = a.hist1 + int64_t(b) * kSelBins;
+        // per staged chunk: every thread tests a run of consecutive float4 groups
+        // (an odd count: conflict-free 16-byte reads), one block scan places its
+        // candidates, so the block comes out in position order
+        uint32_t nbuf = 0;
+#pragma unroll 1
+        for (int i0 = 0; i0 < n4; i0 += T * nld) {
+          const int cn4 = min(T * nld, n4 - i0);
+          if (i0 > 0) {
+            load(i0);
+            store(i0);
+          }
+          __syncthreads();
+          const int m = ((cn4 + T - 1) / T) | 1;
+          const int q0 = min(cn4, tid * m), q1 = min(cn4, q0 + m);
+          uint64_t take = 0;
+#pragma unroll 1
+          for (int qi = q0; qi < q1; ++qi) {
+            const float4 x4 = stage[qi];
+            const float xs[4] = {x4.x, x4.y, x4.z, x4.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const int p = a0 + 4 * (i0 + qi) + e;
+              if (!(xs[e] >= thr || xs[e] != xs[e]) || p < p_lo || p >= p_hi) continue;
+              const uint32_t u = sel_rank_u(__float_as_uint(xs[e]));
+              if ((u >> 21) < b0) continue;
+              take |= 1ull << ((qi - q0) * 4 + e);
+              if ((u >> 21) == b0) atomicAdd(h1row + ((u >> 10) & (kSelBins - 1)), 1u);  // key bits 41..51
+            }
+          }
+          uint32_t tot;
+          uint32_t o = nbuf + sel_excl_scan<T>(uint32_t(__popcll(take)), tot, scratch);
+#pragma unroll 1
+          while (take != 0ull) {
+            const int bit = __ffsll(take) - 1;
+            take &= take - 1ull;
+            const int qi = q0 + (bit >> 2), e = bit & 3;
+            const float x = reinterpret_cast<const float*>(stage + qi)[e];
+            if (o < uint32_t(a.list_cap))
+              buf[o] = sel_key(sel_rank_u(__float_as_uint(x)), a.id_base + a0 + 4 * (i0 + qi) + e);
+            ++o;
+          }
+          nbuf += tot;
+          __syncthreads();  // the chunk is read before the next one is staged
+        }
+        const uint32_t n = min(nbuf, uint32_t(a.list_cap));
+        if (tid == 0) scratch[40] = n ? uint32_t(atomicAdd(state + b, (unsigned long long)n)) : 0u;
+        __syncthreads();
+        const uint32_t base = scratch[40];
+        uint64_t* lrow = a.list + int64_t(b) * a.list_cap;
+#pragma unroll 1
+        for (uint32_t i = tid; i < n; i += T)
+          if (base + i < uint32_t(a.list_cap)) lrow[base + i] = buf[i];
+        if (tid == 0) a.meta[int64_t(b) * gridDim.x + blockIdx.x] = make_uint2(base, n);
+      }
+    }
+    if (!appended && tid == 0) a.meta[int64_t(b) * gridDim.x + blockIdx.x] = make_uint2(0u, 0u);
+    // count in (live or not): the last CTA of the row sees every other CTA's
+    // candidates, digit-1 counts and histogram reads complete, and the list's length
+    __syncthreads();
     if (tid == 0) {
-      __threadfence();
-      scratch[43] = atomicAdd(row_done + b, 1u) == nctas - 1 ? 1u : 0u;
+      const unsigned long long old = atom_add_acq_rel(state + b, 1ull << 32);
+      scratch[43] = uint32_t(old >> 32) == nctas - 1 ? 1u : 0u;
+      scratch[40] = uint32_t(old);
     }
     __syncthreads();
-    if (scratch[43]) {
-      __threadfence();
+    if (!scratch[43]) continue;
+    const uint32_t L = min(scratch[40], uint32_t(a.list_cap));
+    __syncthreads();
+
+    if (live && overflow) {
+      // massive ties: K* over the whole row's scores, then the row in position order
+      int32_t* orow = a.out_ids + int64_t(b) * k;
+      float* oscore = a.out_scores != nullptr ? a.out_scores + int64_t(b) * k : nullptr;
+      const int64_t id0 = a.id_base;
+      auto row_key = [&](int64_t i) -> uint64_t {
+        return sel_key(sel_rank_u(__float_as_uint(__ldcg(srow + i))), id0 + i);
+      };
+      const uint64_t kstar =
+          sel_kstar<T>(row_key, v, uint64_t(b0) << kSelShift[0], uint32_t(k) - above, 1, hist, scratch);
+      uint32_t written = 0;
 #pragma unroll 1
-      for (int i = tid; i < kSelBins; i += T) {
-        a.hist[int64_t(b) * kSelBins + i] = 0u;
-        a.hist1[int64_t(b) * kSelBins + i] = 0u;
+      for (int c0 = 0; c0 < v && written < uint32_t(k); c0 += T * kSelPer) {
+        uint32_t keep = 0;
+        uint64_t keys[kSelPer];
+#pragma unroll
+        for (int j = 0; j < kSelPer; ++j) {
+          const int i = c0 + j * T + tid;
+          keys[j] = i < v ? row_key(i) : 0ull;
+          keep |= uint32_t(i < v && keys[j] >= kstar) << j;
+        }
+        written += sel_compact<T, kSelPer>(keep, written, grp, scratch, [&](uint32_t slot, int j) {
+          if (slot >= uint32_t(k)) return;
+          orow[slot] = sel_key_id(keys[j]);
+          if (oscore != nullptr) oscore[slot] = sel_key_score(keys[j]);
+        });
       }
-      if (tid == 0) {
-        a.list_len[b] = 0u;
-        row_done[b] = 0u;
+    } else if (live) {
+      // the list into shared memory and the digit-1 histogram, all loads in flight
+      uint64_t* lst = reinterpret_cast<uint64_t*>(work);
+      const uint64_t* lrow = a.list + int64_t(b) * a.list_cap;
+      uint64_t kk[kSelListLd];
+      auto load = [&](uint32_t j0) {
+#pragma unroll
+        for (int j = 0; j < kSelListLd; ++j) {
+          const uint32_t i = j0 + j * T + tid;
+          if (i < L) kk[j] = __ldcg(lrow + i);
+        }
+      };
+      auto store = [&](uint32_t j0) {
+#pragma unroll
+        for (int j = 0; j < kSelListLd; ++j) {
+          const uint32_t i = j0 + j * T + tid;
+          if (i < L) lst[i] = kk[j];
+        }
+      };
+      // the row's CTAs in CTA order and their blocks (shared memory after the list)
+      const size_t lbytes = (size_t(L) * 8 + 15) & ~size_t(15);
+      uint32_t* blk_base = reinterpret_cast<uint32_t*>(work + lbytes);
+      uint32_t* blk_n = blk_base + gridDim.x;
+      uint32_t* pc = blk_n + gridDim.x;
+      uint2 m = make_uint2(0u, 0u);
+      if (uint32_t(tid) < nctas) {
+        const uint64_t G = gridDim.x;
+        const uint64_t t = uint64_t(prefix[b]) + (total >= int(G) ? 0u : uint32_t(tid));
+        // the owner of tile t (CTA c holds tiles [floor(total*c/G), floor(total*(c+1)/G)))
+        const uint64_t c = ((t + 1) * G - 1) / uint64_t(total) + (total >= int(G) ? uint32_t(tid) : 0u);
+        m = __ldcg(a.meta + int64_t(b) * G + int64_t(c));
       }
+      load(0);
+      load_hist(hist, a.hist1 + int64_t(b) * kSelBins);
+      store(0);
+      if (uint32_t(tid) < nctas) {  // a block past the list only after a CTA gave up
+        const uint32_t bb = min(m.x, L);
+        blk_base[tid] = bb;
+        blk_n[tid] = min(m.y, L - bb);
+      }
+#pragma unroll 1
+      for (uint32_t j0 = T * kSelListLd; j0 < L; j0 += T * kSelListLd) {
+        load(j0);
+        store(j0);
+      }
+      __syncthreads();
+      // the sub-bin (b0, b1) holding K*: with the whole sub-bin selected K* is its
+      // lower edge, otherwise the need1-th largest of its keys (ranked pairwise
+      // when few, else by the next digits)
+      const uint32_t need0 = uint32_t(k) - above;
+      uint32_t above1;
+      const uint32_t b1 = sel_find_bin<T>(hist, kSelBins, need0, above1, scratch) & uint32_t(kSelBins - 1);
+      const uint32_t need1 = need0 - above1, in_sub = hist[b1];
+      const uint64_t sub = (uint64_t(b0) << kSelShift[0]) | (uint64_t(b1) << kSelShift[1]);
+      __syncthreads();
+      uint64_t kstar = sub;
+      if (in_sub != need1) {
+        if (in_sub <= kSelPairwise) {
+          uint64_t* subk = reinterpret_cast<uint64_t*>(hist);
+          if (tid == 0) {
+            *ncand = 0u;
+            scratch[46] = uint32_t(sub);  // K* stays the edge if the ranking finds none
+            scratch[47] = uint32_t(sub >> 32);
+          }
+          __syncthreads();
+          list_runs(lst, L, [&](uint64_t key) {
+            if ((key >> kSelShift[1]) == (sub >> kSelShift[1])) {
+              const uint32_t at = atomicAdd(ncand, 1u);
+              if (at < kSelPairwise) subk[at] = key;
+            }
+          });
+          __syncthreads();
+          const uint32_t c = min(*ncand, kSelPairwise);
+#pragma unroll 1
+          for (uint32_t i = tid; i < c; i += T) {
+            const uint64_t key = subk[i];
+            uint32_t higher = 0;
+#pragma unroll 1
+            for (uint32_t j = 0; j < c; ++j) higher += subk[j] > key ? 1u : 0u;
+            if (higher == need1 - 1) {
+              scratch[46] = uint32_t(key);
+              scratch[47] = uint32_t(key >> 32);
+            }
+          }
+          __syncthreads();
+          kstar = (uint64_t(scratch[47]) << 32) | scratch[46];
+        } else {
+          kstar = sel_kstar<T>([&](int64_t i) { return lst[i]; }, L, sub, need1, 2, hist, scratch);
+        }
+      }
+      // the ids in position order; they gather in `hist`
+      write_blocks(a, b, srow, lst, blk_base, blk_n, pc, nctas, kstar, hist, scratch);
     }
+    // the row's workspace back to zero for the next launch
+#pragma unroll 1
+    for (int i = tid; i < kSelBins; i += T) {
+      a.hist[int64_t(b) * kSelBins + i] = 0u;
+      a.hist1[int64_t(b) * kSelBins + i] = 0u;
+    }
+    if (tid == 0) state[b] = 0ull;
     __syncthreads();
   }
+
+  // the last CTA to leave resets the barrier counters (every other CTA has passed the barrier)
   if (tid == 0) {
     __threadfence();
     const uint32_t done = atomicAdd(a.ctl + 1, 1u);
-    if (done == gridDim.x - 1) {  // every other CTA has passed both barriers
+    if (done == gridDim.x - 1) {
       a.ctl[0] = 0u;
       a.ctl[1] = 0u;
     }
@@ -793,11 +891,13 @@ __global__ void __launch_bounds__(kIxThreads, 1)
       // flushes the CTA's score histogram of row rb into the row's global histogram
       auto flush = [&](int rb) {
         asm volatile("bar.sync 3, 256;" ::: "memory");
+        // (the fused selection takes every key of a row of at most k keys: no histogram)
+        const bool add = hist != nullptr && (sel.out_ids == nullptr || vis_s[rb] > sel.k);
         if (hist != nullptr)
           for (int i = et; i < kIxHistBins; i += 256) {
             const uint32_t v = hsm[i];
             if (v) {
-              atomicAdd(hist + int64_t(rb) * kIxHistBins + i, v);
+              if (add) atomicAdd(hist + int64_t(rb) * kIxHistBins + i, v);
               hsm[i] = 0u;
             }
           }
@@ -903,6 +1003,12 @@ int launch_ix(const CUtensorMap& map, const float* q, const float* weights, cons
   cfg.dynamicSmemBytes = L::kAlloc;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
+  DSR_REQUIRE(sel.out_ids == nullptr ||
+                  size_t(L::kWOff - L::kStagesOff) >= size_t(sel.list_cap) * 8 + size_t(kSelThreads) * 16,
+              "indexer decode: k %d leaves no shared memory for the selection", sel.k);
+  DSR_REQUIRE(sel.out_ids == nullptr || sm_count() < kSelThreads,
+              "indexer decode: %d SMs: the selection takes one CTA per SM and at most %d", sm_count(),
+              kSelThreads - 1);
   if (sel.out_ids != nullptr) {
     // the selection's grid barriers need every CTA resident at once
     attr[0].id = cudaLaunchAttributeCooperative;
@@ -973,10 +1079,10 @@ int select_args(SelectArgs* a, void* workspace, int64_t batch, int64_t k, int64_
   a->hist = reinterpret_cast<uint32_t*>(base + L.hist);
   a->hist1 = reinterpret_cast<uint32_t*>(base + L.hist1);
   a->ctl = reinterpret_cast<uint32_t*>(base + L.ctl);
-  a->list_len = reinterpret_cast<uint32_t*>(base + L.len);
+  a->row_state = reinterpret_cast<unsigned long long*>(base + L.state);
+  a->meta = reinterpret_cast<uint2*>(base + L.meta);
   a->list = reinterpret_cast<uint64_t*>(base + L.list);
   a->list_cap = int(L.cap);
-  a->meta = reinterpret_cast<uint4*>(base + L.meta);
   return DSR_OK;
 }
 

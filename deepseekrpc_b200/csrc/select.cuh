@@ -10,19 +10,23 @@
 //
 // The indexer kernel runs this after scoring, in every CTA of its cooperative
 // grid (one CTA per SM), on the positions that CTA scored:
-//   1. the epilogue already added every score to its row's digit-0 histogram;
-//      grid barrier 1 completes the histograms;
+//   1. rows of at most k keys take every key (slot = position) before any
+//      synchronisation; the epilogue added every score of the other rows to its
+//      row's digit-0 histogram, and one grid barrier completes the histograms;
 //   2. every CTA finds each of its rows' threshold bin b0, appends its
-//      candidates (digit 0 >= b0) to the row's candidate list in one block, and
-//      counts the digit 1 of its threshold-bin entries into the row's digit-1
-//      histogram; grid barrier 2 completes the lists and digit-1 histograms;
-//   3. every CTA reads each of its rows' digit-1 histogram and list, finds K*
-//      (the whole sub-bin of digit 1 selected, or the rank among its few keys),
-//      counts the selected candidates of lower positions (its output offset)
-//      and writes its own selected ids (and scores) in position order there.
+//      candidates (digit 0 >= b0), in position order, to the row's candidate
+//      list as one block (recorded in meta), counts the digit 1 of its
+//      threshold-bin entries into the row's digit-1 histogram, and counts itself
+//      done with the row (one 64-bit atomic that also returns the list's length);
+//   3. the row's last CTA to finish step 2 (no waiting: the others have left the
+//      row) reads the digit-1 histogram, the list and the blocks, finds K* (the
+//      whole sub-bin of digit 1 selected, or the rank among its few keys), and
+//      walks the blocks in CTA order -- which is position order -- in pieces of
+//      at most 32 keys: one pass counts each piece's keys >= K*, a scan gives the
+//      pieces their output offsets, a second pass writes the ids (and scores);
+//      then it clears the row's workspace.
 // A row whose threshold bin holds more entries than its list has room for
-// (massive ties) is resolved whole by the CTA holding its first tile, after
-// barrier 2, from the row's scores.  A row with no more than k keys takes them all.
+// (massive ties) is resolved by its last CTA from the row's scores.
 //
 // This code runs once per CTA and launch, so its loops stay rolled: unrolled
 // straight-line code would be fetched into the instruction cache once and never
@@ -49,27 +53,27 @@ struct SelectArgs {
   uint32_t* hist;      // [batch][2048] digit-0 histograms, built by the indexer epilogue
   uint32_t* hist1;     // [batch][2048] digit-1 histograms of each row's threshold-bin entries
   uint32_t* ctl;       // [64]: [0] barrier arrivals, [1] exits
-  uint32_t* list_len;  // [2 * batch]: list lengths, then per-row counts of CTAs done with the row
-  uint64_t* list;      // [batch][list_cap] candidate rank keys
+  unsigned long long* row_state;  // [batch]: (CTAs done with the row << 32) | candidate-list length
+  uint64_t* list;      // [batch][list_cap] candidate rank keys, one position-ordered block per CTA
   int list_cap;
-  uint4* meta;         // [batch][grid]: per row and CTA {block base, block count, b0, count above b0}
+  uint2* meta;         // [batch][grid]: per row and CTA {block base, block length}
 };
 
-// Workspace: hist | hist1 | ctl | list_len | list | meta.  hist, hist1, ctl and
-// list_len must be zero before the first launch; every completed launch leaves
-// them zero again (meta and list need no clearing).
+// Workspace: hist | hist1 | ctl | row_state | list | meta.  Everything before
+// the list must be zero before the first launch; every completed launch leaves
+// it zero again (list and meta need no clearing).
 struct SelectLayout {
-  size_t hist, hist1, ctl, len, list, meta, total;
+  size_t hist, hist1, ctl, state, list, meta, total;
   int64_t cap;
   __host__ __device__ SelectLayout(int64_t batch, int64_t k, int64_t grid) {
     cap = (kSelBinCap + k + 1) & ~int64_t(1);
     hist = 0;
     hist1 = hist + size_t(batch) * kSelBins * 4;
     ctl = hist1 + size_t(batch) * kSelBins * 4;
-    len = ctl + 256;
-    list = len + ((size_t(batch) * 8 + 255) / 256) * 256;
+    state = ctl + 256;
+    list = state + ((size_t(batch) * 8 + 255) / 256) * 256;
     meta = list + size_t(batch) * size_t(cap) * 8;
-    total = meta + size_t(batch) * size_t(grid) * 16;
+    total = meta + size_t(batch) * size_t(grid) * 8;
   }
   // leading bytes that must be zero at launch
   __host__ __device__ size_t zeroed() const { return list; }
@@ -87,6 +91,15 @@ __device__ __forceinline__ int32_t sel_key_id(uint64_t key) {
 }
 __device__ __forceinline__ float sel_key_score(uint64_t key) { return key_score(uint32_t(key >> 31)); }
 
+// Atomic add with acquire-release semantics at GPU scope: the CTA's writes
+// before it (ordered by a CTA barrier) are visible to whoever observes the new
+// value, and whatever the observed old value published is visible after it.
+__device__ __forceinline__ unsigned long long atom_add_acq_rel(unsigned long long* p, unsigned long long v) {
+  unsigned long long old;
+  asm volatile("atom.acq_rel.gpu.global.add.u64 %0, [%1], %2;" : "=l"(old) : "l"(p), "l"(v) : "memory");
+  return old;
+}
+
 // ---------------------------------------------------------------- grid barrier
 // Every CTA of the (cooperative, fully resident) grid arrives once per barrier;
 // barrier n completes when the arrival count reaches n * gridDim.x.  A wait that
@@ -96,7 +109,7 @@ __device__ __forceinline__ bool grid_barrier(uint32_t* arrivals, uint32_t n, int
   __syncthreads();
   int ok = 1;
   if (threadIdx.x == 0) {
-    __threadfence();
+    // release: the CTA's writes before the barrier (ordered by __syncthreads) go with the arrival
     asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(arrivals) : "memory");
     const uint32_t target = n * gridDim.x;
     const uint64_t start = global_ns();
