@@ -28,7 +28,6 @@ EXT_NAME = "deepseekrpc_cuda"
 CUDA_SOURCES = ["legacy_ops.cu", "topk.cu", "topk_noalloc.cu", "indexer_decode.cu", "indexer_prefill.cu",
                 "candidates.cu", "mla_decode.cu", "append.cu", "decode_step.cu", "p2p.cu", "pool.cu"]
 HOST_SOURCES = ["host_common.cpp"]
-HEADERS = ["common.cuh", "host_common.h"]
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
@@ -65,7 +64,8 @@ def build_library(force: bool = False, verbose: bool = False, ptxas_verbose: boo
     home = cuda_home()
     nvcc = home / "bin" / "nvcc"
     BUILD.mkdir(exist_ok=True)
-    headers = [CSRC / h for h in HEADERS] + [ROOT / "include" / "dsr_b200.h"]
+    # every source includes some of the headers: any header change rebuilds everything
+    headers = sorted(CSRC.glob("*.cuh")) + sorted(CSRC.glob("*.h")) + [ROOT / "include" / "dsr_b200.h"]
     common = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC,-O3", "--expt-relaxed-constexpr",
               "-I", str(ROOT / "include")]
     jobs = []

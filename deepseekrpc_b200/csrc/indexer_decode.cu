@@ -102,8 +102,7 @@ __device__ __forceinline__ int find_row(const int* prefix, int batch, int t) {
 // ---------------------------------------------------------------------------
 constexpr int kSelThreads = 320;  // the indexer CTA: every warp joins the selection
 constexpr int kSelPer = 4;        // entries per thread per compaction chunk
-constexpr int kSelScoreLd = 8;    // float4 score loads in flight per thread
-constexpr int kSelListLd = 16;    // candidate-list loads in flight per thread
+constexpr int kSelScoreLd = 32;   // float4 score groups staged per thread and chunk (at most)
 constexpr uint32_t kSelPairwise = 256;  // sub-bin keys ranked pairwise (more: one more radix level)
 
 __device__ __forceinline__ void select_range(const PoolAddr& pa, const int* prefix, const int* vis_s,
@@ -123,26 +122,23 @@ __device__ __forceinline__ void select_range(const PoolAddr& pa, const int* pref
   p_hi = pos0 + valid;
 }
 
-// 2048 histogram words of global memory into shared memory, every load in flight at once
-__device__ __forceinline__ void load_hist(uint32_t* dst, const uint32_t* src) {
-  constexpr int kPerT = (kSelBins + kSelThreads - 1) / kSelThreads;
-  uint32_t hv[kPerT];
-#pragma unroll
-  for (int j = 0; j < kPerT; ++j) {
-    const int i = threadIdx.x + j * kSelThreads;
-    hv[j] = i < kSelBins ? __ldcg(src + i) : 0u;
-  }
-#pragma unroll
-  for (int j = 0; j < kPerT; ++j) {
-    const int i = threadIdx.x + j * kSelThreads;
-    if (i < kSelBins) dst[i] = hv[j];
-  }
+// 2048 histogram words of global memory into shared memory by 16-byte async
+// copies (complete after cp_async_wait_all + __syncthreads)
+__device__ __forceinline__ void async_hist(uint32_t* dst, const uint32_t* src) {
+#pragma unroll 1
+  for (int i = threadIdx.x; i < kSelBins / 4; i += kSelThreads) cp_async16(smem_u32(dst + 4 * i), src + 4 * i);
+}
+
+// keys[0, n) (16-byte aligned ends; an odd n copies one key past the end) of
+// global memory into shared memory by 16-byte async copies
+__device__ __forceinline__ void async_keys(uint64_t* dst, const uint64_t* src, uint32_t n) {
+#pragma unroll 1
+  for (uint32_t i = threadIdx.x; 2 * i < n; i += kSelThreads) cp_async16(smem_u32(dst + 2 * i), src + 2 * i);
 }
 
 // f(key) for every key of the shared-memory list lst[0, L): every thread takes a
 // run of consecutive keys (an odd count: the 8-byte loads of a half warp fall on
-// distinct banks, and the lanes of a warp hold keys from far-apart places of the
-// list, so their bitmap atomics rarely meet), four loads in flight.
+// distinct banks), four loads in flight.
 template <typename F>
 __device__ __forceinline__ void list_runs(const uint64_t* lst, uint32_t L, F f) {
   constexpr uint32_t T = kSelThreads;
@@ -159,103 +155,182 @@ __device__ __forceinline__ void list_runs(const uint64_t* lst, uint32_t L, F f) 
   }
 }
 
-// The finisher's ordered output of row b: the list's blocks (lst in shared
-// memory, block i of the row's CTA i at blk_base[i], blk_n[i] keys, in position
-// order) walked in CTA order in pieces of at most 32 keys; every thread takes a
-// run of consecutive pieces.  One pass counts the keys >= K* of its pieces, a
-// block scan gives its output offset, a second pass writes the ids.  With
-// k <= 2048 the ids gather in `stage` (2048 words) and leave in one coalesced
-// copy, the scores read back from the row.  `pc` holds nblk + 1 words.
-__device__ void write_blocks(const SelectArgs& a, int b, const float* srow, const uint64_t* lst,
-                             const uint32_t* blk_base, const uint32_t* blk_n, uint32_t* pc, uint32_t nblk,
-                             uint64_t kstar, uint32_t* stage, uint32_t* scratch) {
+// The keys >= K* of the position-ordered shared-memory run keys[0, n), in
+// order, to output slots [off, ...) of row b: every thread takes a run of
+// consecutive keys (list_runs), one block scan gives its slot.  With k <= 2048
+// the ids gather in `stage` (2048 words) and leave in one coalesced copy, the
+// scores read back from the row.
+__device__ void write_selected(const SelectArgs& a, int b, const float* srow, const uint64_t* keys, uint32_t n,
+                               uint64_t kstar, uint32_t off, uint32_t* stage, uint32_t* scratch) {
   constexpr int T = kSelThreads;
   const int tid = threadIdx.x;
-  const int k = a.k;
-  __builtin_assume(__isShared(lst));
-  __builtin_assume(__isShared(blk_base));
-  __builtin_assume(__isShared(blk_n));
-  __builtin_assume(__isShared(pc));
+  const uint32_t k = uint32_t(a.k);
+  __builtin_assume(__isShared(keys));
   __builtin_assume(__isShared(stage));
   __builtin_assume(__isShared(scratch));
   int32_t* orow = a.out_ids + int64_t(b) * k;
   float* oscore = a.out_scores != nullptr ? a.out_scores + int64_t(b) * k : nullptr;
-  const bool staged = k <= kSelBins;
-  // pieces per block, scanned in CTA order (nblk <= the grid <= T)
-  uint32_t npieces;
-  const uint32_t mine = uint32_t(tid) < nblk ? (blk_n[tid] + 31u) >> 5 : 0u;
-  const uint32_t first = sel_excl_scan<T>(mine, npieces, scratch);
-  if (uint32_t(tid) <= nblk) pc[tid] = uint32_t(tid) < nblk ? first : npieces;
-  __syncthreads();
-  const uint32_t ipt = (npieces + T - 1) / T;
-  const uint32_t j0 = min(npieces, tid * ipt), j1 = min(npieces, j0 + ipt);
-  // the block of piece j0: the last block starting at or before it
-  uint32_t blk = 0;
-  if (j0 < j1) {
-    uint32_t lo = 0, hi = nblk - 1;
-    while (lo < hi) {
-      const uint32_t mid = (lo + hi + 1) >> 1;
-      if (pc[mid] <= j0) lo = mid;
-      else hi = mid - 1;
-    }
-    blk = lo;
-  }
-  // visits the keys of this thread's pieces in order: f(key)
-  auto walk = [&](auto f) {
-    uint32_t i = blk;
-#pragma unroll 1
-    for (uint32_t j = j0; j < j1; ++j) {
-      while (pc[i + 1] <= j) ++i;  // empty blocks have no pieces
-      const uint32_t e0 = blk_base[i] + ((j - pc[i]) << 5);
-      const uint32_t e1 = blk_base[i] + min(blk_n[i], ((j - pc[i]) << 5) + 32u);
-#pragma unroll 1
-      for (uint32_t e = e0; e < e1; e += 4) {
-        uint64_t kq[4];
-#pragma unroll
-        for (int u = 0; u < 4; ++u) kq[u] = e + u < e1 ? lst[e + u] : 0ull;
-#pragma unroll
-        for (int u = 0; u < 4; ++u)
-          if (e + u < e1) f(kq[u]);
-      }
-    }
-  };
+  const bool staged = k <= uint32_t(kSelBins);
   uint32_t cnt = 0;
-  walk([&](uint64_t key) { cnt += key >= kstar ? 1u : 0u; });
+  list_runs(keys, n, [&](uint64_t key) { cnt += key >= kstar ? 1u : 0u; });
   uint32_t found;
   uint32_t s = sel_excl_scan<T>(cnt, found, scratch);
-  walk([&](uint64_t key) {
+  list_runs(keys, n, [&](uint64_t key) {
     if (key < kstar) return;
-    if (s < uint32_t(k)) {  // more only after a CTA gave up (its candidates are missing)
+    if (off + s < k) {  // more only after a CTA gave up (its candidates are missing)
       if (staged) {
         stage[s] = uint32_t(sel_key_id(key));
       } else {
-        orow[s] = sel_key_id(key);
-        if (oscore != nullptr) oscore[s] = sel_key_score(key);
+        orow[off + s] = sel_key_id(key);
+        if (oscore != nullptr) oscore[off + s] = sel_key_score(key);
       }
     }
     ++s;
   });
   __syncthreads();
   if (staged) {
-    const uint32_t n = min(found, uint32_t(k));
+    const uint32_t m = off < k ? min(found, k - off) : 0u;
 #pragma unroll 1
-    for (uint32_t i = tid; i < n; i += T) orow[i] = int32_t(stage[i]);
+    for (uint32_t i0 = 0; i0 < m; i0 += T * 4) {
+      uint32_t v4[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const uint32_t i = i0 + u * T + tid;
+        v4[u] = i < m ? stage[i] : 0u;
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const uint32_t i = i0 + u * T + tid;
+        if (i < m) orow[off + i] = int32_t(v4[u]);
+      }
+    }
     if (oscore != nullptr)
 #pragma unroll 1
-      for (uint32_t i0 = 0; i0 < n; i0 += T * 8) {
+      for (uint32_t i0 = 0; i0 < m; i0 += T * 8) {
         float sc[8];
 #pragma unroll
         for (int u = 0; u < 8; ++u) {
           const uint32_t i = i0 + u * T + tid;
-          if (i < n) sc[u] = __ldcg(srow + (int64_t(int32_t(stage[i])) - a.id_base));
+          if (i < m) sc[u] = __ldcg(srow + (int64_t(int32_t(stage[i])) - a.id_base));
         }
 #pragma unroll
         for (int u = 0; u < 8; ++u) {
           const uint32_t i = i0 + u * T + tid;
-          if (i < n) oscore[i] = key_score(sel_rank_u(__float_as_uint(sc[u])));
+          if (i < m) oscore[off + i] = key_score(sel_rank_u(__float_as_uint(sc[u])));
         }
       }
+    __syncthreads();  // the stage is free again
   }
+}
+
+// The row's last CTA for a row without overflow (select.cuh, step 3): L keys in
+// the row's list, nblk appended blocks (their records in arrival order), the
+// row held by nctas CTAs.  Shared memory: the list in position order, the list
+// in arrival order when both fit, then three tables per CTA rank.
+//   1. records, digit-1 histogram and (when both fit) the list, all in flight
+//      (16-byte async copies); without room for both the list comes in step 3,
+//      from global;
+//   2. each rank's block length and base, their offsets in CTA order;
+//   3. the list in position order: one warp copies each rank's block from
+//      rbase[r] of the arrival order to roff[r];
+//   4. K*: the sub-bin (b0, b1) holding it from the digit-1 histogram; its
+//      lower edge when the whole sub-bin is selected, otherwise the need1-th
+//      largest of its keys (ranked pairwise when few, else by the next digits);
+//   5. one ordered compaction of the keys >= K* to the output.
+__device__ void finish_row(const SelectArgs& a, int b, const float* srow, uint32_t L, uint32_t nblk,
+                           uint32_t nctas, uint32_t b0, uint32_t above, uint8_t* work, size_t work_bytes,
+                           uint32_t* hist, uint32_t* scratch) {
+  constexpr int T = kSelThreads;
+  const int tid = threadIdx.x;
+  __builtin_assume(__isShared(work));
+  __builtin_assume(__isShared(hist));
+  __builtin_assume(__isShared(scratch));
+  uint32_t* ncand = scratch + 42;
+  const size_t lbytes = (size_t(L) * 8 + 15) & ~size_t(15);
+  const size_t tables = size_t(3 * gridDim.x + 1) * 4;
+  const bool both = 2 * lbytes + tables <= work_bytes;
+  uint64_t* ord = reinterpret_cast<uint64_t*>(work);
+  uint64_t* arr = reinterpret_cast<uint64_t*>(work + lbytes);
+  uint32_t* rn = reinterpret_cast<uint32_t*>(work + (both ? 2 : 1) * lbytes);
+  uint32_t* rbase = rn + gridDim.x;
+  uint32_t* roff = rbase + gridDim.x;
+  const uint64_t* lrow = a.list + int64_t(b) * a.list_cap;
+
+  // 1.
+#pragma unroll 1
+  for (uint32_t r = tid; r < nctas; r += T) rn[r] = 0u;  // ranks that appended nothing
+  uint4 rec = make_uint4(0u, 0u, ~0u, 0u);
+  if (uint32_t(tid) < nblk) rec = __ldcg(a.blocks + int64_t(b) * gridDim.x + tid);
+  if (both) async_keys(arr, lrow, L);
+  async_hist(hist, a.hist1 + int64_t(b) * kSelBins);
+  cp_async_wait_all();
+  __syncthreads();
+  // 2. (a record past the list only after a CTA gave up)
+  if (rec.z < nctas) {
+    const uint32_t bb = min(rec.x, L);
+    rn[rec.z] = min(rec.y, L - bb);
+    rbase[rec.z] = bb;
+  }
+  __syncthreads();
+  uint32_t Lv;
+  const uint32_t off = sel_excl_scan<T>(uint32_t(tid) < nctas ? rn[tid] : 0u, Lv, scratch);
+  if (uint32_t(tid) < nctas) roff[tid] = off;
+  __syncthreads();
+  Lv = min(Lv, L);
+  // 3. one warp per rank, lanes on consecutive keys (from global without room for both)
+  const int lane = tid & 31, warp = tid >> 5;
+#pragma unroll 1
+  for (uint32_t r = warp; r < nctas; r += T / 32) {
+    const uint32_t n = rn[r], src = rbase[r], dst = roff[r];
+#pragma unroll 1
+    for (uint32_t j = lane; j < n; j += 32) ord[dst + j] = both ? arr[src + j] : __ldcg(lrow + src + j);
+  }
+  __syncthreads();
+  // 4.
+  const uint32_t need0 = uint32_t(a.k) - above;
+  uint32_t above1;
+  const uint32_t b1 = sel_find_bin<T>(hist, kSelBins, need0, above1, scratch) & uint32_t(kSelBins - 1);
+  const uint32_t need1 = need0 - above1, in_sub = hist[b1];
+  const uint64_t sub = (uint64_t(b0) << kSelShift[0]) | (uint64_t(b1) << kSelShift[1]);
+  __syncthreads();
+  uint64_t kstar = sub;
+  if (in_sub != need1) {
+    if (in_sub > kSelPairwise) {
+      kstar = sel_kstar<T>([&](int64_t i) { return ord[i]; }, Lv, sub, need1, 2, hist, scratch);
+    } else {
+      uint64_t* subk = reinterpret_cast<uint64_t*>(hist);
+      if (tid == 0) {
+        *ncand = 0u;
+        scratch[46] = uint32_t(sub);  // K* stays the edge if the ranking finds none
+        scratch[47] = uint32_t(sub >> 32);
+      }
+      __syncthreads();
+      list_runs(ord, Lv, [&](uint64_t key) {
+        if ((key >> kSelShift[1]) == (sub >> kSelShift[1])) {
+          const uint32_t at = atomicAdd(ncand, 1u);
+          if (at < kSelPairwise) subk[at] = key;
+        }
+      });
+      __syncthreads();
+      const uint32_t c = min(*ncand, kSelPairwise);
+#pragma unroll 1
+      for (uint32_t i = tid; i < c; i += T) {
+        const uint64_t key = subk[i];
+        uint32_t higher = 0;
+#pragma unroll 1
+        for (uint32_t j = 0; j < c; ++j) higher += subk[j] > key ? 1u : 0u;
+        if (higher == need1 - 1) {
+          scratch[46] = uint32_t(key);
+          scratch[47] = uint32_t(key >> 32);
+        }
+      }
+      __syncthreads();
+      kstar = (uint64_t(scratch[47]) << 32) | scratch[46];
+      __syncthreads();
+    }
+  }
+  // 5.
+  write_selected(a, b, srow, ord, Lv, kstar, 0u, hist, scratch);
 }
 
 __device__ void select_phase(const SelectArgs& a, const float* __restrict__ scores, int64_t score_stride,
@@ -271,7 +346,6 @@ __device__ void select_phase(const SelectArgs& a, const float* __restrict__ scor
   __builtin_assume(__isShared(hist));
   __builtin_assume(__isShared(scratch));
   uint32_t* grp = scratch + 64;
-  uint32_t* ncand = scratch + 42;
   const int rb0 = t_lo < t_hi ? find_row(prefix, batch, t_lo) : 0;
   const int rb1 = t_lo < t_hi ? find_row(prefix, batch, t_hi - 1) : -1;
   const int total = prefix[batch];
@@ -329,7 +403,7 @@ __device__ void select_phase(const SelectArgs& a, const float* __restrict__ scor
   // threshold-bin entries counted into the row's digit-1 histogram; then the
   // CTA counts itself done with the row, and the row's last CTA finishes it.
   // Shared memory: the candidate buffer (list_cap keys), then the staging of
-  // the scores (each thread's loads all in flight, then read back by rolled loops)
+  // the scores (16-byte async copies, read back by rolled loops)
   uint64_t* buf = reinterpret_cast<uint64_t*>(work);
   float4* stage = reinterpret_cast<float4*>(work + size_t(a.list_cap) * 8);
   const int nld = int(min(size_t(kSelScoreLd), (work_bytes - size_t(a.list_cap) * 8) / (T * 16)));  // >= 1 (host check)
@@ -343,38 +417,32 @@ __device__ void select_phase(const SelectArgs& a, const float* __restrict__ scor
     const float* srow = scores + int64_t(b) * score_stride;
     uint32_t b0 = 0, above = 0;
     bool overflow = false;
-    const bool appended = live;  // (an overflowing row appends an empty block)
+    // this CTA's rank among the row's CTAs (with fewer tiles than CTAs, one tile each)
+    const uint32_t rank = total < int(gridDim.x)
+                              ? uint32_t(t_lo - prefix[b])
+                              : uint32_t(blockIdx.x) -
+                                    uint32_t(((uint64_t(prefix[b]) + 1) * gridDim.x - 1) / uint64_t(total));
     if (live) {
       // the range's scores (aligned float4 groups covering [p_lo, p_hi); the row's
-      // stride is a multiple of 64 floats) go in flight before the histogram loads
+      // stride is a multiple of 64 floats) and the digit-0 histogram, all in flight
       const int a0 = p_lo & ~3;
       const int n4 = (((p_hi + 3) & ~3) - a0) >> 2;
       const float4* s4 = reinterpret_cast<const float4*>(srow + a0);
-      float4 x[kSelScoreLd];
-      auto load = [&](int i0) {
-#pragma unroll
-        for (int j = 0; j < kSelScoreLd; ++j) {
+      auto stage_chunk = [&](int i0) {  // staged entry q - i0 = j * T + tid
+#pragma unroll 1
+        for (int j = 0; j < nld; ++j) {
           const int q = i0 + j * T + tid;
-          if (j < nld && q < n4) x[j] = __ldcg(s4 + q);
+          if (q < n4) cp_async16(smem_u32(stage + j * T + tid), s4 + q);
         }
       };
-      auto store = [&](int i0) {  // a thread reads back only its own staged loads
-#pragma unroll
-        for (int j = 0; j < kSelScoreLd; ++j) {
-          const int q = i0 + j * T + tid;
-          if (j < nld && q < n4) stage[j * T + tid] = x[j];
-        }
-      };
-      load(0);
-      load_hist(hist, a.hist + int64_t(b) * kSelBins);
-      store(0);
-      if (tid == 0) *ncand = 0u;
+      stage_chunk(0);
+      async_hist(hist, a.hist + int64_t(b) * kSelBins);
+      cp_async_wait_all();
       __syncthreads();
       b0 = sel_find_bin<T>(hist, kSelBins, uint32_t(k), above, scratch) & uint32_t(kSelBins - 1);
       // massive ties: more threshold-bin entries than the list has room for; the
       // row's last CTA resolves the row from its scores
       overflow = hist[b0] > uint32_t(a.list_cap - k);
-      if (overflow && tid == 0) a.meta[int64_t(b) * gridDim.x + blockIdx.x] = make_uint2(0u, 0u);
       if (!overflow) {
         // digit 0 >= b0 <=> score >= the lowest score of bin b0 (the key map is
         // monotone; NaN ranks above +inf); bins 0-3 decode to NaN patterns and
@@ -389,8 +457,8 @@ __device__ void select_phase(const SelectArgs& a, const float* __restrict__ scor
         for (int i0 = 0; i0 < n4; i0 += T * nld) {
           const int cn4 = min(T * nld, n4 - i0);
           if (i0 > 0) {
-            load(i0);
-            store(i0);
+            stage_chunk(i0);
+            cp_async_wait_all();
           }
           __syncthreads();
           const int m = ((cn4 + T - 1) / T) | 1;
@@ -425,29 +493,38 @@ __device__ void select_phase(const SelectArgs& a, const float* __restrict__ scor
           nbuf += tot;
           __syncthreads();  // the chunk is read before the next one is staged
         }
+        // the block: one atomic gives its base and arrival number, its record goes under that number
         const uint32_t n = min(nbuf, uint32_t(a.list_cap));
-        if (tid == 0) scratch[40] = n ? uint32_t(atomicAdd(state + b, (unsigned long long)n)) : 0u;
+        if (tid == 0 && n != 0u) {
+          const unsigned long long old = atomicAdd(state + b, (1ull << 32) | n);
+          scratch[40] = uint32_t(old);
+          scratch[41] = uint32_t(old >> 32) & 0xffffu;
+        }
         __syncthreads();
-        const uint32_t base = scratch[40];
-        uint64_t* lrow = a.list + int64_t(b) * a.list_cap;
+        if (n != 0u) {
+          const uint32_t base = scratch[40], seq = scratch[41];
+          uint64_t* lrow = a.list + int64_t(b) * a.list_cap;
 #pragma unroll 1
-        for (uint32_t i = tid; i < n; i += T)
-          if (base + i < uint32_t(a.list_cap)) lrow[base + i] = buf[i];
-        if (tid == 0) a.meta[int64_t(b) * gridDim.x + blockIdx.x] = make_uint2(base, n);
+          for (uint32_t i = tid; i < n; i += T)
+            if (base + i < uint32_t(a.list_cap)) lrow[base + i] = buf[i];
+          if (tid == 0 && seq < gridDim.x) a.blocks[int64_t(b) * gridDim.x + seq] = make_uint4(base, n, rank, 0u);
+        }
       }
     }
-    if (!appended && tid == 0) a.meta[int64_t(b) * gridDim.x + blockIdx.x] = make_uint2(0u, 0u);
     // count in (live or not): the last CTA of the row sees every other CTA's
-    // candidates, digit-1 counts and histogram reads complete, and the list's length
+    // blocks, digit-1 counts and histogram reads complete, the list's length and
+    // the number of blocks
     __syncthreads();
     if (tid == 0) {
-      const unsigned long long old = atom_add_acq_rel(state + b, 1ull << 32);
-      scratch[43] = uint32_t(old >> 32) == nctas - 1 ? 1u : 0u;
+      const unsigned long long old = atom_add_acq_rel(state + b, 1ull << 48);
+      scratch[43] = uint32_t(old >> 48) == nctas - 1 ? 1u : 0u;
       scratch[40] = uint32_t(old);
+      scratch[41] = uint32_t(old >> 32) & 0xffffu;
     }
     __syncthreads();
-    if (!scratch[43]) continue;
+    if (scratch[43] == 0u) continue;
     const uint32_t L = min(scratch[40], uint32_t(a.list_cap));
+    const uint32_t nblk = min(scratch[41], uint32_t(gridDim.x));
     __syncthreads();
 
     if (live && overflow) {
@@ -458,7 +535,7 @@ __device__ void select_phase(const SelectArgs& a, const float* __restrict__ scor
       auto row_key = [&](int64_t i) -> uint64_t {
         return sel_key(sel_rank_u(__float_as_uint(__ldcg(srow + i))), id0 + i);
       };
-      const uint64_t kstar =
+      const uint64_t ks =
           sel_kstar<T>(row_key, v, uint64_t(b0) << kSelShift[0], uint32_t(k) - above, 1, hist, scratch);
       uint32_t written = 0;
 #pragma unroll 1
@@ -469,7 +546,7 @@ __device__ void select_phase(const SelectArgs& a, const float* __restrict__ scor
         for (int j = 0; j < kSelPer; ++j) {
           const int i = c0 + j * T + tid;
           keys[j] = i < v ? row_key(i) : 0ull;
-          keep |= uint32_t(i < v && keys[j] >= kstar) << j;
+          keep |= uint32_t(i < v && keys[j] >= ks) << j;
         }
         written += sel_compact<T, kSelPer>(keep, written, grp, scratch, [&](uint32_t slot, int j) {
           if (slot >= uint32_t(k)) return;
@@ -478,97 +555,7 @@ __device__ void select_phase(const SelectArgs& a, const float* __restrict__ scor
         });
       }
     } else if (live) {
-      // the list into shared memory and the digit-1 histogram, all loads in flight
-      uint64_t* lst = reinterpret_cast<uint64_t*>(work);
-      const uint64_t* lrow = a.list + int64_t(b) * a.list_cap;
-      uint64_t kk[kSelListLd];
-      auto load = [&](uint32_t j0) {
-#pragma unroll
-        for (int j = 0; j < kSelListLd; ++j) {
-          const uint32_t i = j0 + j * T + tid;
-          if (i < L) kk[j] = __ldcg(lrow + i);
-        }
-      };
-      auto store = [&](uint32_t j0) {
-#pragma unroll
-        for (int j = 0; j < kSelListLd; ++j) {
-          const uint32_t i = j0 + j * T + tid;
-          if (i < L) lst[i] = kk[j];
-        }
-      };
-      // the row's CTAs in CTA order and their blocks (shared memory after the list)
-      const size_t lbytes = (size_t(L) * 8 + 15) & ~size_t(15);
-      uint32_t* blk_base = reinterpret_cast<uint32_t*>(work + lbytes);
-      uint32_t* blk_n = blk_base + gridDim.x;
-      uint32_t* pc = blk_n + gridDim.x;
-      uint2 m = make_uint2(0u, 0u);
-      if (uint32_t(tid) < nctas) {
-        const uint64_t G = gridDim.x;
-        const uint64_t t = uint64_t(prefix[b]) + (total >= int(G) ? 0u : uint32_t(tid));
-        // the owner of tile t (CTA c holds tiles [floor(total*c/G), floor(total*(c+1)/G)))
-        const uint64_t c = ((t + 1) * G - 1) / uint64_t(total) + (total >= int(G) ? uint32_t(tid) : 0u);
-        m = __ldcg(a.meta + int64_t(b) * G + int64_t(c));
-      }
-      load(0);
-      load_hist(hist, a.hist1 + int64_t(b) * kSelBins);
-      store(0);
-      if (uint32_t(tid) < nctas) {  // a block past the list only after a CTA gave up
-        const uint32_t bb = min(m.x, L);
-        blk_base[tid] = bb;
-        blk_n[tid] = min(m.y, L - bb);
-      }
-#pragma unroll 1
-      for (uint32_t j0 = T * kSelListLd; j0 < L; j0 += T * kSelListLd) {
-        load(j0);
-        store(j0);
-      }
-      __syncthreads();
-      // the sub-bin (b0, b1) holding K*: with the whole sub-bin selected K* is its
-      // lower edge, otherwise the need1-th largest of its keys (ranked pairwise
-      // when few, else by the next digits)
-      const uint32_t need0 = uint32_t(k) - above;
-      uint32_t above1;
-      const uint32_t b1 = sel_find_bin<T>(hist, kSelBins, need0, above1, scratch) & uint32_t(kSelBins - 1);
-      const uint32_t need1 = need0 - above1, in_sub = hist[b1];
-      const uint64_t sub = (uint64_t(b0) << kSelShift[0]) | (uint64_t(b1) << kSelShift[1]);
-      __syncthreads();
-      uint64_t kstar = sub;
-      if (in_sub != need1) {
-        if (in_sub <= kSelPairwise) {
-          uint64_t* subk = reinterpret_cast<uint64_t*>(hist);
-          if (tid == 0) {
-            *ncand = 0u;
-            scratch[46] = uint32_t(sub);  // K* stays the edge if the ranking finds none
-            scratch[47] = uint32_t(sub >> 32);
-          }
-          __syncthreads();
-          list_runs(lst, L, [&](uint64_t key) {
-            if ((key >> kSelShift[1]) == (sub >> kSelShift[1])) {
-              const uint32_t at = atomicAdd(ncand, 1u);
-              if (at < kSelPairwise) subk[at] = key;
-            }
-          });
-          __syncthreads();
-          const uint32_t c = min(*ncand, kSelPairwise);
-#pragma unroll 1
-          for (uint32_t i = tid; i < c; i += T) {
-            const uint64_t key = subk[i];
-            uint32_t higher = 0;
-#pragma unroll 1
-            for (uint32_t j = 0; j < c; ++j) higher += subk[j] > key ? 1u : 0u;
-            if (higher == need1 - 1) {
-              scratch[46] = uint32_t(key);
-              scratch[47] = uint32_t(key >> 32);
-            }
-          }
-          __syncthreads();
-          kstar = (uint64_t(scratch[47]) << 32) | scratch[46];
-        } else {
-          kstar = sel_kstar<T>([&](int64_t i) { return lst[i]; }, L, sub, need1, 2, hist, scratch);
-        }
-      }
-      // the ids in position order; they gather in `hist`
-      write_blocks(a, b, srow, lst, blk_base, blk_n, pc, nctas, kstar, hist, scratch);
+      finish_row(a, b, srow, L, nblk, nctas, b0, above, work, work_bytes, hist, scratch);
     }
     // the row's workspace back to zero for the next launch
 #pragma unroll 1
@@ -1080,7 +1067,7 @@ int select_args(SelectArgs* a, void* workspace, int64_t batch, int64_t k, int64_
   a->hist1 = reinterpret_cast<uint32_t*>(base + L.hist1);
   a->ctl = reinterpret_cast<uint32_t*>(base + L.ctl);
   a->row_state = reinterpret_cast<unsigned long long*>(base + L.state);
-  a->meta = reinterpret_cast<uint2*>(base + L.meta);
+  a->blocks = reinterpret_cast<uint4*>(base + L.blocks);
   a->list = reinterpret_cast<uint64_t*>(base + L.list);
   a->list_cap = int(L.cap);
   return DSR_OK;

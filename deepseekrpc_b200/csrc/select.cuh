@@ -15,16 +15,17 @@
 //      row's digit-0 histogram, and one grid barrier completes the histograms;
 //   2. every CTA finds each of its rows' threshold bin b0, appends its
 //      candidates (digit 0 >= b0), in position order, to the row's candidate
-//      list as one block (recorded in meta), counts the digit 1 of its
-//      threshold-bin entries into the row's digit-1 histogram, and counts itself
-//      done with the row (one 64-bit atomic that also returns the list's length);
+//      list as one block (one atomic gives its base and arrival number; a
+//      record {base, length, CTA rank} goes under that number), counts the
+//      digit 1 of its threshold-bin entries into the row's digit-1 histogram,
+//      and counts itself done with the row (one 64-bit atomic that also returns
+//      the list's length and the number of blocks);
 //   3. the row's last CTA to finish step 2 (no waiting: the others have left the
-//      row) reads the digit-1 histogram, the list and the blocks, finds K* (the
-//      whole sub-bin of digit 1 selected, or the rank among its few keys), and
-//      walks the blocks in CTA order -- which is position order -- in pieces of
-//      at most 32 keys: one pass counts each piece's keys >= K*, a scan gives the
-//      pieces their output offsets, a second pass writes the ids (and scores);
-//      then it clears the row's workspace.
+//      row) loads the list, the block records and the digit-1 histogram (one
+//      round trip), places the blocks in CTA order -- which is position order --
+//      in shared memory, finds K* (the whole sub-bin of digit 1 selected, or
+//      the rank among its few keys), writes the ids (and scores) of the keys
+//      >= K* by one ordered compaction, and clears the row's workspace.
 // A row whose threshold bin holds more entries than its list has room for
 // (massive ties) is resolved by its last CTA from the row's scores.
 //
@@ -53,17 +54,18 @@ struct SelectArgs {
   uint32_t* hist;      // [batch][2048] digit-0 histograms, built by the indexer epilogue
   uint32_t* hist1;     // [batch][2048] digit-1 histograms of each row's threshold-bin entries
   uint32_t* ctl;       // [64]: [0] barrier arrivals, [1] exits
-  unsigned long long* row_state;  // [batch]: (CTAs done with the row << 32) | candidate-list length
+  // [batch]: (CTAs done with the row << 48) | (blocks appended << 32) | candidate-list length
+  unsigned long long* row_state;
   uint64_t* list;      // [batch][list_cap] candidate rank keys, one position-ordered block per CTA
   int list_cap;
-  uint2* meta;         // [batch][grid]: per row and CTA {block base, block length}
+  uint4* blocks;       // [batch][grid]: the row's i-th appended block {list base, length, CTA rank, -}
 };
 
-// Workspace: hist | hist1 | ctl | row_state | list | meta.  Everything before
+// Workspace: hist | hist1 | ctl | row_state | list | blocks.  Everything before
 // the list must be zero before the first launch; every completed launch leaves
-// it zero again (list and meta need no clearing).
+// it zero again (list and blocks need no clearing).
 struct SelectLayout {
-  size_t hist, hist1, ctl, state, list, meta, total;
+  size_t hist, hist1, ctl, state, list, blocks, total;
   int64_t cap;
   __host__ __device__ SelectLayout(int64_t batch, int64_t k, int64_t grid) {
     cap = (kSelBinCap + k + 1) & ~int64_t(1);
@@ -72,8 +74,8 @@ struct SelectLayout {
     ctl = hist1 + size_t(batch) * kSelBins * 4;
     state = ctl + 256;
     list = state + ((size_t(batch) * 8 + 255) / 256) * 256;
-    meta = list + size_t(batch) * size_t(cap) * 8;
-    total = meta + size_t(batch) * size_t(grid) * 8;
+    blocks = list + size_t(batch) * size_t(cap) * 8;
+    total = blocks + size_t(batch) * size_t(grid) * 16;
   }
   // leading bytes that must be zero at launch
   __host__ __device__ size_t zeroed() const { return list; }
