@@ -341,4 +341,40 @@ __device__ __forceinline__ void pdl_launch_dependents() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
+// The MLA query of the same decode step, FP32 [batch, heads, 576] -> BF16 in the
+// shared-memory image the sparse MLA kernel contracts against: per (sequence,
+// 64-head group) nine 64-column blocks of group_heads rows x 128 B, 128-byte
+// swizzled (dsr_mla_query_image_bytes()).  This CTA converts its share.
+__device__ __forceinline__ void mla_query_image(const float* __restrict__ q, uint16_t* __restrict__ img,
+                                                int batch, int heads, int tid, int nthreads) {
+  const int hg = heads < 64 ? heads : 64;
+  const int64_t total = int64_t(batch) * heads * (DSR_KV_DIM / 4);  // float4 units
+  const int64_t lo = total * blockIdx.x / gridDim.x, hi = total * (blockIdx.x + 1) / gridDim.x;
+  constexpr int kBatch = 8;
+  for (int64_t i0 = lo; i0 < hi; i0 += int64_t(nthreads) * kBatch) {
+    float4 v[kBatch];
+#pragma unroll
+    for (int j = 0; j < kBatch; ++j) {
+      const int64_t i = i0 + int64_t(j) * nthreads + tid;
+      if (i < hi) v[j] = __ldg(reinterpret_cast<const float4*>(q) + i);
+    }
+#pragma unroll
+    for (int j = 0; j < kBatch; ++j) {
+      const int64_t i = i0 + int64_t(j) * nthreads + tid;
+      if (i < hi) {
+        const int64_t bh = i / (DSR_KV_DIM / 4);
+        const int d = int(i % (DSR_KV_DIM / 4)) * 4;
+        const int h = int(bh % heads);
+        const int64_t g = (bh / heads) * (heads / hg) + h / hg;  // (sequence, head group)
+        uint8_t* base = reinterpret_cast<uint8_t*>(img) + (g * (DSR_KV_DIM / 64) + d / 64) * hg * 128;
+        const uint32_t w0 = __bfloat16_as_ushort(__float2bfloat16_rn(v[j].x)) |
+                            (uint32_t(__bfloat16_as_ushort(__float2bfloat16_rn(v[j].y))) << 16);
+        const uint32_t w1 = __bfloat16_as_ushort(__float2bfloat16_rn(v[j].z)) |
+                            (uint32_t(__bfloat16_as_ushort(__float2bfloat16_rn(v[j].w))) << 16);
+        *reinterpret_cast<uint2*>(base + sw128_offset(h % hg, d & 63)) = make_uint2(w0, w1);
+      }
+    }
+  }
+}
+
 }  // namespace dsr

@@ -102,7 +102,8 @@ __device__ __forceinline__ int find_row(const int* prefix, int batch, int t) {
 // ---------------------------------------------------------------------------
 constexpr int kSelThreads = 320;  // the indexer CTA: every warp joins the selection
 constexpr int kSelPer = 4;        // entries per thread per compaction chunk
-constexpr int kSelScoreLd = 32;   // float4 score groups staged per thread and chunk (at most)
+constexpr int kSelScoreLd = 15;   // float4 score groups staged per thread and chunk (at most)
+static_assert(4 * kSelScoreLd <= 64, "a thread's candidate mask (4 bits per group) must fit 64 bits");
 constexpr uint32_t kSelPairwise = 256;  // sub-bin keys ranked pairwise (more: one more radix level)
 
 __device__ __forceinline__ void select_range(const PoolAddr& pa, const int* prefix, const int* vis_s,
@@ -592,42 +593,6 @@ __device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, uint32_t* r) {
   } else {
 #pragma unroll
     for (int j = 0; j < C; j += 16) tmem_ld16(taddr + j, *reinterpret_cast<uint32_t(*)[16]>(r + j));
-  }
-}
-
-// The MLA query of the same decode step, FP32 [batch, heads, 576] -> BF16 in the
-// shared-memory image the sparse MLA kernel contracts against: per (sequence,
-// 64-head group) nine 64-column blocks of group_heads rows x 128 B, 128-byte
-// swizzled (dsr_mla_query_image_bytes()).  This CTA converts its share.
-__device__ __forceinline__ void mla_query_image(const float* __restrict__ q, uint16_t* __restrict__ img,
-                                                int batch, int heads, int tid, int nthreads) {
-  const int hg = heads < 64 ? heads : 64;
-  const int64_t total = int64_t(batch) * heads * (DSR_KV_DIM / 4);  // float4 units
-  const int64_t lo = total * blockIdx.x / gridDim.x, hi = total * (blockIdx.x + 1) / gridDim.x;
-  constexpr int kBatch = 8;
-  for (int64_t i0 = lo; i0 < hi; i0 += int64_t(nthreads) * kBatch) {
-    float4 v[kBatch];
-#pragma unroll
-    for (int j = 0; j < kBatch; ++j) {
-      const int64_t i = i0 + int64_t(j) * nthreads + tid;
-      if (i < hi) v[j] = __ldg(reinterpret_cast<const float4*>(q) + i);
-    }
-#pragma unroll
-    for (int j = 0; j < kBatch; ++j) {
-      const int64_t i = i0 + int64_t(j) * nthreads + tid;
-      if (i < hi) {
-        const int64_t bh = i / (DSR_KV_DIM / 4);
-        const int d = int(i % (DSR_KV_DIM / 4)) * 4;
-        const int h = int(bh % heads);
-        const int64_t g = (bh / heads) * (heads / hg) + h / hg;  // (sequence, head group)
-        uint8_t* base = reinterpret_cast<uint8_t*>(img) + (g * (DSR_KV_DIM / 64) + d / 64) * hg * 128;
-        const uint32_t w0 = __bfloat16_as_ushort(__float2bfloat16_rn(v[j].x)) |
-                            (uint32_t(__bfloat16_as_ushort(__float2bfloat16_rn(v[j].y))) << 16);
-        const uint32_t w1 = __bfloat16_as_ushort(__float2bfloat16_rn(v[j].z)) |
-                            (uint32_t(__bfloat16_as_ushort(__float2bfloat16_rn(v[j].w))) << 16);
-        *reinterpret_cast<uint2*>(base + sw128_offset(h % hg, d & 63)) = make_uint2(w0, w1);
-      }
-    }
   }
 }
 

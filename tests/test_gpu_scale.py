@@ -60,6 +60,19 @@ def test_config5_sequence_through_the_decode_step(cuda):
     check_sequence(inp, 0, lengths[0], out.cpu().numpy(), topk.cpu().numpy(), scores.cpu().numpy(), cfg.scale)
 
 
+def test_config5_batch_of_four_sequences(cuda):
+    """The benchmarked config-5 step: four 1,048,576-key sequences in one call (every
+    CTA's score range spans about 28,000 positions and some two rows)."""
+    cfg = CONFIGS["cfg5"]
+    inp, lengths = make_decode_inputs(cfg, device="cuda", gen_device="cuda", lengths=[cfg.context] * 4)
+    out, topk, scores, code = c_decode_step(inp, cfg.topk, cfg.scale)
+    assert code == 0
+    t, s = topk.cpu().numpy(), scores.cpu().numpy()
+    for b, n in enumerate(lengths):
+        assert np.array_equal(t[b], oracle.tiled_topk(s[b, :n], cfg.topk)), f"sequence {b}: top-k differs"
+    check_sequence(inp, 3, lengths[3], out.cpu().numpy(), t, s, cfg.scale)
+
+
 def test_config4_prefill_geometry(cuda):
     cached, queries, k = 262144, 4096, 2048
     context = cached + queries
