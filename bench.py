@@ -1,7 +1,7 @@
 """Decode-step benchmark of the B200 attention hot path (indexer -> top-k -> sparse MLA).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
-    python bench.py --profile cfg2|cfg5|prefill Q C|topk-rows R C [--steps S]
+    python bench.py --profile cfg2|cfg5 [B]|prefill Q C|topk-rows R C [--steps S]
 
 Every N reports one workload: batch 4, context 1,048,576 per
 sequence, 64 index heads, top-k 2048, 64 MLA heads over 576-wide rows, SWA 128.
@@ -47,7 +47,9 @@ KERNELS_PER_STEP = 4  # indexer, top-k, sparse MLA, LSE combine
 
 # DRAM bytes per launch of the indexer, read from ncu captures of the same
 # kernel (dram__bytes_read.sum + dram__bytes_write.sum; profiles/indexer_decode_*.md)
-INDEXER_TRAFFIC = {"cfg2": 33826816}
+# ncu DRAM bytes (read + write) per indexer launch (profiles/indexer_decode_cfg2.md):
+# config 2 captured directly; config 5 from a one-sequence capture x 4 sequences
+INDEXER_TRAFFIC = {"cfg2": 33875968, "cfg5": 1115352064}
 
 
 # --------------------------------------------------------------------------- utils
@@ -731,7 +733,8 @@ def run_profile(args):
     if what in ("cfg1", "cfg2", "cfg3", "cfg5"):
         cfg = CONFIGS[what]
         if what == "cfg5":
-            lengths = [cfg.context] * cfg.batch
+            # optional: fewer sequences (a profiler capture small enough to replay)
+            lengths = [cfg.context] * (extra[0] if extra else cfg.batch)
             inp = long_context_inputs(cfg, lengths, dev)
         else:
             inp, lengths = make_decode_inputs(cfg, device=dev, gen_device="cuda")
