@@ -104,6 +104,8 @@ constexpr int kSelThreads = 320;  // the indexer CTA: every warp joins the selec
 constexpr int kSelPer = 4;        // entries per thread per compaction chunk
 constexpr int kSelScoreLd = 15;   // float4 score groups staged per thread and chunk (at most)
 static_assert(4 * kSelScoreLd <= 64, "a thread's candidate mask (4 bits per group) must fit 64 bits");
+static_assert(((kSelBinCap + kSelMaxK + 2 + kSelThreads - 1) / kSelThreads | 1) <= 64,
+              "a finisher run (list capacity / threads) must fit a 64-bit mask");
 constexpr uint32_t kSelPairwise = 256;  // sub-bin keys ranked pairwise (more: one more radix level)
 
 __device__ __forceinline__ void select_range(const PoolAddr& pa, const int* prefix, const int* vis_s,
@@ -156,139 +158,55 @@ __device__ __forceinline__ void list_runs(const uint64_t* lst, uint32_t L, F f) 
   }
 }
 
-// The keys >= K* of the position-ordered shared-memory run keys[0, n), in
-// order, to output slots [off, ...) of row b: every thread takes a run of
-// consecutive keys (list_runs), one block scan gives its slot.  With k <= 2048
-// the ids gather in `stage` (2048 words) and leave in one coalesced copy, the
-// scores read back from the row.
-__device__ void write_selected(const SelectArgs& a, int b, const float* srow, const uint64_t* keys, uint32_t n,
-                               uint64_t kstar, uint32_t off, uint32_t* stage, uint32_t* scratch) {
-  constexpr int T = kSelThreads;
-  const int tid = threadIdx.x;
-  const uint32_t k = uint32_t(a.k);
-  __builtin_assume(__isShared(keys));
-  __builtin_assume(__isShared(stage));
-  __builtin_assume(__isShared(scratch));
-  int32_t* orow = a.out_ids + int64_t(b) * k;
-  float* oscore = a.out_scores != nullptr ? a.out_scores + int64_t(b) * k : nullptr;
-  const bool staged = k <= uint32_t(kSelBins);
-  uint32_t cnt = 0;
-  list_runs(keys, n, [&](uint64_t key) { cnt += key >= kstar ? 1u : 0u; });
-  uint32_t found;
-  uint32_t s = sel_excl_scan<T>(cnt, found, scratch);
-  list_runs(keys, n, [&](uint64_t key) {
-    if (key < kstar) return;
-    if (off + s < k) {  // more only after a CTA gave up (its candidates are missing)
-      if (staged) {
-        stage[s] = uint32_t(sel_key_id(key));
-      } else {
-        orow[off + s] = sel_key_id(key);
-        if (oscore != nullptr) oscore[off + s] = sel_key_score(key);
-      }
-    }
-    ++s;
-  });
-  __syncthreads();
-  if (staged) {
-    const uint32_t m = off < k ? min(found, k - off) : 0u;
-#pragma unroll 1
-    for (uint32_t i0 = 0; i0 < m; i0 += T * 4) {
-      uint32_t v4[4];
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const uint32_t i = i0 + u * T + tid;
-        v4[u] = i < m ? stage[i] : 0u;
-      }
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const uint32_t i = i0 + u * T + tid;
-        if (i < m) orow[off + i] = int32_t(v4[u]);
-      }
-    }
-    if (oscore != nullptr)
-#pragma unroll 1
-      for (uint32_t i0 = 0; i0 < m; i0 += T * 8) {
-        float sc[8];
-#pragma unroll
-        for (int u = 0; u < 8; ++u) {
-          const uint32_t i = i0 + u * T + tid;
-          if (i < m) sc[u] = __ldcg(srow + (int64_t(int32_t(stage[i])) - a.id_base));
-        }
-#pragma unroll
-        for (int u = 0; u < 8; ++u) {
-          const uint32_t i = i0 + u * T + tid;
-          if (i < m) oscore[off + i] = key_score(sel_rank_u(__float_as_uint(sc[u])));
-        }
-      }
-    __syncthreads();  // the stage is free again
-  }
-}
-
 // The row's last CTA for a row without overflow (select.cuh, step 3): L keys in
-// the row's list, nblk appended blocks (their records in arrival order), the
-// row held by nctas CTAs.  Shared memory: the list in position order, the list
-// in arrival order when both fit, then three tables per CTA rank.
-//   1. records, digit-1 histogram and (when both fit) the list, all in flight
-//      (16-byte async copies); without room for both the list comes in step 3,
-//      from global;
-//   2. each rank's block length and base, their offsets in CTA order;
-//   3. the list in position order: one warp copies each rank's block from
-//      rbase[r] of the arrival order to roff[r];
-//   4. K*: the sub-bin (b0, b1) holding it from the digit-1 histogram; its
+// the row's list, its nblk blocks in arrival order (block s starts at the list
+// offset of record s; the offsets ascend), the row held by nctas CTAs.
+//   1. records and the list, both in flight (16-byte async copies);
+//   2. the digit-1 histogram of the list's threshold-bin keys (shared-memory
+//      atomics: cheaper here than global atomics in every CTA), then
+//      K*: the sub-bin (b0, b1) holding it from that histogram; its
 //      lower edge when the whole sub-bin is selected, otherwise the need1-th
-//      largest of its keys (ranked pairwise when few, else by the next digits);
-//   5. one ordered compaction of the keys >= K* to the output.
-__device__ void finish_row(const SelectArgs& a, int b, const float* srow, uint32_t L, uint32_t nblk,
-                           uint32_t nctas, uint32_t b0, uint32_t above, uint8_t* work, size_t work_bytes,
-                           uint32_t* hist, uint32_t* scratch) {
+//      largest of its keys (ranked pairwise when few, else by the next
+//      digits).  K* does not depend on the order of the list;
+//   3. every thread takes a run of consecutive list entries and marks its keys
+//      >= K*; one block scan gives the selected keys before each run;
+//   4. from these, the selected keys before each block's start, each block's
+//      count, their exclusive scan in CTA rank order (ranks follow positions,
+//      and every block is in position order) and so each block's first output
+//      slot;
+//   5. every thread writes its selected ids (and scores): slot = its block's
+//      first slot + the selected keys before it in the block.
+// The tables of steps 4-5 live in `hist` (free after step 2; 3 * gridDim.x + 1 +
+// kSelThreads words <= 2048) and after the list's capacity in `work` (12 bytes
+// per thread <= the kSelThreads * 16 bytes the host keeps there).
+__device__ void finish_row(const SelectArgs& a, int b, uint32_t L, uint32_t nblk, uint32_t nctas, uint32_t b0,
+                           uint32_t above, uint8_t* work, uint32_t* hist, uint32_t* scratch) {
   constexpr int T = kSelThreads;
   const int tid = threadIdx.x;
   __builtin_assume(__isShared(work));
   __builtin_assume(__isShared(hist));
   __builtin_assume(__isShared(scratch));
   uint32_t* ncand = scratch + 42;
-  const size_t lbytes = (size_t(L) * 8 + 15) & ~size_t(15);
-  const size_t tables = size_t(3 * gridDim.x + 1) * 4;
-  const bool both = 2 * lbytes + tables <= work_bytes;
-  uint64_t* ord = reinterpret_cast<uint64_t*>(work);
-  uint64_t* arr = reinterpret_cast<uint64_t*>(work + lbytes);
-  uint32_t* rn = reinterpret_cast<uint32_t*>(work + (both ? 2 : 1) * lbytes);
-  uint32_t* rbase = rn + gridDim.x;
-  uint32_t* roff = rbase + gridDim.x;
+  uint64_t* arr = reinterpret_cast<uint64_t*>(work);
   const uint64_t* lrow = a.list + int64_t(b) * a.list_cap;
+  const uint32_t k = uint32_t(a.k);
+  int32_t* orow = a.out_ids + int64_t(b) * k;
+  float* oscore = a.out_scores != nullptr ? a.out_scores + int64_t(b) * k : nullptr;
 
-  // 1.
-#pragma unroll 1
-  for (uint32_t r = tid; r < nctas; r += T) rn[r] = 0u;  // ranks that appended nothing
+  // 1. (thread s holds the record of arrival s; nblk <= gridDim.x < kSelThreads)
   uint4 rec = make_uint4(0u, 0u, ~0u, 0u);
   if (uint32_t(tid) < nblk) rec = __ldcg(a.blocks + int64_t(b) * gridDim.x + tid);
-  if (both) async_keys(arr, lrow, L);
-  async_hist(hist, a.hist1 + int64_t(b) * kSelBins);
+  async_keys(arr, lrow, L);
+#pragma unroll 1
+  for (int i = tid; i < kSelBins; i += T) hist[i] = 0u;
   cp_async_wait_all();
   __syncthreads();
-  // 2. (a record past the list only after a CTA gave up)
-  if (rec.z < nctas) {
-    const uint32_t bb = min(rec.x, L);
-    rn[rec.z] = min(rec.y, L - bb);
-    rbase[rec.z] = bb;
-  }
+  // 2.
+  list_runs(arr, L, [&](uint64_t key) {
+    if ((key >> kSelShift[0]) == b0) atomicAdd(&hist[(key >> kSelShift[1]) & uint64_t(kSelBins - 1)], 1u);
+  });
   __syncthreads();
-  uint32_t Lv;
-  const uint32_t off = sel_excl_scan<T>(uint32_t(tid) < nctas ? rn[tid] : 0u, Lv, scratch);
-  if (uint32_t(tid) < nctas) roff[tid] = off;
-  __syncthreads();
-  Lv = min(Lv, L);
-  // 3. one warp per rank, lanes on consecutive keys (from global without room for both)
-  const int lane = tid & 31, warp = tid >> 5;
-#pragma unroll 1
-  for (uint32_t r = warp; r < nctas; r += T / 32) {
-    const uint32_t n = rn[r], src = rbase[r], dst = roff[r];
-#pragma unroll 1
-    for (uint32_t j = lane; j < n; j += 32) ord[dst + j] = both ? arr[src + j] : __ldcg(lrow + src + j);
-  }
-  __syncthreads();
-  // 4.
-  const uint32_t need0 = uint32_t(a.k) - above;
+  const uint32_t need0 = k - above;
   uint32_t above1;
   const uint32_t b1 = sel_find_bin<T>(hist, kSelBins, need0, above1, scratch) & uint32_t(kSelBins - 1);
   const uint32_t need1 = need0 - above1, in_sub = hist[b1];
@@ -297,7 +215,7 @@ __device__ void finish_row(const SelectArgs& a, int b, const float* srow, uint32
   uint64_t kstar = sub;
   if (in_sub != need1) {
     if (in_sub > kSelPairwise) {
-      kstar = sel_kstar<T>([&](int64_t i) { return ord[i]; }, Lv, sub, need1, 2, hist, scratch);
+      kstar = sel_kstar<T>([&](int64_t i) { return arr[i]; }, L, sub, need1, 2, hist, scratch);
     } else {
       uint64_t* subk = reinterpret_cast<uint64_t*>(hist);
       if (tid == 0) {
@@ -306,7 +224,7 @@ __device__ void finish_row(const SelectArgs& a, int b, const float* srow, uint32
         scratch[47] = uint32_t(sub >> 32);
       }
       __syncthreads();
-      list_runs(ord, Lv, [&](uint64_t key) {
+      list_runs(arr, L, [&](uint64_t key) {
         if ((key >> kSelShift[1]) == (sub >> kSelShift[1])) {
           const uint32_t at = atomicAdd(ncand, 1u);
           if (at < kSelPairwise) subk[at] = key;
@@ -330,8 +248,91 @@ __device__ void finish_row(const SelectArgs& a, int b, const float* srow, uint32
       __syncthreads();
     }
   }
-  // 5.
-  write_selected(a, b, srow, ord, Lv, kstar, 0u, hist, scratch);
+  // 3. (an odd run length: the 8-byte loads of a half warp fall on distinct banks)
+  const uint32_t per = ((L + T - 1) / T) | 1u;
+  const uint32_t l0 = min(L, tid * per), l1 = min(L, l0 + per);
+  uint64_t mask = 0;  // bit j: key l0 + j selected
+#pragma unroll 1
+  for (uint32_t i = l0; i < l1; i += 4) {
+    uint64_t kq[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) kq[u] = i + u < l1 ? arr[i + u] : 0ull;
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+      if (i + u < l1 && kq[u] >= kstar) mask |= 1ull << (i + u - l0);
+  }
+  uint32_t found;
+  const uint32_t p0 = sel_excl_scan<T>(uint32_t(__popcll(mask)), found, scratch);
+  // 4. tables: per rank, its block's count, then its first slot (rslot); per
+  // arrival s, the block's start (abase, abase[nblk] = L) and first slot less
+  // the selected keys before it (sbase); per run, the block holding its first
+  // entry (first), its selected keys before it (runp) and its mask (runm)
+  uint32_t* rslot = hist;
+  uint32_t* abase = rslot + gridDim.x;
+  uint32_t* sbase = abase + gridDim.x + 1;
+  uint32_t* first = sbase + gridDim.x;
+  uint64_t* runm = reinterpret_cast<uint64_t*>(work + size_t(a.list_cap) * 8);  // the list's capacity is 16-byte aligned
+  uint32_t* runp = reinterpret_cast<uint32_t*>(runm + T);
+  runp[tid] = p0;
+  runm[tid] = mask;
+  first[tid] = 0u;
+  if (uint32_t(tid) < nblk) abase[tid] = min(rec.x, L);
+  if (tid == 0) abase[nblk] = L;
+#pragma unroll 1
+  for (uint32_t r = tid; r < nctas; r += T) rslot[r] = 0u;  // ranks that appended nothing
+  __syncthreads();
+  // thread s (arrival s): the selected keys before its block's start and end,
+  // from the runs holding them; its count; the block of every run starting in it
+  const auto before = [&](uint32_t x) -> uint32_t {  // selected keys before list entry x
+    if (x >= L) return found;
+    const uint32_t t = x / per, j = x - t * per;
+    return runp[t] + uint32_t(__popcll(runm[t] & ((1ull << j) - 1ull)));
+  };
+  uint32_t pstart = 0;
+  const bool has_rec = uint32_t(tid) < nblk && rec.z < nctas;
+  if (uint32_t(tid) < nblk) {
+    const uint32_t lo = min(rec.x, L), hi = min(lo + rec.y, L);
+    pstart = before(lo);
+    if (has_rec) rslot[rec.z] = before(hi) - pstart;
+#pragma unroll 1
+    for (uint32_t t = (lo + per - 1) / per; t * per < hi; ++t) first[t] = uint32_t(tid);
+  }
+  __syncthreads();
+  uint32_t total;
+  const uint32_t cnt = uint32_t(tid) < nctas ? rslot[tid] : 0u;  // each thread reads and rewrites its own rank
+  const uint32_t rs = sel_excl_scan<T>(cnt, total, scratch);
+  if (uint32_t(tid) < nctas) rslot[tid] = rs;
+  __syncthreads();
+  if (has_rec) sbase[tid] = rslot[rec.z] - pstart;  // mod 2^32
+  __syncthreads();
+  // 5. (slots past k only after a CTA gave up: its candidates are missing)
+  if (mask != 0ull) {
+    uint32_t cur = first[tid], nxt = abase[cur + 1], p = p0, slot = sbase[cur] + p0;
+#pragma unroll 1
+    for (uint32_t i = l0; i < l1; i += 4) {
+      uint64_t kq[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) kq[u] = i + u < l1 && ((mask >> (i + u - l0)) & 1ull) ? arr[i + u] : 0ull;
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const uint32_t x = i + u;
+        if (x >= l1) break;
+        if (x == nxt && cur + 1 < nblk) {  // the next block starts here (blocks are never empty)
+          ++cur;
+          nxt = abase[cur + 1];
+          slot = sbase[cur] + p;
+        }
+        if ((mask >> (x - l0)) & 1ull) {
+          if (slot < k) {
+            orow[slot] = sel_key_id(kq[u]);
+            if (oscore != nullptr) oscore[slot] = sel_key_score(kq[u]);
+          }
+          ++slot;
+          ++p;
+        }
+      }
+    }
+  }
 }
 
 __device__ void select_phase(const SelectArgs& a, const float* __restrict__ scores, int64_t score_stride,
@@ -400,9 +401,8 @@ __device__ void select_phase(const SelectArgs& a, const float* __restrict__ scor
   unsigned long long* state = a.row_state;
 
   // ---- per row of more than k keys: threshold bin b0, this CTA's candidates
-  // (digit 0 >= b0) appended to the row's list in one block, the digit 1 of its
-  // threshold-bin entries counted into the row's digit-1 histogram; then the
-  // CTA counts itself done with the row, and the row's last CTA finishes it.
+  // (digit 0 >= b0) appended to the row's list in one block; then the CTA
+  // counts itself done with the row, and the row's last CTA finishes it.
   // Shared memory: the candidate buffer (list_cap keys), then the staging of
   // the scores (16-byte async copies, read back by rolled loops)
   uint64_t* buf = reinterpret_cast<uint64_t*>(work);
@@ -449,7 +449,6 @@ __device__ void select_phase(const SelectArgs& a, const float* __restrict__ scor
         // monotone; NaN ranks above +inf); bins 0-3 decode to NaN patterns and
         // hold nothing above -inf, so with b0 < 4 every score passes
         const float thr = b0 < 4u ? -CUDART_INF_F : key_score(b0 << 21);
-        uint32_t* h1row = a.hist1 + int64_t(b) * kSelBins;
         // per staged chunk: every thread tests a run of consecutive float4 groups
         // (an odd count: conflict-free 16-byte reads), one block scan places its
         // candidates, so the block comes out in position order
@@ -465,18 +464,33 @@ __device__ void select_phase(const SelectArgs& a, const float* __restrict__ scor
           const int m = ((cn4 + T - 1) / T) | 1;
           const int q0 = min(cn4, tid * m), q1 = min(cn4, q0 + m);
           uint64_t take = 0;
+          // four groups in flight; most groups have all four scores below the
+          // threshold (NaN compares false and is kept) and need nothing more
 #pragma unroll 1
-          for (int qi = q0; qi < q1; ++qi) {
-            const float4 x4 = stage[qi];
-            const float xs[4] = {x4.x, x4.y, x4.z, x4.w};
+          for (int qa = q0; qa < q1; qa += 4) {
+            float4 x4[4];
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const int p = a0 + 4 * (i0 + qi) + e;
-              if (!(xs[e] >= thr || xs[e] != xs[e]) || p < p_lo || p >= p_hi) continue;
-              const uint32_t u = sel_rank_u(__float_as_uint(xs[e]));
-              if ((u >> 21) < b0) continue;
-              take |= 1ull << ((qi - q0) * 4 + e);
-              if ((u >> 21) == b0) atomicAdd(h1row + ((u >> 10) & (kSelBins - 1)), 1u);  // key bits 41..51
+            for (int u = 0; u < 4; ++u) x4[u] = stage[min(qa + u, q1 - 1)];
+            uint32_t pass = 0;
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+              if (qa + u < q1 && !(x4[u].x < thr && x4[u].y < thr && x4[u].z < thr && x4[u].w < thr))
+                pass |= 1u << u;
+#pragma unroll 1
+            while (pass != 0u) {
+              const int u = __ffs(pass) - 1;
+              pass &= pass - 1u;
+              const float4 g = u == 0 ? x4[0] : (u == 1 ? x4[1] : (u == 2 ? x4[2] : x4[3]));
+              const int qi = qa + u;
+              const float xs[4] = {g.x, g.y, g.z, g.w};
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const int p = a0 + 4 * (i0 + qi) + e;
+                if (!(xs[e] >= thr || xs[e] != xs[e]) || p < p_lo || p >= p_hi) continue;
+                const uint32_t uk = sel_rank_u(__float_as_uint(xs[e]));
+                if ((uk >> 21) < b0) continue;
+                take |= 1ull << ((qi - q0) * 4 + e);
+              }
             }
           }
           uint32_t tot;
@@ -513,8 +527,8 @@ __device__ void select_phase(const SelectArgs& a, const float* __restrict__ scor
       }
     }
     // count in (live or not): the last CTA of the row sees every other CTA's
-    // blocks, digit-1 counts and histogram reads complete, the list's length and
-    // the number of blocks
+    // blocks and histogram reads complete, the list's length and the number of
+    // blocks
     __syncthreads();
     if (tid == 0) {
       const unsigned long long old = atom_add_acq_rel(state + b, 1ull << 48);
@@ -556,13 +570,12 @@ __device__ void select_phase(const SelectArgs& a, const float* __restrict__ scor
         });
       }
     } else if (live) {
-      finish_row(a, b, srow, L, nblk, nctas, b0, above, work, work_bytes, hist, scratch);
+      finish_row(a, b, L, nblk, nctas, b0, above, work, hist, scratch);
     }
     // the row's workspace back to zero for the next launch
 #pragma unroll 1
     for (int i = tid; i < kSelBins; i += T) {
       a.hist[int64_t(b) * kSelBins + i] = 0u;
-      a.hist1[int64_t(b) * kSelBins + i] = 0u;
     }
     if (tid == 0) state[b] = 0ull;
     __syncthreads();
@@ -707,7 +720,10 @@ __global__ void __launch_bounds__(kIxThreads, 1)
       // ------------------------------------------------------------ producer
       // The first pool rows of the 64-row halves of 16 tiles (block-table
       // entries, or ring runs) are resolved by the 32 lanes at once (one load
-      // latency per 16 tiles); lane 0 then issues the TMA boxes.
+      // latency per 16 tiles); lane 0 then issues the TMA boxes.  Every key is
+      // read once: its lines go first when L2 evicts, so the scores, the
+      // selection's state and this kernel's code stay cached.
+      const uint64_t stream_policy = l2_evict_first_policy();
       for (int g0 = t_lo, s0 = 0; g0 < t_hi; g0 += 16, s0 += 16) {
         const int t = g0 + (lane >> 1), blk = lane & 1;
         int32_t hrow = -1;  // -1: a half beyond the tile's keys, not loaded
@@ -739,8 +755,9 @@ __global__ void __launch_bounds__(kIxThreads, 1)
               const uint32_t dst = sbase + L::kStagesOff + stage * kIxStageBytes;
 #pragma unroll
               for (int kh = 0; kh < 2; ++kh) {
-                tma_load_2d(dst + kh * 16384, &kmap, &full[stage], kh * 64, r0);
-                if (nblk == 2) tma_load_2d(dst + kh * 16384 + 8192, &kmap, &full[stage], kh * 64, r1);
+                tma_load_2d_hint(dst + kh * 16384, &kmap, &full[stage], kh * 64, r0, stream_policy);
+                if (nblk == 2)
+                  tma_load_2d_hint(dst + kh * 16384 + 8192, &kmap, &full[stage], kh * 64, r1, stream_policy);
               }
             }
           }
@@ -1021,7 +1038,7 @@ int select_args(SelectArgs* a, void* workspace, int64_t batch, int64_t k, int64_
                 float* out_scores) {
   DSR_REQUIRE(workspace != nullptr && out_ids != nullptr, "select: null workspace or output");
   DSR_REQUIRE((reinterpret_cast<uintptr_t>(workspace) & 255u) == 0, "select: workspace must be 256-byte aligned");
-  DSR_REQUIRE(k > 0 && k <= 8192, "select: k %lld outside [1, 8192]", (long long)k);
+  DSR_REQUIRE(k > 0 && k <= kSelMaxK, "select: k %lld outside [1, %d]", (long long)k, kSelMaxK);
   const SelectLayout L(batch, k, sm_count());
   uint8_t* base = static_cast<uint8_t*>(workspace);
   a->out_ids = out_ids;
@@ -1029,7 +1046,6 @@ int select_args(SelectArgs* a, void* workspace, int64_t batch, int64_t k, int64_
   a->k = int(k);
   a->id_base = id_base;
   a->hist = reinterpret_cast<uint32_t*>(base + L.hist);
-  a->hist1 = reinterpret_cast<uint32_t*>(base + L.hist1);
   a->ctl = reinterpret_cast<uint32_t*>(base + L.ctl);
   a->row_state = reinterpret_cast<unsigned long long*>(base + L.state);
   a->blocks = reinterpret_cast<uint4*>(base + L.blocks);
