@@ -43,7 +43,14 @@ sys.path.insert(0, str(ROOT))
 METRIC = "µs per decode step (indexer+top-k+sparse attn) at 128K/1M ctx; HBM GB/s % peak"
 DATA = ("synthetic: seeded N(0,1) rounded to BF16; long sequences drawn in 65,536-position chunks, "
         "each from a generator seeded by (seed, sequence, chunk), on the GPU")
-KERNELS_PER_STEP = 4  # indexer, top-k, sparse MLA, LSE combine
+
+
+def kernels_per_step(batch, heads, idx_heads, k):
+    """This library's kernels one dsr_decode_step launches for the shape: 1 when
+    the attention and combine run inside the cooperative indexer launch, else 3
+    (indexer with the exact top-k, sparse MLA, LSE combine)."""
+    from deepseekrpc_b200 import _native
+    return int(_native.library().dsr_decode_step_launches(batch, heads, idx_heads, k))
 
 # DRAM bytes per launch of the indexer, read from ncu captures of the same
 # kernel (dram__bytes_read.sum + dram__bytes_write.sum; profiles/indexer_decode_*.md)
@@ -451,7 +458,7 @@ def cfg2_leg(args, dev, stream):
                               "unit": "us", "note": "single-step graph replays, an event pair each"},
         "e2e": {"value": round(e2e * 1e3, 3), "unit": "us", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
         "cpu_baseline": cpu,
-        "gpu_launches_per_step": KERNELS_PER_STEP,
+        "gpu_launches_per_step": kernels_per_step(1, cfg.heads, cfg.idx_heads, cfg.topk),
     }
     del runner, inp
     torch.cuda.empty_cache()
@@ -670,7 +677,7 @@ def run_single(args):
                      "peak_kind": f"{peak_kind} HBM copy bandwidth"},
         "cpu_baseline": cpu,
         "e2e": {"value": round(e2e * 1e3, 3), "unit": "us", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
-        "gpu_launches": KERNELS_PER_STEP * K,
+        "gpu_launches": kernels_per_step(cfg.batch, cfg.heads, cfg.idx_heads, cfg.topk) * K,
         "parity_ok": parity["parity_ok"], "parity": parity,
         "clocks": clocks,
         "cfg2": cfg2,

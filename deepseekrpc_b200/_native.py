@@ -68,6 +68,7 @@ SIGNATURES = {
     "dsr_p2p_free": (c_int, [_P]),
     "dsr_p2p_allgather": (c_int, [_P, c_int64, _P, c_int64, c_int64, c_int64, c_int64, _P, _P]),
     "dsr_decode_workspace_bytes": (c_size_t, [c_int64, c_int64, c_int64, c_int64]),
+    "dsr_decode_step_launches": (c_int, [c_int64, c_int64, c_int64, c_int64]),
     "dsr_indexer_decode_ring": (c_int, [_P, _P, _P, c_int64, _P, _P, _P, c_int64, _P, c_int64, c_int64, _P]),
     "dsr_sparse_mla_decode_ring": (c_int, [_P, _P, c_int64, _P, _P, _P, c_int64, _P, c_int64, _P, _P, _P,
                                            c_float, _P, _P, c_size_t, _P, c_int64, c_int64, _P]),

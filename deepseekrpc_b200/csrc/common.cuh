@@ -200,6 +200,10 @@ __device__ __forceinline__ void tma_load_2d_hint(uint32_t dst, const void* tmap,
       "l"(reinterpret_cast<uint64_t>(tmap)), "r"(smem_u32(bar)), "r"(x), "r"(y), "l"(policy)
       : "memory");
 }
+// L2 prefetch of `bytes` bytes at p (16-byte aligned, a multiple of 16 bytes).
+__device__ __forceinline__ void bulk_prefetch_l2(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
 // An L2 cache policy that marks every line it covers evict-first.
 __device__ __forceinline__ uint64_t l2_evict_first_policy() {
   uint64_t policy;

@@ -1,10 +1,11 @@
 // One sparse-attention decode step: indexer scores -> exact top-k -> sparse MLA
-// attention -> LSE combine, enqueued as four kernels chained with programmatic
-// dependent launch so each kernel's prologue (barrier set-up, TMEM allocation)
-// overlaps the tail of its predecessor.  Replaces, per layer, the host loop of
-// AttentionState.select -> TiledIndexer.select (index_selection.py:79-124)
-// followed by forward_mqa's id assembly and sparse_attention call
-// (vllm_attention.py:231-262).
+// attention -> LSE combine.  When the step's attention tiles fit one per SM, a
+// single cooperative launch does all four; otherwise the indexer launch (scores
+// and top-k) is followed by the MLA and combine kernels, chained with
+// programmatic dependent launch so each prologue overlaps its predecessor.
+// Replaces, per layer, the host loop of AttentionState.select ->
+// TiledIndexer.select (index_selection.py:79-124) followed by forward_mqa's id
+// assembly and sparse_attention call (vllm_attention.py:231-262).
 #include "common.cuh"
 #include "host_common.h"
 #include "select.cuh"
@@ -56,8 +57,17 @@ int decode_step(const float* idx_q, const float* idx_w, int64_t idx_heads, const
   SelectArgs sel;
   int rc = select_args(&sel, sel_ws, batch, k, 0, topk_out, nullptr);
   if (rc != DSR_OK) return rc;
-  // one cooperative launch: the indexer scores, converts the MLA query into the
-  // BF16 image the MLA kernel loads, and selects the exact top-k of the scores
+  // When every attention tile unit gets a CTA of its own, one cooperative launch
+  // does the whole step: scores, exact top-k, attention tiles and combine.
+  // Otherwise the indexer launch scores, selects and converts the MLA query into
+  // the BF16 image the MLA kernels load, and those follow.
+  MlaFuseLaunch plan;  // launch parameters are copied at the launch
+  rc = plan_fused_mla(&plan, indexer_attention_room(idx_heads), q, kv_pool, kv, visible, topk_out, swa, swa_ring,
+                      swa_rows, swa_len, sink, scale, out, mla_ws, mla_bytes, err, batch, heads, k);
+  if (rc != DSR_OK) return rc;
+  if (plan.args.units > 0)
+    return launch_indexer_decode(idx_q, idx_w, index_pool, ix, visible, scores, stride, err, batch, idx_heads, s,
+                                 false, nullptr, nullptr, 0, nullptr, &sel, &plan);
   rc = launch_indexer_decode(idx_q, idx_w, index_pool, ix, visible, scores, stride, err, batch, idx_heads, s,
                              false, q, q_img, heads, nullptr, &sel);
   if (rc != DSR_OK) return rc;
@@ -67,6 +77,11 @@ int decode_step(const float* idx_q, const float* idx_w, int64_t idx_heads, const
 
 }  // namespace
 }  // namespace dsr
+
+extern "C" int dsr_decode_step_launches(int64_t batch, int64_t heads, int64_t idx_heads, int64_t k) {
+  const int units = dsr::fused_mla_units(dsr::indexer_attention_room(idx_heads), batch, heads, k);
+  return units > 0 ? 1 : 3;
+}
 
 extern "C" int dsr_decode_step(const float* idx_q, const float* idx_w, int64_t idx_heads,
                                const uint16_t* index_pool, const float* q,

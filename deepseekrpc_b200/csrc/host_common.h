@@ -64,13 +64,52 @@ size_t topk_workspace_bytes(int64_t rows, int64_t row_stride);
 // Leading bytes of that scratch (histograms, tickets, counts) that must be zero at launch.
 size_t topk_zeroed_prefix_bytes(int64_t rows, int64_t row_stride);
 struct SelectArgs;
+// The sparse MLA attention and LSE combine of a decode step, run inside the
+// cooperative indexer launch after the selection: one tile unit per CTA, so
+// units <= the grid; units == 0: not fused (indexer_decode.cu).
+struct MlaFuse {
+  const float* q;  // [batch, heads, 576] fp32 query
+  const uint16_t* kv_pool;
+  PoolAddr kv;
+  const int64_t* swa_ring;
+  int64_t swa_rows;
+  const int32_t* swa_len;
+  const float* sink;
+  float scale_log2;
+  uint16_t* part_o;  // tile partials, layout of mla_workspace_bytes()
+  float* part_m;
+  float* part_l;
+  float* out;  // [batch, heads, 512]
+  int heads, hg, tiles, units;
+};
+struct MlaFuseLaunch {
+  MlaFuse args;
+  CUtensorMap kv_map, swa_map;  // one-row gather boxes over the KV pool and the SWA rows
+};
+// Plans the fused attention of a decode step: the checks of launch_mla_decode,
+// the head group, the tensor maps.  plan->args.units stays 0 (not an error) when
+// the step has more tile units than CTAs or its tile needs more than `room`
+// bytes of the indexer CTA's shared memory.
+int plan_fused_mla(MlaFuseLaunch* plan, size_t room, const float* q, const uint16_t* kv_pool, const PoolAddr& kv,
+                   const int32_t* visible, const int32_t* topk, const uint16_t* swa, const int64_t* swa_ring,
+                   int64_t swa_rows,
+                   const int32_t* swa_len, const float* sink, float scale, float* out, void* workspace,
+                   size_t workspace_bytes, int32_t* err, int64_t batch, int64_t heads, int64_t k);
+// Tile units of a decode step's attention when it fuses into the indexer
+// launch (room: indexer_attention_room()), else 0.
+int fused_mla_units(size_t room, int64_t batch, int64_t heads, int64_t k);
+// Shared memory of the indexer CTA (idx_heads index heads) a fused attention
+// tile may use.
+size_t indexer_attention_room(int64_t idx_heads);
 // The decode indexer; with `sel`, the exact top-k of its scores in the same
-// (cooperative) launch (select.cuh).
+// (cooperative) launch (select.cuh); with `fuse` (and `sel`), the step's sparse
+// attention and combine too.
 int launch_indexer_decode(const float* q, const float* weights, const uint16_t* index_pool,
                           const PoolAddr& pa, const int32_t* visible, float* scores, int64_t score_stride,
                           int32_t* err, int64_t batch, int64_t heads, cudaStream_t stream,
                           bool pdl, const float* mla_q = nullptr, uint16_t* mla_img = nullptr,
-                          int64_t mla_heads = 0, uint32_t* hist = nullptr, const SelectArgs* sel = nullptr);
+                          int64_t mla_heads = 0, uint32_t* hist = nullptr, const SelectArgs* sel = nullptr,
+                          const MlaFuseLaunch* fuse = nullptr);
 // Bytes of the fused selection's workspace (zero before first use, left zero by every completed launch).
 size_t select_workspace_bytes(int64_t batch, int64_t k);
 // Binds a SelectArgs to a workspace of select_workspace_bytes(batch, k).

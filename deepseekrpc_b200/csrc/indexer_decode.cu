@@ -26,6 +26,7 @@
 // query (q_lo == 0, the FP8-valued reference query) contracts the q_hi rows only.
 #include "common.cuh"
 #include "host_common.h"
+#include "mla_tile.cuh"
 #include "select.cuh"
 
 namespace dsr {
@@ -338,7 +339,7 @@ __device__ void finish_row(const SelectArgs& a, int b, uint32_t L, uint32_t nblk
 __device__ void select_phase(const SelectArgs& a, const float* __restrict__ scores, int64_t score_stride,
                              int batch, const int* prefix, const int* vis_s, const int* run_s, const PoolAddr& pa,
                              int t_lo, int t_hi, uint8_t* work, size_t work_bytes, uint32_t* hist,
-                             uint32_t* scratch, int32_t* err, bool live) {
+                             uint32_t* scratch, int32_t* err, bool live, const MlaFuse& mla) {
   constexpr int T = kSelThreads;
   const int tid = threadIdx.x;
   const int k = a.k;
@@ -416,7 +417,7 @@ __device__ void select_phase(const SelectArgs& a, const float* __restrict__ scor
     if (p_lo >= p_hi || v <= k) continue;
     const uint32_t nctas = row_ctas(b);
     const float* srow = scores + int64_t(b) * score_stride;
-    uint32_t b0 = 0, above = 0;
+    uint32_t b0 = 0, above = 0, nkept = 0;  // nkept: this CTA's candidates in buf
     bool overflow = false;
     // this CTA's rank among the row's CTAs (with fewer tiles than CTAs, one tile each)
     const uint32_t rank = total < int(gridDim.x)
@@ -510,6 +511,7 @@ __device__ void select_phase(const SelectArgs& a, const float* __restrict__ scor
         }
         // the block: one atomic gives its base and arrival number, its record goes under that number
         const uint32_t n = min(nbuf, uint32_t(a.list_cap));
+        nkept = n;
         if (tid == 0 && n != 0u) {
           const unsigned long long old = atomicAdd(state + b, (1ull << 32) | n);
           scratch[40] = uint32_t(old);
@@ -537,7 +539,18 @@ __device__ void select_phase(const SelectArgs& a, const float* __restrict__ scor
       scratch[41] = uint32_t(old >> 32) & 0xffffu;
     }
     __syncthreads();
-    if (scratch[43] == 0u) continue;
+    if (scratch[43] == 0u) {
+      // not the row's finisher: with the attention in this launch, this CTA's
+      // candidates' KV rows go toward L2 while the finisher runs (the top-k is
+      // among them)
+      if (mla.units > 0 && live && !overflow)
+#pragma unroll 1
+        for (uint32_t i = tid; i < nkept; i += T) {
+          const int64_t r = addr_row(mla.kv, b, int64_t(sel_key_id(buf[i])) - a.id_base);
+          if (r >= 0 && r < mla.kv.rows) bulk_prefetch_l2(mla.kv_pool + r * kMlaD, kMlaD * 2);
+        }
+      continue;
+    }
     const uint32_t L = min(scratch[40], uint32_t(a.list_cap));
     const uint32_t nblk = min(scratch[41], uint32_t(gridDim.x));
     __syncthreads();
@@ -572,24 +585,191 @@ __device__ void select_phase(const SelectArgs& a, const float* __restrict__ scor
     } else if (live) {
       finish_row(a, b, L, nblk, nctas, b0, above, work, hist, scratch);
     }
+    // the row's ids are written (every thread's stores precede the barrier)
+    __syncthreads();
+    if (tid == 0) asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(a.ready + b), "r"(1u) : "memory");
     // the row's workspace back to zero for the next launch
 #pragma unroll 1
-    for (int i = tid; i < kSelBins; i += T) {
-      a.hist[int64_t(b) * kSelBins + i] = 0u;
-    }
+    for (int i = tid; i < kSelBins; i += T) a.hist[int64_t(b) * kSelBins + i] = 0u;
     if (tid == 0) state[b] = 0ull;
     __syncthreads();
   }
+}
 
-  // the last CTA to leave resets the barrier counters (every other CTA has passed the barrier)
-  if (tid == 0) {
+// After the selection (and the fused attention): the last CTA to leave resets
+// the counters and the rows' ready flags (every other CTA has passed the barrier
+// and read them).
+__device__ void select_exit(const SelectArgs& a, int batch, uint32_t* scratch) {
+  __syncthreads();
+  if (threadIdx.x == 0) {
     __threadfence();
     const uint32_t done = atomicAdd(a.ctl + 1, 1u);
+    scratch[0] = done == gridDim.x - 1 ? 1u : 0u;
     if (done == gridDim.x - 1) {
       a.ctl[0] = 0u;
       a.ctl[1] = 0u;
+      a.ctl[2] = 0u;
+      a.ctl[3] = 0u;
     }
   }
+  __syncthreads();
+  if (scratch[0] != 0u)
+#pragma unroll 1
+    for (int b = threadIdx.x; b < batch; b += blockDim.x) a.ready[b] = 0u;
+}
+
+// ---------------------------------------------------------------------------
+// The decode step's sparse attention and LSE combine in the same launch
+// (MlaFuse, after the selection).  Every CTA takes one ticket; ticket u < units
+// is the tile unit (tile, sequence, head group) = (u % tiles, (u / tiles) %
+// batch, u / (tiles * batch)) of mla_tile_unit.  A unit of tile >= 1 reads its
+// sequence's top-k ids once they are complete: rows of at most k keys at the
+// grid barrier, the others when their finisher has released ready[b].  Every
+// unit counts itself done; once all are, every CTA combines a share of the
+// outputs, a warp per 128 output columns of one (sequence, head).
+// ---------------------------------------------------------------------------
+// Waits (thread-scalar, bounded) until *p >= target with acquire semantics.
+__device__ __forceinline__ bool wait_count(const uint32_t* p, uint32_t target, int32_t* err) {
+  const uint64_t start = global_ns();
+  for (uint32_t spin = 0;; ++spin) {
+    uint32_t v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    if (int32_t(v - target) >= 0) return true;
+    if ((spin & 15u) == 15u && global_ns() - start > kWaitNs) {
+      flag(err, DSR_ERR_TIMEOUT);
+      return false;
+    }
+  }
+}
+
+template <int H, int HG>
+__device__ void attention_unit(const SelectArgs& sel, const MlaFuse& m, const CUtensorMap* kv_map,
+                               const CUtensorMap* swa_map, const int32_t* visible, const int* vis_s, int batch,
+                               uint8_t* smem, uint32_t u, int32_t* err) {
+  // the tile's shared memory lies below the weights, histogram and tables of
+  // the indexer CTA (the host plans only tiles that fit)
+  if constexpr (MlaLayout<HG>::kBytes <= IxLayout<H>::kWOff) {
+    const int tile = int(u % uint32_t(m.tiles));
+    const int r = int(u / uint32_t(m.tiles));
+    const int b = r % batch, hg = r / batch;
+    const bool wait = vis_s[b] > sel.k;
+    mla_tile_unit<HG>(smem, kv_map, swa_map, m.q, m.kv, m.swa_ring, m.swa_rows, visible, sel.out_ids, sel.k,
+                      m.swa_len, m.scale_log2, m.part_o, m.part_m, m.part_l, err, m.heads, tile, b, hg, m.tiles,
+                      nullptr, sel.id_base, 0, false, [&] {
+                        if (!wait) return;
+                        if (threadIdx.x == 0) wait_count(sel.ready + b, 1u, err);
+                        asm volatile("bar.sync 1, 128;" ::: "memory");  // the 128 key threads
+                      });
+  }
+}
+
+// Output columns [128 q, 128 q + 128) of (sequence b, head h), q = item & 3,
+// (b, h) = item >> 2, by one warp: out = sum_t o_t 2^{m_t - M} / (2^{log2(e)
+// sink_h - M} + sum_t l_t 2^{m_t - M}) over the tile partials t (the equation
+// of lse_combine_kernel).  The statistics and the columns of the first kPre
+// partials are requested together (one memory round trip); `w` holds the
+// warp's tile weights.
+__device__ void combine_item(const MlaFuse& m, int item, float* w, int32_t* err) {
+  constexpr int kPre = 24;
+  const int lane = threadIdx.x & 31;
+  const int pair = item >> 2, quarter = item & 3;
+  const int h = pair % m.heads, tiles = m.tiles;
+  const int64_t pbase = int64_t(pair / m.heads) * tiles * m.heads + h;  // tile t at pbase + t * heads
+  const int d = quarter * 128 + lane * 4;
+  auto col = [&](int t) { return reinterpret_cast<const uint2*>(m.part_o + (pbase + int64_t(t) * m.heads) * kMlaDv + d); };
+  uint2 raw[kPre];
+#pragma unroll
+  for (int j = 0; j < kPre; ++j)
+    if (j < tiles) raw[j] = __ldcg(col(j));
+  float mv[3], lv[3];  // tiles lane, lane + 32, lane + 64 (tiles <= 65: k <= 8192)
+#pragma unroll
+  for (int j = 0; j < 3; ++j) {
+    const int t = lane + 32 * j;
+    mv[j] = t < tiles ? __ldcg(m.part_m + pbase + int64_t(t) * m.heads) : -CUDART_INF_F;
+    lv[j] = t < tiles ? __ldcg(m.part_l + pbase + int64_t(t) * m.heads) : 0.f;
+  }
+  float sk = m.sink[h];
+  if (!isfinite(sk)) {
+    if (lane == 0) flag(err, DSR_ERR_NONFINITE);
+    sk = 0.f;
+  }
+  sk *= kLog2e;
+  float M = fmaxf(sk, fmaxf(mv[0], fmaxf(mv[1], mv[2])));
+#pragma unroll
+  for (int o = 16; o; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+  const float base = M == -CUDART_INF_F ? 0.f : M;
+  float lsum = 0.f;
+#pragma unroll
+  for (int j = 0; j < 3; ++j) {
+    const int t = lane + 32 * j;
+    if (t < tiles) {
+      const float e = exp2f(mv[j] - base);
+      w[t] = e;
+      lsum += lv[j] * e;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) lsum += __shfl_xor_sync(0xffffffffu, lsum, o);
+  lsum += exp2f(sk - base);
+  const float inv = 1.f / lsum;
+  __syncwarp();
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  auto fma4 = [&](uint2 r, float e) {
+    acc.x = fmaf(__uint_as_float(r.x << 16), e, acc.x);
+    acc.y = fmaf(__uint_as_float(r.x & 0xffff0000u), e, acc.y);
+    acc.z = fmaf(__uint_as_float(r.y << 16), e, acc.z);
+    acc.w = fmaf(__uint_as_float(r.y & 0xffff0000u), e, acc.w);
+  };
+#pragma unroll
+  for (int j = 0; j < kPre; ++j)
+    if (j < tiles) fma4(raw[j], w[j]);
+#pragma unroll 1
+  for (int t0 = kPre; t0 < tiles; t0 += 8) {  // partials past kPre, 8 loads at a time
+    uint2 r8[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      if (t0 + j < tiles) r8[j] = __ldcg(col(t0 + j));
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      if (t0 + j < tiles) fma4(r8[j], w[t0 + j]);
+  }
+  const float4 o = make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
+  if (!isfinite(o.x) || !isfinite(o.y) || !isfinite(o.z) || !isfinite(o.w)) flag(err, DSR_ERR_NONFINITE);
+  *reinterpret_cast<float4*>(m.out + int64_t(pair) * kMlaDv + d) = o;
+  __syncwarp();  // w is rewritten by the warp's next item
+}
+
+// `weights`: kIxThreads / 32 * 128 floats of shared memory outside the tile's
+// (tiles <= 128: k <= 8192).
+template <int H>
+__device__ void attention_phase(const SelectArgs& sel, const MlaFuse& m, const CUtensorMap* kv_map,
+                                const CUtensorMap* swa_map, const int32_t* visible, const int* vis_s, int batch,
+                                uint8_t* smem, float* weights, uint32_t* scratch, int32_t* err) {
+  // the selection's generic writes to this shared memory precede the tile's
+  // async-proxy writes (row gathers) and reads (MMA operands)
+  fence_proxy_async_smem();
+  __syncthreads();
+  if (threadIdx.x == 0) scratch[0] = atomicAdd(sel.ctl + 2, 1u);
+  __syncthreads();
+  const uint32_t u = scratch[0];
+  if (u < uint32_t(m.units)) {
+    if (m.hg == 16)
+      attention_unit<H, 16>(sel, m, kv_map, swa_map, visible, vis_s, batch, smem, u, err);
+    else
+      attention_unit<H, 32>(sel, m, kv_map, swa_map, visible, vis_s, batch, smem, u, err);
+    __syncthreads();  // the unit's partial stores precede its count (release)
+    if (threadIdx.x == 0) asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(sel.ctl + 3) : "memory");
+  }
+  if (threadIdx.x == 0) scratch[1] = wait_count(sel.ctl + 3, uint32_t(m.units), err) ? 1u : 0u;
+  __syncthreads();
+  if (scratch[1] == 0u) return;
+  // items spread over the CTAs first (warp w of CTA c: items c + G (w + 10 j))
+  constexpr int kWarps = kIxThreads / 32;
+  const int items = batch * m.heads * (kMlaDv / 128);
+  float* w = weights + (threadIdx.x >> 5) * 128;
+#pragma unroll 1
+  for (int i = int(blockIdx.x) + int(gridDim.x) * int(threadIdx.x >> 5); i < items; i += int(gridDim.x) * kWarps)
+    combine_item(m, i, w, err);
 }
 
 // 32 lanes x 8 consecutive 32-bit TMEM columns
@@ -616,7 +796,8 @@ __global__ void __launch_bounds__(kIxThreads, 1)
                           const int32_t* __restrict__ visible, float* __restrict__ scores, int64_t score_stride,
                           int32_t* err, int batch, const float* __restrict__ mla_q,
                           uint16_t* __restrict__ mla_img, int mla_heads, uint32_t* __restrict__ hist,
-                          const SelectArgs sel) {
+                          const SelectArgs sel, const __grid_constant__ CUtensorMap kv_map,
+                          const __grid_constant__ CUtensorMap swa_map, const MlaFuse mla) {
   using L = IxLayout<H>;
   constexpr int N = L::N;
   constexpr int HH = H / 2;  // heads per epilogue warpgroup
@@ -698,7 +879,7 @@ __global__ void __launch_bounds__(kIxThreads, 1)
   } else {
     if (warp == 1) {
       tmem_alloc(tmem_slot, L::kTmemCols);
-      tmem_relinquish();
+      if (mla.units == 0) tmem_relinquish();  // a fused attention tile allocates again
     } else {
       for (int i = threadIdx.x - 64; i < kIxHistBins; i += kIxThreads - 64) hsm[i] = 0u;
     }
@@ -952,7 +1133,11 @@ __global__ void __launch_bounds__(kIxThreads, 1)
     const bool live = *abort == 0;
     __syncthreads();
     select_phase(sel, scores, score_stride, batch, prefix, vis_s, run_s, pa, t_lo, t_hi, smem + L::kStagesOff,
-                 size_t(L::kWOff - L::kStagesOff), hsm, reinterpret_cast<uint32_t*>(xch), err, live);
+                 size_t(L::kWOff - L::kStagesOff), hsm, reinterpret_cast<uint32_t*>(xch), err, live, mla);
+    if (mla.units > 0)
+      attention_phase<H>(sel, mla, &kv_map, &swa_map, visible, vis_s, batch, smem, reinterpret_cast<float*>(hsm),
+                         reinterpret_cast<uint32_t*>(xch), err);
+    select_exit(sel, batch, reinterpret_cast<uint32_t*>(xch));
   }
 }
 
@@ -960,7 +1145,7 @@ template <int H>
 int launch_ix(const CUtensorMap& map, const float* q, const float* weights, const PoolAddr& pa,
               const int32_t* visible, float* scores, int64_t score_stride, int32_t* err, int batch,
               const float* mla_q, uint16_t* mla_img, int mla_heads, uint32_t* hist,
-              cudaStream_t stream, bool pdl, const SelectArgs& sel) {
+              cudaStream_t stream, bool pdl, const SelectArgs& sel, const MlaFuseLaunch& fuse) {
   using L = IxLayout<H>;
   {
     const int rc = set_max_smem(indexer_decode_kernel<H>, L::kAlloc, "indexer decode");
@@ -978,6 +1163,9 @@ int launch_ix(const CUtensorMap& map, const float* q, const float* weights, cons
   DSR_REQUIRE(sel.out_ids == nullptr || sm_count() < kSelThreads,
               "indexer decode: %d SMs: the selection takes one CTA per SM and at most %d", sm_count(),
               kSelThreads - 1);
+  DSR_REQUIRE(fuse.args.units == 0 || (sel.out_ids != nullptr && fuse.args.units <= sm_count() &&
+                                       (fuse.args.hg == 16 || fuse.args.hg == 32) && fuse.args.tiles <= 128),
+              "indexer decode: invalid fused attention plan");
   if (sel.out_ids != nullptr) {
     // the selection's grid barriers need every CTA resident at once
     attr[0].id = cudaLaunchAttributeCooperative;
@@ -990,7 +1178,8 @@ int launch_ix(const CUtensorMap& map, const float* q, const float* weights, cons
   cfg.numAttrs = (pdl || sel.out_ids != nullptr) ? 1 : 0;
   const cudaError_t e =
       cudaLaunchKernelEx(&cfg, indexer_decode_kernel<H>, map, q, weights, pa, visible, scores, score_stride,
-                         err, batch, mla_q, mla_img, mla_heads, sel.out_ids != nullptr ? sel.hist : hist, sel);
+                         err, batch, mla_q, mla_img, mla_heads, sel.out_ids != nullptr ? sel.hist : hist, sel,
+                         fuse.kv_map, fuse.swa_map, fuse.args);
   if (e != cudaSuccess) return fail(DSR_ECUDA, "indexer launch: %s", cudaGetErrorString(e));
   return DSR_OK;
 }
@@ -1001,8 +1190,9 @@ int launch_indexer_decode(const float* q, const float* weights, const uint16_t* 
                           const PoolAddr& pa, const int32_t* visible, float* scores, int64_t score_stride,
                           int32_t* err, int64_t batch, int64_t heads, cudaStream_t stream,
                           bool pdl, const float* mla_q, uint16_t* mla_img, int64_t mla_heads,
-                          uint32_t* hist, const SelectArgs* sel) {
+                          uint32_t* hist, const SelectArgs* sel, const MlaFuseLaunch* fuse) {
   const SelectArgs none{};
+  static const MlaFuseLaunch no_fuse{};  // units == 0: the maps are never read
   const SelectArgs& sa = sel != nullptr ? *sel : none;
   DSR_REQUIRE(mla_q == nullptr || (mla_img != nullptr && aligned16(mla_q) && aligned16(mla_img) &&
                                    (mla_heads == 16 || mla_heads == 32 || mla_heads == 64 ||
@@ -1022,14 +1212,19 @@ int launch_indexer_decode(const float* q, const float* weights, const uint16_t* 
   switch (heads) {
     case 16:
       return launch_ix<16>(map, q, weights, pa, visible, scores, score_stride, err, int(batch), mla_q, mla_img,
-                           int(mla_heads), hist, stream, pdl, sa);
+                           int(mla_heads), hist, stream, pdl, sa, fuse != nullptr ? *fuse : no_fuse);
     case 32:
       return launch_ix<32>(map, q, weights, pa, visible, scores, score_stride, err, int(batch), mla_q, mla_img,
-                           int(mla_heads), hist, stream, pdl, sa);
+                           int(mla_heads), hist, stream, pdl, sa, fuse != nullptr ? *fuse : no_fuse);
     default:
       return launch_ix<64>(map, q, weights, pa, visible, scores, score_stride, err, int(batch), mla_q, mla_img,
-                           int(mla_heads), hist, stream, pdl, sa);
+                           int(mla_heads), hist, stream, pdl, sa, fuse != nullptr ? *fuse : no_fuse);
   }
+}
+
+size_t indexer_attention_room(int64_t idx_heads) {
+  return idx_heads == 16 ? size_t(IxLayout<16>::kWOff)
+                         : (idx_heads == 32 ? size_t(IxLayout<32>::kWOff) : size_t(IxLayout<64>::kWOff));
 }
 
 size_t select_workspace_bytes(int64_t batch, int64_t k) { return SelectLayout(batch, k, sm_count()).total; }
@@ -1049,6 +1244,7 @@ int select_args(SelectArgs* a, void* workspace, int64_t batch, int64_t k, int64_
   a->ctl = reinterpret_cast<uint32_t*>(base + L.ctl);
   a->row_state = reinterpret_cast<unsigned long long*>(base + L.state);
   a->blocks = reinterpret_cast<uint4*>(base + L.blocks);
+  a->ready = reinterpret_cast<uint32_t*>(base + L.ready);
   a->list = reinterpret_cast<uint64_t*>(base + L.list);
   a->list_cap = int(L.cap);
   return DSR_OK;

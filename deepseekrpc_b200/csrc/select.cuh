@@ -52,26 +52,30 @@ struct SelectArgs {
   int k;
   int64_t id_base;     // id of position p = id_base + p
   uint32_t* hist;      // [batch][2048] digit-0 histograms, built by the indexer epilogue
-  uint32_t* ctl;       // [64]: [0] barrier arrivals, [1] exits
+  uint32_t* ctl;       // [64]: [0] barrier arrivals, [1] exits, [2] attention tickets, [3] attention units done
   // [batch]: (CTAs done with the row << 48) | (blocks appended << 32) | candidate-list length
   unsigned long long* row_state;
   uint64_t* list;      // [batch][list_cap] candidate rank keys, one position-ordered block per CTA
   int list_cap;
   uint4* blocks;       // [batch][grid]: the row's i-th appended block {list base, length, CTA rank, -}
+  // [batch]: 1 once a row of more than k keys has its top-k written (released by
+  // its finisher; read by the fused attention); the grid's last CTA clears it
+  uint32_t* ready;
 };
 
-// Workspace: hist | ctl | row_state | list | blocks.  Everything before the
-// list must be zero before the first launch; every completed launch leaves it
-// zero again (list and blocks need no clearing).
+// Workspace: hist | ctl | row_state | ready | list | blocks.  Everything before
+// the list must be zero before the first launch; every completed launch leaves
+// it zero again (list and blocks need no clearing).
 struct SelectLayout {
-  size_t hist, ctl, state, list, blocks, total;
+  size_t hist, ctl, state, ready, list, blocks, total;
   int64_t cap;
   __host__ __device__ SelectLayout(int64_t batch, int64_t k, int64_t grid) {
     cap = (kSelBinCap + k + 1) & ~int64_t(1);
     hist = 0;
     ctl = hist + size_t(batch) * kSelBins * 4;
     state = ctl + 256;
-    list = state + ((size_t(batch) * 8 + 255) / 256) * 256;
+    ready = state + ((size_t(batch) * 8 + 255) / 256) * 256;
+    list = ready + ((size_t(batch) * 4 + 255) / 256) * 256;
     blocks = list + size_t(batch) * size_t(cap) * 8;
     total = blocks + size_t(batch) * size_t(grid) * 16;
   }

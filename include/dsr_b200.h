@@ -303,6 +303,12 @@ int dsr_lse_combine(const float* part_o, const float* part_m, const float* part_
  * that must start at zero cleared again); calls sharing it must not overlap. */
 size_t dsr_decode_workspace_bytes(int64_t batch, int64_t max_visible, int64_t heads,
                                   int64_t k);
+/* Kernels one dsr_decode_step (or _ring) call enqueues for this shape on the
+ * current device: 1 when every attention tile unit (tile, sequence, head group)
+ * gets a CTA of its own, so the attention and the combine run inside the
+ * cooperative indexer launch after the selection; else 3 (indexer with the
+ * selection, sparse MLA, combine). */
+int dsr_decode_step_launches(int64_t batch, int64_t heads, int64_t idx_heads, int64_t k);
 int dsr_decode_step(const float* idx_q, const float* idx_w, int64_t idx_heads,
                     const uint16_t* index_pool, const float* q, const uint16_t* kv_pool,
                     int64_t heads, int64_t pool_blocks, const int32_t* block_table,

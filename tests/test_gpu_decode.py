@@ -144,13 +144,18 @@ def test_decode_step_multiwave_batch(cuda):
     run_step_and_check(cfg, lengths=[300, 2047, 2048, 2049, 4000, 5100, 6000, 6500, 7000, 8191, 8192, 9000])
 
 
-def test_decode_step_ties_empty_rows_and_short_rows(cuda):
+@pytest.mark.parametrize("heads", [64, 16])
+def test_decode_step_ties_empty_rows_and_short_rows(cuda, heads):
     """The fused selection's paths in one batch: a row whose keys repeat 16 patterns
     (heavy ties, threshold bin within the parallel path), a row of 200,000 keys with
     one repeated pattern (every score equal: the threshold bin overflows and the
     row's first CTA resolves it alone; the lowest ids win), a row shorter than k
-    (every key taken), an empty row (all padding) and an ordinary row."""
-    cfg = small_config("cfg3", batch=5, seed=38)
+    (every key taken), an empty row (all padding) and an ordinary row.  With 64
+    heads the attention runs as separate kernels (340 tile units); with 16 heads
+    (85 units) inside the indexer launch, where each row's tiles wait for that
+    row's ids (rows of at most k keys: the grid barrier; longer rows: the
+    finisher's ready flag)."""
+    cfg = small_config("cfg3", batch=5, seed=38, heads=heads)
     lengths = [9000, 200000, 1500, 0, 30000]
     inp, _ = make_decode_inputs(cfg, lengths=[max(n, 1) for n in lengths])
     inp["visible"] = torch.tensor(lengths, dtype=torch.int32, device="cuda")
@@ -174,11 +179,13 @@ def test_decode_step_ties_empty_rows_and_short_rows(cuda):
     assert np.all(t[3] == -1)
 
 
-def test_decode_step_repeated_calls_reuse_the_workspace(cuda):
-    """The fused selection leaves its workspace zeroed: the same workspace serves
-    three calls in a row (different batches and lengths) with the same results as
-    fresh workspaces."""
-    cfg = small_config("cfg3", batch=3, seed=39)
+@pytest.mark.parametrize("heads", [64, 16])
+def test_decode_step_repeated_calls_reuse_the_workspace(cuda, heads):
+    """The fused selection leaves its workspace zeroed (counters, histograms, row
+    states and ready flags): the same workspace serves three calls in a row with
+    the same results as fresh workspaces, with the attention in separate kernels
+    (64 heads) and in the indexer launch (16 heads)."""
+    cfg = small_config("cfg3", batch=3, seed=39, heads=heads)
     inp, lengths = make_decode_inputs(cfg, lengths=[40000, 2500, 70000])
     b, h, k = 3, cfg.heads, cfg.topk
     lib = _native.library()
