@@ -1,7 +1,7 @@
 """Decode-step benchmark of the B200 attention hot path (indexer -> top-k -> sparse MLA).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
-    python bench.py --profile cfg2|cfg5 [B]|prefill Q C|topk-rows R C [--steps S]
+    python bench.py --profile cfg2|cfg5 [B]|mla-cfg2|prefill Q C|topk-rows R C [--steps S]
 
 Every N reports one workload: batch 4, context 1,048,576 per
 sequence, 64 index heads, top-k 2048, 64 MLA heads over 576-wide rows, SWA 128.
@@ -53,10 +53,10 @@ def kernels_per_step(batch, heads, idx_heads, k):
     return int(_native.library().dsr_decode_step_launches(batch, heads, idx_heads, k))
 
 # DRAM bytes per launch of the indexer, read from ncu captures of the same
-# kernel (dram__bytes_read.sum + dram__bytes_write.sum; profiles/indexer_decode_*.md)
-# ncu DRAM bytes (read + write) per indexer launch (profiles/indexer_decode_cfg2.md):
-# config 2 captured directly; config 5 from a one-sequence capture x 4 sequences
-INDEXER_TRAFFIC = {"cfg2": 33875968, "cfg5": 1115352064}
+# kernel (dram__bytes_read.sum + dram__bytes_write.sum; profiles/indexer_decode_cfg2.md):
+# config 2 from a capture of the scores + top-k launch; config 5 from a
+# one-sequence capture of the step's launch x 4 sequences
+INDEXER_TRAFFIC = {"cfg2": 33875968, "cfg5": 1113096192}
 
 
 # --------------------------------------------------------------------------- utils
@@ -750,6 +750,18 @@ def run_profile(args):
             runner.step(0)
         err = runner.err
         label = f"{args.steps} decode steps of {cfg.name}"
+    elif what == "mla-cfg2":
+        # the standalone sparse MLA + combine (the path of batches whose tiles
+        # exceed one per SM, and of the sharded partials) at the config-2 shape,
+        # over the top-k one decode step selected
+        cfg = CONFIGS["cfg2"]
+        inp, lengths = make_decode_inputs(cfg, device=dev, gen_device="cuda")
+        runner = DecodeRunner(inp, lengths, cfg, 1, 1)
+        runner.step(0)
+        for _ in range(args.steps):
+            runner.mla_only(0)
+        err = runner.err
+        label = f"{args.steps} standalone sparse MLA launches at the config-2 shape"
     elif what == "prefill":
         queries, context = extra
         inp, _ = make_decode_inputs(small_config("cfg2"), device=dev, gen_device="cuda", lengths=[context])
@@ -801,7 +813,7 @@ def main(argv=None):
     parser.add_argument("--no-prefill", action="store_true", help="skip the config-4 prefill indexer leg")
     parser.add_argument("--no-batched", action="store_true", help="skip the config-3 batched decode leg")
     parser.add_argument("--profile", nargs="+", metavar="WORKLOAD",
-                        help="cfg1|cfg2|cfg3|cfg5, `prefill QUERIES CONTEXT` or `topk-rows ROWS CONTEXT`: "
+                        help="cfg1|cfg2|cfg3|cfg5 [B], mla-cfg2, `prefill QUERIES CONTEXT` or `topk-rows ROWS CONTEXT`: "
                              "--steps eager launches for a profiler, then exit")
     args = parser.parse_args(argv)
     if args.profile:
