@@ -17,8 +17,9 @@ inline int64_t round_up(int64_t x, int64_t m) { return (x + m - 1) / m * m; }
 extern "C" size_t dsr_decode_workspace_bytes(int64_t batch, int64_t max_visible, int64_t heads,
                                              int64_t k) {
   const int64_t stride = round_up(max_visible > 0 ? max_visible : 1, 64);
-  return round_up(int64_t(dsr::select_workspace_bytes(batch, k)), 256) + size_t(batch) * size_t(stride) * 4 +
-         dsr::mla_query_image_bytes(batch, heads) + dsr::mla_workspace_bytes(batch, heads, k) + 256;
+  return round_up(int64_t(dsr::select_workspace_bytes(batch, k)), 256) + dsr::select_group_bytes(batch, stride) +
+         size_t(batch) * size_t(stride) * 4 + dsr::mla_query_image_bytes(batch, heads) +
+         dsr::mla_workspace_bytes(batch, heads, k) + 256;
 }
 
 namespace dsr {
@@ -43,11 +44,12 @@ int decode_step(const float* idx_q, const float* idx_w, int64_t idx_heads, const
   DSR_REQUIRE((reinterpret_cast<uintptr_t>(workspace) & 255u) == 0,
               "decode_step: workspace must be 256-byte aligned");
   const int64_t stride = round_up(max_visible, 64);
-  // [selection state (zero between calls) | scores | MLA query image | MLA partials]
+  // [selection state (zero between calls) | group maxima | scores | MLA query image | MLA partials]
   uint8_t* sel_ws = static_cast<uint8_t*>(workspace);
   const size_t sel_bytes = size_t(round_up(int64_t(select_workspace_bytes(batch, k)), 256));
-  uint8_t* ws = sel_ws + sel_bytes;
-  workspace_bytes -= sel_bytes;
+  const size_t group_bytes = select_group_bytes(batch, stride);
+  uint8_t* ws = sel_ws + sel_bytes + group_bytes;
+  workspace_bytes -= sel_bytes + group_bytes;
   float* scores = scores_out != nullptr ? scores_out : reinterpret_cast<float*>(ws);
   uint16_t* q_img = reinterpret_cast<uint16_t*>(ws + size_t(batch) * stride * 4);
   uint8_t* mla_ws = ws + size_t(batch) * stride * 4 + mla_query_image_bytes(batch, heads);
@@ -57,6 +59,8 @@ int decode_step(const float* idx_q, const float* idx_w, int64_t idx_heads, const
   SelectArgs sel;
   int rc = select_args(&sel, sel_ws, batch, k, 0, topk_out, nullptr);
   if (rc != DSR_OK) return rc;
+  sel.gmax = reinterpret_cast<uint16_t*>(sel_ws + sel_bytes);
+  sel.gstride = select_group_stride(stride);
   // When every attention tile unit gets a CTA of its own, one cooperative launch
   // does the whole step: scores, exact top-k, attention tiles and combine.
   // Otherwise the indexer launch scores, selects and converts the MLA query into
@@ -132,8 +136,8 @@ extern "C" int dsr_decode_step_ring(const float* idx_q, const float* idx_w, int6
 // decode, and the dense TiledIndexer.select of index_selection.py:79-124).
 extern "C" size_t dsr_indexer_topk_workspace_bytes(int64_t batch, int64_t max_visible) {
   const int64_t stride = round_up(max_visible > 0 ? max_visible : 1, 64);
-  return round_up(int64_t(dsr::select_workspace_bytes(batch, 8192)), 256) + size_t(batch) * size_t(stride) * 4 +
-         256;
+  return round_up(int64_t(dsr::select_workspace_bytes(batch, 8192)), 256) + dsr::select_group_bytes(batch, stride) +
+         size_t(batch) * size_t(stride) * 4 + 256;
 }
 
 extern "C" int dsr_indexer_topk_decode(const float* idx_q, const float* idx_w, int64_t idx_heads,
@@ -158,9 +162,12 @@ extern "C" int dsr_indexer_topk_decode(const float* idx_q, const float* idx_w, i
   DSR_REQUIRE(id_base >= 0 && id_base + max_visible < (int64_t(1) << 31) - 1,
               "indexer_topk: id_base %lld + visible keys exceed int32 ids", (long long)id_base);
   const int64_t stride = round_up(max_visible, 64);
+  // [selection state (zero between calls) | group maxima | scores]
   uint8_t* sel_ws = static_cast<uint8_t*>(workspace);
   const size_t sel_bytes = size_t(round_up(int64_t(select_workspace_bytes(batch, 8192)), 256));
-  float* scores = scores_out != nullptr ? scores_out : reinterpret_cast<float*>(sel_ws + sel_bytes);
+  const size_t group_bytes = select_group_bytes(batch, stride);
+  float* scores =
+      scores_out != nullptr ? scores_out : reinterpret_cast<float*>(sel_ws + sel_bytes + group_bytes);
   const cudaStream_t s = as_stream(stream);
   PoolAddr pa;
   int rc = paged_addr(&pa, block_table, table_stride, pool_blocks, "indexer_topk");
@@ -168,6 +175,8 @@ extern "C" int dsr_indexer_topk_decode(const float* idx_q, const float* idx_w, i
   SelectArgs sel;
   rc = select_args(&sel, sel_ws, batch, k, id_base, out_ids, out_scores);
   if (rc != DSR_OK) return rc;
+  sel.gmax = reinterpret_cast<uint16_t*>(sel_ws + sel_bytes);
+  sel.gstride = select_group_stride(stride);
   return launch_indexer_decode(idx_q, idx_w, index_pool, pa, visible, scores, stride, err, batch, idx_heads, s,
                                false, nullptr, nullptr, 0, nullptr, &sel);
 }

@@ -115,6 +115,12 @@ size_t select_workspace_bytes(int64_t batch, int64_t k);
 // Binds a SelectArgs to a workspace of select_workspace_bytes(batch, k).
 int select_args(SelectArgs* a, void* workspace, int64_t batch, int64_t k, int64_t id_base, int32_t* out_ids,
                 float* out_scores);
+// Bytes of the per-group maxima (SelectArgs::gmax) for rows of score_stride
+// scores, and their row pitch in groups.
+inline int64_t select_group_stride(int64_t score_stride) { return 4 * (score_stride / 128 + 2); }
+inline size_t select_group_bytes(int64_t batch, int64_t score_stride) {
+  return ((size_t(batch) * size_t(select_group_stride(score_stride)) * 2 + 255) / 256) * 256;
+}
 int launch_indexer_prefill(const float* q, const float* weights, const uint16_t* index_pool,
                            int64_t pool_blocks, const int32_t* block_table, int64_t table_stride,
                            const int32_t* visible, float* scores, int64_t score_stride, int32_t* err,

@@ -425,19 +425,35 @@ __device__ void select_phase(const SelectArgs& a, const float* __restrict__ scor
                               : uint32_t(blockIdx.x) -
                                     uint32_t(((uint64_t(prefix[b]) + 1) * gridDim.x - 1) / uint64_t(total));
     if (live) {
-      // the range's scores (aligned float4 groups covering [p_lo, p_hi); the row's
-      // stride is a multiple of 64 floats) and the digit-0 histogram, all in flight
+      // The range's scores in staged slots of 16 bytes.  Full mode: slot q is the
+      // float4 at a0 + 4q of the aligned groups covering [p_lo, p_hi) (the row's
+      // stride is a multiple of 64 floats); it is issued before the threshold is
+      // known, with the histogram.  Group mode (a range of more than one staging
+      // chunk, with the epilogue's group maxima): windows of the range's 32-key
+      // groups; slot q holds float4 q % 9 of the window's (q / 9)-th group whose
+      // largest digit 0 reaches the threshold bin, groups in position order.
       const int a0 = p_lo & ~3;
       const int n4 = (((p_hi + 3) & ~3) - a0) >> 2;
-      const float4* s4 = reinterpret_cast<const float4*>(srow + a0);
-      auto stage_chunk = [&](int i0) {  // staged entry q - i0 = j * T + tid
+      const size_t used = size_t(a.list_cap) * 8 + size_t(nld) * T * 16;
+      const int win = a.gmax == nullptr || work_bytes < used
+                          ? 0
+                          : int(min(size_t(2048), (work_bytes - used) / 8) / T * T);
+      const bool groups = win >= T && n4 > T * nld;
+      uint32_t* gtab = reinterpret_cast<uint32_t*>(work + used);  // [win] group starts, [win] ends
+      auto slot_base = [&](int q) -> int { return groups ? (int(gtab[q / 9]) & ~3) + 4 * (q % 9) : a0 + 4 * q; };
+      auto slot_lo = [&](int q) -> int { return groups ? int(gtab[q / 9]) : p_lo; };
+      auto slot_hi = [&](int q) -> int { return groups ? int(gtab[win + q / 9]) : p_hi; };
+      auto stage_chunk = [&](int i0, int ns) {  // staged slot q - i0 = j * T + tid
 #pragma unroll 1
         for (int j = 0; j < nld; ++j) {
           const int q = i0 + j * T + tid;
-          if (q < n4) cp_async16(smem_u32(stage + j * T + tid), s4 + q);
+          if (q < ns) {
+            const int base = slot_base(q);
+            if (base < slot_hi(q)) cp_async16(smem_u32(stage + j * T + tid), srow + base);
+          }
         }
       };
-      stage_chunk(0);
+      if (!groups) stage_chunk(0, n4);
       async_hist(hist, a.hist + int64_t(b) * kSelBins);
       cp_async_wait_all();
       __syncthreads();
@@ -450,64 +466,99 @@ __device__ void select_phase(const SelectArgs& a, const float* __restrict__ scor
         // monotone; NaN ranks above +inf); bins 0-3 decode to NaN patterns and
         // hold nothing above -inf, so with b0 < 4 every score passes
         const float thr = b0 < 4u ? -CUDART_INF_F : key_score(b0 << 21);
-        // per staged chunk: every thread tests a run of consecutive float4 groups
-        // (an odd count: conflict-free 16-byte reads), one block scan places its
+        // per staged chunk: every thread tests a run of consecutive slots (an odd
+        // count: conflict-free 16-byte reads), one block scan places its
         // candidates, so the block comes out in position order
         uint32_t nbuf = 0;
+        const int ta = max(t_lo, prefix[b]) - prefix[b], tb = min(t_hi, prefix[b + 1]) - prefix[b];
+        const int g_end = groups ? 4 * tb : 1;
 #pragma unroll 1
-        for (int i0 = 0; i0 < n4; i0 += T * nld) {
-          const int cn4 = min(T * nld, n4 - i0);
-          if (i0 > 0) {
-            stage_chunk(i0);
-            cp_async_wait_all();
+        for (int g0 = groups ? 4 * ta : 0; g0 < g_end; g0 += groups ? win : 1) {
+          int ns = n4;
+          if (groups) {
+            // this window's groups that reach the threshold bin: thread tid tests r
+            // consecutive groups, one block scan places them in position order
+            const int g1 = min(g_end, g0 + win), r = (g1 - g0 + T - 1) / T;  // r <= 2048 / T
+            const uint16_t* grow = a.gmax + int64_t(b) * a.gstride;
+            uint32_t pick = 0;
+#pragma unroll 1
+            for (int i = 0; i < r; ++i) {
+              const int g = g0 + r * tid + i;
+              if (g < g1 && uint32_t(__ldcg(grow + g)) >= b0) pick |= 1u << i;
+            }
+            uint32_t nsel;
+            uint32_t slot = sel_excl_scan<T>(uint32_t(__popc(pick)), nsel, scratch);
+#pragma unroll 1
+            for (int i = 0; i < r; ++i)
+              if ((pick >> i) & 1u) {
+                const int g = g0 + r * tid + i;
+                int pos0, valid;
+                int64_t row0;
+                tile_span(pa, b, g >> 2, vis_s[b], run_s[b], pos0, row0, valid);
+                const int gs = pos0 + 32 * (g & 3);
+                gtab[slot] = uint32_t(gs);
+                gtab[win + slot] = uint32_t(max(gs, min(pos0 + valid, gs + 32)));
+                ++slot;
+              }
+            __syncthreads();
+            ns = 9 * int(nsel);
           }
-          __syncthreads();
-          const int m = ((cn4 + T - 1) / T) | 1;
-          const int q0 = min(cn4, tid * m), q1 = min(cn4, q0 + m);
-          uint64_t take = 0;
-          // four groups in flight; most groups have all four scores below the
-          // threshold (NaN compares false and is kept) and need nothing more
 #pragma unroll 1
-          for (int qa = q0; qa < q1; qa += 4) {
-            float4 x4[4];
-#pragma unroll
-            for (int u = 0; u < 4; ++u) x4[u] = stage[min(qa + u, q1 - 1)];
-            uint32_t pass = 0;
-#pragma unroll
-            for (int u = 0; u < 4; ++u)
-              if (qa + u < q1 && !(x4[u].x < thr && x4[u].y < thr && x4[u].z < thr && x4[u].w < thr))
-                pass |= 1u << u;
+          for (int i0 = 0; i0 < ns; i0 += T * nld) {
+            const int cn4 = min(T * nld, ns - i0);
+            if (groups || i0 > 0) {
+              stage_chunk(i0, ns);
+              cp_async_wait_all();
+            }
+            __syncthreads();
+            const int m = ((cn4 + T - 1) / T) | 1;
+            const int q0 = min(cn4, tid * m), q1 = min(cn4, q0 + m);
+            uint64_t take = 0;
+            // four slots in flight; most slots have all four scores below the
+            // threshold (NaN compares false and is kept) and need nothing more
 #pragma unroll 1
-            while (pass != 0u) {
-              const int u = __ffs(pass) - 1;
-              pass &= pass - 1u;
-              const float4 g = u == 0 ? x4[0] : (u == 1 ? x4[1] : (u == 2 ? x4[2] : x4[3]));
-              const int qi = qa + u;
-              const float xs[4] = {g.x, g.y, g.z, g.w};
+            for (int qa = q0; qa < q1; qa += 4) {
+              float4 x4[4];
 #pragma unroll
-              for (int e = 0; e < 4; ++e) {
-                const int p = a0 + 4 * (i0 + qi) + e;
-                if (!(xs[e] >= thr || xs[e] != xs[e]) || p < p_lo || p >= p_hi) continue;
-                const uint32_t uk = sel_rank_u(__float_as_uint(xs[e]));
-                if ((uk >> 21) < b0) continue;
-                take |= 1ull << ((qi - q0) * 4 + e);
+              for (int u = 0; u < 4; ++u) x4[u] = stage[min(qa + u, q1 - 1)];
+              uint32_t pass = 0;
+#pragma unroll
+              for (int u = 0; u < 4; ++u)
+                if (qa + u < q1 && !(x4[u].x < thr && x4[u].y < thr && x4[u].z < thr && x4[u].w < thr))
+                  pass |= 1u << u;
+#pragma unroll 1
+              while (pass != 0u) {
+                const int u = __ffs(pass) - 1;
+                pass &= pass - 1u;
+                const float4 g = u == 0 ? x4[0] : (u == 1 ? x4[1] : (u == 2 ? x4[2] : x4[3]));
+                const int qi = qa + u;
+                const float xs[4] = {g.x, g.y, g.z, g.w};
+                const int base = slot_base(i0 + qi), lo = slot_lo(i0 + qi), hi = slot_hi(i0 + qi);
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                  const int p = base + e;  // slots past a group's end were not copied: p >= hi
+                  if (!(xs[e] >= thr || xs[e] != xs[e]) || p < lo || p >= hi) continue;
+                  const uint32_t uk = sel_rank_u(__float_as_uint(xs[e]));
+                  if ((uk >> 21) < b0) continue;
+                  take |= 1ull << ((qi - q0) * 4 + e);
+                }
               }
             }
-          }
-          uint32_t tot;
-          uint32_t o = nbuf + sel_excl_scan<T>(uint32_t(__popcll(take)), tot, scratch);
+            uint32_t tot;
+            uint32_t o = nbuf + sel_excl_scan<T>(uint32_t(__popcll(take)), tot, scratch);
 #pragma unroll 1
-          while (take != 0ull) {
-            const int bit = __ffsll(take) - 1;
-            take &= take - 1ull;
-            const int qi = q0 + (bit >> 2), e = bit & 3;
-            const float x = reinterpret_cast<const float*>(stage + qi)[e];
-            if (o < uint32_t(a.list_cap))
-              buf[o] = sel_key(sel_rank_u(__float_as_uint(x)), a.id_base + a0 + 4 * (i0 + qi) + e);
-            ++o;
+            while (take != 0ull) {
+              const int bit = __ffsll(take) - 1;
+              take &= take - 1ull;
+              const int qi = q0 + (bit >> 2), e = bit & 3;
+              const float x = reinterpret_cast<const float*>(stage + qi)[e];
+              if (o < uint32_t(a.list_cap))
+                buf[o] = sel_key(sel_rank_u(__float_as_uint(x)), a.id_base + slot_base(i0 + qi) + e);
+              ++o;
+            }
+            nbuf += tot;
+            __syncthreads();  // the chunk is read before the next one is staged
           }
-          nbuf += tot;
-          __syncthreads();  // the chunk is read before the next one is staged
         }
         // the block: one atomic gives its base and arrival number, its record goes under that number
         const uint32_t n = min(nbuf, uint32_t(a.list_cap));
@@ -1110,12 +1161,21 @@ __global__ void __launch_bounds__(kIxThreads, 1)
         const bool mine = row_in_tile < valid;
         if (live && mine && !isfinite(check)) flag(err, DSR_ERR_NONFINITE);
         asm volatile("bar.sync 3, 256;" ::: "memory");
-        if (live && wg == 0 && mine) {
-          score += xch[(s & 1) * 128 + row_in_tile];
-          if (!isfinite(score)) flag(err, DSR_ERR_NONFINITE);
-          scores[int64_t(b) * score_stride + p] = score;
-          // NaN ranks above +inf, as in the top-k kernel's key mapping
-          atomicAdd(&hsm[isnan(score) ? kIxHistBins - 1 : score_key(score) >> 21], 1u);
+        if (wg == 0) {  // warp-uniform
+          uint32_t digit = 0;  // digit 0 of the score's rank key; 0: no key here
+          if (live && mine) {
+            score += xch[(s & 1) * 128 + row_in_tile];
+            if (!isfinite(score)) flag(err, DSR_ERR_NONFINITE);
+            scores[int64_t(b) * score_stride + p] = score;
+            // NaN ranks above +inf, as in the top-k kernel's key mapping
+            digit = isnan(score) ? kIxHistBins - 1 : score_key(score) >> 21;
+            atomicAdd(&hsm[digit], 1u);
+          }
+          // the warp's 32 keys are group (tile, warp & 3) of the row: its largest digit 0
+          if (sel.gmax != nullptr && vis_s[b] > sel.k) {
+            const uint32_t top = __reduce_max_sync(0xffffffffu, digit);
+            if (lane == 0) sel.gmax[int64_t(b) * sel.gstride + int64_t(t - prefix[b]) * 4 + (warp & 3)] = uint16_t(top);
+          }
         }
       }
       flush(b);
@@ -1245,6 +1305,8 @@ int select_args(SelectArgs* a, void* workspace, int64_t batch, int64_t k, int64_
   a->row_state = reinterpret_cast<unsigned long long*>(base + L.state);
   a->blocks = reinterpret_cast<uint4*>(base + L.blocks);
   a->ready = reinterpret_cast<uint32_t*>(base + L.ready);
+  a->gmax = nullptr;  // bound by callers that reserve select_group_bytes()
+  a->gstride = 0;
   a->list = reinterpret_cast<uint64_t*>(base + L.list);
   a->list_cap = int(L.cap);
   return DSR_OK;

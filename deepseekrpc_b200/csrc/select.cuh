@@ -61,6 +61,12 @@ struct SelectArgs {
   // [batch]: 1 once a row of more than k keys has its top-k written (released by
   // its finisher; read by the fused attention); the grid's last CTA clears it
   uint32_t* ready;
+  // [batch][gstride] (nullable): per 32-key group (4 per 128-key tile, tile index
+  // within the row) the largest digit 0 of its scores, 0 for an empty group;
+  // written by the indexer epilogue for rows of more than k keys, so a CTA with a
+  // long range stages only the groups that reach the threshold bin
+  uint16_t* gmax;
+  int64_t gstride;
 };
 
 // Workspace: hist | ctl | row_state | ready | list | blocks.  Everything before
