@@ -162,10 +162,9 @@ __device__ __forceinline__ void list_runs(const uint64_t* lst, uint32_t L, F f) 
 // The row's last CTA for a row without overflow (select.cuh, step 3): L keys in
 // the row's list, its nblk blocks in arrival order (block s starts at the list
 // offset of record s; the offsets ascend), the row held by nctas CTAs.
-//   1. records and the list, both in flight (16-byte async copies);
-//   2. the digit-1 histogram of the list's threshold-bin keys (shared-memory
-//      atomics: cheaper here than global atomics in every CTA), then
-//      K*: the sub-bin (b0, b1) holding it from that histogram; its
+//   1. records, the list and the row's digit-1 histogram, all in flight (16-byte
+//      async copies);
+//   2. K*: the sub-bin (b0, b1) holding it from that histogram; its
 //      lower edge when the whole sub-bin is selected, otherwise the need1-th
 //      largest of its keys (ranked pairwise when few, else by the next
 //      digits).  K* does not depend on the order of the list;
@@ -198,15 +197,10 @@ __device__ void finish_row(const SelectArgs& a, int b, uint32_t L, uint32_t nblk
   uint4 rec = make_uint4(0u, 0u, ~0u, 0u);
   if (uint32_t(tid) < nblk) rec = __ldcg(a.blocks + int64_t(b) * gridDim.x + tid);
   async_keys(arr, lrow, L);
-#pragma unroll 1
-  for (int i = tid; i < kSelBins; i += T) hist[i] = 0u;
+  async_hist(hist, a.hist1 + int64_t(b) * kSelBins);
   cp_async_wait_all();
   __syncthreads();
   // 2.
-  list_runs(arr, L, [&](uint64_t key) {
-    if ((key >> kSelShift[0]) == b0) atomicAdd(&hist[(key >> kSelShift[1]) & uint64_t(kSelBins - 1)], 1u);
-  });
-  __syncthreads();
   const uint32_t need0 = k - above;
   uint32_t above1;
   const uint32_t b1 = sel_find_bin<T>(hist, kSelBins, need0, above1, scratch) & uint32_t(kSelBins - 1);
@@ -563,6 +557,15 @@ __device__ void select_phase(const SelectArgs& a, const float* __restrict__ scor
         // the block: one atomic gives its base and arrival number, its record goes under that number
         const uint32_t n = min(nbuf, uint32_t(a.list_cap));
         nkept = n;
+        // digit 1 of the block's threshold-bin candidates into the row's digit-1
+        // histogram before this CTA counts in: one thread per candidate, so a
+        // thread issues one or two atomics, none of them inside a scan loop
+        uint32_t* h1row = a.hist1 + int64_t(b) * kSelBins;
+#pragma unroll 1
+        for (uint32_t i = tid; i < n; i += T) {
+          const uint64_t key = buf[i];
+          if (uint32_t(key >> kSelShift[0]) == b0) atomicAdd(h1row + ((key >> kSelShift[1]) & uint64_t(kSelBins - 1)), 1u);
+        }
         if (tid == 0 && n != 0u) {
           const unsigned long long old = atomicAdd(state + b, (1ull << 32) | n);
           scratch[40] = uint32_t(old);
@@ -641,7 +644,10 @@ __device__ void select_phase(const SelectArgs& a, const float* __restrict__ scor
     if (tid == 0) asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(a.ready + b), "r"(1u) : "memory");
     // the row's workspace back to zero for the next launch
 #pragma unroll 1
-    for (int i = tid; i < kSelBins; i += T) a.hist[int64_t(b) * kSelBins + i] = 0u;
+    for (int i = tid; i < kSelBins; i += T) {
+      a.hist[int64_t(b) * kSelBins + i] = 0u;
+      a.hist1[int64_t(b) * kSelBins + i] = 0u;
+    }
     if (tid == 0) state[b] = 0ull;
     __syncthreads();
   }
@@ -1301,6 +1307,7 @@ int select_args(SelectArgs* a, void* workspace, int64_t batch, int64_t k, int64_
   a->k = int(k);
   a->id_base = id_base;
   a->hist = reinterpret_cast<uint32_t*>(base + L.hist);
+  a->hist1 = reinterpret_cast<uint32_t*>(base + L.hist1);
   a->ctl = reinterpret_cast<uint32_t*>(base + L.ctl);
   a->row_state = reinterpret_cast<unsigned long long*>(base + L.state);
   a->blocks = reinterpret_cast<uint4*>(base + L.blocks);

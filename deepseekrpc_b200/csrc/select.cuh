@@ -16,12 +16,13 @@
 //   2. every CTA finds each of its rows' threshold bin b0, appends its
 //      candidates (digit 0 >= b0), in position order, to the row's candidate
 //      list as one block (one atomic gives its base and arrival number; a
-//      record {base, length, CTA rank} goes under that number), and counts
-//      itself done with the row (one 64-bit atomic that also returns the list's
-//      length and the number of blocks);
+//      record {base, length, CTA rank} goes under that number), adds the digit 1
+//      of its threshold-bin candidates to the row's digit-1 histogram (one
+//      thread per candidate), and counts itself done with the row (one 64-bit
+//      atomic that also returns the list's length and the number of blocks);
 //   3. the row's last CTA to finish step 2 (no waiting: the others have left the
-//      row) loads the list and the block records (one round trip), counts the
-//      digit 1 of the list's threshold-bin keys, finds K* (the whole sub-bin of
+//      row) loads the list, the block records and the digit-1 histogram (one
+//      round trip), finds K* (the whole sub-bin of
 //      digit 1 selected, or the rank among its few keys), writes the ids (and
 //      scores) of the keys >= K* in position order -- blocks follow their CTAs,
 //      whose ranks follow positions -- and clears the row's workspace.
@@ -52,6 +53,7 @@ struct SelectArgs {
   int k;
   int64_t id_base;     // id of position p = id_base + p
   uint32_t* hist;      // [batch][2048] digit-0 histograms, built by the indexer epilogue
+  uint32_t* hist1;     // [batch][2048] digit-1 histograms of each row's threshold-bin candidates
   uint32_t* ctl;       // [64]: [0] barrier arrivals, [1] exits, [2] attention tickets, [3] attention units done
   // [batch]: (CTAs done with the row << 48) | (blocks appended << 32) | candidate-list length
   unsigned long long* row_state;
@@ -69,16 +71,17 @@ struct SelectArgs {
   int64_t gstride;
 };
 
-// Workspace: hist | ctl | row_state | ready | list | blocks.  Everything before
-// the list must be zero before the first launch; every completed launch leaves
-// it zero again (list and blocks need no clearing).
+// Workspace: hist | hist1 | ctl | row_state | ready | list | blocks.  Everything
+// before the list must be zero before the first launch; every completed launch
+// leaves it zero again (list and blocks need no clearing).
 struct SelectLayout {
-  size_t hist, ctl, state, ready, list, blocks, total;
+  size_t hist, hist1, ctl, state, ready, list, blocks, total;
   int64_t cap;
   __host__ __device__ SelectLayout(int64_t batch, int64_t k, int64_t grid) {
     cap = (kSelBinCap + k + 1) & ~int64_t(1);
     hist = 0;
-    ctl = hist + size_t(batch) * kSelBins * 4;
+    hist1 = hist + size_t(batch) * kSelBins * 4;
+    ctl = hist1 + size_t(batch) * kSelBins * 4;
     state = ctl + 256;
     ready = state + ((size_t(batch) * 8 + 255) / 256) * 256;
     list = ready + ((size_t(batch) * 4 + 255) / 256) * 256;
