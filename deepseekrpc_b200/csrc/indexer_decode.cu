@@ -1222,7 +1222,7 @@ int launch_ix(const CUtensorMap& map, const float* q, const float* weights, cons
   cfg.blockDim = dim3(kIxThreads, 1, 1);
   cfg.dynamicSmemBytes = L::kAlloc;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   DSR_REQUIRE(sel.out_ids == nullptr ||
                   size_t(L::kWOff - L::kStagesOff) >= size_t(sel.list_cap) * 8 + size_t(kSelThreads) * 16,
               "indexer decode: k %d leaves no shared memory for the selection", sel.k);
@@ -1232,16 +1232,21 @@ int launch_ix(const CUtensorMap& map, const float* q, const float* weights, cons
   DSR_REQUIRE(fuse.args.units == 0 || (sel.out_ids != nullptr && fuse.args.units <= sm_count() &&
                                        (fuse.args.hg == 16 || fuse.args.hg == 32) && fuse.args.tiles <= 128),
               "indexer decode: invalid fused attention plan");
+  // with the selection: cooperative (its grid barriers need every CTA resident
+  // at once) and, like the plain form, free to start while the preceding kernel
+  // ends: every thread waits (griddepcontrol.wait) before it reads anything a
+  // preceding kernel writes, so only the launch itself overlaps
+  int n = 0;
   if (sel.out_ids != nullptr) {
-    // the selection's grid barriers need every CTA resident at once
-    attr[0].id = cudaLaunchAttributeCooperative;
-    attr[0].val.cooperative = 1;
-  } else {
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[n].id = cudaLaunchAttributeCooperative;
+    attr[n++].val.cooperative = 1;
+  }
+  if (pdl || sel.out_ids != nullptr) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n++].val.programmaticStreamSerializationAllowed = 1;
   }
   cfg.attrs = attr;
-  cfg.numAttrs = (pdl || sel.out_ids != nullptr) ? 1 : 0;
+  cfg.numAttrs = n;
   const cudaError_t e =
       cudaLaunchKernelEx(&cfg, indexer_decode_kernel<H>, map, q, weights, pa, visible, scores, score_stride,
                          err, batch, mla_q, mla_img, mla_heads, sel.out_ids != nullptr ? sel.hist : hist, sel,
