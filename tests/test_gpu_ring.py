@@ -22,7 +22,7 @@ from oracle.append import ERR_NONFINITE, ERR_SCATTER, append_kv_index_ring, ring
 from _helpers import assert_bf16_close, c_decode_step, c_indexer, finish, host, oracle_attention, status
 from deepseekrpc_b200 import _native
 from deepseekrpc_b200._native import call, ptr, stream_handle
-from deepseekrpc_b200.workloads import make_decode_inputs, small_config
+from deepseekrpc_b200.workloads import CONFIGS, make_decode_inputs, small_config
 
 pytestmark = pytest.mark.gpu
 
@@ -150,6 +150,28 @@ def test_ring_decode_step_matches_the_paged_step_and_the_oracle(cuda):
     for b in range(len(lengths)):
         assert torch.equal(scores_r[b, :lengths[b]], scores_p[b, :lengths[b]])
         assert_bf16_close(out_r[b].cpu().numpy(), oracle_attention(h, b, t[b], cfg.scale))
+    assert (out_r - out_p).abs().max().item() < 1e-3
+
+
+def test_ring_decode_step_at_the_million_key_geometry(cuda):
+    """Four ragged sequences near 1,048,576 keys: every CTA's score range spans
+    more than one staging chunk, so the selection stages only the 32-key groups
+    whose maxima reach the threshold bin, and in the wrapped second run those
+    groups start at positions off the 128-key tile grid."""
+    cfg = CONFIGS["cfg5"]
+    lengths = [1048576, 1000003, 917505, 1040001]
+    inp, lengths = make_decode_inputs(cfg, device="cuda", gen_device="cuda", lengths=lengths)
+    r = ring_inputs(inp, lengths)
+    out_p, topk_p, scores_p, code = c_decode_step(inp, cfg.topk, cfg.scale)
+    assert code == 0
+    out_r, topk_r, scores_r, code = c_decode_step_ring(r, cfg.topk, cfg.scale)
+    assert code == 0
+    assert torch.equal(topk_r, topk_p), "the ring step selected other rows"
+    for b, n in enumerate(lengths):
+        assert torch.equal(scores_r[b, :n], scores_p[b, :n]), f"sequence {b}: ring scores differ"
+    t, s = topk_r.cpu().numpy(), scores_r.cpu().numpy()
+    for b, n in enumerate(lengths):
+        assert np.array_equal(t[b], oracle.tiled_topk(s[b, :n], cfg.topk)), f"sequence {b}: top-k differs"
     assert (out_r - out_p).abs().max().item() < 1e-3
 
 
