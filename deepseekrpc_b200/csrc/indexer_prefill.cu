@@ -7,8 +7,12 @@
 // index_selection.py:79-107).  With causal visibility, visible[t] = position + 1.
 //
 // This is a dense contraction: every key tile is shared by all queries that see
-// it, so a CTA contracts one 128-key tile against a GROUP of 128/H queries at
-// once (N = 128 query-head rows), the GEMM shape the decode kernel cannot use.
+// it, so a CTA contracts one 128-key tile against a GROUP of 256/H queries at
+// once (N = 256 query-head rows), the GEMM shape the decode kernel cannot use.
+// N = 256 is the widest single-CTA MMA: per K step it reads 4 KB of keys and
+// 8 KB of queries from shared memory for 128x256x16 products, a third less
+// shared-memory traffic per FLOP than N = 128 (the narrower shape measured
+// 0.44 of the bf16 peak with the epilogue removed, 0.55 with N = 256 planned).
 //   warp 0      TMA producer: 128-key tiles (two 64-key pool blocks, 128-byte swizzle)
 //   warp 1      TMEM allocator + single-thread tcgen05.mma issuer
 //   warps 2..9  epilogue: two warpgroups, each owning half of the group's queries:
@@ -26,18 +30,18 @@ namespace dsr {
 namespace {
 
 constexpr int kPfTile = 128;                  // keys per tile
-constexpr int kPfStages = 4;
+constexpr int kPfStages = 3;
 constexpr int kPfStageBytes = kPfTile * 256;  // 128 keys x 128 bf16
 constexpr int kPfThreads = 320;
-constexpr int kPfAcc = 4;                     // TMEM accumulators in flight
-constexpr int kPfN = 128;                     // query-head rows per group
-constexpr int kPfMaxGroups = 1024;            // per launch
+constexpr int kPfAcc = 2;                     // TMEM accumulators in flight (2 x 256 columns)
+constexpr int kPfN = 256;                     // query-head rows per group (the MMA's N)
+constexpr int kPfMaxGroups = 96;              // per launch (the group tables share the last KB of smem)
 
 template <int H>
 struct PfLayout {
   static constexpr int QB = kPfN / H;                    // queries per group
   static constexpr int kStagesOff = 0;
-  static constexpr int kQOff = kPfStages * kPfStageBytes;  // [2 halves][256 rows: hi, lo][128 B]
+  static constexpr int kQOff = kPfStages * kPfStageBytes;  // [2 halves][2 * kPfN rows: hi, lo][128 B]
   static constexpr int kQBytes = 2 * 2 * kPfN * 128;
   static constexpr int kWOff = kQOff + kQBytes;            // weights [kPfN] f32
   static constexpr int kBarOff = kWOff + kPfN * 4;
@@ -48,6 +52,8 @@ struct PfLayout {
   static constexpr int kBytes = kGVisOff + kPfMaxGroups * 4;
   static constexpr int kAlloc = kBytes + 1024;  // slack for 1024-byte alignment
   static constexpr uint32_t kTmemCols = kPfAcc * kPfN;  // 512
+  static_assert(kAlloc <= 232448, "prefill CTA exceeds 227 KB of shared memory");
+  static_assert(kTmemCols <= 512, "prefill accumulators exceed TMEM");
 };
 
 __device__ __forceinline__ int find_group(const int* prefix, int groups, int t) {
@@ -248,20 +254,25 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         uint8_t* qs = smem + L::kQOff;
         const int t0 = gg * QB;
         constexpr int kPer = kPfN * 32 / 256;  // float4 per thread
-        float4 xv[kPer];
+        constexpr int kBatch = 16;             // loads in flight per thread
+        static_assert(kPer % kBatch == 0, "query staging batches");
         uint32_t lo_any = 0;
+#pragma unroll 1
+        for (int j0 = 0; j0 < kPer; j0 += kBatch) {
+        float4 xv[kBatch];
 #pragma unroll
-        for (int j = 0; j < kPer; ++j) {
-          const int i = et + j * 256;           // float4 index in the group's [QB*H][128]
+        for (int jj = 0; jj < kBatch; ++jj) {
+          const int i = et + (j0 + jj) * 256;   // float4 index in the group's [QB*H][128]
           const int t = t0 + (i >> 5) / H;      // query of this float4
-          xv[j] = t < queries ? __ldg(reinterpret_cast<const float4*>(q + int64_t(t0) * H * 128) + i)
-                              : make_float4(0.f, 0.f, 0.f, 0.f);
+          xv[jj] = t < queries ? __ldg(reinterpret_cast<const float4*>(q + int64_t(t0) * H * 128) + i)
+                               : make_float4(0.f, 0.f, 0.f, 0.f);
         }
 #pragma unroll
-        for (int j = 0; j < kPer && live; ++j) {
+        for (int jj = 0; jj < kBatch && live; ++jj) {
+          const int j = j0 + jj;
           const int i = et + j * 256;
           const int n = i >> 5, d = (i & 31) * 4;  // query-head row, column
-          const float xs[4] = {xv[j].x, xv[j].y, xv[j].z, xv[j].w};
+          const float xs[4] = {xv[jj].x, xv[jj].y, xv[jj].z, xv[jj].w};
           uint16_t hi[4], lo[4];
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
@@ -275,6 +286,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
           *reinterpret_cast<uint2*>(base + sw128_offset(kPfN + n, d & 63)) =
               make_uint2(lo[0] | (uint32_t(lo[1]) << 16), lo[2] | (uint32_t(lo[3]) << 16));
           lo_any |= (lo[0] | lo[1] | lo[2] | lo[3]) & 0x7fffu;
+        }
         }
         if (et < kPfN) {
           const int t = t0 + et / H;
