@@ -11,8 +11,8 @@
 // once (N = 256 query-head rows), the GEMM shape the decode kernel cannot use.
 // N = 256 is the widest single-CTA MMA: per K step it reads 4 KB of keys and
 // 8 KB of queries from shared memory for 128x256x16 products, a third less
-// shared-memory traffic per FLOP than N = 128 (the narrower shape measured
-// 0.44 of the bf16 peak with the epilogue removed, 0.55 with N = 256 planned).
+// shared-memory traffic per FLOP than N = 128, and half the key-tile loads
+// (config 4 on a B200: 24.5 ms at N = 128, 19.5 ms at N = 256).
 //   warp 0      TMA producer: 128-key tiles (two 64-key pool blocks, 128-byte swizzle)
 //   warp 1      TMEM allocator + single-thread tcgen05.mma issuer
 //   warps 2..9  epilogue: two warpgroups, each owning half of the group's queries:
