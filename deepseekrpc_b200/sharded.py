@@ -359,10 +359,10 @@ def _timed_steps(fn, steps, stream, dev, group=None) -> float:
     return float(ms.item())
 
 
-# kernels of this library launched per sharded step: indexer, local top-k,
-# list exchange, merge, MLA partial (tiles + in-shard combine), partial
-# exchange, cross-shard combine
-LAUNCHES_PER_STEP = 8
+# kernels of this library launched per sharded step: indexer with its local
+# top-k (one cooperative launch), list exchange, merge, MLA partial (tiles +
+# in-shard combine), partial exchange, cross-shard combine
+LAUNCHES_PER_STEP = 7
 
 
 def replicas_for_cold_l2(per_rank_bytes: int, device) -> int:
@@ -419,6 +419,49 @@ def parity_against_single_gpu(cfg, lengths, ids, out, device, seq: int = 0, grou
     return {"parity_ok": bool(ok.item()), "sequence": seq, "topk_identical": ids_ok,
             "out_max_abs": max_abs, "out_mean_abs": mean_abs,
             "against": "dsr_decode_step of the same sequence on one GPU (same seeded rows)"}
+
+
+PHASES = ("indexer_topk", "exchange_lists", "merge", "mla_partial", "exchange_partials", "combine")
+
+
+def phase_breakdown(dec: "ShardedDecoder", replicas, stream, dev, steps: int = 20) -> dict:
+    """What each launch of a step adds (PHASES order), the way the benchmark runs
+    it: for n = 1..6 the first n launches of every step captured as CUDA graphs
+    (one step per pool replica, all ranks together), timed over `steps` replays
+    like the step itself (max over ranks); a phase's cost is the growth of that
+    time when it joins.  An exchange's cost includes waiting for the slowest
+    peer."""
+    R = len(replicas)
+
+    def prefix(n):
+        def one(inp):
+            lists = dec.select_local(inp["idx_q"], inp["idx_w"], inp["index_pool"], inp["block_table"], stream)
+            if n >= 2:
+                gathered = dec._gather(0, lists, None, stream)
+            if n >= 3:
+                dec.merge(gathered, stream)
+            if n >= 4:
+                partial = dec.attend_local(inp["q"], inp["kv_pool"], inp["block_table"], inp["swa"], stream)
+            if n >= 5:
+                gathered = dec._gather(1, partial, None, stream)
+            if n >= 6:
+                dec.combine(gathered, stream)
+        return lambda: [one(replicas[i]) for i in range(R)]
+
+    cumulative = []
+    for n in range(1, len(PHASES) + 1):
+        fn = prefix(n)
+        with torch.cuda.stream(stream):
+            fn()
+        graph = _capture(fn, stream)
+        run = (lambda i: graph.replay()) if graph is not None else (lambda i: fn())
+        cumulative.append(_timed_steps(run, steps, stream, dev) / R * 1e3)
+        graph = None
+    added = [cumulative[0]] + [cumulative[i] - cumulative[i - 1] for i in range(1, len(PHASES))]
+    return {"note": "us per step of CUDA graphs holding the first n launches of every step, n = 1..6; "
+                    "each phase = the growth when it joins; max over ranks",
+            "cumulative": [round(x, 2) for x in cumulative],
+            **{name: round(x, 2) for name, x in zip(PHASES, added)}}
 
 
 def bench_main(args, metric: str, config: dict, data: str) -> None:
@@ -524,6 +567,7 @@ def bench_main(args, metric: str, config: dict, data: str) -> None:
         assert int(dec.err.item()) == 0 and dec.exchange_status() == 0
         assert torch.equal(h_out, dec.out.cpu()), "e2e output differs from the device-resident run"
 
+        phases = phase_breakdown(dec, replicas, stream, dev)
         parity = parity_against_single_gpu(cfg, lengths, dec.ids, dec.out, dev)
         graph = tail = e2e_graph = None  # graphs holding exchange work go before the process group
         if rank == 0:
@@ -538,7 +582,7 @@ def bench_main(args, metric: str, config: dict, data: str) -> None:
                         "h2d_bytes_per_step": world * h_in.numel() * 4,
                         "d2h_bytes_per_step": world * h_out.numel() * 4},
                 "gpu_launches": LAUNCHES_PER_STEP * K,
-                "parity_ok": parity["parity_ok"], "parity": parity,
+                "parity_ok": parity["parity_ok"], "parity": parity, "phases_us": phases,
                 "exchange": ("NVLink peer stores (dsr_p2p_allgather)" if exchange == "peer" else "NCCL all_gather"),
                 "replicas": R,
                 "l2": f"{R} pool replica(s) per rank rotated, {R * total_bytes // world / 1e6:.0f} MB per rotation "
