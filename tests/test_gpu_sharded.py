@@ -14,7 +14,7 @@ from deepseekrpc_b200.workloads import make_decode_inputs, small_config
 pytestmark = pytest.mark.gpu
 
 
-@pytest.mark.parametrize("world", [2, 3, 4])
+@pytest.mark.parametrize("world", [2, 3, 4, 8])
 def test_sharded_step_matches_unsharded(cuda, world):
     cfg = small_config("cfg2")
     lengths = [20000, 13000, 700]

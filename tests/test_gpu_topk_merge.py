@@ -60,9 +60,10 @@ def merge(lists, k):
 
 
 @pytest.mark.parametrize("world,k", [(1, 2048), (2, 2048), (3, 2048), (4, 2048), (8, 2048), (8, 512),
-                                     (5, 100), (16, 2048), (3, 8192)])
+                                     (5, 100), (5, 1999), (7, 2048), (16, 2048), (3, 8192)])
 def test_merge_matches_the_ranking_rule(cuda, world, k):
-    # world * k up to 16384 takes the one-CTA-per-row merge, above it the staged select
+    # world * k up to 8192 takes the one-CTA-per-row merge, up to 16384 a cluster of
+    # eight CTAs per row (5 x 1999: runs that straddle shards), above it the staged select
     rng = np.random.default_rng(100 + world * 7 + k)
     lists = shard_lists(rng, world, 4, k, 4 * k, short={(0, 1), (world - 1, 2)})
     assert np.array_equal(merge(lists, k), expected(lists, k))
